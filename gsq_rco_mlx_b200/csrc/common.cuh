@@ -1,0 +1,117 @@
+// Shared device helpers of the GSQ / GPTQ / RCO kernels (sm_100a).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gsq_rco_b200.h"
+
+#define GSQ_CHECK_LAUNCH()                                     \
+  do {                                                         \
+    cudaError_t e_ = cudaGetLastError();                       \
+    if (e_ != cudaSuccess) return GSQ_ECUDA;                   \
+  } while (0)
+
+namespace gsq {
+
+// ---------------------------------------------------------------- Philox4x32-10 ---
+// Salmon, Moraes, Dror, Shaw, SC'11. Ten rounds, Weyl key schedule.
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(0xD2511F53u, c.x), lo0 = 0xD2511F53u * c.x;
+    const uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z), lo1 = 0xCD9E8D57u * c.z;
+    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c;
+}
+
+// u = ((x >> 8) + 0.5) 2^-24, clipped to [1e-7, 1 - 1e-7]; g = -log(-log u) in float32.
+__device__ __forceinline__ float gumbel_from_bits(uint32_t x) {
+  float u = __fmul_rn(__fadd_rn((float)(x >> 8), 0.5f), 5.9604644775390625e-08f);
+  u = fminf(fmaxf(u, 1e-7f), 1.0f - 1e-7f);
+  return -logf(-logf(u));
+}
+
+// Gumbel noise of one weight: planes 0..3 from counter block 0, plane 4 from block 1.
+struct NoiseKey {
+  uint32_t k0, k1, step, resample;
+};
+
+__host__ __device__ inline NoiseKey make_noise_key(uint64_t seed, uint32_t linear_id,
+                                                   uint32_t step, uint32_t resample) {
+  NoiseKey k;
+  k.k0 = (uint32_t)(seed & 0xFFFFFFFFull);
+  k.k1 = (uint32_t)(seed >> 32) ^ linear_id;
+  k.step = step;
+  k.resample = resample;
+  return k;
+}
+
+template <int K>
+__device__ __forceinline__ void gumbel_weight(const NoiseKey& nk, uint32_t i, float g[K]) {
+  const uint4 r0 = philox4x32_10(make_uint4(i, 0u, nk.step, nk.resample), nk.k0, nk.k1);
+  g[0] = gumbel_from_bits(r0.x);
+  g[1] = gumbel_from_bits(r0.y);
+  g[2] = gumbel_from_bits(r0.z);
+  g[3] = gumbel_from_bits(r0.w);
+  if (K > 4) {
+    const uint4 r1 = philox4x32_10(make_uint4(i, 1u, nk.step, nk.resample), nk.k0, nk.k1);
+    g[K - 1] = gumbel_from_bits(r1.x);
+  }
+}
+
+// -------------------------------------------------------------------- bf16 split ---
+// x = hi + mid + lo to float32 precision: each term is the bf16 rounding of the residual.
+__device__ __forceinline__ void split3_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& mid,
+                                            __nv_bfloat16& lo) {
+  hi = __float2bfloat16_rn(x);
+  const float r1 = __fsub_rn(x, __bfloat162float(hi));
+  mid = __float2bfloat16_rn(r1);
+  const float r2 = __fsub_rn(r1, __bfloat162float(mid));
+  lo = __float2bfloat16_rn(r2);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_max_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__host__ __device__ inline float grid_value(int bits, int code) {
+  // quant.get_grid: arange(2^b) - 2^(b-1); ternary (bits 1) is [-1, 0, 1]
+  return bits == 1 ? (float)(code - 1) : (float)(code - (1 << (bits - 1)));
+}
+
+inline int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+}  // namespace gsq
+
+namespace gsq {
+template <typename TIn, typename T>
+int gemm_simt(int M, int N, int K, T alpha, const TIn* A, int64_t sam, int64_t sak, const TIn* B,
+              int64_t sbk, int64_t sbn, T beta, T* C, int64_t ldc, int tri, cudaStream_t st);
+}  // namespace gsq

@@ -1,0 +1,158 @@
+/* gsq_rco_b200.h: C ABI of the B200 (sm_100a) kernels behind the GSQ / GPTQ / RCO hot path.
+ *
+ * The reference (egesabanci/gsq-rco-mlx) is pure Python: its "boundary" is its module API.
+ * Each entry point below replaces the reference function cited beside it; the Python
+ * package gsq_rco_mlx_b200 binds them through ctypes and keeps the reference's names,
+ * argument meaning and error behaviour.
+ *
+ * Conventions
+ *   - Every pointer is DEVICE memory unless stated otherwise; sizes are element counts.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Calls are asynchronous.
+ *   - Return value: GSQ_OK (0) or a nonzero status; a bad argument never launches a kernel.
+ *     Kernels never trap: device-side failures (e.g. a non-positive-definite Hessian) are
+ *     reported through a device `info` word that the caller reads back.
+ *   - Row-major everywhere. GSQ logits and their momentum are plane-major [K][d]
+ *     (K = 5 local-shift candidates for 3..7 bits, K = 4 grid values for 2 bits),
+ *     d = out_f * in_f, weight index i = row * in_f + col. Group scales are [out_f][G],
+ *     G = ceil(in_f / group_size).
+ */
+#ifndef GSQ_RCO_B200_H
+#define GSQ_RCO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  GSQ_OK = 0,
+  GSQ_EINVAL = 1,   /* bad argument or size */
+  GSQ_ECUDA = 2,    /* CUDA launch / runtime error */
+  GSQ_ETIMEOUT = 3, /* a bounded device wait gave up */
+  GSQ_ENOTSUP = 4   /* valid request that this build does not implement */
+};
+
+/* ABI revision of this header; bumps on any signature change. */
+int gsq_abi_version(void);
+/* Static, human-readable text of a status code. */
+const char *gsq_status_string(int status);
+
+/* ------------------------------------------------------------------ GSQ ---------- */
+
+/* Soft weight of one Gumbel-softmax draw:
+ *   p = softmax((kappa * l + g) / tau) over the K candidates, c = sum_k p_k C_k,
+ *   w_bar[o, i] = scales[o, i / group_size] * c,  out = w_bar - w_ref (w_ref may be NULL).
+ * C_k = grid[clip(j0 + k - 2)] (bits 3..7) or grid[k] (bits 2). Gumbel g comes from `noise`
+ * ([K][d] float32, host-supplied) or, if noise == NULL, from Philox4x32-10 with
+ * key (seed, linear_id) and counter (i, block, step, resample).
+ * Outputs (any may be NULL): w_out float32 [out_f][in_f]; w_hi / w_mid / w_lo bf16 [out_f][in_f]
+ * with out == hi + mid + lo to float32 precision.
+ * Replaces: src/gsq_rco/gsq/staged.py:271-298 (_Linear.soft) with :82-84 (_gs_softmax),
+ * :92-96 (_gumbel), :99-106 (_grid_rows, _shift_rows); the residual of staged.py:327. */
+int gsq_soft_fwd(const float *logits, const uint8_t *j0, const float *scales, const float *noise,
+                 uint64_t seed, uint32_t linear_id, uint32_t step, uint32_t resample,
+                 int out_f, int in_f, int group_size, int bits, float tau, float kappa,
+                 const float *w_ref, float *w_out, void *w_hi, void *w_mid, void *w_lo,
+                 void *stream);
+
+/* Fused soft backward + Lion for one linear. grad_w holds dL/dw_bar of each resample,
+ * [resamples][out_f][in_f]. For each resample the probabilities are recomputed from the same
+ * noise as gsq_soft_fwd (noise [resamples][K][d], or Philox when NULL), and
+ *   u_k = s G C_k,  dL/dl = (kappa / tau) p (u - <p, u>),  dL/ds = sum over the group of G c;
+ * the gradients are summed over resamples and divided by their count, then one Lion step
+ *   m' = b1 m + (1 - b1) g;  p <- p - lr (sign(m') + wd p);  m <- b2 m + (1 - b2) g
+ * updates logits/mom_logits (lr_logits) and scales/mom_scales (lr_scales; 0 freezes them).
+ * The betas and wd are the caller's float64 values: b, 1 - b and wd are each rounded to
+ * float32 once, as MLX does for Python scalars. resamples: 1..8.
+ * Replaces: the MLX autodiff of staged.py:322-329 through :271-298, the resample average of
+ * staged.py:383-390, and lion_update src/gsq_rco/gsq/lion.py:44-56. */
+int gsq_soft_bwd_lion(float *logits, float *mom_logits, const uint8_t *j0, float *scales,
+                      float *mom_scales, const float *grad_w, const float *noise,
+                      uint64_t seed, uint32_t linear_id, uint32_t step, int resamples,
+                      int out_f, int in_f, int group_size, int bits, float tau, float kappa,
+                      float lr_logits, float lr_scales, double wd, double beta1, double beta2,
+                      void *stream);
+
+/* Argmax decode of trained logits to uint8 codes [out_f][in_f] (first maximum wins;
+ * local shift clipped to the grid). Replaces staged.py:300-314 (_Linear.hard_codes) and
+ * src/gsq_rco/gsq/quant.py:75-83 (local_shift_indices). */
+int gsq_harden(const float *logits, const uint8_t *j0, int out_f, int in_f, int bits,
+               uint8_t *codes, void *stream);
+
+/* One Lion step on a flat float32 tensor. Replaces src/gsq_rco/gsq/lion.py:44-56. */
+int gsq_lion_f32(float *param, float *mom, const float *grad, int64_t n, float lr, double wd,
+                 double beta1, double beta2, void *stream);
+
+/* ------------------------------------------------------------- contractions ------ */
+
+/* C[m, n] = alpha * sum_k A(m, k) B(k, n) + beta * C[m, n], float32 CUDA-core GEMM with
+ * arbitrary element strides: A(m, k) = A[m*sam + k*sak], B(k, n) = B[k*sbk + n*sbn].
+ * Replaces the float32 products of staged.py:327 (X (W_bar - W)^T and its MLX backward). */
+int gsq_gemm_f32(int M, int N, int K, float alpha, const float *A, int64_t sam, int64_t sak,
+                 const float *B, int64_t sbk, int64_t sbn, float beta, float *C, int64_t ldc,
+                 void *stream);
+
+/* Same in float64; tri = 1 computes only the lower triangle n <= m of C.
+ * Replaces the float64 products of src/gsq_rco/gsq/gptq.py:98,118,154,182,186. */
+int gsq_gemm_f64(int M, int N, int K, double alpha, const double *A, int64_t sam, int64_t sak,
+                 const double *B, int64_t sbk, int64_t sbn, double beta, double *C, int64_t ldc,
+                 int tri, void *stream);
+
+/* out[0] = sum_i x[i]^2 in float64 (deterministic two-pass). partials: >= 1024 doubles.
+ * Replaces the mean of R^2 in staged.py:328 (the caller divides by the count). */
+int gsq_sumsq_f32(const float *x, int64_t n, double *partials, double *out, void *stream);
+
+/* ------------------------------------------------------------------- GPTQ -------- */
+
+/* Streaming Hessian H <- H * n_prev / (n_prev + m) + 2 / (n_prev + m) X^T X, float64 H
+ * [k][k], float32 rows X [m][k]. Replaces src/gsq_rco/gsq/gptq.py:89-101
+ * (hessian_from_inputs) and src/gsq_rco/gsq/staged.py:143-155 (hessian_add). */
+int hessian_accum(const float *X, int64_t m, int k, double *H, int64_t n_prev, void *stream);
+
+/* Upper factor U of (H + damp * mean(diag H) I)^-1 = U^T U, after the dead-input rule
+ * (H_ii == 0 -> H_ii = 1, flagged in dead[i]). U [n][n] float64 (upper triangle; the strict
+ * lower triangle is zero). workspace: 2*n*n + 64 doubles. info (device int): 0, or j + 1 if the
+ * damped Hessian is not positive definite at column j.
+ * Replaces src/gsq_rco/gsq/gptq.py:143-157 and _tri_inv_lower :104-120. */
+int gptq_factor(const double *H, int n, double damp, double *U, uint8_t *dead,
+                double *workspace, int *info, void *stream);
+
+/* Blocked GPTQ column sweep with signed group scales and lazy block updates, every output
+ * row independent. W float32 [out_f][in_f]; codes uint8 [out_f][in_f]; scales float32
+ * [out_f][G]; Wwork float64 [out_f][in_f] scratch.
+ * Replaces src/gsq_rco/gsq/gptq.py:159-182 with _encode :31-36 and _group_scales :43-51. */
+int gptq_sweep(const float *W, const double *U, const uint8_t *dead, int out_f, int in_f,
+               int bits, int group_size, int block_size, int signed_scale, uint8_t *codes,
+               float *scales, double *Wwork, void *stream);
+
+/* w_q[o, i] = scales[o, i / group_size] * grid[codes[o, i]] (float32).
+ * Replaces src/gsq_rco/gsq/gptq.py:63-73 and src/gsq_rco/rco/database.py:244-256. */
+int gptq_dequant(const uint8_t *codes, const float *scales, int out_f, int in_f, int bits,
+                 int group_size, float *w_q, void *stream);
+
+/* err[0] = 1/2 tr(D H D^T), D = w_q - W (float64). workspace: 2*out_f*in_f + 1024 doubles.
+ * Replaces src/gsq_rco/gsq/gptq.py:184-186. */
+int gptq_err(const float *w_q, const float *W, const double *H, int out_f, int in_f,
+             double *err, double *workspace, void *stream);
+
+/* --------------------------------------------------------------------- RCO -------- */
+
+/* Exact multiple-choice knapsack DP, one CTA per instance (Gumbel sample):
+ * maximise sum_i s[i, k_i] subject to sum_i step[i, k_i] <= budget, float64 values, strict
+ * '>' (lowest option keeps ties), backtrack from the smallest budget reaching the optimum.
+ * scores [n_inst][N][K] float64, step [N][K] int64 (w_i * c_k), choice_ws uint8
+ * [n_inst][N][budget + 1] scratch, z_out int32 [n_inst][N] chosen option per group.
+ * The two DP rows live in shared memory when 2 * (budget + 1) doubles fit (budget <= 13823);
+ * larger budgets use dp_ws float64 [n_inst][2][budget + 1] (may be NULL otherwise).
+ * Replaces src/gsq_rco/rco/manifold.py:304-334 (_mckp_dp). */
+int mckp_dp_f64(const double *scores, const int64_t *step, int n_inst, int N, int K,
+                int64_t budget, uint8_t *choice_ws, double *dp_ws, int32_t *z_out,
+                void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSQ_RCO_B200_H */

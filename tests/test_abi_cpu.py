@@ -1,0 +1,102 @@
+"""CPU checks: the C-ABI library loads and exports every declared symbol; the host-side
+RCO math and validation follow the reference (golden vectors); no GPU needed."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+from gsq_rco_mlx_b200 import _lib
+from gsq_rco_mlx_b200.gsq import quant
+from gsq_rco_mlx_b200.rco import loop, manifold
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLD = os.path.join(ROOT, "tests", "golden")
+
+
+def declared_symbols():
+    names = []
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if fn.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", fn)).read()
+            names += re.findall(r"^(?:int|const char \*)\s*(\w+)\(", text, flags=re.M)
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_symbols()
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(_lib.SIGNATURES) | {"gsq_status_string"} >= set(names)
+    assert lib.gsq_abi_version() == 1
+    assert lib.gsq_status_string(1) == b"invalid argument"
+
+
+def test_bad_arguments_are_rejected_without_launch():
+    """Argument validation happens before any CUDA call (no device needed)."""
+    lib = _lib.load()
+    assert lib.gsq_soft_fwd(None, None, None, None, 0, 0, 0, 0, 4, 4, 64, 3, 1.0, 100.0,
+                            None, None, None, None, None, None) == _lib.GSQ_EINVAL
+    assert lib.gsq_soft_fwd(None, None, None, None, 0, 0, 0, 0, 4, 4, 64, 8, 1.0, 100.0,
+                            None, None, None, None, None, None) == _lib.GSQ_ENOTSUP
+    assert lib.mckp_dp_f64(None, None, 1, 3, 2, 10, None, None, None, None) == _lib.GSQ_EINVAL
+    assert lib.gptq_sweep(None, None, None, 4, 4, 3, 64, 128, 1, None, None, None,
+                          None) == _lib.GSQ_EINVAL
+
+
+def test_product_path_refuses_to_run_without_gpu():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(RuntimeError):
+        _lib.lib()
+
+
+def test_host_grid_and_schedules():
+    z = np.load(os.path.join(GOLD, "gsq.npz"))
+    for b in range(1, 9):
+        assert np.array_equal(quant.get_grid(b), z[f"grid{b}"])
+    assert np.array_equal(np.array([quant.gs_schedules(t, 200) for t in range(200)]), z["sched"])
+    assert np.array_equal(quant.local_shift_values(z["ls_j0"], quant.get_grid(3)), z["ls_C"])
+    assert np.array_equal(quant.local_shift_indices(z["ls_j0"], z["ls_logits"], 8), z["ls_idx"])
+
+
+def test_host_manifold_matches_reference():
+    z = np.load(os.path.join(GOLD, "rco_host.npz"))
+    a, c, w = z["a"], z["costs"], z["w"]
+    np.testing.assert_allclose(manifold.softmax(a), z["softmax"], rtol=1e-15)
+    assert manifold.expected_cost(a, c, w) == pytest.approx(float(z["expected_cost"]), rel=1e-15)
+    np.testing.assert_allclose(manifold.normal_vector(a, c, w), z["normal"], rtol=1e-14, atol=1e-16)
+    np.testing.assert_allclose(manifold.project_tangent(z["g"], z["normal"]), z["proj"],
+                               rtol=1e-13, atol=1e-15)
+    np.testing.assert_array_equal(manifold.retract(a, c, w, budget=52.0), z["retract_B52"])
+    np.testing.assert_array_equal(manifold.retract(z["abig"], z["close"], w, budget=2.15 * 20),
+                                  z["retract_big"])
+    assert np.array_equal(np.array([loop.tau_schedule(t, 10) for t in range(10)]), z["tau"])
+    np.testing.assert_allclose(loop.ste_grad(z["up"], manifold.softmax(a), 0.3), z["ste"],
+                               rtol=1e-14, atol=1e-16)
+    ci, wi, Bi = loop.to_int_grid(c, np.arange(1, 21), 2.5 * 210, ticks=2)
+    assert np.array_equal(ci, z["tig_c"]) and np.array_equal(wi, z["tig_w"]) and Bi == int(z["tig_B"])
+    with pytest.raises(ValueError):
+        manifold.retract(a, c, w, budget=160.5)
+    with pytest.raises(RuntimeError):
+        manifold.retract(a, c, w, budget=52.0, iters=3)
+
+
+def test_integer_weights_and_dp_validation():
+    w, unit = loop.integer_weights(np.array([802816, 114688, 114688, 802816,
+                                             4358144, 4358144, 4358144] * 24))
+    z = np.load(os.path.join(GOLD, "dp.npz"))
+    assert unit == int(z["qwen_unit"]) == 114688
+    assert np.array_equal(w, z["qwen_w_int"])
+    with pytest.raises(ValueError):
+        manifold.dp_knapsack(np.zeros((3, 2)), np.array([2, 3]), np.ones(3, dtype=int), 5)
+    with pytest.raises(ValueError):
+        manifold.dp_knapsack(np.zeros((3, 2)), np.array([2.5, 3.0]), np.ones(3, dtype=int), 9)
+    # K = 2 uniform weights decodes on the host (no GPU needed), as in the reference
+    for n in range(int(z["dp_n"])):
+        s, c, wv, B = z[f"dp{n}_s"], z[f"dp{n}_c"], z[f"dp{n}_w"], int(z[f"dp{n}_B"])
+        if s.shape[1] == 2 and np.all(wv == wv[0]):
+            assert np.array_equal(manifold.dp_knapsack(s, c, wv, B), z[f"dp{n}_z"])
