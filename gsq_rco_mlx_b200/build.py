@@ -44,7 +44,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     LIB_DIR.mkdir(exist_ok=True)
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH, *FLAGS, "-I", str(INCLUDE), "-o", str(tmp),
-           *[str(s) for s in sources()], "-lcuda"]
+           *[str(s) for s in sources()]]
     r = subprocess.run(cmd, capture_output=True, text=True)
     log = LIB_DIR / "build.log"
     log.write_text(r.stdout + r.stderr)

@@ -52,3 +52,86 @@ class SumSq:
         _lib.call("gsq_sumsq_f32", _lib.ptr(x), x.numel(), _lib.ptr(self.partials), _lib.ptr(out),
                   _lib.stream_ptr())
         return out
+
+
+# ------------------------------------------------------------ tensor-core engine ---
+
+import ctypes as _C
+
+
+def pad8(n: int) -> int:
+    """Leading dimension for TMA: rows of a multiple of 16 bytes (8 bf16)."""
+    return (int(n) + 7) // 8 * 8
+
+
+class Terms:
+    """An fp32 matrix held as up to three bf16 terms [rows, ld] (K-major GEMM operand)."""
+
+    def __init__(self, rows, cols, n_terms=3, device=None, ld=None):
+        self.rows, self.cols, self.n = int(rows), int(cols), int(n_terms)
+        self.ld = pad8(cols) if ld is None else int(ld)
+        dev = device or _lib.device()
+        self.t = [torch.zeros(self.rows, self.ld, device=dev, dtype=torch.bfloat16)
+                  for _ in range(self.n)]
+
+    def ptrs(self, n=None):
+        n = self.n if n is None else n
+        arr = (_C.c_void_p * 3)()
+        for i in range(n):
+            arr[i] = self.t[i].data_ptr()
+        return arr
+
+    def value(self):
+        """fp32 reconstruction (tests)."""
+        v = self.t[0][:, :self.cols].float()
+        for t in self.t[1:]:
+            v = v + t[:, :self.cols].float()
+        return v
+
+
+def split_into(x, terms: Terms, transpose=False):
+    """Write fp32 x [r, c] (or x^T) into ``terms``."""
+    _f32(x)
+    r, c = x.shape
+    if transpose:
+        assert (terms.rows, terms.cols) == (c, r)
+    else:
+        assert (terms.rows, terms.cols) == (r, c)
+    p = [terms.t[i] if i < terms.n else None for i in range(3)]
+    _lib.call("gsq_split_bf16", _lib.ptr(x), r, c, c, int(transpose), _lib.ptr(p[0]),
+              _lib.ptr(p[1]), _lib.ptr(p[2]), terms.ld, _lib.stream_ptr())
+    return terms
+
+
+_ERR = {}
+
+
+def err_flag(dev):
+    if dev not in _ERR:
+        _ERR[dev] = torch.zeros(1, device=dev, dtype=torch.int32)
+    return _ERR[dev]
+
+
+def check_err(dev):
+    e = int(err_flag(dev).item())
+    if e:
+        raise _lib.GsqError(f"tensor-core GEMM: bounded wait timed out (code {e})")
+
+
+def gemm_tc(A: Terms, B: Terms, na=None, nb=None, order=2, alpha=1.0, C=None, beta=0.0,
+            c_terms: Terms = None, ct_terms: Terms = None, sq_partial=None):
+    """C = alpha A B^T on tcgen05 with split-bf16 operands (see include/gsq_rco_b200.h)."""
+    na = A.n if na is None else na
+    nb = B.n if nb is None else nb
+    if A.cols != B.cols:
+        raise ValueError(f"inner dims differ: {A.cols} vs {B.cols}")
+    M, N, K = A.rows, B.rows, A.cols
+    dev = A.t[0].device
+    _lib.call("gsq_gemm_tc", M, N, K, A.ptrs(na), na, A.ld, B.ptrs(nb), nb, B.ld, int(order),
+              float(alpha), _lib.ptr(C), N if C is None else C.stride(0), float(beta),
+              None if c_terms is None else c_terms.ptrs(), 0 if c_terms is None else c_terms.n,
+              0 if c_terms is None else c_terms.ld,
+              None if ct_terms is None else ct_terms.ptrs(), 0 if ct_terms is None else ct_terms.n,
+              0 if ct_terms is None else ct_terms.ld, _lib.ptr(sq_partial),
+              _lib.ptr(err_flag(dev)), _lib.stream_ptr())
+    return C

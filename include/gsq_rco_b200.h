@@ -100,6 +100,29 @@ int gsq_gemm_f64(int M, int N, int K, double alpha, const double *A, int64_t sam
                  const double *B, int64_t sbk, int64_t sbn, double beta, double *C, int64_t ldc,
                  int tri, void *stream);
 
+/* Float32-faithful tensor-core GEMM (tcgen05, TMEM accumulator, TMA-fed):
+ *   C[m, n] = alpha * sum_k A(m, k) B(n, k) (+ beta * C[m, n])
+ * A and B arrive as na / nb bf16 terms (A = sum_i A_i), each K-major [M][lda] / [N][ldb]
+ * (lda, ldb multiples of 8, 16-byte aligned bases); the products A_i B_j with i + j <= order
+ * are accumulated in float32 (three terms per side, order 2: float32 operands to 2^-24;
+ * an exactly-bf16 operand needs one term). Epilogue outputs (each optional):
+ *   C float32 [M][ldc];  c_terms: C as ncs bf16 terms [M][ldcs];
+ *   ct_terms: C^T as nct bf16 terms [N][ldct] (the K-major operand of a reduction over m);
+ *   sq_partial: float64 per 128 x 128 tile, the sum of C^2 (ceil(M/128) * ceil(N/128)).
+ * err: device int, nonzero if a bounded wait timed out.
+ * Replaces the float32 matmuls of staged.py:327 and their MLX backward, and the block
+ * matmuls of src/gsq_rco/gsq/e2e.py:132-134,166,170,173 inside the stage losses. */
+int gsq_gemm_tc(int M, int N, int K, const void *const *a_terms, int na, int64_t lda,
+                const void *const *b_terms, int nb, int64_t ldb, int order, float alpha,
+                float *C, int64_t ldc, float beta, void *const *c_terms, int ncs, int64_t ldcs,
+                void *const *ct_terms, int nct, int64_t ldct, double *sq_partial, int *err,
+                void *stream);
+
+/* x float32 [rows][ld_in] -> bf16 terms t0 (+ t1, t2 if non-NULL) with x = t0 + t1 + t2 to
+ * float32 precision; transpose = 1 writes [cols][ld_out]. */
+int gsq_split_bf16(const float *x, int rows, int cols, int64_t ld_in, int transpose, void *t0,
+                   void *t1, void *t2, int64_t ld_out, void *stream);
+
 /* out[0] = sum_i x[i]^2 in float64 (deterministic two-pass). partials: >= 1024 doubles.
  * Replaces the mean of R^2 in staged.py:328 (the caller divides by the count). */
 int gsq_sumsq_f32(const float *x, int64_t n, double *partials, double *out, void *stream);

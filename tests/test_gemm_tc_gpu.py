@@ -1,0 +1,87 @@
+"""Tensor-core split-bf16 GEMM (tcgen05) vs float64 matmul: float32-level accuracy with
+three terms per side, bf16 accuracy with one; epilogue outputs (C, C terms, C^T terms,
+per-tile sum of squares); ragged and padded shapes."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def run(M, N, K, na, nb, seed=0, alpha=1.0, scale_b=1.0):
+    from gsq_rco_mlx_b200.gemm import Terms, check_err, gemm_tc, split_into
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    A = torch.randn(M, K, generator=g, dtype=torch.float64)
+    B = torch.randn(N, K, generator=g, dtype=torch.float64) * scale_b
+    Ad, Bd = A.float().to(DEV), B.float().to(DEV)
+    At, Bt = Terms(M, K, 3), Terms(N, K, 3)
+    split_into(Ad, At)
+    split_into(Bd, Bt)
+    C = torch.empty(M, N, device=DEV)
+    gemm_tc(At, Bt, na=na, nb=nb, alpha=alpha, C=C)
+    torch.cuda.synchronize()
+    check_err(torch.device(DEV))
+    # reference on the same float32-rounded operands, each cut to the terms used
+    Ar = sum(t[:, :K].double() for t in At.t[:na]).cpu()
+    Br = sum(t[:, :K].double() for t in Bt.t[:nb]).cpu()
+    ref = alpha * (Ar @ Br.T)
+    return C.double().cpu(), ref, Ad.double().cpu() @ Bd.double().cpu().T * alpha
+
+
+def test_gemm_tc_single_tile_exact_bf16():
+    """1 term per side, one 128 x 128 x 64 tile: exact bf16 products, fp32 accumulation."""
+    C, ref, _ = run(128, 128, 64, 1, 1)
+    err = (C - ref).abs().max() / ref.abs().max()
+    assert err < 1e-6, err
+
+
+@pytest.mark.parametrize("shape", [(128, 128, 256), (300, 200, 100), (1022, 640, 896),
+                                   (96, 4864, 1022)])
+def test_gemm_tc_fp32_faithful(shape):
+    M, N, K = shape
+    C, ref, full = run(M, N, K, 3, 3, seed=M)
+    scale = full.abs().max()
+    assert (C - full).abs().max() / scale < 2e-6
+    rel = ((C - full).norm() / full.norm()).item()
+    assert rel < 1e-6, rel
+
+
+def test_gemm_tc_epilogue_outputs():
+    from gsq_rco_mlx_b200.gemm import Terms, check_err, gemm_tc, split_into
+    M, N, K = 515, 260, 200
+    torch.manual_seed(0)
+    A = torch.randn(M, K, device=DEV)
+    B = torch.randn(N, K, device=DEV)
+    At, Bt = split_into(A, Terms(M, K)), split_into(B, Terms(N, K))
+    C = torch.empty(M, N, device=DEV)
+    cs, ct = Terms(M, N), Terms(N, M)
+    tiles = ((M + 127) // 128) * ((N + 127) // 128)
+    sq = torch.zeros(tiles, device=DEV, dtype=torch.float64)
+    gemm_tc(At, Bt, alpha=0.5, C=C, c_terms=cs, ct_terms=ct, sq_partial=sq)
+    torch.cuda.synchronize()
+    check_err(torch.device(DEV))
+    ref = 0.5 * (A.double() @ B.double().T)
+    assert ((C.double() - ref).norm() / ref.norm()).item() < 1e-6
+    assert torch.equal(cs.value(), C)
+    assert torch.equal(ct.value(), C.T)
+    assert abs(sq.sum().item() - (C.double() ** 2).sum().item()) <= 1e-9 * (C.double() ** 2).sum().item()
+    # beta accumulation into C
+    C2 = C.clone()
+    gemm_tc(At, Bt, alpha=0.5, C=C2, beta=1.0)
+    torch.cuda.synchronize()
+    assert ((C2.double() - 2 * ref).norm() / ref.norm()).item() < 2e-6
+
+
+def test_gemm_tc_exact_operand_three_products():
+    """An exactly-bf16 A (one term) against a three-term B: float32-level result."""
+    from gsq_rco_mlx_b200.gemm import Terms, gemm_tc, split_into
+    M, N, K = 1022, 384, 896
+    torch.manual_seed(1)
+    A = torch.randn(M, K, device=DEV).bfloat16().float()
+    B = torch.randn(N, K, device=DEV)
+    At, Bt = split_into(A, Terms(M, K, 1)), split_into(B, Terms(N, K))
+    C = torch.empty(M, N, device=DEV)
+    gemm_tc(At, Bt, C=C)
+    ref = A.double() @ B.double().T
+    assert ((C.double() - ref).norm() / ref.norm()).item() < 1e-6
