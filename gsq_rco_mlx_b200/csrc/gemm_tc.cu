@@ -40,39 +40,56 @@ struct GemmParams {
   double* sq_partial;  // [tiles] sum of (alpha acc)^2 per tile
   int* err;
   int stages;
+  int kb_per_chunk;  // k-blocks accumulated in TMEM before promotion to registers
 };
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// TMEM columns: two buffers, each a "big" accumulator (the hi x hi products) and a "small"
+// one (every other product, 2^8 smaller). Tensor-core accumulation into TMEM is not IEEE
+// round-to-nearest; folding each chunk of k-blocks into float32 registers with IEEE adds
+// keeps the error of the 3-term products at the level of a float32 GEMM.
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint64_t full_bar[8];
   __shared__ uint64_t empty_bar[8];
-  __shared__ uint64_t acc_bar;
+  __shared__ uint64_t accf_bar[2];
+  __shared__ uint64_t acce_bar[2];
   __shared__ uint32_t tmem_base;
   __shared__ double red[4];
 
   constexpr uint32_t kTileA = BM * BK * 2;  // bytes of one A term tile
   constexpr uint32_t kTileB = BN * BK * 2;
+  constexpr uint32_t kCols = 4 * BN;        // 2 buffers x (big, small)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_m = blockIdx.y * BM, tile_n = blockIdx.x * BN;
   const int S = p.stages;
   const uint32_t stage_bytes = p.na * kTileA + p.nb * kTileB;
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int num_kb = (p.K + BK - 1) / BK;
+  const int P = p.kb_per_chunk;
+  const int n_chunks = (num_kb + P - 1) / P;
+  const bool has_small = (p.na > 1 || p.nb > 1) && p.order > 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&acc_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf_bar[b], 1);
+      mbar_init(&acce_bar[b], 4);
+    }
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     for (int i = 0; i < p.na; ++i) tma_prefetch_desc(&p.tma_a[i]);
     for (int i = 0; i < p.nb; ++i) tma_prefetch_desc(&p.tma_b[i]);
   }
-  if (warp == 1) tmem_alloc(&tmem_base, BN);
+  if (warp == 1) tmem_alloc(&tmem_base, kCols);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
@@ -97,51 +114,85 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(BM, BN);
       bool ok = true;
-      for (int kb = 0; kb < num_kb && ok; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = (uint32_t)(kb / S) & 1u;
-        if (!mbar_wait(&full_bar[s], ph, p.err, 2)) { ok = false; break; }
+      for (int c = 0; c < n_chunks && ok; ++c) {
+        const int b = c & 1;
+        if (!mbar_wait(&acce_bar[b], ((uint32_t)(c >> 1) & 1u) ^ 1u, p.err, 4)) break;
         fence_after_sync();
-        const uint32_t st = smem_u32(smem + (size_t)s * stage_bytes);
-        for (int i = 0; i < p.na; ++i) {
-          for (int j = 0; j < p.nb; ++j) {
-            if (i + j > p.order) continue;
-            const uint32_t a0 = st + i * kTileA;
-            const uint32_t b0 = st + p.na * kTileA + j * kTileB;
+        const uint32_t big = tmem + (uint32_t)(b * 2 * BN), small = big + BN;
+        bool big_init = false, small_init = false;
+        const int kb_end = min(num_kb, (c + 1) * P);
+        for (int kb = c * P; kb < kb_end; ++kb) {
+          const int s = kb % S;
+          const uint32_t ph = (uint32_t)(kb / S) & 1u;
+          if (!mbar_wait(&full_bar[s], ph, p.err, 2)) { ok = false; break; }
+          fence_after_sync();
+          const uint32_t st = smem_u32(smem + (size_t)s * stage_bytes);
+          for (int i = 0; i < p.na; ++i) {
+            for (int j = 0; j < p.nb; ++j) {
+              if (i + j > p.order) continue;
+              const uint32_t a0 = st + i * kTileA;
+              const uint32_t b0 = st + p.na * kTileA + j * kTileB;
+              const bool to_big = (i + j == 0);
+              const uint32_t d = to_big ? big : small;
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k) {
-              const uint32_t acc = (kb > 0 || i > 0 || j > 0 || k > 0) ? 1u : 0u;
-              umma_bf16(tmem, umma_desc_k_sw128(a0 + k * 32), umma_desc_k_sw128(b0 + k * 32),
-                        idesc, acc);
+              for (int k = 0; k < BK / 16; ++k) {
+                const uint32_t acc = to_big ? (uint32_t)big_init : (uint32_t)small_init;
+                umma_bf16(d, umma_desc_k_sw128(a0 + k * 32), umma_desc_k_sw128(b0 + k * 32),
+                          idesc, acc);
+                if (to_big) big_init = true; else small_init = true;
+              }
             }
           }
+          umma_commit(&empty_bar[s]);
         }
-        umma_commit(&empty_bar[s]);
+        umma_commit(&accf_bar[b]);
       }
-      umma_commit(&acc_bar);
     }
   } else {
-    // epilogue warps 2..5: TMEM lanes 32 * (warp % 4) .. + 31
+    // epilogue warps 2..5: TMEM lanes 32 * (warp % 4) .. + 31, one output row per thread
     const int q = warp & 3;
     const int row = tile_m + q * 32 + lane;
-    // warp-uniform: tcgen05.ld is a warp-collective instruction
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_bar, 0, p.err, 3));
-    fence_after_sync();
-    double sq = 0.0;
-    if (ok) {
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    float acc[BN];
+#pragma unroll
+    for (int t = 0; t < BN; ++t) acc[t] = 0.f;
+    bool ok = true;
+    for (int c = 0; c < n_chunks; ++c) {
+      const int b = c & 1;
+      ok = __all_sync(0xffffffffu, ok && mbar_wait(&accf_bar[b], (uint32_t)(c >> 1) & 1u,
+                                                   p.err, 3));
+      if (!ok) break;
+      fence_after_sync();
+      const uint32_t big = tmem + lane_off + (uint32_t)(b * 2 * BN), small = big + BN;
+#pragma unroll
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-        if (row >= p.M) continue;
+        tmem_ld16(big + (uint32_t)c0, v);
+        if (has_small) {
+          float w[16];
+          tmem_ld16(small + (uint32_t)c0, w);
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const int col = tile_n + c0 + t;
-          if (col >= p.N) break;
-          float x = p.alpha * v[t];
+          for (int t = 0; t < 16; ++t) acc[c0 + t] = __fadd_rn(acc[c0 + t], __fadd_rn(v[t], w[t]));
+        } else {
+#pragma unroll
+          for (int t = 0; t < 16; ++t) acc[c0 + t] = __fadd_rn(acc[c0 + t], v[t]);
+        }
+      }
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce_bar[b]);
+    }
+    double sq = 0.0;
+    if (ok && row < p.M) {
+#pragma unroll
+      for (int t = 0; t < BN; ++t) {
+        const int col = tile_n + t;
+        if (col < p.N) {
+          float x = __fmul_rn(p.alpha, acc[t]);
           if (p.C) {
-            float* c = p.C + (int64_t)row * p.ldc + col;
-            if (p.beta != 0.f) x = fmaf(p.beta, *c, x);
-            *c = x;
+            float* cp = p.C + (int64_t)row * p.ldc + col;
+            if (p.beta != 0.f) x = __fadd_rn(x, __fmul_rn(p.beta, *cp));
+            *cp = x;
           }
           if (p.sq_partial) sq += (double)x * (double)x;
           if (p.ncs > 0 || p.nct > 0) {
@@ -164,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     p.sq_partial[blockIdx.y * gridDim.x + blockIdx.x] = red[0] + red[1] + red[2] + red[3];
   if (warp == 1) {
     fence_after_sync();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, kCols);
   }
 }
 
@@ -210,6 +261,10 @@ static int launch(GemmParams& p, cudaStream_t st) {
   if (S > 8) S = 8;
   if (S < 2) return GSQ_ENOTSUP;
   p.stages = S;
+  int products = 0;
+  for (int i = 0; i < p.na; ++i)
+    for (int j = 0; j < p.nb; ++j) products += (i + j <= p.order);
+  p.kb_per_chunk = products >= 3 ? 1 : (products == 2 ? 2 : 4);
   const size_t smem = (size_t)S * stage_bytes + 1024;
   if (cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem) != cudaSuccess)
