@@ -121,10 +121,9 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
     from gsq_rco_mlx_b200 import _lib
-    from gsq_rco_mlx_b200.gemm import SumSq, mm_nt, mm_tn
     from gsq_rco_mlx_b200.gsq import gptq
     from gsq_rco_mlx_b200.gsq.quant import gs_schedules
-    from gsq_rco_mlx_b200.gsq.staged import SoftLinear
+    from gsq_rco_mlx_b200.gsq.staged import BlockOpts, LinearStep, SoftLinear
 
     rank, world, local = dist_setup(args.gpus)
     _lib.lib()
@@ -137,12 +136,11 @@ def run_ours(args):
     g = gptq.quantize_gptq(Wd, H, 3, 64, device=True)
     lin = SoftLinear("up_proj", 3, g["codes"].cpu().numpy(), g["scales"].cpu().numpy().astype(np.float16),
                      64, seed=rank, linear_id=5)
-    Xs = Xd.view(N_SEQ, T_SEQ, IN_F)[:, 1:]
     rng = np.random.default_rng(1)
     M = MICRO * (T_SEQ - 1)
-    grads = torch.empty(RESAMPLES, OUT_F, IN_F, device=dev)
-    loss = torch.zeros(RESAMPLES, device=dev, dtype=torch.float64)
-    sumsq = SumSq(dev)
+    opts = BlockOpts(resamples=RESAMPLES, micro_batch=MICRO)
+    lstep = LinearStep([lin], M, IN_F, RESAMPLES, x_terms=3)
+    targets = {"up_proj": Wd}
     Xmb = torch.empty(M, IN_F, device=dev)
     Xpin = torch.from_numpy(np.ascontiguousarray(X.reshape(N_SEQ, T_SEQ, IN_F)[:, 1:])).pin_memory()
     loss_host = torch.empty(RESAMPLES, dtype=torch.float64).pin_memory()
@@ -155,22 +153,19 @@ def run_ours(args):
         if host_inputs:
             for j, s in enumerate(idx):
                 Xmb[j * (T_SEQ - 1):(j + 1) * (T_SEQ - 1)].copy_(Xpin[s], non_blocking=True)
+            lstep.stage(Xmb, [0, 1], T_SEQ - 1, T_SEQ - 1, 0)
         else:
-            torch.cat([Xs[int(s)] for s in idx], out=Xmb)
-        for r in range(RESAMPLES):
-            D = lin.soft(tau, kappa, t, r, 77, w_ref=Wd)
-            Rm = mm_nt(Xmb, D)
-            sumsq(Rm, loss[r:r + 1])
-            mm_tn(Rm, Xmb, alpha=2.0 / (M * OUT_F), out=grads[r])
+            lstep.stage(Xd, idx, T_SEQ - 1, T_SEQ, 1)
+        lstep.forward_backward(targets, t, tau, kappa, 77)
         if time_bwd:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-        lin.backward_lion(grads, tau, kappa, t, 77)
+        lstep.update(t, tau, kappa, 77, opts)
         if time_bwd:
             e1.record(stream)
             bwd_events.append((e0, e1))
         if host_inputs:
-            loss_host.copy_(loss, non_blocking=True)
+            loss_host.copy_(lstep.loss, non_blocking=True)
 
     def barrier():
         if world > 1:
@@ -228,7 +223,7 @@ def run_ours(args):
                    "parallelism": f"replicas x{world}", "l2": "per-step working set > L2 (126 MB)"},
         "e2e": {"value": round(world * args.steps / (ms_e2e * 1e-3), 3), "unit": "steps/s",
                 "h2d_bytes_per_step": M * IN_F * 4, "d2h_bytes_per_step": RESAMPLES * 8},
-        "gpu_launches": args.steps * (RESAMPLES * 5 + 1),
+        "gpu_launches": args.steps * (RESAMPLES * 4 + 2),
         "roofline": {"kernel": "soft_bwd_lion_kernel", "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "traffic": None, "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)"

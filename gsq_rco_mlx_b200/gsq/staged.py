@@ -23,7 +23,7 @@ import numpy as np
 import torch
 
 from .. import _lib
-from ..gemm import SumSq, mm_nt, mm_tn
+from ..gemm import Terms, err_flag, check_err, gemm_tc, pad8
 from .gptq import init_logits_2bit_from_codes, init_shift_logits
 from .lion import BETAS, LR_LOGITS, LR_SCALES, WEIGHT_DECAY, scale_lr
 from .quant import gs_schedules
@@ -80,15 +80,21 @@ class SoftLinear:
     def d(self):
         return self.out_f * self.in_f
 
-    def soft(self, tau, kappa, step, resample, seed, w_ref=None, out=None, noise=None):
-        """w_bar (or w_bar - w_ref) float32 [out, in] of one Gumbel draw."""
-        out = torch.empty(self.shape, device=self.logits.device, dtype=torch.float32) \
-            if out is None else out
+    def soft(self, tau, kappa, step, resample, seed, w_ref=None, out=None, noise=None,
+             terms: Terms = None):
+        """w_bar (or w_bar - w_ref) of one Gumbel draw: float32 [out, in] into ``out``, and/or
+        as three bf16 terms (the K-major B operand of the residual GEMM) into ``terms``."""
+        if out is None and terms is None:
+            out = torch.empty(self.shape, device=self.logits.device, dtype=torch.float32)
+        if terms is not None and (terms.ld != self.in_f or terms.n != 3):
+            raise ValueError("soft-weight terms must be 3 x [out, in] with ld == in")
+        t = terms.t if terms is not None else [None, None, None]
         _lib.call("gsq_soft_fwd", _lib.ptr(self.logits), _lib.ptr(self.j0), _lib.ptr(self.scales),
                   _lib.ptr(noise), int(seed) & (2 ** 64 - 1), self.linear_id, int(step),
                   int(resample), self.out_f, self.in_f, self.group_size, self.bits, float(tau),
-                  float(kappa), _lib.ptr(w_ref), _lib.ptr(out), None, None, None, _lib.stream_ptr())
-        return out
+                  float(kappa), _lib.ptr(w_ref), _lib.ptr(out), _lib.ptr(t[0]), _lib.ptr(t[1]),
+                  _lib.ptr(t[2]), _lib.stream_ptr())
+        return out if out is not None else terms
 
     def backward_lion(self, grad_w, tau, kappa, step, seed, lr_logits=LR_LOGITS,
                       lr_scales=LR_SCALES, noise=None):
@@ -117,48 +123,101 @@ class SoftLinear:
         return self.logits.T.cpu().numpy()
 
 
-def train_linears(lins, rows_of, targets, n_seqs, opts: BlockOpts, seed, noise_of=None,
-                  noise_seed=None, sync_timing=True):
+class LinearStep:
+    """The qk-stage step of the linears that read the same rows X [M, in] (staged.py:322-329):
+    per resample, soft weight terms (w_bar - W), the residual R = X (w_bar - W)^T on the
+    tensor cores with the loss partials and R^T terms written by its epilogue, then the
+    weight gradient G = 2 / (M out) R^T X; finally one fused backward + Lion per linear.
+    All operands are bf16 terms (three for float32 data, one for exactly-bf16 rows)."""
+
+    def __init__(self, lins, M, in_f, resamples, x_terms=3):
+        dev = lins[0].logits.device
+        self.lins, self.M, self.in_f, self.R = lins, int(M), int(in_f), int(resamples)
+        self.nx = int(x_terms)
+        self.X = Terms(M, in_f, self.nx, dev)        # A of the residual GEMM
+        self.XT = Terms(in_f, M, self.nx, dev)       # B of the weight-gradient GEMM
+        self.D = {l.name: Terms(l.out_f, l.in_f, 3, dev, ld=l.in_f) for l in lins}
+        self.RT = {l.name: Terms(l.out_f, M, 3, dev) for l in lins}
+        self.grads = {l.name: torch.empty((self.R,) + l.shape, device=dev, dtype=torch.float32)
+                      for l in lins}
+        tiles = max(((M + 127) // 128) * ((l.out_f + 127) // 128) for l in lins)
+        self.sq = torch.zeros(tiles, device=dev, dtype=torch.float64)
+        self.loss = torch.zeros(len(lins) * self.R, device=dev, dtype=torch.float64)
+        self.seq = torch.zeros(64, device=dev, dtype=torch.int32)
+        self.dev = dev
+
+    def stage(self, x_all, seq_ids, per_seq, seq_stride, offset):
+        """Gather rows of x_all (float32 [n_rows, in]) into the X and X^T operand terms."""
+        ids = torch.as_tensor(np.asarray(seq_ids, dtype=np.int32))
+        self.seq[:len(ids)].copy_(ids, non_blocking=True)
+        rows = len(ids) * per_seq
+        if rows != self.M:
+            raise ValueError(f"micro-batch has {rows} rows, step expects {self.M}")
+        _lib.call("gsq_gather_split", _lib.ptr(x_all), x_all.shape[-1], _lib.ptr(self.seq),
+                  int(per_seq), int(seq_stride), int(offset), self.M, self.in_f, self.nx,
+                  self.X.ptrs(), self.X.ld, self.XT.ptrs(), self.XT.ld, _lib.stream_ptr())
+
+    def forward_backward(self, targets, t, tau, kappa, noise_seed, noise_of=None):
+        """Residuals, losses and weight gradients of every linear and resample."""
+        for li, lin in enumerate(self.lins):
+            D, RT, G = self.D[lin.name], self.RT[lin.name], self.grads[lin.name]
+            for r in range(self.R):
+                noise = None if noise_of is None else noise_of(t, r, lin)
+                lin.soft(tau, kappa, t, r, noise_seed, w_ref=targets[lin.name], noise=noise,
+                         terms=D)
+                gemm_tc(self.X, D, ct_terms=RT, sq_partial=self.sq)
+                tiles = ((self.M + 127) // 128) * ((lin.out_f + 127) // 128)
+                slot = self.loss[li * self.R + r:li * self.R + r + 1]
+                _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(slot),
+                          _lib.stream_ptr())
+                gemm_tc(RT, self.XT, alpha=2.0 / (self.M * lin.out_f), C=G[r])
+
+    def update(self, t, tau, kappa, noise_seed, opts, noise_of=None):
+        for lin in self.lins:
+            stacked = None
+            if noise_of is not None:
+                stacked = torch.stack([noise_of(t, r, lin) for r in range(self.R)]).contiguous()
+            lin.backward_lion(self.grads[lin.name], tau, kappa, t, noise_seed, opts.lr_logits,
+                              opts.lr_scales, noise=stacked)
+
+    def mean_loss(self):
+        """sum over linears of mean R^2, averaged over resamples (staged.py:386-394)."""
+        la = self.loss.view(len(self.lins), self.R).cpu().numpy()
+        denom = np.array([self.M * lin.out_f for lin in self.lins], dtype=np.float64)[:, None]
+        return float((la / denom).sum(axis=0).sum() / self.R)
+
+
+def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=None,
+                  noise_seed=None, exact_bf16_rows=False, sync_timing=True):
     """qk-stage optimiser: loss = sum over linears of mean ||X (W_bar - W)^T||^2.
 
-    rows_of(idx) returns the device float32 rows X [M, in] of the sorted sequence ids idx;
-    targets[name] is the float32 CUDA weight W of each linear. noise_of(t, r, lin), if given,
-    returns host-supplied Gumbel planes [K, d] (parity runs); otherwise the kernels draw
-    Philox noise keyed by ``noise_seed`` (default: seed). Returns (history, median_ms)."""
+    x_all: float32 CUDA tensor [n_seqs, T, in] of the linears' inputs; each step draws a sorted
+    micro-batch of sequences from the reference's numpy stream (staged.py:373,380) and uses
+    their positions 1..T-1. targets[name] is the float32 CUDA weight W. noise_of(t, r, lin),
+    if given, returns host-supplied Gumbel planes [K, d] (parity runs); otherwise the kernels
+    draw Philox noise keyed by ``noise_seed`` (default: seed). exact_bf16_rows declares the
+    rows exactly representable in bf16 (one operand term instead of three).
+    Returns (history, median_ms)."""
     if not lins or opts.steps == 0:
         return [], None
     rng = np.random.default_rng(seed)
     m = min(opts.micro_batch, n_seqs)
-    R = opts.resamples
+    n_seq, T, in_f = x_all.shape
     noise_seed = seed if noise_seed is None else noise_seed
-    dev = lins[0].logits.device
-    sumsq = SumSq(dev)
-    loss_acc = torch.zeros(len(lins) * R, device=dev, dtype=torch.float64)
-    grads = {lin.name: torch.empty((R,) + lin.shape, device=dev, dtype=torch.float32)
-             for lin in lins}
+    step = LinearStep(lins, m * (T - 1), in_f, opts.resamples, 1 if exact_bf16_rows else 3)
+    flat = x_all.view(n_seq * T, in_f)
+    err_flag(step.dev).zero_()
     history, step_s = [], []
     for t in range(opts.steps):
         t0 = time.perf_counter()
         tau, kappa = gs_schedules(t, opts.steps)
         idx = np.sort(rng.choice(n_seqs, size=m, replace=False))
-        X = rows_of(idx)
-        M = X.shape[0]
-        for li, lin in enumerate(lins):
-            for r in range(R):
-                noise = None if noise_of is None else noise_of(t, r, lin)
-                D = lin.soft(tau, kappa, t, r, noise_seed, w_ref=targets[lin.name], noise=noise)
-                Rm = mm_nt(X, D)
-                sumsq(Rm, loss_acc[li * R + r:li * R + r + 1])
-                mm_tn(Rm, X, alpha=2.0 / (M * lin.out_f), out=grads[lin.name][r])
-            stacked = None
-            if noise_of is not None:
-                stacked = torch.stack([noise_of(t, r, lin) for r in range(R)]).contiguous()
-            lin.backward_lion(grads[lin.name], tau, kappa, t, noise_seed, opts.lr_logits,
-                              opts.lr_scales, noise=stacked)
-        la = loss_acc.view(len(lins), R).cpu().numpy()
-        denom = np.array([M * lin.out_f for lin in lins], dtype=np.float64)[:, None]
-        history.append(float((la / denom).sum(axis=0).sum() / R))
+        step.stage(flat, idx, T - 1, T, 1)
+        step.forward_backward(targets, t, tau, kappa, noise_seed, noise_of)
+        step.update(t, tau, kappa, noise_seed, opts, noise_of)
+        history.append(step.mean_loss())
         if sync_timing:
             torch.cuda.synchronize()
         step_s.append(time.perf_counter() - t0)
+    check_err(step.dev)
     return history, round(1000 * float(np.median(step_s[3:] or step_s)), 1)

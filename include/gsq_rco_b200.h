@@ -123,6 +123,19 @@ int gsq_gemm_tc(int M, int N, int K, const void *const *a_terms, int na, int64_t
 int gsq_split_bf16(const float *x, int rows, int cols, int64_t ld_in, int transpose, void *t0,
                    void *t1, void *t2, int64_t ld_out, void *stream);
 
+/* Micro-batch operand staging of the GSQ step: output row r is source row
+ * seq[r / per_seq] * seq_stride + offset + r % per_seq of x float32 [.][ld_x] (positions 1..T-1
+ * of the chosen sequences: per_seq = T - 1, seq_stride = T, offset = 1). Writes n_terms bf16
+ * terms row-major [rows][ld_t] (row_terms) and/or transposed [cols][ld_u] (col_terms).
+ * Replaces the micro-batch draw of staged.py:380 with _rows :128-130 (and _take :124-125). */
+int gsq_gather_split(const float *x, int64_t ld_x, const int32_t *seq, int per_seq,
+                     int64_t seq_stride, int offset, int rows, int cols, int n_terms,
+                     void *const *row_terms, int64_t ld_t, void *const *col_terms, int64_t ld_u,
+                     void *stream);
+
+/* out[0] = sum of x[0..n) in float64 (one block; the loss from per-tile partials). */
+int gsq_sum_f64(const double *x, int n, double *out, void *stream);
+
 /* out[0] = sum_i x[i]^2 in float64 (deterministic two-pass). partials: >= 1024 doubles.
  * Replaces the mean of R^2 in staged.py:328 (the caller divides by the count). */
 int gsq_sumsq_f32(const float *x, int64_t n, double *partials, double *out, void *stream);

@@ -133,12 +133,11 @@ def _qk_parity(host_noise: bool):
     hist_o = ogsq.train_linear(st, lambda idx: Xs[idx].reshape(-1, in_f), W, n_seq, 200, seed=1,
                                noise_seed=77)
     lin = SoftLinear("q_proj", 3, codes, s16, 64, seed=0, linear_id=1)
-    Xd = torch.as_tensor(np.ascontiguousarray(Xs), device=DEV)
+    Xd = torch.as_tensor(X.reshape(n_seq, T, in_f), device=DEV)
     noise_of = None
     if host_noise:
         noise_of = lambda t, r, l: torch.as_tensor(gumbel_planes(77, 1, t, r, W.size, 5), device=DEV)
-    hist, _ = train_linears([lin], lambda idx: Xd[torch.as_tensor(idx, device=DEV)].reshape(-1, in_f),
-                            {"q_proj": torch.as_tensor(W, device=DEV)}, n_seq,
+    hist, _ = train_linears([lin], Xd, {"q_proj": torch.as_tensor(W, device=DEV)}, n_seq,
                             BlockOpts(steps=200), seed=1, noise_of=noise_of, noise_seed=77)
     rl = np.linalg.norm(lin.logits.cpu().numpy() - st.logits) / np.linalg.norm(st.logits)
     rs = np.linalg.norm(lin.scales.cpu().numpy() - st.scales) / np.linalg.norm(st.scales)
@@ -149,6 +148,25 @@ def _qk_parity(host_noise: bool):
 
 @pytest.mark.parametrize("host_noise", [True, False])
 def test_qk_stage_200_steps_parity(host_noise):
+    """200 Lion steps of the qk stage, tensor-core contractions, vs the oracle (float64 GEMMs)."""
     rl, rs, rloss, codes_eq = _qk_parity(host_noise)
+    print(f"parity: logits {rl:.2e} scales {rs:.2e} loss {rloss:.2e} codes {codes_eq:.6f}")
     assert rl <= 1e-3 and rs <= 1e-3 and rloss <= 1e-3, (rl, rs, rloss)
     assert codes_eq >= 0.999, codes_eq
+
+
+def test_qk_stage_exact_bf16_rows():
+    """Rows that are exactly bf16 (normed block inputs) use one operand term: same result."""
+    from gsq_rco_mlx_b200.gsq.staged import BlockOpts, SoftLinear, train_linears
+    rng = np.random.default_rng(2)
+    out_f, in_f, n_seq, T = 64, 256, 8, 129
+    W = (0.02 * rng.standard_normal((out_f, in_f))).astype(np.float32)
+    X = torch.as_tensor(rng.standard_normal((n_seq, T, in_f)).astype(np.float32)).bfloat16().float()
+    r = og.quantize_rtn(W, 3, 64)
+    res = []
+    for exact in (False, True):
+        lin = SoftLinear("k_proj", 3, r["codes"], r["scales"].astype(np.float16), 64, seed=0)
+        train_linears([lin], X.to(DEV), {"k_proj": torch.as_tensor(W, device=DEV)}, n_seq,
+                      BlockOpts(steps=20), seed=3, exact_bf16_rows=exact)
+        res.append(lin.logits.cpu().numpy())
+    assert np.linalg.norm(res[0] - res[1]) / np.linalg.norm(res[0]) < 1e-4
