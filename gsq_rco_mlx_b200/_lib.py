@@ -44,6 +44,7 @@ SIGNATURES = {
     "gptq_dequant": [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp],
     "gptq_err": [_vp, _vp, _vp, _i32, _i32, _vp, _vp, _vp],
     "mckp_dp_f64": [_vp, _vp, _i32, _i32, _i32, _i64, _vp, _vp, _vp, _vp],
+    "mckp_dp_f64_noalloc": [_vp, _vp, _i32, _i32, _i32, _i64, _vp, _vp],
 }
 
 _lib = None

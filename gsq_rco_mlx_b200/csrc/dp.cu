@@ -8,6 +8,8 @@
 // value reaches dp[B] (the cheapest optimum).
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace gsq {
@@ -87,6 +89,64 @@ extern "C" int mckp_dp_f64(const double* scores, const int64_t* step, int n_inst
     return GSQ_ECUDA;
   mckp_dp_kernel<<<n_inst, kDPThreads, smem, st>>>(scores, step, N, K, budget, choice_ws,
                                                    in_smem ? nullptr : dp_ws, z_out);
+  GSQ_CHECK_LAUNCH();
+  return GSQ_OK;
+}
+
+// ------------------------------------------------------------- allocation-free variant ---
+// Some callers cannot allocate device memory: a runtime that owns every device byte through
+// its own pool, or a host language whose binding has no CUDA allocator. For them the DP's
+// scratch (the choice table) lives in this fixed array, which every GPU that loads the
+// library holds until the process exits. Calls share it and it keeps the last call's
+// contents: two calls whose kernels overlap on the same GPU (e.g. on different streams) race
+// on it, so a caller serialises them.
+namespace gsq {
+
+constexpr size_t kStaticChoiceBytes = 16u << 20;  // 16 MiB: n_inst * N * (budget + 1) bytes
+static __device__ __align__(256) uint8_t g_dp_choice_scratch[kStaticChoiceBytes];
+
+constexpr int kMaxDevices = 64;
+static void* g_dp_choice_addr[kMaxDevices] = {nullptr};
+static std::mutex g_dp_choice_mu;
+
+// Device address of the array on the current device; the first call on a device looks it up
+// (host code must not use the symbol itself: on the host it is only a stand-in).
+static int static_choice_addr(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GSQ_ECUDA;
+  std::lock_guard<std::mutex> lock(g_dp_choice_mu);
+  if (!g_dp_choice_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_dp_choice_scratch) != cudaSuccess || !p) return GSQ_ECUDA;
+    g_dp_choice_addr[dev] = p;
+  }
+  *out = g_dp_choice_addr[dev];
+  return GSQ_OK;
+}
+
+}  // namespace gsq
+
+extern "C" int mckp_dp_f64_noalloc(const double* scores, const int64_t* step, int n_inst, int N,
+                                   int K, int64_t budget, int32_t* z_out, void* stream) {
+  if (!scores || !step || !z_out || n_inst < 1 || N < 1 || K < 1 || K > 255 || budget < 0)
+    return GSQ_EINVAL;
+  // limits of this variant: the DP rows in shared memory, the choice table in the fixed array
+  if (budget > kDPSmemBudget) return GSQ_EINVAL;
+  if ((uint64_t)n_inst * (uint64_t)N * (uint64_t)(budget + 1) > kStaticChoiceBytes)
+    return GSQ_EINVAL;
+  void* choice = nullptr;
+  const int rc = static_choice_addr(&choice);
+  if (rc != GSQ_OK) return rc;
+  const size_t smem = sizeof(double) * 2 * (size_t)(budget + 1);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(mckp_dp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return GSQ_ECUDA;
+  // every choice entry of every group is written before the backtrack reads it, so the
+  // contents left by an earlier call need no clearing
+  mckp_dp_kernel<<<n_inst, kDPThreads, smem, st>>>(scores, step, N, K, budget,
+                                                   (uint8_t*)choice, nullptr, z_out);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }

@@ -187,6 +187,18 @@ int mckp_dp_f64(const double *scores, const int64_t *step, int n_inst, int N, in
                 int64_t budget, uint8_t *choice_ws, double *dp_ws, int32_t *z_out,
                 void *stream);
 
+/* Allocation-free variant of mckp_dp_f64, for callers that cannot allocate device memory
+ * (a runtime that owns every device byte through its own pool, a host language binding
+ * without a CUDA allocator). No counterpart in the reference, whose DP runs in numpy.
+ * The choice table lives in a fixed 16 MiB array inside the library (every GPU that loads the
+ * library holds it until exit); the DP rows live in shared memory. Limits: budget <= 13823 and
+ * n_inst * N * (budget + 1) <= 16 MiB, else GSQ_EINVAL. The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress): make it before any stream capture.
+ * Calls share the array: calls whose kernels overlap on one GPU race, so serialise them.
+ * Nothing is allocated or freed. Same results as mckp_dp_f64. */
+int mckp_dp_f64_noalloc(const double *scores, const int64_t *step, int n_inst, int N, int K,
+                        int64_t budget, int32_t *z_out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
