@@ -147,6 +147,8 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
     bwd_events = []
 
+    lstep.first_forward(targets, 0, *gs_schedules(0, STAGE_STEPS), 77)
+
     def step(t, host_inputs=False, time_bwd=False):
         tau, kappa = gs_schedules(t % STAGE_STEPS, STAGE_STEPS)
         idx = np.sort(rng.choice(N_SEQ, size=MICRO, replace=False))
@@ -156,11 +158,13 @@ def run_ours(args):
             lstep.stage(Xmb, [0, 1], T_SEQ - 1, T_SEQ - 1, 0)
         else:
             lstep.stage(Xd, idx, T_SEQ - 1, T_SEQ, 1)
-        lstep.forward_backward(targets, t, tau, kappa, 77)
+        lstep.contract()
         if time_bwd:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-        lstep.update(t, tau, kappa, 77, opts)
+        t1 = t + 1
+        lstep.update(targets, t, tau, kappa, opts, 77,
+                     nxt=(t1, *gs_schedules(t1 % STAGE_STEPS, STAGE_STEPS)))
         if time_bwd:
             e1.record(stream)
             bwd_events.append((e0, e1))
@@ -204,9 +208,12 @@ def run_ours(args):
     ms_e2e = max_over_ranks(e2.elapsed_time(e3))
 
     d = OUT_F * IN_F
-    # algorithmic bytes of the fused backward + Lion: read logits, momentum (20 + 20 B), codes
-    # (1 B), R weight gradients (4 B each); write logits and momentum (40 B); noise regenerated
-    bwd_bytes = d * (20 + 20 + 1 + 4 * RESAMPLES + 40) + 2 * 4 * (OUT_F * (IN_F // 64)) * 2
+    # algorithmic bytes of the fused step pass per weight: read logits + momentum (40 B), code
+    # (1), FP weight (4), per resample the stored probabilities (20) and the weight gradient
+    # (4); write logits + momentum (40), per resample the next probabilities (20) and the next
+    # soft weight as three bf16 terms (6); plus the group scales and their momentum
+    bwd_bytes = d * (40 + 1 + 4 + 40 + RESAMPLES * (20 + 4 + 20 + 6)) + \
+        4 * 4 * OUT_F * (IN_F // 64)
     achieved = bwd_bytes / (bwd_ms * 1e-3) / 1e9
     peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) \
         if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
@@ -224,7 +231,7 @@ def run_ours(args):
         "e2e": {"value": round(world * args.steps / (ms_e2e * 1e-3), 3), "unit": "steps/s",
                 "h2d_bytes_per_step": M * IN_F * 4, "d2h_bytes_per_step": RESAMPLES * 8},
         "gpu_launches": args.steps * (RESAMPLES * 4 + 2),
-        "roofline": {"kernel": "soft_bwd_lion_kernel", "bound": "hbm", "achieved": round(achieved, 1),
+        "roofline": {"kernel": "soft_step_kernel", "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "traffic": None, "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)"
                      if "hbm_gbs" in peaks else "fallback 6650 GB/s"},

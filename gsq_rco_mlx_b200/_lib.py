@@ -22,9 +22,10 @@ _vp, _i32, _i64, _u32, _u64, _f32, _f64 = (C.c_void_p, C.c_int, C.c_int64, C.c_u
 SIGNATURES = {
     "gsq_abi_version": [],
     "gsq_soft_fwd": [_vp, _vp, _vp, _vp, _u64, _u32, _u32, _u32, _i32, _i32, _i32, _i32, _f32,
-                     _f32, _vp, _vp, _vp, _vp, _vp, _vp],
-    "gsq_soft_bwd_lion": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u64, _u32, _u32, _i32, _i32, _i32,
-                          _i32, _i32, _f32, _f32, _f32, _f32, _f64, _f64, _f64, _vp],
+                     _f32, _vp, _vp, _vp, _vp, _vp],
+    "gsq_soft_step": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32,
+                      _f32, _f32, _f32, _f64, _f64, _f64, _i32, _vp, _u64, _u32, _u32, _f32,
+                      _f32, _vp, _vp, _vp, _vp],
     "gsq_harden": [_vp, _vp, _i32, _i32, _i32, _vp, _vp],
     "gsq_lion_f32": [_vp, _vp, _vp, _i64, _f32, _f64, _f64, _f64, _vp],
     "gsq_gemm_f32": [_i32, _i32, _i32, _f32, _vp, _i64, _i64, _vp, _i64, _i64, _f32, _vp, _i64,

@@ -1,7 +1,7 @@
 // Library identity and status strings of the C ABI.
 #include "common.cuh"
 
-extern "C" int gsq_abi_version(void) { return 1; }
+extern "C" int gsq_abi_version(void) { return 2; }
 
 extern "C" const char* gsq_status_string(int status) {
   switch (status) {

@@ -28,14 +28,8 @@ __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1
   return c;
 }
 
-// u = ((x >> 8) + 0.5) 2^-24, clipped to [1e-7, 1 - 1e-7]; g = -log(-log u) in float32.
-__device__ __forceinline__ float gumbel_from_bits(uint32_t x) {
-  float u = __fmul_rn(__fadd_rn((float)(x >> 8), 0.5f), 5.9604644775390625e-08f);
-  u = fminf(fmaxf(u, 1e-7f), 1.0f - 1e-7f);
-  return -logf(-logf(u));
-}
-
-// Gumbel noise of one weight: planes 0..3 from counter block 0, plane 4 from block 1.
+// Gumbel noise of one weight and draw: one Philox call (counter (i, 0, step, resample)),
+// planes 0..3 from the high 24 bits of x0..x3, plane 4 from their low bytes.
 struct NoiseKey {
   uint32_t k0, k1, step, resample;
 };
@@ -50,17 +44,20 @@ __host__ __device__ inline NoiseKey make_noise_key(uint64_t seed, uint32_t linea
   return k;
 }
 
+__device__ __forceinline__ float gumbel_from_24(uint32_t b) {
+  float u = __fmul_rn(__fadd_rn((float)b, 0.5f), 5.9604644775390625e-08f);
+  u = fminf(fmaxf(u, 1e-7f), 1.0f - 1e-7f);
+  return -logf(-logf(u));
+}
+
 template <int K>
 __device__ __forceinline__ void gumbel_weight(const NoiseKey& nk, uint32_t i, float g[K]) {
-  const uint4 r0 = philox4x32_10(make_uint4(i, 0u, nk.step, nk.resample), nk.k0, nk.k1);
-  g[0] = gumbel_from_bits(r0.x);
-  g[1] = gumbel_from_bits(r0.y);
-  g[2] = gumbel_from_bits(r0.z);
-  g[3] = gumbel_from_bits(r0.w);
-  if (K > 4) {
-    const uint4 r1 = philox4x32_10(make_uint4(i, 1u, nk.step, nk.resample), nk.k0, nk.k1);
-    g[K - 1] = gumbel_from_bits(r1.x);
-  }
+  const uint4 x = philox4x32_10(make_uint4(i, 0u, nk.step, nk.resample), nk.k0, nk.k1);
+  g[0] = gumbel_from_24(x.x >> 8);
+  g[1] = gumbel_from_24(x.y >> 8);
+  g[2] = gumbel_from_24(x.z >> 8);
+  g[3] = gumbel_from_24(x.w >> 8);
+  if (K > 4) g[K - 1] = gumbel_from_24((x.x & 255u) | ((x.y & 255u) << 8) | ((x.z & 255u) << 16));
 }
 
 // -------------------------------------------------------------------- bf16 split ---

@@ -20,7 +20,8 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemBudget = 200 * 1024;
 
 struct GemmParams {
@@ -31,10 +32,11 @@ struct GemmParams {
   float alpha, beta;
   float* C;
   int64_t ldc;
-  __nv_bfloat16* cs[3];  // C as bf16 terms [M][ldcs]
+  int c_vec;             // C rows 16-byte aligned: float4 stores
+  __nv_bfloat16* cs[3];  // C as bf16 terms [M][ldcs], ldcs % 8 == 0
   int ncs;
   int64_t ldcs;
-  __nv_bfloat16* ct[3];  // C^T as bf16 terms [N][ldct]
+  __nv_bfloat16* ct[3];  // C^T as bf16 terms [N][ldct], ldct % 8 == 0, ldct >= pad8(M)
   int nct;
   int64_t ldct;
   double* sq_partial;  // [tiles] sum of (alpha acc)^2 per tile
@@ -47,10 +49,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+__device__ __forceinline__ void epi_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
+}
+
 // TMEM columns: two buffers, each a "big" accumulator (the hi x hi products) and a "small"
 // one (every other product, 2^8 smaller). Tensor-core accumulation into TMEM is not IEEE
 // round-to-nearest; folding each chunk of k-blocks into float32 registers with IEEE adds
-// keeps the error of the 3-term products at the level of a float32 GEMM.
+// keeps the error of the 3-term products at the level of a float32 GEMM. Eight epilogue warps
+// fold: warp w reads TMEM lanes 32 (w % 4) .. + 31 (one output row per thread) and 64 of the
+// tile's 128 columns.
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -59,11 +67,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   __shared__ uint64_t accf_bar[2];
   __shared__ uint64_t acce_bar[2];
   __shared__ uint32_t tmem_base;
-  __shared__ double red[4];
+  __shared__ double red[kEpiWarps];
 
   constexpr uint32_t kTileA = BM * BK * 2;  // bytes of one A term tile
   constexpr uint32_t kTileB = BN * BK * 2;
   constexpr uint32_t kCols = 4 * BN;        // 2 buffers x (big, small)
+  constexpr int kHalf = BN / 2;             // columns per epilogue warp
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_m = blockIdx.y * BM, tile_n = blockIdx.x * BN;
   const int S = p.stages;
@@ -81,7 +90,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf_bar[b], 1);
-      mbar_init(&acce_bar[b], 4);
+      mbar_init(&acce_bar[b], kEpiWarps);
     }
     fence_barrier_init();
   }
@@ -149,13 +158,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       }
     }
   } else {
-    // epilogue warps 2..5: TMEM lanes 32 * (warp % 4) .. + 31, one output row per thread
-    const int q = warp & 3;
-    const int row = tile_m + q * 32 + lane;
+    const int ew = warp - 2;                  // epilogue warp 0..7
+    const int q = warp & 3;                   // TMEM lane quadrant (hardware rule: warp % 4)
+    const int h = ew >> 2;                    // column half of the tile
+    const int r_loc = q * 32 + lane;
+    const int row = tile_m + r_loc;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    float acc[BN];
+    float acc[kHalf];
 #pragma unroll
-    for (int t = 0; t < BN; ++t) acc[t] = 0.f;
+    for (int t = 0; t < kHalf; ++t) acc[t] = 0.f;
     bool ok = true;
     for (int c = 0; c < n_chunks; ++c) {
       const int b = c & 1;
@@ -163,56 +174,116 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                                                    p.err, 3));
       if (!ok) break;
       fence_after_sync();
-      const uint32_t big = tmem + lane_off + (uint32_t)(b * 2 * BN), small = big + BN;
+      const uint32_t big = tmem + lane_off + (uint32_t)(b * 2 * BN + h * kHalf);
+      const uint32_t small = big + BN;
 #pragma unroll
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(big + (uint32_t)c0, v);
+      for (int c0 = 0; c0 < kHalf; c0 += 32) {
+        uint32_t v[32], w[32];
+        tmem_ld32_nowait(big + (uint32_t)c0, v);
+        if (has_small) tmem_ld32_nowait(small + (uint32_t)c0, w);
+        tmem_wait_ld();
         if (has_small) {
-          float w[16];
-          tmem_ld16(small + (uint32_t)c0, w);
 #pragma unroll
-          for (int t = 0; t < 16; ++t) acc[c0 + t] = __fadd_rn(acc[c0 + t], __fadd_rn(v[t], w[t]));
+          for (int t = 0; t < 32; ++t)
+            acc[c0 + t] = __fadd_rn(acc[c0 + t],
+                                    __fadd_rn(__uint_as_float(v[t]), __uint_as_float(w[t])));
         } else {
 #pragma unroll
-          for (int t = 0; t < 16; ++t) acc[c0 + t] = __fadd_rn(acc[c0 + t], v[t]);
+          for (int t = 0; t < 32; ++t) acc[c0 + t] = __fadd_rn(acc[c0 + t], __uint_as_float(v[t]));
         }
       }
       fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[b]);
     }
+    // ---- outputs (the pipeline stages are idle now: every MMA and TMA load has completed)
+    const bool live = ok && row < p.M;
+    const int n0 = tile_n + h * kHalf;
     double sq = 0.0;
-    if (ok && row < p.M) {
 #pragma unroll
-      for (int t = 0; t < BN; ++t) {
-        const int col = tile_n + t;
-        if (col < p.N) {
-          float x = __fmul_rn(p.alpha, acc[t]);
-          if (p.C) {
-            float* cp = p.C + (int64_t)row * p.ldc + col;
-            if (p.beta != 0.f) x = __fadd_rn(x, __fmul_rn(p.beta, *cp));
-            *cp = x;
+    for (int t = 0; t < kHalf; ++t) acc[t] = __fmul_rn(p.alpha, acc[t]);
+    if (live && p.C) {
+      float* crow = p.C + (int64_t)row * p.ldc + n0;
+      if (p.c_vec && n0 + kHalf <= p.N) {
+#pragma unroll
+        for (int t = 0; t < kHalf; t += 4) {
+          float4 x = make_float4(acc[t], acc[t + 1], acc[t + 2], acc[t + 3]);
+          if (p.beta != 0.f) {
+            const float4 o = *reinterpret_cast<const float4*>(crow + t);
+            x.x = __fadd_rn(x.x, __fmul_rn(p.beta, o.x));
+            x.y = __fadd_rn(x.y, __fmul_rn(p.beta, o.y));
+            x.z = __fadd_rn(x.z, __fmul_rn(p.beta, o.z));
+            x.w = __fadd_rn(x.w, __fmul_rn(p.beta, o.w));
           }
-          if (p.sq_partial) sq += (double)x * (double)x;
-          if (p.ncs > 0 || p.nct > 0) {
-            __nv_bfloat16 h[3];
-            split3_bf16(x, h[0], h[1], h[2]);
-            for (int i = 0; i < p.ncs; ++i) p.cs[i][(int64_t)row * p.ldcs + col] = h[i];
-            for (int i = 0; i < p.nct; ++i) p.ct[i][(int64_t)col * p.ldct + row] = h[i];
+          *reinterpret_cast<float4*>(crow + t) = x;
+          acc[t] = x.x; acc[t + 1] = x.y; acc[t + 2] = x.z; acc[t + 3] = x.w;
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < kHalf; ++t) {
+          if (n0 + t < p.N) {
+            float x = acc[t];
+            if (p.beta != 0.f) x = __fadd_rn(x, __fmul_rn(p.beta, crow[t]));
+            crow[t] = x;
+            acc[t] = x;
           }
         }
       }
     }
+    if (live && p.sq_partial) {
+#pragma unroll
+      for (int t = 0; t < kHalf; ++t)
+        if (n0 + t < p.N) sq += (double)acc[t] * (double)acc[t];
+    }
+    if (live && p.ncs > 0) {
+      // row-major terms straight from registers, 16-byte stores (8 bf16)
+#pragma unroll
+      for (int t = 0; t < kHalf; t += 8) {
+        if (n0 + t >= p.N) break;
+        __align__(16) __nv_bfloat16 hv[3][8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) split3_bf16(acc[t + u], hv[0][u], hv[1][u], hv[2][u]);
+        for (int i = 0; i < p.ncs; ++i)
+          *reinterpret_cast<uint4*>(p.cs[i] + (int64_t)row * p.ldcs + n0 + t) =
+              *reinterpret_cast<const uint4*>(hv[i]);
+      }
+    }
+    if (p.nct > 0) {
+      // transposed terms: stage [term][n][m] bf16 tiles in shared memory, then 16-byte
+      // coalesced row stores of C^T
+      __nv_bfloat16* T = reinterpret_cast<__nv_bfloat16*>(smem);
+#pragma unroll
+      for (int t = 0; t < kHalf; ++t) {
+        __nv_bfloat16 hv[3];
+        split3_bf16(live ? acc[t] : 0.f, hv[0], hv[1], hv[2]);
+        const int n_loc = h * kHalf + t;
+        for (int i = 0; i < p.nct; ++i) T[(i * BN + n_loc) * BM + r_loc] = hv[i];
+      }
+      epi_sync();
+      const int tid = threadIdx.x - 64;
+      const int chunks = p.nct * BN * (BM / 8);
+      for (int e = tid; e < chunks; e += 32 * kEpiWarps) {
+        const int i = e / (BN * (BM / 8));
+        const int rem = e - i * (BN * (BM / 8));
+        const int n_loc = rem / (BM / 8), m8 = (rem % (BM / 8)) * 8;
+        const int n = tile_n + n_loc, m = tile_m + m8;
+        if (n < p.N && m < p.M && ok)
+          *reinterpret_cast<uint4*>(p.ct[i] + (int64_t)n * p.ldct + m) =
+              *reinterpret_cast<const uint4*>(T + (i * BN + n_loc) * BM + m8);
+      }
+    }
     if (p.sq_partial) {
       sq = warp_sum_d(sq);
-      if (lane == 0) red[q] = sq;
+      if (lane == 0) red[ew] = sq;
     }
   }
   fence_before_sync();
   __syncthreads();
-  if (p.sq_partial && threadIdx.x == 0)
-    p.sq_partial[blockIdx.y * gridDim.x + blockIdx.x] = red[0] + red[1] + red[2] + red[3];
+  if (p.sq_partial && threadIdx.x == 0) {
+    double t = 0.0;
+    for (int i = 0; i < kEpiWarps; ++i) t += red[i];
+    p.sq_partial[blockIdx.y * gridDim.x + blockIdx.x] = t;
+  }
   if (warp == 1) {
     fence_after_sync();
     tmem_dealloc(tmem, kCols);
@@ -290,8 +361,13 @@ extern "C" int gsq_gemm_tc(int M, int N, int K, const void* const* a_terms, int 
       (ncs > 0 && !c_terms) || (nct > 0 && !ct_terms))
     return GSQ_EINVAL;
   if (!C && ncs == 0 && nct == 0 && !sq_partial) return GSQ_EINVAL;
-  if (lda < K || ldb < K || (C && ldc < N) || (ncs > 0 && ldcs < N) || (nct > 0 && ldct < M))
+  if (lda < K || ldb < K || (C && ldc < N) || (ncs > 0 && (ldcs < N || (ldcs & 7))) ||
+      (nct > 0 && (ldct < ((M + 7) / 8) * 8 || (ldct & 7))))
     return GSQ_EINVAL;
+  for (int i = 0; i < ncs; ++i)
+    if ((uintptr_t)c_terms[i] & 15) return GSQ_EINVAL;
+  for (int i = 0; i < nct; ++i)
+    if ((uintptr_t)ct_terms[i] & 15) return GSQ_EINVAL;
   tc::GemmParams p;
   memset(&p, 0, sizeof(p));
   const int BN = 128;
@@ -303,6 +379,7 @@ extern "C" int gsq_gemm_tc(int M, int N, int K, const void* const* a_terms, int 
   p.na = na; p.nb = nb; p.order = order;
   p.alpha = alpha; p.beta = beta;
   p.C = C; p.ldc = ldc;
+  p.c_vec = (C && ((uintptr_t)C & 15) == 0 && (ldc & 3) == 0) ? 1 : 0;
   for (int i = 0; i < ncs; ++i) p.cs[i] = (__nv_bfloat16*)c_terms[i];
   p.ncs = ncs; p.ldcs = ldcs;
   for (int i = 0; i < nct; ++i) p.ct[i] = (__nv_bfloat16*)ct_terms[i];

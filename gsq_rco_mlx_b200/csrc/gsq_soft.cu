@@ -1,8 +1,12 @@
-// GSQ soft-quantized linear: Gumbel-softmax soft weight (forward), fused soft backward +
-// Lion (one HBM pass over the training state), argmax decode, and a flat Lion step.
+// GSQ soft-quantized linear, elementwise side: the Gumbel-softmax soft weight (forward), and the
+// fused per-step pass backward(step t) + Lion + forward(step t + 1) over the training state,
+// argmax decode, and a flat Lion step.
 //
-// Elementwise arithmetic uses explicit round-to-nearest intrinsics so that no multiply-add is
-// contracted: every product and sum is rounded as in the float32 arrays of the reference.
+// The forward stores the probabilities p of every draw (float32, exact), so the backward never
+// regenerates noise: one pass per step reads logits, momentum, codes, the stored p and the
+// weight gradients, and writes logits, momentum, the next step's p and the next step's soft
+// weights as bf16 GEMM terms. Elementwise arithmetic uses explicit round-to-nearest intrinsics,
+// so no multiply-add is contracted and every product and sum is rounded as a float32 array op.
 #include <math.h>
 
 #include "common.cuh"
@@ -11,15 +15,14 @@ namespace gsq {
 
 template <int K>
 struct SoftMath {
-  // p = softmax((kappa * l + g) / tau) and the candidate values C_k of weight i.
-  __device__ __forceinline__ static void probs(const float* __restrict__ logits, int64_t d,
-                                               int64_t i, const float g[K], float tau,
+  // p = softmax((kappa * l + g) * (1 / tau)), sums and maxima in candidate order.
+  __device__ __forceinline__ static void probs(const float l[K], const float g[K], float inv_tau,
                                                float kappa, float p[K]) {
     float y[K];
     float m = -INFINITY;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      y[k] = __fdiv_rn(__fadd_rn(__fmul_rn(kappa, logits[k * d + i]), g[k]), tau);
+      y[k] = __fmul_rn(__fadd_rn(__fmul_rn(kappa, l[k]), g[k]), inv_tau);
       m = fmaxf(m, y[k]);
     }
     float sum = 0.f;
@@ -28,8 +31,9 @@ struct SoftMath {
       y[k] = expf(__fsub_rn(y[k], m));
       sum = k == 0 ? y[0] : __fadd_rn(sum, y[k]);
     }
+    const float inv = __frcp_rn(sum);
 #pragma unroll
-    for (int k = 0; k < K; ++k) p[k] = __fdiv_rn(y[k], sum);
+    for (int k = 0; k < K; ++k) p[k] = __fmul_rn(y[k], inv);
   }
 
   __device__ __forceinline__ static void candidates(int bits, int j0, float C[K]) {
@@ -39,10 +43,7 @@ struct SoftMath {
     } else {
       const int top = (1 << bits) - 1;
 #pragma unroll
-      for (int k = 0; k < K; ++k) {
-        const int j = min(max(j0 + k - 2, 0), top);
-        C[k] = grid_value(bits, j);
-      }
+      for (int k = 0; k < K; ++k) C[k] = grid_value(bits, min(max(j0 + k - 2, 0), top));
     }
   }
 
@@ -55,36 +56,51 @@ struct SoftMath {
       gumbel_weight<K>(nk, (uint32_t)i, g);
     }
   }
+
+  __device__ __forceinline__ static float value(const float p[K], const float C[K]) {
+    float c = __fmul_rn(p[0], C[0]);
+#pragma unroll
+    for (int k = 1; k < K; ++k) c = __fadd_rn(c, __fmul_rn(p[k], C[k]));
+    return c;
+  }
 };
+
+// Output of one soft weight w = s c (- w_ref): float32 and/or three bf16 terms.
+__device__ __forceinline__ void store_soft(float w, int64_t i, int64_t d, float* w_out,
+                                           __nv_bfloat16* terms) {
+  if (w_out) w_out[i] = w;
+  if (terms) {
+    __nv_bfloat16 h, m, l;
+    split3_bf16(w, h, m, l);
+    terms[i] = h;
+    terms[d + i] = m;
+    terms[2 * d + i] = l;
+  }
+}
 
 template <int K>
 __global__ void __launch_bounds__(256)
 soft_fwd_kernel(const float* __restrict__ logits, const uint8_t* __restrict__ j0,
                 const float* __restrict__ scales, const float* __restrict__ noise, NoiseKey nk,
-                int out_f, int in_f, int G, int gs, int bits, float tau, float kappa,
+                int out_f, int in_f, int G, int gs, int bits, float inv_tau, float kappa,
                 const float* __restrict__ w_ref, float* __restrict__ w_out,
-                __nv_bfloat16* __restrict__ w_hi, __nv_bfloat16* __restrict__ w_mid,
-                __nv_bfloat16* __restrict__ w_lo) {
+                __nv_bfloat16* __restrict__ terms, float* __restrict__ p_out) {
   const int64_t d = (int64_t)out_f * in_f;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < d;
        i += (int64_t)gridDim.x * blockDim.x) {
-    float g[K], p[K], C[K];
-    SoftMath<K>::noise(noise, d, i, nk, g);
-    SoftMath<K>::probs(logits, d, i, g, tau, kappa, p);
-    SoftMath<K>::candidates(bits, K == 5 ? (int)j0[i] : 0, C);
-    float c = __fmul_rn(p[0], C[0]);
+    float l[K], g[K], p[K], C[K];
 #pragma unroll
-    for (int k = 1; k < K; ++k) c = __fadd_rn(c, __fmul_rn(p[k], C[k]));
+    for (int k = 0; k < K; ++k) l[k] = logits[k * d + i];
+    SoftMath<K>::noise(noise, d, i, nk, g);
+    SoftMath<K>::probs(l, g, inv_tau, kappa, p);
+    SoftMath<K>::candidates(bits, K == 5 ? (int)j0[i] : 0, C);
     const int row = (int)(i / in_f), col = (int)(i - (int64_t)row * in_f);
-    float w = __fmul_rn(scales[(int64_t)row * G + col / gs], c);
+    float w = __fmul_rn(scales[(int64_t)row * G + col / gs], SoftMath<K>::value(p, C));
     if (w_ref) w = __fsub_rn(w, w_ref[i]);
-    if (w_out) w_out[i] = w;
-    if (w_hi) {
-      __nv_bfloat16 h, m, l;
-      split3_bf16(w, h, m, l);
-      w_hi[i] = h;
-      if (w_mid) w_mid[i] = m;
-      if (w_lo) w_lo[i] = l;
+    store_soft(w, i, d, w_out, terms);
+    if (p_out) {
+#pragma unroll
+      for (int k = 0; k < K; ++k) p_out[k * d + i] = p[k];
     }
   }
 }
@@ -104,85 +120,123 @@ __device__ __forceinline__ void lion1(float& p, float& m, float g, float lr, con
 
 constexpr int kMaxResamples = 8;
 
-// One warp per (row, group): the group's weights are strided over the lanes (MAXW per lane),
-// the scale gradient of each resample is a warp reduction, and lane 0 applies the scale's
-// Lion step. The resample loop is outermost so that only the per-weight gradient sums stay
-// live across resamples.
+struct StepArgs {
+  float* logits;
+  float* mom;
+  const uint8_t* j0;
+  float* scales;
+  float* mom_s;
+  float* probs;          // [R][K][d]: this step's p in, the next step's p out
+  const float* grad_w;   // [R][d]
+  int R, out_f, in_f, G, gs, bits;
+  float kt;              // kappa_t / tau_t of this step
+  float lr_l, lr_s;
+  LionConst lc;
+  int next;              // run the forward of the next step
+  const float* noise;    // [R][K][d] host-supplied noise of the next step, or NULL
+  uint64_t seed;
+  uint32_t linear_id, next_step;
+  float inv_tau1, kappa1;
+  const float* w_ref;
+  float* w_out;          // [R][d]
+  __nv_bfloat16* terms;  // [R][3][d]
+};
+
+// One warp per (row, group): the group's weights are strided over the lanes (MAXW per lane).
+// Backward of this step from the stored p: u_k = s G C_k, dL/dl = (kappa/tau) p (u - <p, u>),
+// dL/ds = sum over the group of G c (warp reduction); the sums over resamples are divided by R;
+// Lion on logits (per lane) and on the group scale (lane 0, broadcast); then the forward of the
+// next step with the updated logits and scale.
 template <int K, int MAXW>
-__global__ void __launch_bounds__(256)
-soft_bwd_lion_kernel(float* __restrict__ logits, float* __restrict__ mom,
-                     const uint8_t* __restrict__ j0, float* __restrict__ scales,
-                     float* __restrict__ mom_s, const float* __restrict__ grad_w,
-                     const float* __restrict__ noise, uint64_t seed, uint32_t linear_id,
-                     uint32_t step, int R, int out_f, int in_f, int G, int gs, int bits,
-                     float tau, float kappa, float lr_l, float lr_s, LionConst lc) {
-  const int64_t d = (int64_t)out_f * in_f;
+__global__ void __launch_bounds__(256) soft_step_kernel(const StepArgs a) {
+  const int64_t d = (int64_t)a.out_f * a.in_f;
   const int lane = threadIdx.x & 31;
-  const int64_t n_units = (int64_t)out_f * G;
-  const float kt = __fdiv_rn(kappa, tau);
-  const float fR = (float)R;
+  const int64_t n_units = (int64_t)a.out_f * a.G;
+  const float fR = (float)a.R;
   for (int64_t unit = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; unit < n_units;
        unit += ((int64_t)gridDim.x * blockDim.x) >> 5) {
-    const int row = (int)(unit / G), grp = (int)(unit - (int64_t)row * G);
-    const float s = scales[unit];
-    const int c_begin = grp * gs, c_end = min(c_begin + gs, in_f);
-    float acc[MAXW][K];
+    const int row = (int)(unit / a.G), grp = (int)(unit - (int64_t)row * a.G);
+    const float s = a.scales[unit];
+    const int c_begin = grp * a.gs, c_end = min(c_begin + a.gs, a.in_f);
+    float C[MAXW][K], acc[MAXW][K];
+#pragma unroll
+    for (int t = 0; t < MAXW; ++t) {
+      const int col = c_begin + lane + 32 * t;
+      const int64_t i = (int64_t)row * a.in_f + min(col, c_end - 1);
+      SoftMath<K>::candidates(a.bits, K == 5 ? (int)a.j0[i] : 0, C[t]);
+    }
     float gsum = 0.f;
 #pragma unroll 1
-    for (int r = 0; r < R; ++r) {
-      const NoiseKey nk = make_noise_key(seed, linear_id, step, (uint32_t)r);
-      const float* noise_r = noise ? noise + (int64_t)r * K * d : nullptr;
-      const float* grad_r = grad_w + (int64_t)r * d;
+    for (int r = 0; r < a.R; ++r) {
+      const float* p_r = a.probs + (int64_t)r * K * d;
+      const float* g_r = a.grad_w + (int64_t)r * d;
       double part = 0.0;
 #pragma unroll
       for (int t = 0; t < MAXW; ++t) {
         const int col = c_begin + lane + 32 * t;
         if (col >= c_end) continue;
-        const int64_t i = (int64_t)row * in_f + col;
-        float C[K], g[K], p[K];
-        SoftMath<K>::candidates(bits, K == 5 ? (int)j0[i] : 0, C);
-        SoftMath<K>::noise(noise_r, d, i, nk, g);
-        SoftMath<K>::probs(logits, d, i, g, tau, kappa, p);
-        float c = __fmul_rn(p[0], C[0]);
+        const int64_t i = (int64_t)row * a.in_f + col;
+        float p[K];
 #pragma unroll
-        for (int k = 1; k < K; ++k) c = __fadd_rn(c, __fmul_rn(p[k], C[k]));
-        const float G_r = grad_r[i];
-        part += (double)G_r * (double)c;
-        const float sG = __fmul_rn(s, G_r);
+        for (int k = 0; k < K; ++k) p[k] = p_r[k * d + i];
+        const float Gr = g_r[i];
+        part += (double)Gr * (double)SoftMath<K>::value(p, C[t]);
+        const float sG = __fmul_rn(s, Gr);
         float u[K];
         float pu = 0.f;
 #pragma unroll
         for (int k = 0; k < K; ++k) {
-          u[k] = __fmul_rn(sG, C[k]);
+          u[k] = __fmul_rn(sG, C[t][k]);
           pu = k == 0 ? __fmul_rn(p[0], u[0]) : __fadd_rn(pu, __fmul_rn(p[k], u[k]));
         }
 #pragma unroll
         for (int k = 0; k < K; ++k) {
-          const float gl = __fmul_rn(kt, __fmul_rn(p[k], __fsub_rn(u[k], pu)));
+          const float gl = __fmul_rn(a.kt, __fmul_rn(p[k], __fsub_rn(u[k], pu)));
           acc[t][k] = r == 0 ? gl : __fadd_rn(acc[t][k], gl);
         }
       }
       const float gr = (float)warp_sum_d(part);
       gsum = r == 0 ? gr : __fadd_rn(gsum, gr);
     }
+    // Lion on the group scale (lane 0), the new scale broadcast for the forward
+    float s_new = s;
+    if (lane == 0) {
+      float mv = a.mom_s[unit];
+      lion1(s_new, mv, __fdiv_rn(gsum, fR), a.lr_s, a.lc);
+      a.scales[unit] = s_new;
+      a.mom_s[unit] = mv;
+    }
+    s_new = __shfl_sync(0xffffffffu, s_new, 0);
 #pragma unroll
     for (int t = 0; t < MAXW; ++t) {
       const int col = c_begin + lane + 32 * t;
       if (col >= c_end) continue;
-      const int64_t i = (int64_t)row * in_f + col;
+      const int64_t i = (int64_t)row * a.in_f + col;
+      float l[K];
 #pragma unroll
       for (int k = 0; k < K; ++k) {
-        float pv = logits[k * d + i], mv = mom[k * d + i];
-        lion1(pv, mv, __fdiv_rn(acc[t][k], fR), lr_l, lc);
-        logits[k * d + i] = pv;
-        mom[k * d + i] = mv;
+        float pv = a.logits[k * d + i], mv = a.mom[k * d + i];
+        lion1(pv, mv, __fdiv_rn(acc[t][k], fR), a.lr_l, a.lc);
+        a.logits[k * d + i] = pv;
+        a.mom[k * d + i] = mv;
+        l[k] = pv;
       }
-    }
-    if (lane == 0) {
-      float sv = s, mv = mom_s[unit];
-      lion1(sv, mv, __fdiv_rn(gsum, fR), lr_s, lc);
-      scales[unit] = sv;
-      mom_s[unit] = mv;
+      if (!a.next) continue;
+      const float wr = a.w_ref ? a.w_ref[i] : 0.f;
+#pragma unroll 1
+      for (int r = 0; r < a.R; ++r) {
+        float g[K], p[K];
+        const NoiseKey nk = make_noise_key(a.seed, a.linear_id, a.next_step, (uint32_t)r);
+        SoftMath<K>::noise(a.noise ? a.noise + (int64_t)r * K * d : nullptr, d, i, nk, g);
+        SoftMath<K>::probs(l, g, a.inv_tau1, a.kappa1, p);
+        float w = __fmul_rn(s_new, SoftMath<K>::value(p, C[t]));
+        if (a.w_ref) w = __fsub_rn(w, wr);
+        store_soft(w, i, d, a.w_out ? a.w_out + (int64_t)r * d : nullptr,
+                   a.terms ? a.terms + (int64_t)r * 3 * d : nullptr);
+        float* pn = a.probs + (int64_t)r * K * d;
+#pragma unroll
+        for (int k = 0; k < K; ++k) pn[k * d + i] = p[k];
+      }
     }
   }
 }
@@ -241,71 +295,80 @@ using namespace gsq;
 extern "C" int gsq_soft_fwd(const float* logits, const uint8_t* j0, const float* scales,
                             const float* noise, uint64_t seed, uint32_t linear_id, uint32_t step,
                             uint32_t resample, int out_f, int in_f, int group_size, int bits,
-                            float tau, float kappa, const float* w_ref, float* w_out, void* w_hi,
-                            void* w_mid, void* w_lo, void* stream) {
+                            float tau, float kappa, const float* w_ref, float* w_out,
+                            void* w_terms, float* p_out, void* stream) {
   const int K = n_logit_planes(bits);
   if (K == 0) return GSQ_ENOTSUP;
   if (out_f <= 0 || in_f <= 0 || group_size <= 0 || !logits || !scales || (K == 5 && !j0) ||
       !(tau > 0.f))
     return GSQ_EINVAL;
   if ((int64_t)out_f * in_f > 0xFFFFFFFFll) return GSQ_EINVAL;  // Philox counter is 32-bit
-  if (!w_out && !w_hi) return GSQ_EINVAL;
+  if (!w_out && !w_terms && !p_out) return GSQ_EINVAL;
   const int G = (in_f + group_size - 1) / group_size;
   const NoiseKey nk = make_noise_key(seed, linear_id, step, resample);
   const int64_t d = (int64_t)out_f * in_f;
+  const float inv_tau = 1.0f / tau;  // IEEE division on the host
   cudaStream_t st = (cudaStream_t)stream;
-  auto* hi = (__nv_bfloat16*)w_hi;
-  auto* mid = (__nv_bfloat16*)w_mid;
-  auto* lo = (__nv_bfloat16*)w_lo;
+  auto* terms = (__nv_bfloat16*)w_terms;
   if (K == 5)
     soft_fwd_kernel<5><<<grid_for(d, 256), 256, 0, st>>>(logits, j0, scales, noise, nk, out_f,
-                                                        in_f, G, group_size, bits, tau, kappa,
-                                                        w_ref, w_out, hi, mid, lo);
+                                                        in_f, G, group_size, bits, inv_tau,
+                                                        kappa, w_ref, w_out, terms, p_out);
   else
     soft_fwd_kernel<4><<<grid_for(d, 256), 256, 0, st>>>(logits, j0, scales, noise, nk, out_f,
-                                                        in_f, G, group_size, bits, tau, kappa,
-                                                        w_ref, w_out, hi, mid, lo);
+                                                        in_f, G, group_size, bits, inv_tau,
+                                                        kappa, w_ref, w_out, terms, p_out);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }
 
-extern "C" int gsq_soft_bwd_lion(float* logits, float* mom_logits, const uint8_t* j0,
-                                 float* scales, float* mom_scales, const float* grad_w,
-                                 const float* noise, uint64_t seed, uint32_t linear_id,
-                                 uint32_t step, int resamples, int out_f, int in_f,
-                                 int group_size, int bits, float tau, float kappa,
-                                 float lr_logits, float lr_scales, double wd, double beta1,
-                                 double beta2, void* stream) {
+extern "C" int gsq_soft_step(float* logits, float* mom_logits, const uint8_t* j0, float* scales,
+                             float* mom_scales, float* probs, const float* grad_w, int resamples,
+                             int out_f, int in_f, int group_size, int bits, float tau,
+                             float kappa, float lr_logits, float lr_scales, double wd,
+                             double beta1, double beta2, int next, const float* noise_next,
+                             uint64_t seed, uint32_t linear_id, uint32_t next_step,
+                             float tau_next, float kappa_next, const float* w_ref,
+                             float* w_out, void* w_terms, void* stream) {
   const int K = n_logit_planes(bits);
   if (K == 0) return GSQ_ENOTSUP;
   if (out_f <= 0 || in_f <= 0 || group_size <= 0 || resamples < 1 ||
       resamples > kMaxResamples || !logits || !mom_logits || !scales || !mom_scales ||
-      !grad_w || (K == 5 && !j0) || !(tau > 0.f))
+      !probs || !grad_w || (K == 5 && !j0) || !(tau > 0.f))
     return GSQ_EINVAL;
+  if (next && (!(tau_next > 0.f) || (!w_out && !w_terms))) return GSQ_EINVAL;
   if ((int64_t)out_f * in_f > 0xFFFFFFFFll) return GSQ_EINVAL;
-  const int G = (in_f + group_size - 1) / group_size;
-  const int64_t units = (int64_t)out_f * G;
-  const LionConst lc = lion_const(wd, beta1, beta2);
-  cudaStream_t st = (cudaStream_t)stream;
-  const unsigned grid = grid_for(units * 32, 256);
   const int per_lane = (group_size + 31) / 32;
-#define GSQ_BWD_LAUNCH(KK, MW)                                                               \
-  soft_bwd_lion_kernel<KK, MW><<<grid, 256, 0, st>>>(                                        \
-      logits, mom_logits, j0, scales, mom_scales, grad_w, noise, seed, linear_id, step,     \
-      resamples, out_f, in_f, G, group_size, bits, tau, kappa, lr_logits, lr_scales, lc)
   if (per_lane > 8) return GSQ_ENOTSUP;
+  StepArgs a;
+  a.logits = logits; a.mom = mom_logits; a.j0 = j0; a.scales = scales; a.mom_s = mom_scales;
+  a.probs = probs; a.grad_w = grad_w;
+  a.R = resamples; a.out_f = out_f; a.in_f = in_f;
+  a.G = (in_f + group_size - 1) / group_size; a.gs = group_size; a.bits = bits;
+  a.kt = kappa / tau;
+  a.lr_l = lr_logits; a.lr_s = lr_scales;
+  a.lc = lion_const(wd, beta1, beta2);
+  a.next = next; a.noise = noise_next; a.seed = seed; a.linear_id = linear_id;
+  a.next_step = next_step;
+  a.inv_tau1 = next ? 1.0f / tau_next : 0.f;
+  a.kappa1 = kappa_next;
+  a.w_ref = w_ref; a.w_out = w_out; a.terms = (__nv_bfloat16*)w_terms;
+  const int64_t units = (int64_t)out_f * a.G;
+  const unsigned grid = grid_for(units * 32, 256);
+  cudaStream_t st = (cudaStream_t)stream;
+#define GSQ_STEP_LAUNCH(KK, MW) soft_step_kernel<KK, MW><<<grid, 256, 0, st>>>(a)
   if (K == 5) {
-    if (per_lane == 1) GSQ_BWD_LAUNCH(5, 1);
-    else if (per_lane == 2) GSQ_BWD_LAUNCH(5, 2);
-    else if (per_lane <= 4) GSQ_BWD_LAUNCH(5, 4);
-    else GSQ_BWD_LAUNCH(5, 8);
+    if (per_lane == 1) GSQ_STEP_LAUNCH(5, 1);
+    else if (per_lane == 2) GSQ_STEP_LAUNCH(5, 2);
+    else if (per_lane <= 4) GSQ_STEP_LAUNCH(5, 4);
+    else GSQ_STEP_LAUNCH(5, 8);
   } else {
-    if (per_lane == 1) GSQ_BWD_LAUNCH(4, 1);
-    else if (per_lane == 2) GSQ_BWD_LAUNCH(4, 2);
-    else if (per_lane <= 4) GSQ_BWD_LAUNCH(4, 4);
-    else GSQ_BWD_LAUNCH(4, 8);
+    if (per_lane == 1) GSQ_STEP_LAUNCH(4, 1);
+    else if (per_lane == 2) GSQ_STEP_LAUNCH(4, 2);
+    else if (per_lane <= 4) GSQ_STEP_LAUNCH(4, 4);
+    else GSQ_STEP_LAUNCH(4, 8);
   }
-#undef GSQ_BWD_LAUNCH
+#undef GSQ_STEP_LAUNCH
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }

@@ -67,9 +67,15 @@ def pad8(n: int) -> int:
 class Terms:
     """An fp32 matrix held as up to three bf16 terms [rows, ld] (K-major GEMM operand)."""
 
-    def __init__(self, rows, cols, n_terms=3, device=None, ld=None):
+    def __init__(self, rows, cols, n_terms=3, device=None, ld=None, tensors=None):
         self.rows, self.cols, self.n = int(rows), int(cols), int(n_terms)
         self.ld = pad8(cols) if ld is None else int(ld)
+        if tensors is not None:
+            # views of existing storage, e.g. one slice of a [R][3][rows][ld] buffer
+            self.t = list(tensors)[:self.n]
+            for t in self.t:
+                assert t.dtype == torch.bfloat16 and t.shape == (self.rows, self.ld)
+            return
         dev = device or _lib.device()
         self.t = [torch.zeros(self.rows, self.ld, device=dev, dtype=torch.bfloat16)
                   for _ in range(self.n)]

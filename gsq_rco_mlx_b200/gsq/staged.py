@@ -2,14 +2,15 @@
 
 ``SoftLinear`` is the device-resident training state of one linear (staged.py:230-317):
 plane-major logits and their Lion momentum, group scales and their momentum, and the GPTQ
-codes j0. Its ``soft`` builds one Gumbel-softmax soft weight (staged.py:271-298) and its
-``backward_lion`` runs the fused soft backward + resample average + Lion
-(staged.py:383-392 with lion.py:44-56), both as single CUDA launches.
+codes j0. Its ``soft`` builds one Gumbel-softmax soft weight (staged.py:271-298) and stores
+the draw's probabilities; its ``step`` is one fused pass: the soft backward from the stored
+probabilities, the resample mean and Lion (staged.py:383-392 with lion.py:44-56), and the next
+step's soft weights.
 
 ``train_linears`` is the qk-stage optimiser (staged.py:357-400 with the linear loss of
 :322-329): per step the schedules, a sorted micro-batch draw from the numpy stream, R
-resamples of (soft weight, residual GEMM, loss, weight-gradient GEMM), then one fused
-backward + Lion launch per linear.
+resamples of (residual GEMM with the loss in its epilogue, weight-gradient GEMM), then one
+fused step launch per linear.
 
 Gumbel noise: Philox4x32-10 keyed by (stage seed, linear id) with counter (weight, block,
 step, resample), drawn inside the kernels, or host-supplied planes for parity runs.
@@ -81,31 +82,35 @@ class SoftLinear:
         return self.out_f * self.in_f
 
     def soft(self, tau, kappa, step, resample, seed, w_ref=None, out=None, noise=None,
-             terms: Terms = None):
+             terms=None, probs=None):
         """w_bar (or w_bar - w_ref) of one Gumbel draw: float32 [out, in] into ``out``, and/or
-        as three bf16 terms (the K-major B operand of the residual GEMM) into ``terms``."""
-        if out is None and terms is None:
+        three bf16 terms into ``terms`` (a [3, out, in] tensor, the residual GEMM's B operand);
+        ``probs`` ([K, d] float32) receives the draw's probabilities for the backward."""
+        if out is None and terms is None and probs is None:
             out = torch.empty(self.shape, device=self.logits.device, dtype=torch.float32)
-        if terms is not None and (terms.ld != self.in_f or terms.n != 3):
-            raise ValueError("soft-weight terms must be 3 x [out, in] with ld == in")
-        t = terms.t if terms is not None else [None, None, None]
         _lib.call("gsq_soft_fwd", _lib.ptr(self.logits), _lib.ptr(self.j0), _lib.ptr(self.scales),
                   _lib.ptr(noise), int(seed) & (2 ** 64 - 1), self.linear_id, int(step),
                   int(resample), self.out_f, self.in_f, self.group_size, self.bits, float(tau),
-                  float(kappa), _lib.ptr(w_ref), _lib.ptr(out), _lib.ptr(t[0]), _lib.ptr(t[1]),
-                  _lib.ptr(t[2]), _lib.stream_ptr())
-        return out if out is not None else terms
+                  float(kappa), _lib.ptr(w_ref), _lib.ptr(out), _lib.ptr(terms), _lib.ptr(probs),
+                  _lib.stream_ptr())
+        return out
 
-    def backward_lion(self, grad_w, tau, kappa, step, seed, lr_logits=LR_LOGITS,
-                      lr_scales=LR_SCALES, noise=None):
-        """Fused soft backward over grad_w [R, out, in], resample mean and Lion step."""
+    def step(self, probs, grad_w, tau, kappa, lr_logits=LR_LOGITS, lr_scales=LR_SCALES,
+             nxt=None):
+        """Fused backward of this step (stored probs [R, K, d], grad_w [R, out, in]), resample
+        mean and Lion; with nxt = dict(step, tau, kappa, seed, w_ref, terms | out, noise) also
+        the next step's forward (probs updated in place, soft weights written)."""
         R = grad_w.shape[0]
-        _lib.call("gsq_soft_bwd_lion", _lib.ptr(self.logits), _lib.ptr(self.mom), _lib.ptr(self.j0),
-                  _lib.ptr(self.scales), _lib.ptr(self.mom_s), _lib.ptr(grad_w), _lib.ptr(noise),
-                  int(seed) & (2 ** 64 - 1), self.linear_id, int(step), int(R), self.out_f,
-                  self.in_f, self.group_size, self.bits, float(tau), float(kappa),
-                  float(lr_logits), float(scale_lr(lr_scales, self.bits)), float(WEIGHT_DECAY),
-                  float(BETAS[0]), float(BETAS[1]), _lib.stream_ptr())
+        n = nxt or {}
+        _lib.call("gsq_soft_step", _lib.ptr(self.logits), _lib.ptr(self.mom), _lib.ptr(self.j0),
+                  _lib.ptr(self.scales), _lib.ptr(self.mom_s), _lib.ptr(probs), _lib.ptr(grad_w),
+                  int(R), self.out_f, self.in_f, self.group_size, self.bits, float(tau),
+                  float(kappa), float(lr_logits), float(scale_lr(lr_scales, self.bits)),
+                  float(WEIGHT_DECAY), float(BETAS[0]), float(BETAS[1]), int(nxt is not None),
+                  _lib.ptr(n.get("noise")), int(n.get("seed", 0)) & (2 ** 64 - 1), self.linear_id,
+                  int(n.get("step", 0)), float(n.get("tau", 1.0)), float(n.get("kappa", 1.0)),
+                  _lib.ptr(n.get("w_ref")), _lib.ptr(n.get("out")), _lib.ptr(n.get("terms")),
+                  _lib.stream_ptr())
 
     def hard_codes(self) -> np.ndarray:
         """Argmax codes of the learned logits (staged.py:300-314)."""
@@ -124,11 +129,11 @@ class SoftLinear:
 
 
 class LinearStep:
-    """The qk-stage step of the linears that read the same rows X [M, in] (staged.py:322-329):
-    per resample, soft weight terms (w_bar - W), the residual R = X (w_bar - W)^T on the
-    tensor cores with the loss partials and R^T terms written by its epilogue, then the
-    weight gradient G = 2 / (M out) R^T X; finally one fused backward + Lion per linear.
-    All operands are bf16 terms (three for float32 data, one for exactly-bf16 rows)."""
+    """The qk-stage step of the linears that read the same rows X [M, in] (staged.py:322-329).
+    Per resample r: R_r = X (w_bar_r - W)^T on the tensor cores (epilogue: loss partials and
+    R_r^T as bf16 terms), then G_r = 2 / (M out) R_r^T X. One fused pass per linear then runs
+    the backward, the resample mean, Lion, and the next step's soft weights and probabilities.
+    All GEMM operands are bf16 terms (three for float32 data, one for exactly-bf16 rows)."""
 
     def __init__(self, lins, M, in_f, resamples, x_terms=3):
         dev = lins[0].logits.device
@@ -136,13 +141,19 @@ class LinearStep:
         self.nx = int(x_terms)
         self.X = Terms(M, in_f, self.nx, dev)        # A of the residual GEMM
         self.XT = Terms(in_f, M, self.nx, dev)       # B of the weight-gradient GEMM
-        self.D = {l.name: Terms(l.out_f, l.in_f, 3, dev, ld=l.in_f) for l in lins}
+        R = self.R
+        self.Dbuf = {l.name: torch.zeros(R, 3, l.out_f, l.in_f, device=dev, dtype=torch.bfloat16)
+                     for l in lins}
+        self.D = {l.name: [Terms(l.out_f, l.in_f, 3, ld=l.in_f, tensors=self.Dbuf[l.name][r])
+                           for r in range(R)] for l in lins}
+        self.probs = {l.name: torch.zeros(R, l.K, l.d, device=dev, dtype=torch.float32)
+                      for l in lins}
         self.RT = {l.name: Terms(l.out_f, M, 3, dev) for l in lins}
-        self.grads = {l.name: torch.empty((self.R,) + l.shape, device=dev, dtype=torch.float32)
+        self.grads = {l.name: torch.empty((R,) + l.shape, device=dev, dtype=torch.float32)
                       for l in lins}
         tiles = max(((M + 127) // 128) * ((l.out_f + 127) // 128) for l in lins)
         self.sq = torch.zeros(tiles, device=dev, dtype=torch.float64)
-        self.loss = torch.zeros(len(lins) * self.R, device=dev, dtype=torch.float64)
+        self.loss = torch.zeros(len(lins) * R, device=dev, dtype=torch.float64)
         self.seq = torch.zeros(64, device=dev, dtype=torch.int32)
         self.dev = dev
 
@@ -157,28 +168,39 @@ class LinearStep:
                   int(per_seq), int(seq_stride), int(offset), self.M, self.in_f, self.nx,
                   self.X.ptrs(), self.X.ld, self.XT.ptrs(), self.XT.ld, _lib.stream_ptr())
 
-    def forward_backward(self, targets, t, tau, kappa, noise_seed, noise_of=None):
-        """Residuals, losses and weight gradients of every linear and resample."""
-        for li, lin in enumerate(self.lins):
-            D, RT, G = self.D[lin.name], self.RT[lin.name], self.grads[lin.name]
+    def first_forward(self, targets, t, tau, kappa, noise_seed, noise_of=None):
+        """Soft weights and probabilities of the first step of the stage."""
+        for lin in self.lins:
             for r in range(self.R):
                 noise = None if noise_of is None else noise_of(t, r, lin)
                 lin.soft(tau, kappa, t, r, noise_seed, w_ref=targets[lin.name], noise=noise,
-                         terms=D)
-                gemm_tc(self.X, D, ct_terms=RT, sq_partial=self.sq)
-                tiles = ((self.M + 127) // 128) * ((lin.out_f + 127) // 128)
+                         terms=self.Dbuf[lin.name][r], probs=self.probs[lin.name][r])
+
+    def contract(self):
+        """Residuals, losses and weight gradients of every linear and resample."""
+        for li, lin in enumerate(self.lins):
+            RT, G = self.RT[lin.name], self.grads[lin.name]
+            tiles = ((self.M + 127) // 128) * ((lin.out_f + 127) // 128)
+            for r in range(self.R):
+                gemm_tc(self.X, self.D[lin.name][r], ct_terms=RT, sq_partial=self.sq)
                 slot = self.loss[li * self.R + r:li * self.R + r + 1]
                 _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(slot),
                           _lib.stream_ptr())
                 gemm_tc(RT, self.XT, alpha=2.0 / (self.M * lin.out_f), C=G[r])
 
-    def update(self, t, tau, kappa, noise_seed, opts, noise_of=None):
+    def update(self, targets, t, tau, kappa, opts, noise_seed, nxt=None, noise_of=None):
+        """Fused backward + Lion of step t; nxt = (t1, tau1, kappa1) also runs step t1's forward."""
         for lin in self.lins:
-            stacked = None
-            if noise_of is not None:
-                stacked = torch.stack([noise_of(t, r, lin) for r in range(self.R)]).contiguous()
-            lin.backward_lion(self.grads[lin.name], tau, kappa, t, noise_seed, opts.lr_logits,
-                              opts.lr_scales, noise=stacked)
+            n = None
+            if nxt is not None:
+                t1, tau1, kappa1 = nxt
+                noise = None
+                if noise_of is not None:
+                    noise = torch.stack([noise_of(t1, r, lin) for r in range(self.R)]).contiguous()
+                n = {"step": t1, "tau": tau1, "kappa": kappa1, "seed": noise_seed,
+                     "w_ref": targets[lin.name], "terms": self.Dbuf[lin.name], "noise": noise}
+            lin.step(self.probs[lin.name], self.grads[lin.name], tau, kappa, opts.lr_logits,
+                     opts.lr_scales, nxt=n)
 
     def mean_loss(self):
         """sum over linears of mean R^2, averaged over resamples (staged.py:386-394)."""
@@ -208,13 +230,16 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
     flat = x_all.view(n_seq * T, in_f)
     err_flag(step.dev).zero_()
     history, step_s = [], []
+    tau, kappa = gs_schedules(0, opts.steps)
+    step.first_forward(targets, 0, tau, kappa, noise_seed, noise_of)
     for t in range(opts.steps):
         t0 = time.perf_counter()
         tau, kappa = gs_schedules(t, opts.steps)
         idx = np.sort(rng.choice(n_seqs, size=m, replace=False))
         step.stage(flat, idx, T - 1, T, 1)
-        step.forward_backward(targets, t, tau, kappa, noise_seed, noise_of)
-        step.update(t, tau, kappa, noise_seed, opts, noise_of)
+        step.contract()
+        nxt = (t + 1, *gs_schedules(t + 1, opts.steps)) if t + 1 < opts.steps else None
+        step.update(targets, t, tau, kappa, opts, noise_seed, nxt=nxt, noise_of=noise_of)
         history.append(step.mean_loss())
         if sync_timing:
             torch.cuda.synchronize()

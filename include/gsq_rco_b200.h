@@ -41,39 +41,46 @@ const char *gsq_status_string(int status);
 
 /* ------------------------------------------------------------------ GSQ ---------- */
 
-/* Soft weight of one Gumbel-softmax draw:
- *   p = softmax((kappa * l + g) / tau) over the K candidates, c = sum_k p_k C_k,
+/* Soft weight of one Gumbel-softmax draw (the forward of the first step of a stage):
+ *   p = softmax((kappa * l + g) * (1 / tau)) over the K candidates, c = sum_k p_k C_k,
  *   w_bar[o, i] = scales[o, i / group_size] * c,  out = w_bar - w_ref (w_ref may be NULL).
  * C_k = grid[clip(j0 + k - 2)] (bits 3..7) or grid[k] (bits 2). Gumbel g comes from `noise`
- * ([K][d] float32, host-supplied) or, if noise == NULL, from Philox4x32-10 with
- * key (seed, linear_id) and counter (i, block, step, resample).
- * Outputs (any may be NULL): w_out float32 [out_f][in_f]; w_hi / w_mid / w_lo bf16 [out_f][in_f]
- * with out == hi + mid + lo to float32 precision.
+ * ([K][d] float32, host-supplied) or, if noise == NULL, from one Philox4x32-10 call per
+ * weight with key (seed, linear_id) and counter (i, 0, step, resample): plane k < 4 from the
+ * high 24 bits of word k, plane 4 from the low bytes of words 0..2; g = -log(-log u) with
+ * u = (bits + 0.5) 2^-24 clipped to [1e-7, 1 - 1e-7].
+ * Outputs (at least one): w_out float32 [out_f][in_f]; w_terms bf16 [3][out_f][in_f] with
+ * out == t0 + t1 + t2 to float32 precision (the GEMM operand); p_out float32 [K][d].
  * Replaces: src/gsq_rco/gsq/staged.py:271-298 (_Linear.soft) with :82-84 (_gs_softmax),
  * :92-96 (_gumbel), :99-106 (_grid_rows, _shift_rows); the residual of staged.py:327. */
 int gsq_soft_fwd(const float *logits, const uint8_t *j0, const float *scales, const float *noise,
                  uint64_t seed, uint32_t linear_id, uint32_t step, uint32_t resample,
                  int out_f, int in_f, int group_size, int bits, float tau, float kappa,
-                 const float *w_ref, float *w_out, void *w_hi, void *w_mid, void *w_lo,
-                 void *stream);
+                 const float *w_ref, float *w_out, void *w_terms, float *p_out, void *stream);
 
-/* Fused soft backward + Lion for one linear. grad_w holds dL/dw_bar of each resample,
- * [resamples][out_f][in_f]. For each resample the probabilities are recomputed from the same
- * noise as gsq_soft_fwd (noise [resamples][K][d], or Philox when NULL), and
- *   u_k = s G C_k,  dL/dl = (kappa / tau) p (u - <p, u>),  dL/ds = sum over the group of G c;
- * the gradients are summed over resamples and divided by their count, then one Lion step
- *   m' = b1 m + (1 - b1) g;  p <- p - lr (sign(m') + wd p);  m <- b2 m + (1 - b2) g
- * updates logits/mom_logits (lr_logits) and scales/mom_scales (lr_scales; 0 freezes them).
- * The betas and wd are the caller's float64 values: b, 1 - b and wd are each rounded to
- * float32 once, as MLX does for Python scalars. resamples: 1..8.
+/* One fused pass per GSQ step over the training state of a linear:
+ *   backward of this step from the stored probabilities probs [R][K][d] and the weight
+ *   gradients grad_w [R][out_f][in_f] (dL/dw_bar per resample):
+ *     u_k = s G C_k,  dL/dl = (kappa / tau) p (u - <p, u>),  dL/ds = sum over the group of G c,
+ *   summed over the R resamples and divided by R; one Lion step
+ *     m' = b1 m + (1 - b1) g;  p <- p - lr (sign(m') + wd p);  m <- b2 m + (1 - b2) g
+ *   on logits/mom_logits (lr_logits) and scales/mom_scales (lr_scales; 0 freezes them);
+ *   then, if next != 0, the forward of step next_step with the updated state: new
+ *   probabilities into probs (in place) and the soft weights (minus w_ref) into w_out
+ *   [R][out_f][in_f] float32 and/or w_terms bf16 [R][3][out_f][in_f]. noise_next: host-supplied
+ *   Gumbel planes [R][K][d] of the next step, or NULL for Philox (as gsq_soft_fwd).
+ * The betas and wd are the caller's float64 values, each of b, 1 - b, wd rounded to float32
+ * once (MLX's treatment of Python scalars). resamples: 1..8; group_size <= 256.
  * Replaces: the MLX autodiff of staged.py:322-329 through :271-298, the resample average of
- * staged.py:383-390, and lion_update src/gsq_rco/gsq/lion.py:44-56. */
-int gsq_soft_bwd_lion(float *logits, float *mom_logits, const uint8_t *j0, float *scales,
-                      float *mom_scales, const float *grad_w, const float *noise,
-                      uint64_t seed, uint32_t linear_id, uint32_t step, int resamples,
-                      int out_f, int in_f, int group_size, int bits, float tau, float kappa,
-                      float lr_logits, float lr_scales, double wd, double beta1, double beta2,
-                      void *stream);
+ * staged.py:383-390, lion_update src/gsq_rco/gsq/lion.py:44-56, and the next step's
+ * _Linear.soft (staged.py:271-298). */
+int gsq_soft_step(float *logits, float *mom_logits, const uint8_t *j0, float *scales,
+                  float *mom_scales, float *probs, const float *grad_w, int resamples, int out_f,
+                  int in_f, int group_size, int bits, float tau, float kappa, float lr_logits,
+                  float lr_scales, double wd, double beta1, double beta2, int next,
+                  const float *noise_next, uint64_t seed, uint32_t linear_id, uint32_t next_step,
+                  float tau_next, float kappa_next, const float *w_ref, float *w_out,
+                  void *w_terms, void *stream);
 
 /* Argmax decode of trained logits to uint8 codes [out_f][in_f] (first maximum wins;
  * local shift clipped to the grid). Replaces staged.py:300-314 (_Linear.hard_codes) and

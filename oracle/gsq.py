@@ -127,13 +127,16 @@ def scale_lr(lr_scales: float, bits: int) -> float:
 # ----------------------------------------------------------- soft weight ---
 
 def gs_probs(logits_kd, noise_kd, tau, kappa):
-    """staged.py:82-84: p = softmax((kappa * l + g) / tau) over the candidate axis, float32."""
-    tau = np.float32(tau)
+    """staged.py:82-84: p = softmax((kappa * l + g) / tau) over the candidate axis, float32.
+    The division by tau and by the sum are multiplications by the float32 reciprocals, the
+    order of operations of the CUDA kernels."""
+    inv_tau = np.float32(1.0) / np.float32(tau)
     kappa = np.float32(kappa)
-    y = (kappa * logits_kd.astype(np.float32) + noise_kd.astype(np.float32)) / tau
+    y = (kappa * logits_kd.astype(np.float32) + noise_kd.astype(np.float32)) * inv_tau
     y = y - y.max(axis=0, keepdims=True)
     e = np.exp(y)
-    return e / e.sum(axis=0, keepdims=True)
+    inv = np.float32(1.0) / e.sum(axis=0, keepdims=True)
+    return e * inv
 
 
 def expand_scales(scales, in_f, group_size):

@@ -12,8 +12,9 @@ g = -log(-log u) in float32 (staged.py:95-96).
 
 Counter / key assignment (the CUDA kernels use the same):
   key     = (seed_lo32, seed_hi32 ^ linear_id)
-  counter = (i, block, step, resample)   block 0 -> logit planes 0..3, block 1 -> plane 4
-  u       = ((x >> 8) + 0.5) * 2^-24     (24 random bits, strictly inside (0, 1))
+  counter = (i, 0, step, resample)       one Philox call per weight and draw, x0..x3
+  bits    = plane k < 4: x_k >> 8;  plane 4: (x0 & 255) | (x1 & 255) << 8 | (x2 & 255) << 16
+  u       = (bits + 0.5) * 2^-24         (24 random bits, strictly inside (0, 1))
 """
 from __future__ import annotations
 
@@ -51,9 +52,15 @@ def philox4x32_10(c0, c1, c2, c3, k0, k1):
 
 
 def uniform_from_bits(x):
-    """24-bit uniform in (0, 1), float32: ((x >> 8) + 0.5) * 2^-24."""
+    """24-bit uniform in (0, 1), float32, from the high 24 bits: ((x >> 8) + 0.5) * 2^-24."""
     x = np.asarray(x, dtype=np.uint32)
-    return ((x >> np.uint32(8)).astype(np.float32) + np.float32(0.5)) * np.float32(2.0 ** -24)
+    return uniform_from_24(x >> np.uint32(8))
+
+
+def uniform_from_24(b):
+    """(b + 0.5) * 2^-24 in float32 for 24-bit integers b."""
+    return (np.asarray(b, dtype=np.uint32).astype(np.float32) + np.float32(0.5)) * \
+        np.float32(2.0 ** -24)
 
 
 def gumbel_from_uniform(u):
@@ -69,10 +76,11 @@ def gumbel_planes(seed: int, linear_id: int, step: int, resample: int, d: int, n
     k1 = ((seed >> 32) ^ int(linear_id)) & 0xFFFFFFFF
     i = np.arange(d, dtype=np.uint32)
     out = np.empty((n_planes, d), dtype=np.float32)
-    r0 = philox4x32_10(i, 0, step, resample, k0, k1)
+    x = philox4x32_10(i, 0, step, resample, k0, k1)
     for k in range(min(4, n_planes)):
-        out[k] = gumbel_from_uniform(uniform_from_bits(r0[k]))
+        out[k] = gumbel_from_uniform(uniform_from_bits(x[k]))
     if n_planes > 4:
-        r1 = philox4x32_10(i, 1, step, resample, k0, k1)
-        out[4] = gumbel_from_uniform(uniform_from_bits(r1[0]))
+        lo = (x[0] & np.uint32(255)) | ((x[1] & np.uint32(255)) << np.uint32(8)) | \
+             ((x[2] & np.uint32(255)) << np.uint32(16))
+        out[4] = gumbel_from_uniform(uniform_from_24(lo))
     return out

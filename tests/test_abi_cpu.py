@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), n
     assert set(_lib.SIGNATURES) | {"gsq_status_string"} >= set(names)
-    assert lib.gsq_abi_version() == 1
+    assert lib.gsq_abi_version() == 2
     assert lib.gsq_status_string(1) == b"invalid argument"
 
 
@@ -38,9 +38,9 @@ def test_bad_arguments_are_rejected_without_launch():
     """Argument validation happens before any CUDA call (no device needed)."""
     lib = _lib.load()
     assert lib.gsq_soft_fwd(None, None, None, None, 0, 0, 0, 0, 4, 4, 64, 3, 1.0, 100.0,
-                            None, None, None, None, None, None) == _lib.GSQ_EINVAL
+                            None, None, None, None, None) == _lib.GSQ_EINVAL
     assert lib.gsq_soft_fwd(None, None, None, None, 0, 0, 0, 0, 4, 4, 64, 8, 1.0, 100.0,
-                            None, None, None, None, None, None) == _lib.GSQ_ENOTSUP
+                            None, None, None, None, None) == _lib.GSQ_ENOTSUP
     assert lib.mckp_dp_f64(None, None, 1, 3, 2, 10, None, None, None, None) == _lib.GSQ_EINVAL
     assert lib.gptq_sweep(None, None, None, 4, 4, 3, 64, 128, 1, None, None, None,
                           None) == _lib.GSQ_EINVAL

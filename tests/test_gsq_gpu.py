@@ -64,7 +64,10 @@ def test_backward_lion_one_step():
         acc_s = gsc if acc_s is None else acc_s + gsc
     ogsq.lion_step(st, acc_g / np.float32(2), acc_s / np.float32(2))
     grads = torch.as_tensor(np.stack(Gs), device=DEV)
-    lin.backward_lion(grads, tau, kappa, 5, 9)
+    P = torch.empty(2, 5, W.size, device=DEV)
+    for r in range(2):
+        lin.soft(tau, kappa, 5, r, 9, probs=P[r])
+    lin.step(P, grads, tau, kappa)
     lg, mm = lin.logits.cpu().numpy(), lin.mom.cpu().numpy()
     # Lion moves by +-lr: a sign decided by rounding differs by 2 lr on a handful of entries
     diff = np.abs(lg - st.logits)
@@ -89,18 +92,47 @@ def test_gradient_matches_reference_oracle_2bit():
     noises = torch.as_tensor(np.ascontiguousarray(z["lg_noise"].transpose(0, 2, 1)), device=DEV)
     Xt, Wt = torch.as_tensor(X, device=DEV), torch.as_tensor(W, device=DEV)
     grads = torch.empty(3, *W.shape, device=DEV)
+    P = torch.empty(3, 4, W.size, device=DEV)
     loss = 0.0
     for r in range(3):
-        D = lin.soft(tau, kappa, 0, r, 0, w_ref=Wt, noise=noises[r].contiguous())
+        D = lin.soft(tau, kappa, 0, r, 0, w_ref=Wt, noise=noises[r].contiguous(),
+                     out=torch.empty(W.shape, device=DEV), probs=P[r])
         Rm = mm_nt(Xt, D)
         loss += float((Rm.double() ** 2).mean())
         mm_tn(Rm, Xt, alpha=2.0 / (X.shape[0] * W.shape[0]), out=grads[r])
-    lin.backward_lion(grads, tau, kappa, 0, 0, lr_logits=0.0, lr_scales=0.0, noise=noises)
+    lin.step(P, grads, tau, kappa, lr_logits=0.0, lr_scales=0.0)
     g_log = lin.mom.cpu().numpy().T / np.float32(0.05)
     g_sc = lin.mom_s.cpu().numpy() / np.float32(0.05)
     assert abs(loss / 3 - float(z["lg_loss"])) <= 1e-5 * float(z["lg_loss"])
     np.testing.assert_allclose(g_log, z["lg_glog"], rtol=2e-3, atol=2e-4 * np.abs(z["lg_glog"]).max())
     np.testing.assert_allclose(g_sc, z["lg_gscale"], rtol=2e-3, atol=2e-4 * np.abs(z["lg_gscale"]).max())
+
+
+def test_fused_step_forward_equals_fresh_forward():
+    """The next-step forward inside the fused pass equals a separate soft() of the updated
+    state: same probabilities and the same bf16 terms."""
+    W, lin, st = make_linear()
+    rng = np.random.default_rng(8)
+    tau, kappa = ogsq.gs_schedules(10, 200)
+    tau1, kappa1 = ogsq.gs_schedules(11, 200)
+    Wt = torch.as_tensor(W, device=DEV)
+    P = torch.empty(2, 5, W.size, device=DEV)
+    for r in range(2):
+        lin.soft(tau, kappa, 10, r, 4, w_ref=Wt, probs=P[r])
+    grads = torch.as_tensor((1e-3 * rng.standard_normal((2,) + W.shape)).astype(np.float32), device=DEV)
+    terms = torch.zeros(2, 3, *W.shape, device=DEV, dtype=torch.bfloat16)
+    lin.step(P, grads, tau, kappa, nxt={"step": 11, "tau": tau1, "kappa": kappa1, "seed": 4,
+                                        "w_ref": Wt, "terms": terms})
+    for r in range(2):
+        Pf = torch.empty(5, W.size, device=DEV)
+        Tf = torch.zeros(3, *W.shape, device=DEV, dtype=torch.bfloat16)
+        lin.soft(tau1, kappa1, 11, r, 4, w_ref=Wt, terms=Tf, probs=Pf)
+        assert torch.equal(Pf, P[r])
+        assert torch.equal(Tf, terms[r])
+    # the terms reconstruct w_bar - W to float32 precision
+    wf = lin.soft(tau1, kappa1, 11, 0, 4, w_ref=Wt)
+    rec = terms[0].float().sum(0)
+    assert torch.equal(rec, wf) or (rec - wf).abs().max() <= 1e-7 * wf.abs().max()
 
 
 def test_harden_matches_oracle():
