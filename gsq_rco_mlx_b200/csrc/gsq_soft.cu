@@ -241,6 +241,167 @@ __global__ void __launch_bounds__(256) soft_step_kernel(const StepArgs a) {
   }
 }
 
+// Vectorised form of soft_step_kernel for group sizes that are multiples of 64 and a
+// compile-time resample count: a warp owns one (row, group), each lane two adjacent columns of
+// every 64-column chunk (8-byte loads and stores), and every input of a lane's two weights is
+// loaded before any arithmetic, so each lane keeps ~2 (2K + R(K + 1) + 2) loads in flight.
+template <int K, int R>
+__global__ void __launch_bounds__(256) soft_step_v2_kernel(const StepArgs a) {
+  const int64_t d = (int64_t)a.out_f * a.in_f;
+  const int lane = threadIdx.x & 31;
+  const int64_t n_units = (int64_t)a.out_f * a.G;
+  const float fR = (float)R;
+  const int n_chunks = a.gs / 64;
+  for (int64_t unit = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; unit < n_units;
+       unit += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int row = (int)(unit / a.G), grp = (int)(unit - (int64_t)row * a.G);
+    const float s = a.scales[unit];
+    // pass 1: gradients of every chunk; the per-weight sums stay in registers only for one
+    // chunk, so a chunk is re-read in pass 2 (Lion and the next forward)
+    float gsum_r[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) gsum_r[r] = 0.f;
+    double part[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) part[r] = 0.0;
+    for (int ch = 0; ch < n_chunks; ++ch) {
+      const int col = grp * a.gs + ch * 64 + 2 * lane;
+      if (col >= a.in_f) continue;  // in_f is a multiple of 64 on this path
+      const int64_t i = (int64_t)row * a.in_f + col;
+      float2 pv[R][K];
+      float2 Gv[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+          pv[r][k] = *reinterpret_cast<const float2*>(a.probs + ((int64_t)r * K + k) * d + i);
+        Gv[r] = *reinterpret_cast<const float2*>(a.grad_w + (int64_t)r * d + i);
+      }
+      const uchar2 jj = K == 5 ? *reinterpret_cast<const uchar2*>(a.j0 + i) : make_uchar2(0, 0);
+      float C0[K], C1[K];
+      SoftMath<K>::candidates(a.bits, jj.x, C0);
+      SoftMath<K>::candidates(a.bits, jj.y, C1);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float p0[K], p1[K];
+#pragma unroll
+        for (int k = 0; k < K; ++k) { p0[k] = pv[r][k].x; p1[k] = pv[r][k].y; }
+        part[r] += (double)Gv[r].x * (double)SoftMath<K>::value(p0, C0);
+        part[r] += (double)Gv[r].y * (double)SoftMath<K>::value(p1, C1);
+      }
+    }
+    float gsum = 0.f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float gr = (float)warp_sum_d(part[r]);
+      gsum = r == 0 ? gr : __fadd_rn(gsum, gr);
+    }
+    float s_new = s;
+    if (lane == 0) {
+      float mv = a.mom_s[unit];
+      lion1(s_new, mv, __fdiv_rn(gsum, fR), a.lr_s, a.lc);
+      a.scales[unit] = s_new;
+      a.mom_s[unit] = mv;
+    }
+    s_new = __shfl_sync(0xffffffffu, s_new, 0);
+    (void)gsum_r;
+    // pass 2: logit gradients, Lion, next forward
+    for (int ch = 0; ch < n_chunks; ++ch) {
+      const int col = grp * a.gs + ch * 64 + 2 * lane;
+      if (col >= a.in_f) continue;
+      const int64_t i = (int64_t)row * a.in_f + col;
+      float2 lv[K], mv[K], pv[R][K];
+      float2 Gv[R];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        lv[k] = *reinterpret_cast<const float2*>(a.logits + k * d + i);
+        mv[k] = *reinterpret_cast<const float2*>(a.mom + k * d + i);
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+          pv[r][k] = *reinterpret_cast<const float2*>(a.probs + ((int64_t)r * K + k) * d + i);
+        Gv[r] = *reinterpret_cast<const float2*>(a.grad_w + (int64_t)r * d + i);
+      }
+      const uchar2 jj = K == 5 ? *reinterpret_cast<const uchar2*>(a.j0 + i) : make_uchar2(0, 0);
+      const float2 wr = a.w_ref && a.next ? *reinterpret_cast<const float2*>(a.w_ref + i)
+                                          : make_float2(0.f, 0.f);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float C[K], acc[K], l[K], m[K];
+        SoftMath<K>::candidates(a.bits, e ? jj.y : jj.x, C);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float p[K];
+#pragma unroll
+          for (int k = 0; k < K; ++k) p[k] = e ? pv[r][k].y : pv[r][k].x;
+          const float sG = __fmul_rn(s, e ? Gv[r].y : Gv[r].x);
+          float u[K];
+          float pu = 0.f;
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+            u[k] = __fmul_rn(sG, C[k]);
+            pu = k == 0 ? __fmul_rn(p[0], u[0]) : __fadd_rn(pu, __fmul_rn(p[k], u[k]));
+          }
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+            const float gl = __fmul_rn(a.kt, __fmul_rn(p[k], __fsub_rn(u[k], pu)));
+            acc[k] = r == 0 ? gl : __fadd_rn(acc[k], gl);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          l[k] = e ? lv[k].y : lv[k].x;
+          m[k] = e ? mv[k].y : mv[k].x;
+          lion1(l[k], m[k], __fdiv_rn(acc[k], fR), a.lr_l, a.lc);
+          if (e) { lv[k].y = l[k]; mv[k].y = m[k]; } else { lv[k].x = l[k]; mv[k].x = m[k]; }
+        }
+        if (a.next) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            float g[K], p[K];
+            const NoiseKey nk = make_noise_key(a.seed, a.linear_id, a.next_step, (uint32_t)r);
+            SoftMath<K>::noise(a.noise ? a.noise + (int64_t)r * K * d : nullptr, d, i + e, nk, g);
+            SoftMath<K>::probs(l, g, a.inv_tau1, a.kappa1, p);
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+              if (e) pv[r][k].y = p[k]; else pv[r][k].x = p[k];
+            }
+            float w = __fmul_rn(s_new, SoftMath<K>::value(p, C));
+            if (a.w_ref) w = __fsub_rn(w, e ? wr.y : wr.x);
+            Gv[r].x = e ? Gv[r].x : w;  // reuse: slot x/y holds the new soft weight
+            Gv[r].y = e ? w : Gv[r].y;
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        *reinterpret_cast<float2*>(a.logits + k * d + i) = lv[k];
+        *reinterpret_cast<float2*>(a.mom + k * d + i) = mv[k];
+      }
+      if (a.next) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+#pragma unroll
+          for (int k = 0; k < K; ++k)
+            *reinterpret_cast<float2*>(a.probs + ((int64_t)r * K + k) * d + i) = pv[r][k];
+          if (a.w_out) *reinterpret_cast<float2*>(a.w_out + (int64_t)r * d + i) = Gv[r];
+          if (a.terms) {
+            __nv_bfloat16 h0, m0, l0, h1, m1, l1;
+            split3_bf16(Gv[r].x, h0, m0, l0);
+            split3_bf16(Gv[r].y, h1, m1, l1);
+            __nv_bfloat16* tb = a.terms + (int64_t)r * 3 * d + i;
+            *reinterpret_cast<__nv_bfloat162*>(tb) = __halves2bfloat162(h0, h1);
+            *reinterpret_cast<__nv_bfloat162*>(tb + d) = __halves2bfloat162(m0, m1);
+            *reinterpret_cast<__nv_bfloat162*>(tb + 2 * d) = __halves2bfloat162(l0, l1);
+          }
+        }
+      }
+    }
+  }
+}
+
 template <int K>
 __global__ void harden_kernel(const float* __restrict__ logits, const uint8_t* __restrict__ j0,
                               int64_t d, int bits, uint8_t* __restrict__ codes) {
@@ -356,6 +517,20 @@ extern "C" int gsq_soft_step(float* logits, float* mom_logits, const uint8_t* j0
   const int64_t units = (int64_t)out_f * a.G;
   const unsigned grid = grid_for(units * 32, 256);
   cudaStream_t st = (cudaStream_t)stream;
+  // vectorised path: 64-column chunks, 8-byte aligned planes, resamples 1 or 2
+  const bool vec = (group_size % 64 == 0) && (in_f % 64 == 0) && (resamples <= 2) &&
+                   ((uintptr_t)logits % 8 == 0) && ((uintptr_t)mom_logits % 8 == 0) &&
+                   ((uintptr_t)probs % 8 == 0) && ((uintptr_t)grad_w % 8 == 0) &&
+                   (!w_ref || (uintptr_t)w_ref % 8 == 0) && (!w_out || (uintptr_t)w_out % 8 == 0) &&
+                   (!w_terms || (uintptr_t)w_terms % 4 == 0) && ((uintptr_t)j0 % 2 == 0);
+  if (vec) {
+    if (K == 5 && resamples == 2) soft_step_v2_kernel<5, 2><<<grid, 256, 0, st>>>(a);
+    else if (K == 5) soft_step_v2_kernel<5, 1><<<grid, 256, 0, st>>>(a);
+    else if (resamples == 2) soft_step_v2_kernel<4, 2><<<grid, 256, 0, st>>>(a);
+    else soft_step_v2_kernel<4, 1><<<grid, 256, 0, st>>>(a);
+    GSQ_CHECK_LAUNCH();
+    return GSQ_OK;
+  }
 #define GSQ_STEP_LAUNCH(KK, MW) soft_step_kernel<KK, MW><<<grid, 256, 0, st>>>(a)
   if (K == 5) {
     if (per_lane == 1) GSQ_STEP_LAUNCH(5, 1);
