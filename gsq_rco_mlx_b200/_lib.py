@@ -36,6 +36,7 @@ SIGNATURES = {
     "gsq_gemm_tc": [_i32, _i32, _i32, _vp, _i32, _i64, _vp, _i32, _i64, _i32, _f32, _vp, _i64,
                     _f32, _vp, _i32, _i64, _vp, _i32, _i64, _vp, _vp, _vp],
     "gsq_split_bf16": [_vp, _i32, _i32, _i64, _i32, _vp, _vp, _vp, _i64, _vp],
+    "gsq_gemm": [_vp, _vp],
     "gsq_gather_split": [_vp, _i64, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp,
                          _i64, _vp],
     "gsq_sum_f64": [_vp, _i32, _vp, _vp],

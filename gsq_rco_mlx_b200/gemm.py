@@ -124,6 +124,87 @@ def check_err(dev):
         raise _lib.GsqError(f"tensor-core GEMM: bounded wait timed out (code {e})")
 
 
+class GemmDesc(_C.Structure):
+    """ctypes mirror of gsq_gemm_desc (include/gsq_rco_b200.h)."""
+    _fields_ = [
+        ("M", _C.c_int), ("N", _C.c_int), ("K", _C.c_int), ("batch", _C.c_int),
+        ("a", _C.c_void_p * 3), ("na", _C.c_int), ("lda", _C.c_int64), ("a_rows", _C.c_int64),
+        ("b", _C.c_void_p * 3), ("b2", _C.c_void_p * 3), ("nb", _C.c_int), ("ldb", _C.c_int64),
+        ("b_rows", _C.c_int64),
+        ("order", _C.c_int), ("causal", _C.c_int), ("epi", _C.c_int), ("bn", _C.c_int),
+        ("alpha", _C.c_float), ("beta", _C.c_float),
+        ("C", _C.c_void_p), ("ldc", _C.c_int64),
+        ("cs", _C.c_void_p * 3), ("ncs", _C.c_int), ("ldcs", _C.c_int64),
+        ("ct", _C.c_void_p * 3), ("nct", _C.c_int), ("ldct", _C.c_int64), ("ct_up_rows", _C.c_int64),
+        ("sq_partial", _C.c_void_p), ("bias", _C.c_void_p), ("resid", _C.c_void_p),
+        ("target", _C.c_void_p), ("ld_rt", _C.c_int64), ("out_scale", _C.c_float),
+        ("aux0", _C.c_void_p), ("aux1", _C.c_void_p), ("ld_aux", _C.c_int64),
+        ("a_div", _C.c_int), ("a_s1", _C.c_int64), ("a_s2", _C.c_int64),
+        ("b_div", _C.c_int), ("b_s1", _C.c_int64), ("b_s2", _C.c_int64),
+        ("c_div", _C.c_int), ("c_s1", _C.c_int64), ("c_s2", _C.c_int64),
+        ("t_div", _C.c_int), ("t_r1", _C.c_int64), ("t_r2", _C.c_int64), ("t_c1", _C.c_int64),
+        ("t_c2", _C.c_int64),
+        ("err", _C.c_void_p),
+    ]
+
+
+def _tp(t):
+    return None if t is None else t.data_ptr()
+
+
+def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, alpha=1.0,
+         beta=0.0, C=None, ldc=None, c_terms: Terms = None, ct_terms: Terms = None,
+         sq_partial=None, bias=None, resid=None, target=None, ld_rt=None, out_scale=1.0,
+         aux0=None, aux1=None, ld_aux=None, B2: Terms = None, epi=0, bn=128, causal=False,
+         batch=1, a_off=(1, 0, 0), b_off=(1, 0, 0), c_off=(1, 0, 0), t_off=(1, 0, 0, 0, 0),
+         ct_up_rows=0):
+    """One (batched) tensor-core GEMM with a fused epilogue; see gsq_gemm in the C header.
+    M, N, K default to the operand shapes; a_off/b_off/c_off = (div, s1, s2),
+    t_off = (div, row_s1, row_s2, col_s1, col_s2)."""
+    d = GemmDesc()
+    d.M = A.rows if M is None else M
+    d.N = (B.rows if epi != 2 else 2 * B.rows) if N is None else N
+    d.K = A.cols if K is None else K
+    d.batch = batch
+    na = A.n if na is None else na
+    nb = B.n if nb is None else nb
+    for i in range(na):
+        d.a[i] = A.t[i].data_ptr()
+    d.na, d.lda, d.a_rows = na, A.ld, A.rows
+    for j in range(nb):
+        d.b[j] = B.t[j].data_ptr()
+        if B2 is not None:
+            d.b2[j] = B2.t[j].data_ptr()
+    d.nb, d.ldb, d.b_rows = nb, B.ld, B.rows
+    d.order, d.causal, d.epi, d.bn = order, int(causal), epi, bn
+    d.alpha, d.beta = alpha, beta
+    d.C = _tp(C)
+    d.ldc = (C.stride(0) if C is not None and C.dim() == 2 else d.N) if ldc is None else ldc
+    if c_terms is not None:
+        for i in range(c_terms.n):
+            d.cs[i] = c_terms.t[i].data_ptr()
+        d.ncs, d.ldcs = c_terms.n, c_terms.ld
+    if ct_terms is not None:
+        for i in range(ct_terms.n):
+            d.ct[i] = ct_terms.t[i].data_ptr()
+        d.nct, d.ldct = ct_terms.n, ct_terms.ld
+    d.ct_up_rows = ct_up_rows
+    d.sq_partial = _tp(sq_partial)
+    d.bias, d.resid, d.target = _tp(bias), _tp(resid), _tp(target)
+    d.ld_rt = (d.N if ld_rt is None else ld_rt)
+    d.out_scale = out_scale
+    d.aux0, d.aux1 = _tp(aux0), _tp(aux1)
+    d.ld_aux = (d.N // 2 if epi == 2 else d.N) if ld_aux is None else ld_aux
+    d.a_div, d.a_s1, d.a_s2 = a_off
+    d.b_div, d.b_s1, d.b_s2 = b_off
+    d.c_div, d.c_s1, d.c_s2 = c_off
+    d.t_div, d.t_r1, d.t_r2, d.t_c1, d.t_c2 = t_off
+    dev = A.t[0].device
+    d.err = err_flag(dev).data_ptr()
+    _lib.call("gsq_gemm", _C.byref(d), _lib.stream_ptr())
+    return C
+
+
 def gemm_tc(A: Terms, B: Terms, na=None, nb=None, order=2, alpha=1.0, C=None, beta=0.0,
             c_terms: Terms = None, ct_terms: Terms = None, sq_partial=None):
     """C = alpha A B^T on tcgen05 with split-bf16 operands (see include/gsq_rco_b200.h)."""

@@ -107,6 +107,67 @@ int gsq_gemm_f64(int M, int N, int K, double alpha, const double *A, int64_t sam
                  const double *B, int64_t sbk, int64_t sbn, double beta, double *C, int64_t ldc,
                  int tri, void *stream);
 
+/* Descriptor of one (batched) tensor-core GEMM with a fused epilogue, gsq_gemm below.
+ * Batch z of `batch`: A rows start at a_off(z), B rows at b_off(z), C / cs / resid / target /
+ * aux elements at c_off(z), C^T rows / columns at t_row(z) / t_col(z), where an offset is
+ * (z / div) * s1 + (z % div) * s2. a_rows / b_rows: total rows of the A / B matrices. */
+typedef struct {
+  int M, N, K, batch;
+  const void *a[3];
+  int na;
+  int64_t lda;
+  int64_t a_rows;
+  const void *b[3];
+  const void *b2[3]; /* SwiGLU forward: the "up" rows, paired with the "gate" rows of b */
+  int nb;
+  int64_t ldb;
+  int64_t b_rows;
+  int order, causal, epi, bn;
+  float alpha, beta;
+  float *C;
+  int64_t ldc;
+  void *cs[3];
+  int ncs;
+  int64_t ldcs;
+  void *ct[3];
+  int nct;
+  int64_t ldct;
+  int64_t ct_up_rows;
+  double *sq_partial;
+  const float *bias;
+  const void *resid;
+  const void *target;
+  int64_t ld_rt;
+  float out_scale;
+  float *aux0;
+  float *aux1;
+  int64_t ld_aux;
+  int a_div;
+  int64_t a_s1, a_s2;
+  int b_div;
+  int64_t b_s1, b_s2;
+  int c_div;
+  int64_t c_s1, c_s2;
+  int t_div;
+  int64_t t_r1, t_r2, t_c1, t_c2;
+  int *err;
+} gsq_gemm_desc;
+
+/* Batched float32-faithful tensor-core GEMM with a fused epilogue (see gsq_gemm_tc for the
+ * arithmetic). bn: tile width 64 or 128. causal: batch rows m only reduce over k < the end of
+ * their 128-row tile (a causal probability matrix whose upper triangle is zero).
+ * epi 0: x = alpha acc + bias[n] (+ beta C) -> C, cs terms, ct terms, per-tile sum of x^2.
+ * epi 1: r = alpha acc + bias[n] + resid[m, n] - target[m, n] (bf16 resid / target, resid may
+ *        be NULL); per-tile sum of r^2; x = out_scale r -> C, cs, ct (the stage-loss residual
+ *        and its gradient).
+ * epi 2: SwiGLU forward. B rows: 64-row blocks of b (gate) and b2 (up) interleaved per tile,
+ *        N = 2 * width. g, u -> aux0, aux1 float32 [M][ld_aux]; silu(g) u -> cs, ct.
+ * epi 3: SwiGLU backward. acc = dL/d(silu(g) u) of column n; with g, u from aux0 / aux1:
+ *        dL/dg -> ct rows n, dL/du -> ct rows n + ct_up_rows.
+ * Replaces the block matmuls of src/gsq_rco/gsq/e2e.py:132-134,155,166,170,173 in the stage
+ * losses of src/gsq_rco/gsq/staged.py:332-354 and their MLX backward. */
+int gsq_gemm(const gsq_gemm_desc *desc, void *stream);
+
 /* Float32-faithful tensor-core GEMM (tcgen05, TMEM accumulator, TMA-fed):
  *   C[m, n] = alpha * sum_k A(m, k) B(n, k) (+ beta * C[m, n])
  * A and B arrive as na / nb bf16 terms (A = sum_i A_i), each K-major [M][lda] / [N][ldb]

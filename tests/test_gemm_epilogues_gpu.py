@@ -1,0 +1,114 @@
+"""Batched / causal / fused-epilogue forms of the tensor-core GEMM (gsq_gemm) against float64
+torch references of the same float32 operands."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def terms_of(x, n=3):
+    from gsq_rco_mlx_b200.gemm import Terms, split_into
+    return split_into(x.contiguous(), Terms(x.shape[0], x.shape[1], n))
+
+
+def rel(a, b):
+    return ((a.double() - b.double()).norm() / b.double().norm()).item()
+
+
+def check():
+    from gsq_rco_mlx_b200.gemm import check_err
+    torch.cuda.synchronize()
+    check_err(torch.device(DEV))
+
+
+def test_batched_affine_offsets_bn64():
+    """28 (head, sequence) products P_h V_kv(h) with 7 heads per kv head, N = 64 tiles."""
+    from gsq_rco_mlx_b200.gemm import Terms, gemm
+    torch.manual_seed(0)
+    S, Hq, Hkv, T, D = 2, 14, 2, 256, 64
+    P = torch.randn(S * Hq * T, T, device=DEV)
+    V = torch.randn(S * Hkv * D, T, device=DEV)          # V^T per (seq, kv head): [64, T]
+    Pt, Vt = terms_of(P, 1), terms_of(V)
+    out = torch.zeros(S * Hq * T, D, device=DEV)
+    # batch z = s * 14 + h: A rows z * T; B rows (z // 7) * 64; C offset z * T * D
+    gemm(Pt, Vt, M=T, N=D, K=T, batch=S * Hq, bn=64, C=out, ldc=D,
+         a_off=(1, T, 0), b_off=(7, D, 0), c_off=(1, T * D, 0))
+    check()
+    ref = torch.empty_like(out, dtype=torch.float64)
+    for z in range(S * Hq):
+        ref[z * T:(z + 1) * T] = P[z * T:(z + 1) * T].double() @ V[(z // 7) * D:(z // 7 + 1) * D].double().T
+    assert rel(out, ref) < 2e-6
+
+
+def test_causal_skips_upper_blocks():
+    from gsq_rco_mlx_b200.gemm import gemm
+    torch.manual_seed(1)
+    T, N = 1024, 192
+    P = torch.tril(torch.rand(T, T, device=DEV)).bfloat16().float()
+    B = torch.randn(N, T, device=DEV)
+    out = torch.zeros(T, N, device=DEV)
+    gemm(terms_of(P, 1), terms_of(B), C=out, causal=True)
+    check()
+    assert rel(out, P.double() @ B.double().T) < 2e-6
+
+
+def test_residual_loss_epilogue():
+    """r = acc + bias + resid - target, per-tile sum r^2, out_scale r as C, row and
+    transposed terms."""
+    from gsq_rco_mlx_b200.gemm import Terms, gemm
+    torch.manual_seed(2)
+    M, N, K = 300, 256, 192
+    A, B = torch.randn(M, K, device=DEV), torch.randn(N, K, device=DEV)
+    bias = torch.randn(N, device=DEV)
+    resid = torch.randn(M, N, device=DEV).bfloat16()
+    target = torch.randn(M, N, device=DEV).bfloat16()
+    tiles = 3 * 2
+    sq = torch.zeros(tiles, device=DEV, dtype=torch.float64)
+    C = torch.empty(M, N, device=DEV)
+    cs, ct = Terms(M, N), Terms(N, M)
+    gemm(terms_of(A), terms_of(B), C=C, bias=bias, resid=resid, target=target, epi=1,
+         out_scale=0.25, sq_partial=sq, c_terms=cs, ct_terms=ct)
+    check()
+    r = A.double() @ B.double().T + bias.double() + resid.double() - target.double()
+    assert abs(sq.sum().item() - (r ** 2).sum().item()) <= 2e-6 * (r ** 2).sum().item()
+    assert rel(C, 0.25 * r) < 2e-6
+    assert torch.equal(cs.value(), C) and torch.equal(ct.value(), C.T)
+
+
+def _silu(g):
+    return g * torch.sigmoid(g)
+
+
+def test_swiglu_forward_and_backward_epilogues():
+    from gsq_rco_mlx_b200.gemm import Terms, gemm
+    torch.manual_seed(3)
+    M, W, K = 260, 384, 256      # W = intermediate width (gate/up rows each)
+    X = torch.randn(M, K, device=DEV).bfloat16().float()   # exactly bf16 rows (normed input)
+    Wg, Wu = 0.05 * torch.randn(W, K, device=DEV), 0.05 * torch.randn(W, K, device=DEV)
+    g_out = torch.empty(M, W, device=DEV)
+    u_out = torch.empty(M, W, device=DEV)
+    d_row, d_t = Terms(M, W), Terms(W, M)
+    gemm(terms_of(X, 1), terms_of(Wg), B2=terms_of(Wu), epi=2, aux0=g_out, aux1=u_out,
+         c_terms=d_row, ct_terms=d_t)
+    check()
+    g_ref = X.double() @ Wg.double().T
+    u_ref = X.double() @ Wu.double().T
+    assert rel(g_out, g_ref) < 2e-6 and rel(u_out, u_ref) < 2e-6
+    d_ref = _silu(g_out.double()) * u_out.double()
+    assert rel(d_row.value(), d_ref) < 1e-6
+    assert torch.equal(d_t.value(), d_row.value().T)
+    # backward: dd = dR w_down, with the gate/up stored above
+    Nout = 128
+    dR = torch.randn(M, Nout, device=DEV)
+    Wd = 0.05 * torch.randn(Nout, W, device=DEV)
+    grads_t = Terms(2 * W, M)
+    gemm(terms_of(dR), terms_of(Wd.T.contiguous()), epi=3, aux0=g_out, aux1=u_out,
+         ct_terms=grads_t, ct_up_rows=W)
+    check()
+    dd = dR.double() @ Wd.double()
+    g, u = g_out.double().requires_grad_(), u_out.double().requires_grad_()
+    (_silu(g) * u * dd).sum().backward()
+    got = grads_t.value()
+    assert rel(got[:W].T, g.grad) < 2e-6
+    assert rel(got[W:].T, u.grad) < 2e-6
