@@ -37,8 +37,16 @@ SIGNATURES = {
                     _f32, _vp, _i32, _i64, _vp, _i32, _i64, _vp, _vp, _vp],
     "gsq_split_bf16": [_vp, _i32, _i32, _i64, _i32, _vp, _vp, _vp, _i64, _vp],
     "gsq_gemm": [_vp, _vp],
-    "gsq_gather_split": [_vp, _i64, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp,
-                         _i64, _vp],
+    "gsq_rmsnorm": [_vp, _i64, _vp, _i32, _i32, _f32, _vp, _i64, _vp, _i64, _i32, _i32, _vp],
+    "gsq_rope_split": [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp],
+    "gsq_softmax_causal": [_vp, _i32, _i32, _vp, _vp, _vp],
+    "gsq_embed": [_vp, _i64, _vp, _i32, _vp, _vp],
+    "gsq_hess_accum": [_vp, _vp, _i64, _f64, _f64, _vp],
+    "gsq_zero_cols": [_vp, _i32, _i64, _i32, _i32, _vp],
+    "gsq_gather_split": [_vp, _i32, _i64, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _vp, _i64,
+                         _vp, _i64, _vp],
+    "gsq_transpose_bf16": [_vp, _i32, _i32, _i64, _i64, _vp, _i64, _i64, _i32, _vp],
+    "gsq_head_group_sum_t": [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
     "gsq_sum_f64": [_vp, _i32, _vp, _vp],
     "hessian_accum": [_vp, _i64, _i32, _vp, _i64, _vp],
     "gptq_factor": [_vp, _i32, _f64, _vp, _vp, _vp, _vp, _vp],

@@ -71,6 +71,10 @@ __device__ __forceinline__ void split3_bf16(float x, __nv_bfloat16& hi, __nv_bfl
   lo = __float2bfloat16_rn(r2);
 }
 
+__device__ __forceinline__ float bf16r_dev(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

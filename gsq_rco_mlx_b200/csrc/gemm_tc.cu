@@ -24,7 +24,14 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemBudget = 200 * 1024;
 
-enum Epi { EPI_PLAIN = 0, EPI_RESID = 1, EPI_SWIGLU_FWD = 2, EPI_SWIGLU_BWD = 3 };
+enum Epi {
+  EPI_PLAIN = 0,
+  EPI_RESID = 1,
+  EPI_SWIGLU_FWD = 2,
+  EPI_SWIGLU_BWD = 3,
+  EPI_BF16 = 4,        // bf16 chain: x = bf16(acc); x = bf16(x + bias); x = bf16(resid + x)
+  EPI_SWIGLU_BF16 = 5  // bf16 SwiGLU: g, u = bf16(acc); bf16(bf16(g bf16(sigmoid(g))) u)
+};
 
 struct Aff {
   int div;
@@ -64,6 +71,8 @@ struct GemmParams {
   int* err;
   int stages;
   int kb_per_chunk;
+  int skip_upper;  // output tiles entirely above the diagonal (n >= m) are not computed
+  int row_period;  // epi 1: rows with (row % row_period) == 0 have a zero residual
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -77,6 +86,8 @@ __device__ __forceinline__ void epi_sync() {
 __device__ __forceinline__ float sigmoid_f(float x) {
   return __frcp_rn(__fadd_rn(1.0f, expf(-x)));
 }
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // One 128 x BN output tile per CTA (grid z = batch). TMEM: two buffers of a "big" accumulator
 // (the hi x hi products) and a "small" one (every other product, 2^8 smaller); tensor-core
@@ -102,11 +113,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int z = blockIdx.z;
   const int tile_m = blockIdx.y * BM, tile_n = blockIdx.x * BN;
+  if (p.skip_upper && tile_n >= tile_m + BM) return;  // uniform across the CTA
   const int S = p.stages;
   const uint32_t stage_bytes = p.na * kTileA + p.nb * kTileB;
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  int num_kb = (p.K + BK - 1) / BK;
-  if (p.causal) num_kb = min(num_kb, (tile_m + BM + BK - 1) / BK);
+  // k-block range: causal 1 = lower-triangular A (k < end of this row tile), causal 2 =
+  // upper-triangular A (k >= start of this row tile)
+  const int kb_total = (p.K + BK - 1) / BK;
+  const int kb0 = p.causal == 2 ? min(tile_m / BK, kb_total - 1) : 0;
+  const int kb1 = p.causal == 1 ? min(kb_total, (tile_m + BM + BK - 1) / BK) : kb_total;
+  const int num_kb = kb1 - kb0;
   const int P = p.kb_per_chunk;
   const int n_chunks = (num_kb + P - 1) / P;
   const bool has_small = (p.na > 1 || p.nb > 1) && p.order > 0;
@@ -146,14 +162,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         uint8_t* st = smem + (size_t)s * stage_bytes;
         mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
         for (int i = 0; i < p.na; ++i)
-          tma_load_2d(st + i * kTileA, &p.tma_a[i], &full_bar[s], kb * BK, a_row);
+          tma_load_2d(st + i * kTileA, &p.tma_a[i], &full_bar[s], (kb0 + kb) * BK, a_row);
         for (int j = 0; j < p.nb; ++j) {
           uint8_t* bt = st + p.na * kTileA + j * kTileB;
           if (p.dual_b) {
-            tma_load_2d(bt, &p.tma_b[j], &full_bar[s], kb * BK, b_row);
-            tma_load_2d(bt + kTileB / 2, &p.tma_b2[j], &full_bar[s], kb * BK, b_row);
+            tma_load_2d(bt, &p.tma_b[j], &full_bar[s], (kb0 + kb) * BK, b_row);
+            tma_load_2d(bt + kTileB / 2, &p.tma_b2[j], &full_bar[s], (kb0 + kb) * BK, b_row);
           } else {
-            tma_load_2d(bt, &p.tma_b[j], &full_bar[s], kb * BK, b_row);
+            tma_load_2d(bt, &p.tma_b[j], &full_bar[s], (kb0 + kb) * BK, b_row);
           }
         }
       }
@@ -244,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     // column of accumulator slot t: n_of(t) = tile_n + 64 (t / 32) + 32 h + t % 32
 #pragma unroll
     for (int t = 0; t < kAcc; ++t) acc[t] = __fmul_rn(p.alpha, acc[t]);
-    if (EPI == EPI_PLAIN || EPI == EPI_RESID) {
+    if (EPI == EPI_PLAIN || EPI == EPI_RESID || EPI == EPI_BF16) {
 #pragma unroll
       for (int jc = 0; jc < kNC; ++jc) {
         const int n0 = tile_n + 64 * jc + 32 * h;
@@ -252,11 +268,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         for (int t = 0; t < 32; ++t) {
           const int n = n0 + t;
           float x = acc[32 * jc + t];
+          if (EPI == EPI_BF16) {
+            x = bf16r(x);
+            if (p.bias && n < p.N) x = bf16r(__fadd_rn(x, p.bias[n]));
+            if (p.resid && live && n < p.N)
+              x = bf16r(__fadd_rn(__bfloat162float(p.resid[coff + (int64_t)row * p.ld_rt + n]), x));
+            acc[32 * jc + t] = x;
+            continue;
+          }
           if (p.bias && n < p.N) x = __fadd_rn(x, p.bias[n]);
           if (EPI == EPI_RESID && live && n < p.N) {
             const int64_t o = coff + (int64_t)row * p.ld_rt + n;
             if (p.resid) x = __fadd_rn(x, __bfloat162float(p.resid[o]));
             x = __fsub_rn(x, __bfloat162float(p.target[o]));
+            if (p.row_period > 0 && (row % p.row_period) == 0) x = 0.f;
             sq += (double)x * (double)x;
             x = __fmul_rn(p.out_scale, x);
           }
@@ -299,6 +324,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           for (int t = 0; t < 32; ++t)
             if (n0 + t < p.N) sq += (double)acc[32 * jc + t] * (double)acc[32 * jc + t];
         }
+      }
+    } else if (EPI == EPI_SWIGLU_BF16) {
+#pragma unroll
+      for (int t = 0; t < 32; ++t) {
+        const float g = bf16r(acc[t]), u = bf16r(acc[32 + t]);
+        acc[t] = bf16r(__fmul_rn(bf16r(__fmul_rn(g, bf16r(sigmoid_f(g)))), u));
       }
     } else if (EPI == EPI_SWIGLU_FWD) {
       // slots [0, 32): gate of column j = tile_n / 2 + 32 h + t; slots [32, 64): up of the same j
@@ -346,12 +377,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     // ---- bf16 term outputs
     const int n_out_cols = EPI == EPI_SWIGLU_FWD ? 32 * kNC / 2 : 0;  // (unused marker)
     (void)n_out_cols;
-    if (EPI == EPI_PLAIN || EPI == EPI_RESID || EPI == EPI_SWIGLU_FWD) {
+    constexpr bool kHalfOut = (EPI == EPI_SWIGLU_FWD || EPI == EPI_SWIGLU_BF16);
+    if (EPI != EPI_SWIGLU_BWD) {
       if (live && p.ncs > 0) {
-        const int nch = EPI == EPI_SWIGLU_FWD ? 1 : kNC;
+        const int nch = kHalfOut ? 1 : kNC;
         for (int jc = 0; jc < nch; ++jc) {
-          const int n0 = EPI == EPI_SWIGLU_FWD ? tile_n / 2 + 32 * h : tile_n + 64 * jc + 32 * h;
-          const int n_lim = EPI == EPI_SWIGLU_FWD ? p.N / 2 : p.N;
+          const int n0 = kHalfOut ? tile_n / 2 + 32 * h : tile_n + 64 * jc + 32 * h;
+          const int n_lim = kHalfOut ? p.N / 2 : p.N;
 #pragma unroll
           for (int t = 0; t < 32; t += 8) {
             if (n0 + t >= n_lim) break;
@@ -370,9 +402,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       // transposed terms: stage [plane][term][n_loc][m_loc] bf16 in shared memory, then 16-byte
       // coalesced row stores of C^T (plane 1: the up-gradient rows of the SwiGLU backward)
       __nv_bfloat16* T = reinterpret_cast<__nv_bfloat16*>(smem);
-      const int rows_t = EPI == EPI_SWIGLU_FWD ? BN / 2 : BN;
+      const int rows_t = kHalfOut ? BN / 2 : BN;
       const int planes = EPI == EPI_SWIGLU_BWD ? 2 : 1;
-      if (EPI == EPI_SWIGLU_FWD) {
+      if (kHalfOut) {
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
           __nv_bfloat16 hv[3];
@@ -394,8 +426,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       }
       epi_sync();
       const int tid = threadIdx.x - 64;
-      const int n_first = EPI == EPI_SWIGLU_FWD ? tile_n / 2 : tile_n;
-      const int n_lim = EPI == EPI_SWIGLU_FWD ? p.N / 2 : p.N;
+      const int n_first = kHalfOut ? tile_n / 2 : tile_n;
+      const int n_lim = kHalfOut ? p.N / 2 : p.N;
       const int64_t r_base = p.t_row.at(z), c_base = p.t_col.at(z);
       const int per_plane = p.nct * rows_t * (BM / 8);
       for (int e = tid; e < planes * per_plane; e += 32 * kEpiWarps) {
@@ -472,7 +504,7 @@ static int launch(GemmParams& p, int batch, cudaStream_t st) {
   if (S < 2) return GSQ_ENOTSUP;
   p.stages = S;
   // the transposed-term staging reuses the pipeline stages
-  const int rows_t = EPI == EPI_SWIGLU_FWD ? BN / 2 : BN;
+  const int rows_t = (EPI == EPI_SWIGLU_FWD || EPI == EPI_SWIGLU_BF16) ? BN / 2 : BN;
   const size_t stage_need = (size_t)(EPI == EPI_SWIGLU_BWD ? 2 : 1) * p.nct * rows_t * BM * 2;
   if (stage_need > (size_t)S * stage_bytes) return GSQ_ENOTSUP;
   int products = 0;
@@ -480,7 +512,7 @@ static int launch(GemmParams& p, int batch, cudaStream_t st) {
     for (int j = 0; j < p.nb; ++j) products += (i + j <= p.order);
   p.kb_per_chunk = products >= 3 ? 1 : (products == 2 ? 2 : 4);
   const size_t smem = (size_t)S * stage_bytes + 1024;
-  static bool attr_set[2][4] = {{false}};
+  static bool attr_set[2][6] = {{false}};
   bool& done = attr_set[BN == 128][EPI];
   if (!done) {
     if (cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>,
@@ -513,12 +545,12 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   const int M = d->M, N = d->N, K = d->K;
   if (M <= 0 || N <= 0 || K <= 0 || d->batch < 1 || d->batch > 65535 || d->na < 1 ||
       d->na > 3 || d->nb < 1 || d->nb > 3 || d->order < 0 || !d->err || d->ncs < 0 ||
-      d->ncs > 3 || d->nct < 0 || d->nct > 3 || d->epi < 0 || d->epi > 3)
+      d->ncs > 3 || d->nct < 0 || d->nct > 3 || d->epi < 0 || d->epi > 5)
     return GSQ_EINVAL;
   if (d->bn != 64 && d->bn != 128) return GSQ_EINVAL;
   const int epi = d->epi;
   if (!d->C && d->ncs == 0 && d->nct == 0 && !d->sq_partial) return GSQ_EINVAL;
-  if (d->lda < K || d->ldb < K || (d->C && d->ldc < (epi == 2 ? N / 2 : N)))
+  if (d->lda < K || d->ldb < K || (d->C && d->ldc < ((epi == 2 || epi == 5) ? N / 2 : N)))
     return GSQ_EINVAL;
   if (d->ncs > 0 && (d->ldcs & 7)) return GSQ_EINVAL;
   if (d->nct > 0 && (d->ldct & 7)) return GSQ_EINVAL;
@@ -528,22 +560,25 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
     if (!d->ct[i] || ((uintptr_t)d->ct[i] & 15)) return GSQ_EINVAL;
   if (epi == 1 && !d->target) return GSQ_EINVAL;
   if ((epi == 2 || epi == 3) && (!d->aux0 || !d->aux1 || d->bn != 128)) return GSQ_EINVAL;
-  if (epi == 2 && (!d->b2[0] || (N % 128) != 0)) return GSQ_EINVAL;
-  if (d->causal && d->K < M) return GSQ_EINVAL;
+  if ((epi == 2 || epi == 5) && (!d->b2[0] || (N % 128) != 0 || d->bn != 128)) return GSQ_EINVAL;
+  if (d->causal < 0 || d->causal > 2 || (d->causal && d->K < M)) return GSQ_EINVAL;
   tc::GemmParams p;
   memset(&p, 0, sizeof(p));
   const int BN = d->bn;
-  const int b_box = epi == 2 ? BN / 2 : BN;
+  const bool dual = (epi == 2 || epi == 5);
+  const int b_box = dual ? BN / 2 : BN;
   for (int i = 0; i < d->na; ++i)
     if (!tc::make_map(&p.tma_a[i], d->a[i], d->a_rows, K, d->lda, tc::BM)) return GSQ_EINVAL;
   for (int j = 0; j < d->nb; ++j) {
     if (!tc::make_map(&p.tma_b[j], d->b[j], d->b_rows, K, d->ldb, b_box)) return GSQ_EINVAL;
-    if (epi == 2 && !tc::make_map(&p.tma_b2[j], d->b2[j], d->b_rows, K, d->ldb, b_box))
+    if (dual && !tc::make_map(&p.tma_b2[j], d->b2[j], d->b_rows, K, d->ldb, b_box))
       return GSQ_EINVAL;
   }
   p.M = M; p.N = N; p.K = K;
   p.na = d->na; p.nb = d->nb; p.order = d->order; p.causal = d->causal;
-  p.dual_b = epi == 2;
+  p.dual_b = dual;
+  p.skip_upper = d->skip_upper;
+  p.row_period = d->row_period;
   p.alpha = d->alpha; p.beta = d->beta;
   p.C = d->C; p.ldc = d->ldc;
   p.c_vec = (d->C && ((uintptr_t)d->C & 15) == 0 && (d->ldc & 3) == 0 &&
@@ -569,13 +604,16 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   if (BN == 64) {
     if (epi == 0) return tc::launch<64, 0>(p, d->batch, st);
     if (epi == 1) return tc::launch<64, 1>(p, d->batch, st);
+    if (epi == 4) return tc::launch<64, 4>(p, d->batch, st);
     return GSQ_EINVAL;
   }
   switch (epi) {
     case 0: return tc::launch<128, 0>(p, d->batch, st);
     case 1: return tc::launch<128, 1>(p, d->batch, st);
     case 2: return tc::launch<128, 2>(p, d->batch, st);
-    default: return tc::launch<128, 3>(p, d->batch, st);
+    case 3: return tc::launch<128, 3>(p, d->batch, st);
+    case 4: return tc::launch<128, 4>(p, d->batch, st);
+    default: return tc::launch<128, 5>(p, d->batch, st);
   }
 }
 

@@ -7,7 +7,8 @@
 
 namespace gsq {
 
-__global__ void gather_split_kernel(const float* __restrict__ x, int64_t ld_x,
+template <typename TS>
+__global__ void gather_split_kernel(const TS* __restrict__ x, int64_t ld_x,
                                     const int32_t* __restrict__ seq, int per_seq,
                                     int64_t seq_stride, int offset, int rows, int cols,
                                     int n_terms, __nv_bfloat16* __restrict__ t0,
@@ -23,7 +24,7 @@ __global__ void gather_split_kernel(const float* __restrict__ x, int64_t ld_x,
     float v = 0.f;
     if (r < rows && c < cols) {
       const int64_t src = (int64_t)seq[r / per_seq] * seq_stride + offset + (r % per_seq);
-      v = x[src * ld_x + c];
+      v = (float)x[src * ld_x + c];
       if (t0) {
         __nv_bfloat16 h, m, l;
         split3_bf16(v, h, m, l);
@@ -64,14 +65,90 @@ __global__ void sum_f64_kernel(const double* __restrict__ x, int n, double* out)
   }
 }
 
+// out[z][c][r] = in[z][r][c] for bf16 matrices [rows][ld_in] -> [cols][ld_out] (32 x 32 tiles)
+__global__ void transpose_bf16_kernel(const __nv_bfloat16* __restrict__ in, int rows, int cols,
+                                      int64_t ld_in, int64_t bs_in, __nv_bfloat16* __restrict__ out,
+                                      int64_t ld_out, int64_t bs_out) {
+  __shared__ __nv_bfloat16 S[32][34];
+  const int z = blockIdx.z;
+  const __nv_bfloat16* src = in + z * bs_in;
+  __nv_bfloat16* dst = out + z * bs_out;
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  for (int rr = threadIdx.y; rr < 32; rr += 8) {
+    const int r = r0 + rr, c = c0 + threadIdx.x;
+    S[rr][threadIdx.x] = (r < rows && c < cols) ? src[(int64_t)r * ld_in + c] : __float2bfloat16_rn(0.f);
+  }
+  __syncthreads();
+  for (int cc = threadIdx.y; cc < 32; cc += 8) {
+    const int c = c0 + cc, r = r0 + threadIdx.x;
+    if (c < cols && r < rows) dst[(int64_t)c * ld_out + r] = S[threadIdx.x][cc];
+  }
+}
+
+// dV of a kv head = sum of the dV of its `rep` query heads, written as three bf16 terms
+// transposed: in float32 [S * nh][T][64] (z = s * nh + h), out[kv * 64 + d][s * T + t].
+__global__ void head_group_sum_t_kernel(const float* __restrict__ dv, int S, int nh, int rep, int T,
+                                        __nv_bfloat16* __restrict__ o0, __nv_bfloat16* __restrict__ o1,
+                                        __nv_bfloat16* __restrict__ o2, int64_t ld_o) {
+  __shared__ float tile[32][33];
+  const int nkv = nh / rep;
+  const int sk = blockIdx.z;  // s * nkv + kv
+  const int s = sk / nkv, kv = sk % nkv;
+  const int t0 = blockIdx.y * 32, d0 = blockIdx.x * 32;
+  for (int tt = threadIdx.y; tt < 32; tt += 8) {
+    const int t = t0 + tt, dd = d0 + threadIdx.x;
+    float acc = 0.f;
+    if (t < T && dd < 64)
+      for (int r = 0; r < rep; ++r) {
+        const int64_t z = (int64_t)s * nh + kv * rep + r;
+        acc = __fadd_rn(acc, dv[(z * T + t) * 64 + dd]);
+      }
+    tile[tt][threadIdx.x] = acc;
+  }
+  __syncthreads();
+  for (int di = threadIdx.y; di < 32; di += 8) {
+    const int dd = d0 + di, t = t0 + threadIdx.x;
+    if (dd < 64 && t < T) {
+      __nv_bfloat16 h, m, l;
+      split3_bf16(tile[threadIdx.x][di], h, m, l);
+      const int64_t o = (int64_t)(kv * 64 + dd) * ld_o + (int64_t)s * T + t;
+      o0[o] = h; o1[o] = m; o2[o] = l;
+    }
+  }
+}
+
 }  // namespace gsq
 
 using namespace gsq;
 
-extern "C" int gsq_gather_split(const float* x, int64_t ld_x, const int32_t* seq, int per_seq,
-                                int64_t seq_stride, int offset, int rows, int cols, int n_terms,
-                                void* const* row_terms, int64_t ld_t, void* const* col_terms,
-                                int64_t ld_u, void* stream) {
+extern "C" int gsq_transpose_bf16(const void* in, int rows, int cols, int64_t ld_in, int64_t bs_in,
+                                  void* out, int64_t ld_out, int64_t bs_out, int batch,
+                                  void* stream) {
+  if (!in || !out || rows <= 0 || cols <= 0 || batch <= 0 || ld_in < cols || ld_out < rows)
+    return GSQ_EINVAL;
+  dim3 g((cols + 31) / 32, (rows + 31) / 32, batch);
+  transpose_bf16_kernel<<<g, dim3(32, 8), 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)in, rows, cols, ld_in, bs_in, (__nv_bfloat16*)out, ld_out, bs_out);
+  GSQ_CHECK_LAUNCH();
+  return GSQ_OK;
+}
+
+extern "C" int gsq_head_group_sum_t(const float* dv, int S, int nh, int rep, int T, void* o0,
+                                    void* o1, void* o2, int64_t ld_o, void* stream) {
+  if (!dv || !o0 || !o1 || !o2 || S <= 0 || nh <= 0 || rep <= 0 || nh % rep || T <= 0 ||
+      ld_o < (int64_t)S * T)
+    return GSQ_EINVAL;
+  dim3 g(2, (T + 31) / 32, S * (nh / rep));
+  head_group_sum_t_kernel<<<g, dim3(32, 8), 0, (cudaStream_t)stream>>>(
+      dv, S, nh, rep, T, (__nv_bfloat16*)o0, (__nv_bfloat16*)o1, (__nv_bfloat16*)o2, ld_o);
+  GSQ_CHECK_LAUNCH();
+  return GSQ_OK;
+}
+
+extern "C" int gsq_gather_split(const void* x, int src_bf16, int64_t ld_x, const int32_t* seq,
+                                int per_seq, int64_t seq_stride, int offset, int rows, int cols,
+                                int n_terms, void* const* row_terms, int64_t ld_t,
+                                void* const* col_terms, int64_t ld_u, void* stream) {
   if (!x || !seq || per_seq <= 0 || rows <= 0 || cols <= 0 || n_terms < 1 || n_terms > 3 ||
       ld_x < cols || (!row_terms && !col_terms) || (row_terms && ld_t < cols) ||
       (col_terms && ld_u < rows))
@@ -83,9 +160,14 @@ extern "C" int gsq_gather_split(const float* x, int64_t ld_x, const int32_t* seq
     if (col_terms) u[i] = (__nv_bfloat16*)col_terms[i];
   }
   dim3 g((cols + 31) / 32, (rows + 31) / 32);
-  gather_split_kernel<<<g, dim3(32, 8), 0, (cudaStream_t)stream>>>(
-      x, ld_x, seq, per_seq, seq_stride, offset, rows, cols, n_terms, t[0], t[1], t[2], ld_t,
-      u[0], u[1], u[2], ld_u);
+  if (src_bf16)
+    gather_split_kernel<__nv_bfloat16><<<g, dim3(32, 8), 0, (cudaStream_t)stream>>>(
+        (const __nv_bfloat16*)x, ld_x, seq, per_seq, seq_stride, offset, rows, cols, n_terms,
+        t[0], t[1], t[2], ld_t, u[0], u[1], u[2], ld_u);
+  else
+    gather_split_kernel<float><<<g, dim3(32, 8), 0, (cudaStream_t)stream>>>(
+        (const float*)x, ld_x, seq, per_seq, seq_stride, offset, rows, cols, n_terms, t[0], t[1],
+        t[2], ld_t, u[0], u[1], u[2], ld_u);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }

@@ -145,6 +145,8 @@ class GemmDesc(_C.Structure):
         ("t_div", _C.c_int), ("t_r1", _C.c_int64), ("t_r2", _C.c_int64), ("t_c1", _C.c_int64),
         ("t_c2", _C.c_int64),
         ("err", _C.c_void_p),
+        ("skip_upper", _C.c_int),
+        ("row_period", _C.c_int),
     ]
 
 
@@ -157,13 +159,13 @@ def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, 
          sq_partial=None, bias=None, resid=None, target=None, ld_rt=None, out_scale=1.0,
          aux0=None, aux1=None, ld_aux=None, B2: Terms = None, epi=0, bn=128, causal=False,
          batch=1, a_off=(1, 0, 0), b_off=(1, 0, 0), c_off=(1, 0, 0), t_off=(1, 0, 0, 0, 0),
-         ct_up_rows=0):
+         ct_up_rows=0, skip_upper=False, row_period=0):
     """One (batched) tensor-core GEMM with a fused epilogue; see gsq_gemm in the C header.
     M, N, K default to the operand shapes; a_off/b_off/c_off = (div, s1, s2),
     t_off = (div, row_s1, row_s2, col_s1, col_s2)."""
     d = GemmDesc()
     d.M = A.rows if M is None else M
-    d.N = (B.rows if epi != 2 else 2 * B.rows) if N is None else N
+    d.N = (B.rows if epi not in (2, 5) else 2 * B.rows) if N is None else N
     d.K = A.cols if K is None else K
     d.batch = batch
     na = A.n if na is None else na
@@ -195,6 +197,8 @@ def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, 
     d.out_scale = out_scale
     d.aux0, d.aux1 = _tp(aux0), _tp(aux1)
     d.ld_aux = (d.N // 2 if epi == 2 else d.N) if ld_aux is None else ld_aux
+    d.skip_upper = int(skip_upper)
+    d.row_period = int(row_period)
     d.a_div, d.a_s1, d.a_s2 = a_off
     d.b_div, d.b_s1, d.b_s2 = b_off
     d.c_div, d.c_s1, d.c_s2 = c_off

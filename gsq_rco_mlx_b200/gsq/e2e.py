@@ -1,0 +1,211 @@
+"""Qwen2 decoder block on the GPU (reference src/gsq_rco/gsq/e2e.py), for the GSQ stages.
+
+The reference runs one sequence at a time through MLX (``Qwen2Stream``). Here a chunk of S
+sequences x T positions runs at once, bf16 storage exactly where the reference's arrays are
+bf16, as seven tensor-core GEMMs with fused epilogues plus four elementwise kernels:
+
+  hn  = rmsnorm(h)                                     gsq_rmsnorm
+  q|k = bf16(bf16(hn [Wq|Wk]^T) + [bq|bk])             gemm, bf16-chain epilogue (one GEMM)
+  v^T = bf16(bf16(hn Wv^T) + bv), transposed per seq   gemm, batched over sequences
+  rope(q), rope(k) as float32 operand terms            gsq_rope_split
+  S   = rope(q) rope(k)^T / 8 (float32-faithful)       gemm, batched (seq, head), causal tiles
+  P   = bf16(softmax(S)) (causal)                      gsq_softmax_causal
+  o   = bf16(P v)                                      gemm, batched (seq, head), causal k-range
+  h1  = bf16(h + bf16(o Wo^T))                         gemm, bf16 chain with residual
+  mn  = rmsnorm(h1)                                    gsq_rmsnorm
+  d   = bf16(bf16(g bf16(sigmoid g)) u), g|u = mn [Wg|Wu]^T    gemm, dual-B bf16 SwiGLU epilogue
+  out = bf16(h1 + bf16(d Wd^T))                        gemm, bf16 chain with residual
+
+Optional transposed taps (the K-major operands of the Hessian GEMMs) of the four linear inputs
+(hn, o, mn, d), with the columns of position 0 zeroed because every Hessian skips position 0
+(staged.py:14-15). ``hessian_add`` folds X^T X of a tap into a float64 Hessian.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from .. import _lib
+from ..gemm import Terms, err_flag, gemm, pad8
+
+LIN_ORDER = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+TAPS = ("hn", "o", "mn", "d_in")  # inputs of q/k/v, o, gate/up, down
+
+
+@dataclass(frozen=True)
+class BlockConfig:
+    hidden: int = 896
+    n_heads: int = 14
+    n_kv: int = 2
+    head_dim: int = 64
+    inter: int = 4864
+    eps: float = 1e-6
+    theta: float = 1e6
+
+    @property
+    def rep(self):
+        return self.n_heads // self.n_kv
+
+
+def rope_tables(T, head_dim=64, theta=1e6):
+    """cos / sin [T, head_dim / 2] float32 (e2e.py:96-100)."""
+    ex = np.arange(0, head_dim, 2, dtype=np.float32) / np.float32(head_dim)
+    freq = (np.float32(1.0) / (np.float32(theta) ** ex)).astype(np.float32)
+    ang = np.arange(T, dtype=np.float32)[:, None] * freq[None, :]
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def wterms(W):
+    """A bf16 [out, in] weight as a one-term GEMM operand."""
+    return Terms(W.shape[0], W.shape[1], 1, ld=W.shape[1], tensors=[W])
+
+
+class BlockWeights:
+    """bf16 CUDA weights of one block plus the stacked forms the fused GEMMs read."""
+
+    def __init__(self, W: dict):
+        self.W = {k: v.contiguous() for k, v in W.items()}
+        w = self.W
+        self.qk = torch.cat([w["q_proj"], w["k_proj"]]).contiguous()
+        self.qk_bias = torch.cat([w["q_bias"], w["k_bias"]]).float().contiguous()
+        self.v_bias = w["v_bias"].float().contiguous()
+
+    def replace(self, **kw):
+        W = dict(self.W)
+        W.update(kw)
+        return BlockWeights(W)
+
+
+class Qwen2Block:
+    """Buffers and launches of the block forward for chunks of up to S sequences of T."""
+
+    def __init__(self, cfg: BlockConfig, S: int, T: int, device=None):
+        self.cfg, self.S, self.T = cfg, int(S), int(T)
+        dev = device or _lib.device()
+        self.dev = dev
+        c = cfg
+        R = S * T
+        bf = torch.bfloat16
+        self.hn = torch.empty(R, c.hidden, device=dev, dtype=bf)
+        self.qk = torch.empty(R, (c.n_heads + c.n_kv) * c.head_dim, device=dev, dtype=bf)
+        self.vT = Terms(S * c.n_kv * c.head_dim, T, 1, dev)
+        self.q_rot = Terms(S * c.n_heads * T, c.head_dim, 3, dev)
+        self.k_rot = Terms(S * c.n_kv * T, c.head_dim, 3, dev)
+        self.scores = torch.empty(S * c.n_heads, T, T, device=dev, dtype=torch.float32)
+        self.P = Terms(S * c.n_heads * T, T, 1, dev, ld=T)
+        self.o = torch.empty(R, c.hidden, device=dev, dtype=bf)
+        self.h1 = torch.empty(R, c.hidden, device=dev, dtype=bf)
+        self.mn = torch.empty(R, c.hidden, device=dev, dtype=bf)
+        self.d_in = torch.empty(R, c.inter, device=dev, dtype=bf)
+        self.taps_t = {}
+        cos, sin = rope_tables(T, c.head_dim, c.theta)
+        self.cos = torch.as_tensor(cos, device=dev)
+        self.sin = torch.as_tensor(sin, device=dev)
+
+    def tap(self, name):
+        """Transposed tap buffer [width, S*T] (bf16), allocated on first use."""
+        if name not in self.taps_t:
+            width = self.cfg.inter if name == "d_in" else self.cfg.hidden
+            self.taps_t[name] = Terms(width, self.S * self.T, 1, self.dev)
+        return self.taps_t[name]
+
+    # ------------------------------------------------------------------------ forward ---
+    def attention(self, hn, W: BlockWeights, S, o_out, o_tap=None, probs_t=None):
+        """Causal GQA self-attention before o_proj of S sequences: o_out bf16 [S*T, H]."""
+        c, T = self.cfg, self.T
+        R = S * T
+        st = _lib.stream_ptr()
+        hnT = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[hn])
+        # q | k in one GEMM, bf16 chain with bias
+        gemm(hnT, wterms(W.qk), M=R, epi=4, bias=W.qk_bias,
+             c_terms=Terms(R, self.qk.shape[1], 1, ld=self.qk.shape[1], tensors=[self.qk]))
+        # v^T per sequence: [s][kv * 64 + d][t]
+        nkvd = c.n_kv * c.head_dim
+        gemm(hnT, wterms(W.W["v_proj"]), M=T, batch=S, epi=4, bias=W.v_bias,
+             a_off=(1, T, 0), ct_terms=self.vT, t_off=(1, nkvd, 0, 0, 0))
+        qd = c.n_heads * c.head_dim
+        t = self.q_rot.t
+        _lib.call("gsq_rope_split", _lib.ptr(self.qk), self.qk.shape[1], S, T, c.n_heads,
+                  _lib.ptr(self.cos), _lib.ptr(self.sin), _lib.ptr(t[0]), _lib.ptr(t[1]),
+                  _lib.ptr(t[2]), st)
+        t = self.k_rot.t
+        kview = self.qk[:, qd:]
+        _lib.call("gsq_rope_split", C_ptr(kview), self.qk.shape[1], S, T, c.n_kv,
+                  _lib.ptr(self.cos), _lib.ptr(self.sin), _lib.ptr(t[0]), _lib.ptr(t[1]),
+                  _lib.ptr(t[2]), st)
+        # scores (seq, head) = q_rot k_rot^T / sqrt(64), causal tiles only
+        B = S * c.n_heads
+        gemm(self.q_rot, self.k_rot, M=T, N=T, K=c.head_dim, batch=B, alpha=1.0 / 8.0,
+             C=self.scores, ldc=T, a_off=(1, T, 0), b_off=(c.rep, T, 0), c_off=(1, T * T, 0),
+             skip_upper=True)
+        _lib.call("gsq_softmax_causal", _lib.ptr(self.scores), B, T, _lib.ptr(self.P.t[0]),
+                  _lib.ptr(probs_t), st)
+        # o (seq, head) = P v, written at columns h * 64 of row s * T + t
+        Ot = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[o_out])
+        gemm(self.P, self.vT, M=T, N=c.head_dim, K=T, batch=B, bn=64, causal=1, epi=4,
+             a_off=(1, T, 0), b_off=(c.rep, c.head_dim, 0),
+             c_off=(c.n_heads, T * c.hidden, c.head_dim), c_terms=Ot,
+             ct_terms=o_tap, t_off=(c.n_heads, 0, c.head_dim, T, 0))
+
+    def forward(self, h, W: BlockWeights, S=None, out=None, taps=(), attn_out=None):
+        """Block forward of S sequences h bf16 [S*T, H] -> out bf16 [S*T, H] (or only the
+        attention output after o_proj into attn_out, the vo-stage target). taps: names of
+        TAPS to write transposed (self.tap(name)), position-0 columns zeroed."""
+        c, T = self.cfg, self.T
+        S = self.S if S is None else S
+        R = S * T
+        st = _lib.stream_ptr()
+        hn_tap = self.tap("hn") if "hn" in taps else None
+        _lib.call("gsq_rmsnorm", _lib.ptr(h), c.hidden, _lib.ptr(W.W["in_norm"]), R, c.hidden,
+                  float(c.eps), _lib.ptr(self.hn), c.hidden,
+                  _lib.ptr(hn_tap.t[0] if hn_tap else None), hn_tap.ld if hn_tap else 0, T, 1, st)
+        o_tap = self.tap("o") if "o" in taps else None
+        self.attention(self.hn, W, S, self.o, o_tap=o_tap)
+        if o_tap is not None:
+            _lib.call("gsq_zero_cols", _lib.ptr(o_tap.t[0]), c.hidden, o_tap.ld, R, T, st)
+        Ot = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[self.o])
+        if attn_out is not None:
+            gemm(Ot, wterms(W.W["o_proj"]), epi=4,
+                 c_terms=Terms(R, c.hidden, 1, ld=c.hidden, tensors=[attn_out]))
+            return attn_out
+        gemm(Ot, wterms(W.W["o_proj"]), epi=4, resid=h, ld_rt=c.hidden,
+             c_terms=Terms(R, c.hidden, 1, ld=c.hidden, tensors=[self.h1]))
+        mn_tap = self.tap("mn") if "mn" in taps else None
+        _lib.call("gsq_rmsnorm", _lib.ptr(self.h1), c.hidden, _lib.ptr(W.W["post_norm"]), R,
+                  c.hidden, float(c.eps), _lib.ptr(self.mn), c.hidden,
+                  _lib.ptr(mn_tap.t[0] if mn_tap else None), mn_tap.ld if mn_tap else 0, T, 1, st)
+        d_tap = self.tap("d_in") if "d_in" in taps else None
+        MNt = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[self.mn])
+        gemm(MNt, wterms(W.W["gate_proj"]), B2=wterms(W.W["up_proj"]), epi=5,
+             c_terms=Terms(R, c.inter, 1, ld=c.inter, tensors=[self.d_in]), ct_terms=d_tap)
+        if d_tap is not None:
+            _lib.call("gsq_zero_cols", _lib.ptr(d_tap.t[0]), c.inter, d_tap.ld, R, T, st)
+        out = torch.empty(R, c.hidden, device=self.dev, dtype=torch.bfloat16) if out is None else out
+        Dt = Terms(R, c.inter, 1, ld=c.inter, tensors=[self.d_in])
+        gemm(Dt, wterms(W.W["down_proj"]), epi=4, resid=self.h1, ld_rt=c.hidden,
+             c_terms=Terms(R, c.hidden, 1, ld=c.hidden, tensors=[out]))
+        return out
+
+    def hessian_add(self, name, H, n, S=None):
+        """Fold X^T X of tap `name` (positions 1.. of S sequences) into the float64 Hessian
+        H (reference gptq.py:89-101 / staged.py:143-155): H <- H n/(n+m) + 2/(n+m) X^T X.
+        Returns the new count n + m."""
+        S = self.S if S is None else S
+        tp = self.tap(name)
+        m = S * (self.T - 1)
+        width = tp.rows
+        G = torch.empty(width, width, device=self.dev, dtype=torch.float32)
+        gemm(tp, tp, K=S * self.T, C=G)
+        total = n + m
+        _lib.call("gsq_hess_accum", _lib.ptr(H), _lib.ptr(G), width * width, float(n / total),
+                  float(2.0 / total), _lib.stream_ptr())
+        return total
+
+
+def C_ptr(t):
+    """Device pointer of a (possibly strided) tensor view, for kernels that take a leading
+    dimension argument."""
+    import ctypes
+    return ctypes.c_void_p(t.data_ptr())

@@ -164,7 +164,8 @@ class LinearStep:
         rows = len(ids) * per_seq
         if rows != self.M:
             raise ValueError(f"micro-batch has {rows} rows, step expects {self.M}")
-        _lib.call("gsq_gather_split", _lib.ptr(x_all), x_all.shape[-1], _lib.ptr(self.seq),
+        _lib.call("gsq_gather_split", _lib.ptr(x_all), int(x_all.dtype == torch.bfloat16),
+                  x_all.shape[-1], _lib.ptr(self.seq),
                   int(per_seq), int(seq_stride), int(offset), self.M, self.in_f, self.nx,
                   self.X.ptrs(), self.X.ld, self.XT.ptrs(), self.XT.ld, _lib.stream_ptr())
 

@@ -151,6 +151,8 @@ typedef struct {
   int t_div;
   int64_t t_r1, t_r2, t_c1, t_c2;
   int *err;
+  int skip_upper; /* skip output tiles with n >= m (all above the diagonal): causal scores */
+  int row_period; /* epi 1: rows m with m % row_period == 0 get a zero residual (position 0) */
 } gsq_gemm_desc;
 
 /* Batched float32-faithful tensor-core GEMM with a fused epilogue (see gsq_gemm_tc for the
@@ -164,6 +166,11 @@ typedef struct {
  *        N = 2 * width. g, u -> aux0, aux1 float32 [M][ld_aux]; silu(g) u -> cs, ct.
  * epi 3: SwiGLU backward. acc = dL/d(silu(g) u) of column n; with g, u from aux0 / aux1:
  *        dL/dg -> ct rows n, dL/du -> ct rows n + ct_up_rows.
+ * epi 4: bf16 chain of a bf16 model: x = bf16(alpha acc); x = bf16(x + bias[n]) if bias;
+ *        x = bf16(resid[m, n] + x) if resid -> C (float32 of the bf16 value), cs, ct (1 term
+ *        each is the bf16 value itself).
+ * epi 5: bf16 SwiGLU (b / b2 as in epi 2): g, u = bf16(acc); bf16(bf16(g bf16(sigmoid(g))) u)
+ *        -> cs, ct.
  * Replaces the block matmuls of src/gsq_rco/gsq/e2e.py:132-134,155,166,170,173 in the stage
  * losses of src/gsq_rco/gsq/staged.py:332-354 and their MLX backward. */
 int gsq_gemm(const gsq_gemm_desc *desc, void *stream);
@@ -196,10 +203,20 @@ int gsq_split_bf16(const float *x, int rows, int cols, int64_t ld_in, int transp
  * of the chosen sequences: per_seq = T - 1, seq_stride = T, offset = 1). Writes n_terms bf16
  * terms row-major [rows][ld_t] (row_terms) and/or transposed [cols][ld_u] (col_terms).
  * Replaces the micro-batch draw of staged.py:380 with _rows :128-130 (and _take :124-125). */
-int gsq_gather_split(const float *x, int64_t ld_x, const int32_t *seq, int per_seq,
+int gsq_gather_split(const void *x, int src_bf16, int64_t ld_x, const int32_t *seq, int per_seq,
                      int64_t seq_stride, int offset, int rows, int cols, int n_terms,
                      void *const *row_terms, int64_t ld_t, void *const *col_terms, int64_t ld_u,
                      void *stream);
+
+/* out[z] = in[z]^T for bf16 matrices [rows][ld_in] (batch stride bs_in) -> [cols][ld_out]. */
+int gsq_transpose_bf16(const void *in, int rows, int cols, int64_t ld_in, int64_t bs_in, void *out,
+                       int64_t ld_out, int64_t bs_out, int batch, void *stream);
+
+/* The value gradient of each kv head, summed over its rep query heads (GQA repeat of
+ * src/gsq_rco/gsq/e2e.py:146-148, backward), as three bf16 terms transposed:
+ * dv float32 [S * nh][T][64] -> o[kv * 64 + d][s * T + t]. */
+int gsq_head_group_sum_t(const float *dv, int S, int nh, int rep, int T, void *o0, void *o1,
+                         void *o2, int64_t ld_o, void *stream);
 
 /* out[0] = sum of x[0..n) in float64 (one block; the loss from per-tile partials). */
 int gsq_sum_f64(const double *x, int n, double *out, void *stream);
@@ -207,6 +224,38 @@ int gsq_sum_f64(const double *x, int n, double *out, void *stream);
 /* out[0] = sum_i x[i]^2 in float64 (deterministic two-pass). partials: >= 1024 doubles.
  * Replaces the mean of R^2 in staged.py:328 (the caller divides by the count). */
 int gsq_sumsq_f32(const float *x, int64_t n, double *partials, double *out, void *stream);
+
+/* ------------------------------------------------------------ decoder block -------- */
+
+/* y = bf16((x * (1 / sqrt(mean(x^2) + eps))) * w) per row of x bf16 [rows][ld_x], H columns
+ * (mean from a float64 sum of the float32 squares). y bf16 [rows][ld_y] and/or the transposed
+ * yt bf16 [H][ld_yt]; zero_pos0 writes zeros to yt for rows r with r % seq_len == 0.
+ * Replaces src/gsq_rco/gsq/e2e.py:90-93 (rmsnorm). */
+int gsq_rmsnorm(const void *x, int64_t ld_x, const void *w, int rows, int H, float eps, void *y,
+                int64_t ld_y, void *yt, int64_t ld_yt, int seq_len, int zero_pos0, void *stream);
+
+/* Half-split rotary embedding of bf16 q or k x [S*T][ld_x] (nh heads of 64 at column h*64),
+ * float32 [x1 c - x2 s, x1 s + x2 c] with cos / sin float32 [T][32], written as three bf16
+ * terms head-major o[(s * nh + h) * T + t][64]. Replaces src/gsq_rco/gsq/e2e.py:96-108,145. */
+int gsq_rope_split(const void *x, int64_t ld_x, int S, int T, int nh, const float *cosv,
+                   const float *sinv, void *o0, void *o1, void *o2, void *stream);
+
+/* Causal softmax of score rows S float32 [B*T][T] (keys <= query): P bf16 [B*T][T] with zeros
+ * above the diagonal, and optionally PT bf16 [B][T][T] (P transposed per batch).
+ * Replaces src/gsq_rco/gsq/e2e.py:149-154 (mask, softmax, cast to bf16). */
+int gsq_softmax_causal(const float *S, int B, int T, void *P, void *PT, void *stream);
+
+/* out[r] = E[ids[r]] (bf16 rows of H). Replaces the embedding lookup of the calibration
+ * stream (src/gsq_rco/gsq/pipeline.py's block inputs, e2e.py:64-74). */
+int gsq_embed(const int32_t *ids, int64_t n, const void *E, int H, void *out, void *stream);
+
+/* x[r][c] = 0 (bf16) for the columns c < cols with c % period == 0: position 0 of every
+ * sequence in a transposed activation buffer (Hessians skip it, staged.py:14-15,128-130). */
+int gsq_zero_cols(void *x, int rows, int64_t ld, int cols, int period, void *stream);
+
+/* H <- beta H + alpha G, float64 H and float32 G of n elements (a Gram matrix accumulated by
+ * the tensor cores folded into the float64 Hessian). Replaces gptq.py:97-100. */
+int gsq_hess_accum(double *H, const float *G, int64_t n, double beta, double alpha, void *stream);
 
 /* ------------------------------------------------------------------- GPTQ -------- */
 

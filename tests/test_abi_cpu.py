@@ -100,3 +100,24 @@ def test_integer_weights_and_dp_validation():
         s, c, wv, B = z[f"dp{n}_s"], z[f"dp{n}_c"], z[f"dp{n}_w"], int(z[f"dp{n}_B"])
         if s.shape[1] == 2 and np.all(wv == wv[0]):
             assert np.array_equal(manifold.dp_knapsack(s, c, wv, B), z[f"dp{n}_z"])
+
+
+def test_gemm_descriptor_layout_matches_header(tmp_path):
+    """The ctypes mirror of gsq_gemm_desc has the C struct's size and field offsets."""
+    import ctypes
+    import shutil
+    import subprocess
+    from gsq_rco_mlx_b200.gemm import GemmDesc
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    names = [f[0] for f in GemmDesc._fields_]
+    src = tmp_path / "off.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "gsq_rco_b200.h"\n'
+                   'int main(void){printf("%zu", sizeof(gsq_gemm_desc));\n' +
+                   "".join(f'printf(" %zu", offsetof(gsq_gemm_desc, {n}));\n' for n in names) +
+                   'return 0;}\n')
+    exe = tmp_path / "off"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    vals = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
+    assert vals[0] == ctypes.sizeof(GemmDesc)
+    assert vals[1:] == [getattr(GemmDesc, n).offset for n in names]

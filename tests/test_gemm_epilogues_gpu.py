@@ -27,7 +27,7 @@ def test_batched_affine_offsets_bn64():
     from gsq_rco_mlx_b200.gemm import Terms, gemm
     torch.manual_seed(0)
     S, Hq, Hkv, T, D = 2, 14, 2, 256, 64
-    P = torch.randn(S * Hq * T, T, device=DEV)
+    P = torch.randn(S * Hq * T, T, device=DEV).bfloat16().float()  # one exact term
     V = torch.randn(S * Hkv * D, T, device=DEV)          # V^T per (seq, kv head): [64, T]
     Pt, Vt = terms_of(P, 1), terms_of(V)
     out = torch.zeros(S * Hq * T, D, device=DEV)
