@@ -24,7 +24,7 @@ import numpy as np
 import torch
 
 from .. import _lib
-from ..gemm import Terms, err_flag, check_err, gemm_tc, pad8
+from ..gemm import Terms, check_err, err_flag, gemm, gemm_tc, pad8
 from .gptq import init_logits_2bit_from_codes, init_shift_logits
 from .lion import BETAS, LR_LOGITS, LR_SCALES, WEIGHT_DECAY, scale_lr
 from .quant import gs_schedules
@@ -247,3 +247,427 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
         step_s.append(time.perf_counter() - t0)
     check_err(step.dev)
     return history, round(1000 * float(np.median(step_s[3:] or step_s)), 1)
+
+
+# ------------------------------------------------------------------------- block stages ---
+
+def _seq_ids(dev, ids):
+    return torch.as_tensor(np.asarray(ids, dtype=np.int32)).to(dev, non_blocking=True)
+
+
+def _gather(src, ids_t, per_seq, stride, offset, rows, cols, n_terms, row_terms=None,
+            col_terms=None):
+    """Rows seq * stride + offset + r (r < per_seq) of src into operand terms."""
+    _lib.call("gsq_gather_split", _lib.ptr(src), int(src.dtype == torch.bfloat16), src.shape[-1],
+              _lib.ptr(ids_t), int(per_seq), int(stride), int(offset), int(rows), int(cols),
+              int(n_terms), None if row_terms is None else row_terms.ptrs(),
+              0 if row_terms is None else row_terms.ld,
+              None if col_terms is None else col_terms.ptrs(),
+              0 if col_terms is None else col_terms.ld, _lib.stream_ptr())
+
+
+def _bf16_rows(x):
+    """A bf16 tensor [rows, cols] as a one-term operand."""
+    return Terms(x.shape[0], x.shape[1], 1, ld=x.shape[1], tensors=[x])
+
+
+class _StageBase:
+    """Soft-weight buffers and the fused update shared by the vo and mlp stage steps."""
+
+    def _init_soft(self, lins, R, dev):
+        self.lins, self.R, self.dev = lins, int(R), dev
+        self.Dbuf = {l.name: torch.zeros(R, 3, l.out_f, l.in_f, device=dev, dtype=torch.bfloat16)
+                     for l in lins}
+        self.D = {l.name: [Terms(l.out_f, l.in_f, 3, ld=l.in_f, tensors=self.Dbuf[l.name][r])
+                           for r in range(R)] for l in lins}
+        self.probs = {l.name: torch.zeros(R, l.K, l.d, device=dev, dtype=torch.float32)
+                      for l in lins}
+        self.loss = torch.zeros(R, device=dev, dtype=torch.float64)
+
+    def first_forward(self, t, tau, kappa, noise_seed, noise_of=None):
+        for lin in self.lins:
+            for r in range(self.R):
+                noise = None if noise_of is None else noise_of(t, r, lin)
+                lin.soft(tau, kappa, t, r, noise_seed, noise=noise, terms=self.Dbuf[lin.name][r],
+                         probs=self.probs[lin.name][r])
+
+    def update(self, t, tau, kappa, opts, noise_seed, nxt=None, noise_of=None):
+        for lin in self.lins:
+            n = None
+            if nxt is not None:
+                t1, tau1, kappa1 = nxt
+                noise = None
+                if noise_of is not None:
+                    noise = torch.stack([noise_of(t1, r, lin) for r in range(self.R)]).contiguous()
+                n = {"step": t1, "tau": tau1, "kappa": kappa1, "seed": noise_seed,
+                     "terms": self.Dbuf[lin.name], "noise": noise}
+            lin.step(self.probs[lin.name], self.grad_of(lin), tau, kappa, opts.lr_logits,
+                     opts.lr_scales, nxt=n)
+
+    def mean_loss(self):
+        return float(self.loss.sum().item() / (self.R * self.count))
+
+
+class MLPStep(_StageBase):
+    """The mlp stage step (staged.py:345-354): Y = h1 + (silu(mn Wg^T) * (mn Wu^T)) Wd^T with soft
+    gate / up / down, loss mean((Y - Y_fp)^2) over positions 1.. of the micro-batch. The
+    attention is hard, so its outputs h1 and mn = rmsnorm(h1) are fixed per sequence and come
+    from a cache. Per resample, five tensor-core GEMMs with fused epilogues:
+      F1  gate | up = mn [Wg|Wu]^T       SwiGLU epilogue: g, u (float32), d = silu(g) u as terms
+      F3  r = h1 + d Wd^T - Y_fp         residual-loss epilogue: loss partials, dR = 2 r / count
+      B1  dL/dWd = dR^T d
+      B2  dd = dR Wd                     SwiGLU-backward epilogue: dL/dg, dL/du (transposed)
+      B3  [dL/dWg; dL/dWu] = [dg; du]^T mn
+    """
+
+    def __init__(self, lins, cfg, m, T, R):
+        gate, up, down = lins
+        dev = gate.logits.device
+        self._init_soft(lins, R, dev)
+        H, I = cfg.hidden, cfg.inter
+        M = m * (T - 1)
+        self.cfg, self.m, self.T, self.M, self.count = cfg, m, T, M, M * H
+        bf = torch.bfloat16
+        self.MN = Terms(M, H, 1, dev)
+        self.MNT = Terms(H, M, 1, dev)
+        self.H1 = Terms(M, H, 1, dev)
+        self.Y = Terms(M, H, 1, dev)
+        self.g = torch.empty(M, I, device=dev, dtype=torch.float32)
+        self.u = torch.empty(M, I, device=dev, dtype=torch.float32)
+        self.DIN, self.DINT = Terms(M, I, 3, dev), Terms(I, M, 3, dev)
+        self.DR, self.DRT = Terms(M, H, 3, dev), Terms(H, M, 3, dev)
+        self.GUT = Terms(2 * I, M, 3, dev)
+        self.DdT = Terms(I, H, 3, dev)
+        self.grad_gu = torch.empty(2, R, I, H, device=dev, dtype=torch.float32)
+        self.grad_d = torch.empty(R, H, I, device=dev, dtype=torch.float32)
+        tiles = ((M + 127) // 128) * ((H + 127) // 128)
+        self.sq = torch.zeros(tiles, device=dev, dtype=torch.float64)
+        self.names = (gate.name, up.name, down.name)
+
+    def grad_of(self, lin):
+        g, u, d = self.names
+        return self.grad_gu[0] if lin.name == g else (self.grad_gu[1] if lin.name == u else self.grad_d)
+
+    def stage(self, mn_all, h1_all, y_all, seq_ids):
+        """Positions 1.. of the chosen sequences of the caches (bf16 [N*T, H])."""
+        H, T = self.cfg.hidden, self.T
+        ids = _seq_ids(self.dev, seq_ids)
+        _gather(mn_all, ids, T - 1, T, 1, self.M, H, 1, self.MN, self.MNT)
+        _gather(h1_all, ids, T - 1, T, 1, self.M, H, 1, self.H1)
+        _gather(y_all, ids, T - 1, T, 1, self.M, H, 1, self.Y)
+
+    def contract(self):
+        H, I, M = self.cfg.hidden, self.cfg.inter, self.M
+        gname, uname, dname = self.names
+        tiles = self.sq.numel()
+        for r in range(self.R):
+            gemm(self.MN, self.D[gname][r], B2=self.D[uname][r], epi=2, aux0=self.g, aux1=self.u,
+                 c_terms=self.DIN, ct_terms=self.DINT)
+            gemm(self.DIN, self.D[dname][r], epi=1, resid=self.H1.t[0], target=self.Y.t[0],
+                 ld_rt=self.H1.ld, out_scale=2.0 / self.count, sq_partial=self.sq,
+                 c_terms=self.DR, ct_terms=self.DRT)
+            _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(self.loss[r:r + 1]),
+                      _lib.stream_ptr())
+            gemm(self.DRT, self.DINT, C=self.grad_d[r])
+            for i in range(3):
+                _lib.call("gsq_transpose_bf16", _lib.ptr(self.Dbuf[dname][r][i]), H, I, I, 0,
+                          _lib.ptr(self.DdT.t[i]), self.DdT.ld, 0, 1, _lib.stream_ptr())
+            gemm(self.DR, self.DdT, epi=3, aux0=self.g, aux1=self.u, ct_terms=self.GUT,
+                 ct_up_rows=I)
+            gemm(self.GUT, self.MNT, M=I, batch=2, C=self.grad_gu[0, r], ldc=H,
+                 a_off=(1, I, 0), c_off=(1, self.R * I * H, 0))
+
+
+class VOStep(_StageBase):
+    """The vo stage step (staged.py:332-342): A = (P v) Wo^T with soft v / o, loss
+    mean((A - A_fp)^2) over positions 1.. per sequence, averaged over the micro-batch. q and k
+    are hard, so the probabilities P come from the cached q / k of the chosen sequences. Per
+    resample:
+      V     v^T = (hn Wv^T + bv)^T per sequence             bias epilogue, transposed terms
+      PV    o = P v per (sequence, head)                    causal k-range, row / transposed terms
+      Y     r = o Wo^T - A_fp (0 at position 0)             residual-loss epilogue: dY = 2 r / n
+      Go    dL/dWo = dY^T o
+      dO    dO^T = (dY Wo)^T per sequence
+      dV    P^T dO per (sequence, head), summed over the heads of each kv head
+      Gv    dL/dWv = dV^T hn
+    """
+
+    def __init__(self, lins, cfg, m, T, R, v_bias):
+        v, o = lins
+        dev = v.logits.device
+        self._init_soft(lins, R, dev)
+        c = cfg
+        H, nh, nkv, hd = c.hidden, c.n_heads, c.n_kv, c.head_dim
+        self.cfg, self.m, self.T, self.count = cfg, m, T, m * (T - 1) * H
+        RT = m * T
+        self.HN, self.HNT = Terms(RT, H, 1, dev), Terms(H, RT, 1, dev)
+        self.A = Terms(RT, H, 1, dev)
+        self.QK = torch.empty(RT, (nh + nkv) * hd, device=dev, dtype=torch.bfloat16)
+        self.q_rot = Terms(m * nh * T, hd, 3, dev)
+        self.k_rot = Terms(m * nkv * T, hd, 3, dev)
+        self.scores = torch.empty(m * nh, T, T, device=dev, dtype=torch.float32)
+        self.P = Terms(m * nh * T, T, 1, dev, ld=T)
+        self.PT = Terms(m * nh * T, T, 1, dev, ld=T)
+        self.VT = Terms(m * nkv * hd, T, 3, dev)
+        self.O, self.OT = Terms(RT, H, 3, dev), Terms(H, RT, 3, dev)
+        self.DY, self.DYT = Terms(RT, H, 3, dev), Terms(H, RT, 3, dev)
+        self.DoT = Terms(H, H, 3, dev)
+        self.DOT = Terms(m * H, T, 3, dev)
+        self.dv = torch.empty(m * nh, T, hd, device=dev, dtype=torch.float32)
+        self.DVT = Terms(nkv * hd, RT, 3, dev)
+        self.grad_v = torch.empty(R, nkv * hd, H, device=dev, dtype=torch.float32)
+        self.grad_o = torch.empty(R, H, H, device=dev, dtype=torch.float32)
+        tiles = ((RT + 127) // 128) * ((H + 127) // 128)
+        self.sq = torch.zeros(tiles, device=dev, dtype=torch.float64)
+        self.v_bias = v_bias.float().contiguous()
+        self.names = (v.name, o.name)
+        from .e2e import rope_tables
+        cos, sin = rope_tables(T, hd, c.theta)
+        self.cos = torch.as_tensor(cos, device=dev)
+        self.sin = torch.as_tensor(sin, device=dev)
+
+    def grad_of(self, lin):
+        return self.grad_v if lin.name == self.names[0] else self.grad_o
+
+    def stage(self, hn_all, a_all, qk_all, seq_ids):
+        """All positions of the chosen sequences: hn, the target A_fp, the hard q|k rows; then
+        the causal probabilities P (and P^T) of the micro-batch."""
+        c, T, m = self.cfg, self.T, self.m
+        H = c.hidden
+        ids = _seq_ids(self.dev, seq_ids)
+        RT = m * T
+        _gather(hn_all, ids, T, T, 0, RT, H, 1, self.HN, self.HNT)
+        _gather(a_all, ids, T, T, 0, RT, H, 1, self.A)
+        qkw = qk_all.shape[1]
+        QKt = Terms(RT, qkw, 1, ld=qkw, tensors=[self.QK])
+        _gather(qk_all, ids, T, T, 0, RT, qkw, 1, QKt)
+        st = _lib.stream_ptr()
+        qd = c.n_heads * c.head_dim
+        t = self.q_rot.t
+        _lib.call("gsq_rope_split", _lib.ptr(self.QK), qkw, m, T, c.n_heads, _lib.ptr(self.cos),
+                  _lib.ptr(self.sin), _lib.ptr(t[0]), _lib.ptr(t[1]), _lib.ptr(t[2]), st)
+        t = self.k_rot.t
+        from .e2e import C_ptr
+        _lib.call("gsq_rope_split", C_ptr(self.QK[:, qd:]), qkw, m, T, c.n_kv, _lib.ptr(self.cos),
+                  _lib.ptr(self.sin), _lib.ptr(t[0]), _lib.ptr(t[1]), _lib.ptr(t[2]), st)
+        B = m * c.n_heads
+        gemm(self.q_rot, self.k_rot, M=T, N=T, K=c.head_dim, batch=B, alpha=1.0 / 8.0,
+             C=self.scores, ldc=T, a_off=(1, T, 0), b_off=(c.rep, T, 0), c_off=(1, T * T, 0),
+             skip_upper=True)
+        _lib.call("gsq_softmax_causal", _lib.ptr(self.scores), B, T, _lib.ptr(self.P.t[0]),
+                  _lib.ptr(self.PT.t[0]), st)
+
+    def contract(self):
+        c, T, m = self.cfg, self.T, self.m
+        H, nh, nkv, hd = c.hidden, c.n_heads, c.n_kv, c.head_dim
+        nkvd = nkv * hd
+        vname, oname = self.names
+        tiles = self.sq.numel()
+        st = _lib.stream_ptr()
+        for r in range(self.R):
+            gemm(self.HN, self.D[vname][r], M=T, batch=m, bias=self.v_bias, a_off=(1, T, 0),
+                 ct_terms=self.VT, t_off=(1, nkvd, 0, 0, 0))
+            gemm(self.P, self.VT, M=T, N=hd, K=T, batch=m * nh, bn=64, causal=1,
+                 a_off=(1, T, 0), b_off=(c.rep, hd, 0), c_off=(nh, T * H, hd),
+                 c_terms=self.O, ct_terms=self.OT, t_off=(nh, 0, hd, T, 0))
+            gemm(self.O, self.D[oname][r], epi=1, target=self.A.t[0], ld_rt=self.A.ld,
+                 row_period=T, out_scale=2.0 / self.count, sq_partial=self.sq,
+                 c_terms=self.DY, ct_terms=self.DYT)
+            _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(self.loss[r:r + 1]), st)
+            gemm(self.DYT, self.OT, C=self.grad_o[r])
+            for i in range(3):
+                _lib.call("gsq_transpose_bf16", _lib.ptr(self.Dbuf[oname][r][i]), H, H, H, 0,
+                          _lib.ptr(self.DoT.t[i]), self.DoT.ld, 0, 1, st)
+            gemm(self.DY, self.DoT, M=T, batch=m, a_off=(1, T, 0), ct_terms=self.DOT,
+                 t_off=(1, H, 0, 0, 0))
+            gemm(self.PT, self.DOT, M=T, N=hd, K=T, batch=m * nh, bn=64, causal=2,
+                 a_off=(1, T, 0), b_off=(1, hd, 0), C=self.dv, ldc=hd, c_off=(1, T * hd, 0))
+            t = self.DVT.t
+            _lib.call("gsq_head_group_sum_t", _lib.ptr(self.dv), m, nh, c.rep, T, _lib.ptr(t[0]),
+                      _lib.ptr(t[1]), _lib.ptr(t[2]), self.DVT.ld, st)
+            gemm(self.DVT, self.HNT, C=self.grad_v[r])
+
+
+def train_stage(step, stage_args_of, n_seqs, opts: BlockOpts, seed, noise_seed=None,
+                noise_of=None, sync_timing=True):
+    """The stage optimiser loop (staged.py:357-400) around a vo / mlp step: schedules, the
+    sorted micro-batch draw of the numpy stream, contractions, the fused update with the next
+    step's forward. stage_args_of(idx) returns the arguments of step.stage for sequence ids idx.
+    Returns (history, median_ms)."""
+    if opts.steps == 0:
+        return [], None
+    rng = np.random.default_rng(seed)
+    m = min(opts.micro_batch, n_seqs)
+    noise_seed = seed if noise_seed is None else noise_seed
+    err_flag(step.dev).zero_()
+    tau, kappa = gs_schedules(0, opts.steps)
+    step.first_forward(0, tau, kappa, noise_seed, noise_of)
+    history, step_s = [], []
+    for t in range(opts.steps):
+        t0 = time.perf_counter()
+        tau, kappa = gs_schedules(t, opts.steps)
+        idx = np.sort(rng.choice(n_seqs, size=m, replace=False))
+        step.stage(*stage_args_of(idx))
+        step.contract()
+        nxt = (t + 1, *gs_schedules(t + 1, opts.steps)) if t + 1 < opts.steps else None
+        step.update(t, tau, kappa, opts, noise_seed, nxt=nxt, noise_of=noise_of)
+        history.append(step.mean_loss())
+        if sync_timing:
+            torch.cuda.synchronize()
+        step_s.append(time.perf_counter() - t0)
+    check_err(step.dev)
+    return history, round(1000 * float(np.median(step_s[3:] or step_s)), 1)
+
+
+# --------------------------------------------------------------------- block quantizer ---
+
+def _hard_bf16(codes_t, scales16, bits, group_size):
+    """Stored form (uint8 codes, fp16 scales) -> the bf16 weight the stream uses
+    (staged.py:194-196): dequantize with the fp16-rounded scales, cast to bf16."""
+    from .gptq import dequantize
+    w = dequantize(codes_t, torch.as_tensor(np.asarray(scales16, dtype=np.float32)), bits,
+                   group_size, device=True)
+    return w.to(torch.bfloat16)
+
+
+def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None, T=None,
+                   chunk_seqs=8, log=print, noise_of=None):
+    """Quantize the seven linears of one block on the calibration stream (staged.py:405-522).
+
+    h: bf16 CUDA [N*T, H], the block inputs of the N calibration sequences (the quantized
+    prefix). W: bf16 CUDA block weights (linears, q/k/v biases, in_norm, post_norm).
+    Returns (shard, stats, Wq): shard[name] = {"codes" uint8 [out, in], "scales" float16, "bits"},
+    Wq the bf16 hard weights of the block. Each stage: GPTQ warm start from the Hessian of its
+    real input, Lion training of logits and group scales, hardening (argmax codes, fp16 scales).
+    """
+    from .e2e import BlockConfig, BlockWeights, LIN_ORDER, Qwen2Block
+    from .gptq import gptq_factor, quantize_gptq
+    cfg = cfg or BlockConfig()
+    H = cfg.hidden
+    N = h.shape[0] // T
+    dev = h.device
+    gs = opts.group_size
+    seed = opts.seed * 1_000_003 + layer * 1_009
+    cs = min(chunk_seqs, N)
+    eng = Qwen2Block(cfg, cs, T, dev)
+    W_fp = BlockWeights(W)
+    Wf = {name: W[name].float().contiguous() for name in LIN_ORDER}
+    Wcur = dict(W)
+    shard, stats = {}, {"stages": {}, "linears": {}}
+    factors = {}
+
+    def chunks():
+        for a in range(0, N, cs):
+            yield a, min(cs, N - a)
+
+    def hessian(site, Wb, extra=None):
+        """Hessian of the input of `site` over positions 1.., under block weights Wb."""
+        width = cfg.inter if site == "d_in" else H
+        Hs = torch.zeros(width, width, device=dev, dtype=torch.float64)
+        n = 0
+        for a, s in chunks():
+            eng.forward(h[a * T:(a + s) * T], Wb, S=s, taps=(site,))
+            n = eng.hessian_add(site, Hs, n, S=s)
+            if extra:
+                extra(a, s)
+        return Hs
+
+    def gptq(name, Hs, pos):
+        key = id(Hs)
+        if key not in factors:
+            factors[key] = gptq_factor(Hs, opts.damp)
+        g = quantize_gptq(Wf[name], Hs, bits[name], gs, opts.damp, opts.block_size, device=True,
+                          factor=factors[key])
+        s16 = g["scales"].cpu().numpy().astype(np.float16)
+        codes = g["codes"].cpu().numpy()
+        Wcur[name] = _hard_bf16(g["codes"], s16, bits[name], gs)
+        stats["linears"].setdefault(name, {"bits": bits[name]})["err_gptq"] = float(g["err"].item())
+        if bits[name] == 8:
+            shard[name] = {"codes": codes, "scales": s16, "bits": 8}
+            return None
+        return SoftLinear(name, bits[name], codes, s16, gs, seed=seed + 10 * pos,
+                          linear_id=layer * 8 + pos)
+
+    def harden(lin):
+        codes = lin.hard_codes()
+        s16 = lin.stored_scales()
+        Wcur[lin.name] = _hard_bf16(torch.as_tensor(codes, device=dev), s16, lin.bits, gs)
+        shard[lin.name] = {"codes": codes, "scales": s16, "bits": lin.bits}
+        stats["linears"][lin.name]["flip_frac"] = float(np.mean(codes != lin.codes0))
+
+    def stage_done(stage, t0, hist, ms):
+        stats["stages"][stage] = {"seconds": round(time.perf_counter() - t0, 3), "steps": len(hist),
+                                  "median_step_ms": ms,
+                                  "soft_loss_first": hist[0] if hist else None,
+                                  "soft_loss_last": hist[-1] if hist else None}
+        log(f"    stage {stage}: {len(hist)} steps, median {ms} ms/step, "
+            f"{stats['stages'][stage]['seconds']:.2f} s")
+
+    # ---- qk: linear reconstruction on hn rows -------------------------------------------
+    t0 = time.perf_counter()
+    hn_all = torch.empty(N * T, H, device=dev, dtype=torch.bfloat16)
+
+    def keep_hn(a, s):
+        hn_all[a * T:(a + s) * T].copy_(eng.hn[:s * T])
+    H_hn = hessian("hn", W_fp, keep_hn)
+    qk = [gptq(n, H_hn, i) for i, n in enumerate(STAGE_LAYERS["qk"])]
+    qk_lins = [l for l in qk if l is not None]
+    hist, ms = train_linears(qk_lins, hn_all.view(N, T, H), Wf, N, opts, seed + 1,
+                             exact_bf16_rows=True, noise_of=noise_of) if qk_lins else ([], None)
+    for lin in qk_lins:
+        harden(lin)
+    stage_done("qk", t0, hist, ms)
+
+    # ---- vo: attention output, q and k hard -----------------------------------------------
+    t0 = time.perf_counter()
+    v_lin = gptq("v_proj", H_hn, 2)
+    H_o = hessian("o", BlockWeights(Wcur))
+    o_lin = gptq("o_proj", H_o, 3)
+    vo_lins = [l for l in (v_lin, o_lin) if l is not None]
+    A_all = torch.empty(N * T, H, device=dev, dtype=torch.bfloat16)
+    qkw = (cfg.n_heads + cfg.n_kv) * cfg.head_dim
+    qk_all = torch.empty(N * T, qkw, device=dev, dtype=torch.bfloat16)
+    Wc = BlockWeights(Wcur)
+    from .e2e import wterms
+    for a, s in chunks():
+        eng.forward(h[a * T:(a + s) * T], W_fp, S=s, attn_out=A_all[a * T:(a + s) * T])
+        # hard q|k rows under the trained q / k (the vo stage's fixed attention pattern)
+        gemm(_bf16_rows(hn_all[a * T:(a + s) * T]), wterms(Wc.qk), epi=4, bias=Wc.qk_bias,
+             c_terms=_bf16_rows(qk_all[a * T:(a + s) * T]))
+    if len(vo_lins) == 2:
+        vstep = VOStep(vo_lins, cfg, min(opts.micro_batch, N), T, opts.resamples, W["v_bias"])
+        hist, ms = train_stage(vstep, lambda idx: (hn_all, A_all, qk_all, idx), N, opts,
+                               seed + 2, noise_of=noise_of)
+    else:
+        hist, ms = [], None  # an 8-bit v or o keeps its GPTQ values (not trained here)
+    for lin in vo_lins:
+        harden(lin)
+    stage_done("vo", t0, hist, ms)
+    del A_all, qk_all
+
+    # ---- mlp: block output, attention hard -------------------------------------------------
+    t0 = time.perf_counter()
+    mn_all = torch.empty(N * T, H, device=dev, dtype=torch.bfloat16)
+    h1_all = torch.empty(N * T, H, device=dev, dtype=torch.bfloat16)
+
+    def keep_mn(a, s):
+        mn_all[a * T:(a + s) * T].copy_(eng.mn[:s * T])
+        h1_all[a * T:(a + s) * T].copy_(eng.h1[:s * T])
+    H_gu = hessian("mn", BlockWeights(Wcur), keep_mn)
+    gate, up = gptq("gate_proj", H_gu, 4), gptq("up_proj", H_gu, 5)
+    H_d = hessian("d_in", BlockWeights(Wcur))
+    down = gptq("down_proj", H_d, 6)
+    mlp_lins = [l for l in (gate, up, down) if l is not None]
+    Y_all = torch.empty(N * T, H, device=dev, dtype=torch.bfloat16)
+    for a, s in chunks():
+        eng.forward(h[a * T:(a + s) * T], W_fp, S=s, out=Y_all[a * T:(a + s) * T])
+    if len(mlp_lins) == 3:
+        mstep = MLPStep(mlp_lins, cfg, min(opts.micro_batch, N), T, opts.resamples)
+        hist, ms = train_stage(mstep, lambda idx: (mn_all, h1_all, Y_all, idx), N, opts,
+                               seed + 3, noise_of=noise_of)
+    else:
+        hist, ms = [], None
+    for lin in mlp_lins:
+        harden(lin)
+    stage_done("mlp", t0, hist, ms)
+    return shard, stats, Wcur

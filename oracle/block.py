@@ -144,3 +144,82 @@ def vo_loss_and_grads(hn_seqs, A_seqs, P_seqs, Wv, bv, Wo, n_heads=14, n_kv=2):
     loss = total / S
     loss.backward()
     return float(loss), wv.grad.numpy(), wo.grad.numpy()
+
+
+# ------------------------------------------------------------- stage optimisers ---
+
+def _soft(state, t, r, noise_seed, tau, kappa):
+    from .gsq import soft_weight
+    noise = state.noise(noise_seed, t, r)
+    w, p, c = soft_weight(state.logits, noise, state.Ckd, state.scales, state.shape,
+                          state.group_size, tau, kappa)
+    return w, p, c
+
+
+def _apply(states, grads_per_r, soft_per_r, tau, kappa, lr_logits, lr_scales):
+    """Resample mean of the soft backward and one Lion step per linear (staged.py:383-392)."""
+    from .gsq import lion_step, soft_backward
+    R = len(grads_per_r)
+    for j, st in enumerate(states):
+        acc_g, acc_s = None, None
+        for r in range(R):
+            _, p, c = soft_per_r[r][j]
+            gl, gsc = soft_backward(grads_per_r[r][j], p, st.Ckd, c, st.scales, st.group_size,
+                                    tau, kappa)
+            gl, gsc = gl.astype(np.float32), gsc.astype(np.float32)
+            acc_g = gl if acc_g is None else acc_g + gl
+            acc_s = gsc if acc_s is None else acc_s + gsc
+        lion_step(st, acc_g / np.float32(R), acc_s / np.float32(R), lr_logits, lr_scales)
+
+
+def train_mlp(states, mn_seqs, h1_seqs, Y_seqs, steps, micro_batch=2, resamples=2, seed=0,
+              noise_seed=0, lr_logits=1e-4, lr_scales=5e-5):
+    """mlp-stage optimiser (staged.py:357-400 with _loss_block): states = gate, up, down
+    LinearStates; per-sequence bf16 caches [T, H]. Returns the loss history."""
+    from .gsq import gs_schedules
+    rng = np.random.default_rng(seed)
+    n = len(mn_seqs)
+    m = min(micro_batch, n)
+    hist = []
+    for t in range(steps):
+        tau, kappa = gs_schedules(t, steps)
+        idx = np.sort(rng.choice(n, size=m, replace=False))
+        mn = torch.cat([mn_seqs[i][1:] for i in idx])
+        h1 = torch.cat([h1_seqs[i][1:] for i in idx])
+        Y = torch.cat([Y_seqs[i][1:] for i in idx])
+        grads, softs, loss = [], [], 0.0
+        for r in range(resamples):
+            sw = [_soft(st, t, r, noise_seed, tau, kappa) for st in states]
+            l, gg, gu, gd = mlp_loss_and_grads(mn, h1, Y, sw[0][0], sw[1][0], sw[2][0])
+            loss += l
+            grads.append([gg, gu, gd])
+            softs.append(sw)
+        _apply(states, grads, softs, tau, kappa, lr_logits, lr_scales)
+        hist.append(loss / resamples)
+    return hist
+
+
+def train_vo(states, hn_seqs, A_seqs, P_of, bv, steps, n_heads, n_kv, micro_batch=2,
+             resamples=2, seed=0, noise_seed=0, lr_logits=1e-4, lr_scales=5e-5):
+    """vo-stage optimiser (staged.py:357-400 with _loss_attn): states = v, o LinearStates;
+    P_of(t, idx) returns the bf16 probabilities [nh, T, T] of each chosen sequence."""
+    from .gsq import gs_schedules
+    rng = np.random.default_rng(seed)
+    n = len(hn_seqs)
+    m = min(micro_batch, n)
+    hist = []
+    for t in range(steps):
+        tau, kappa = gs_schedules(t, steps)
+        idx = np.sort(rng.choice(n, size=m, replace=False))
+        Ps = P_of(t, idx)
+        grads, softs, loss = [], [], 0.0
+        for r in range(resamples):
+            sw = [_soft(st, t, r, noise_seed, tau, kappa) for st in states]
+            l, gv, go = vo_loss_and_grads([hn_seqs[i] for i in idx], [A_seqs[i] for i in idx],
+                                          Ps, sw[0][0], bv, sw[1][0], n_heads, n_kv)
+            loss += l
+            grads.append([gv, go])
+            softs.append(sw)
+        _apply(states, grads, softs, tau, kappa, lr_logits, lr_scales)
+        hist.append(loss / resamples)
+    return hist
