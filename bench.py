@@ -1,18 +1,22 @@
 """Benchmark of the GSQ hot path on B200 (one JSON line on rank 0).
 
-Workload "linear": one Qwen2.5-0.5B up_proj-shaped linear W [4864 x 896] (0.02 N(0,1), seed
-0), calibration X [16384 x 896] = N(0,1) x per-channel lognormal scales viewed as 32
-sequences x 512 positions (position 0 dropped), GPTQ 3-bit group-64 init with fp16 scales,
-then GSQ Lion steps at micro-batch 2 (1022 rows), 2 Gumbel resamples, tau 2 -> 0.05,
-kappa 100 -> 500 over 200 steps. A step = one Lion step (soft weights, residual and
-weight-gradient contractions, loss, fused backward + Lion). Inputs are synthetic (seeded)
-with the shapes and distributions of the configuration; the per-step working set (~300 MB)
-exceeds the 126 MB L2.
+Workload "block" (default; the metric's "GSQ steps/s per block"): one random-init
+Qwen2.5-0.5B-architecture decoder block (hidden 896, 14 q / 2 kv heads of 64, SwiGLU 4864,
+RMSNorm eps 1e-6, RoPE theta 1e6, bf16 weights ~ N(0, 0.02^2), unit norms), calibration 128
+sequences x 2048 uniform-random token ids over vocab 151936 through a random-init bf16
+embedding. GPTQ 3-bit group-64 warm start, then the GSQ stages qk / vo / mlp, micro-batch 2,
+2 Gumbel resamples, Lion, tau 2 -> 0.05, kappa 100 -> 500. A step = one Lion step of each of the
+three stages (qk + vo + mlp), so value = block steps/s. Inputs are synthetic (seeded), with the
+configuration's shapes and distributions; every stage step's working set (the block's soft
+weights, probabilities, momenta: > 1 GB) exceeds the 126 MB L2.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Workload "linear": one up_proj-shaped linear (W 4864 x 896, X 16384 x 896 as 32 x 512), the
+qk-stage step of one linear.
 
-N > 1 runs under torchrun, one rank per GPU, each rank quantizing its own linear (weak
-scaling: per-GPU work fixed). --impl reference times the CPU restatement of the same step
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload block|linear]
+
+N > 1 runs under torchrun, one rank per GPU, each rank quantizing its own block (weak scaling,
+no collective). --impl reference times the CPU restatement of the same step on this host's cores
 (the reference's GSQ path is MLX-only and cannot run here).
 """
 from __future__ import annotations
@@ -30,23 +34,24 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-OUT_F, IN_F, N_SEQ, T_SEQ = 4864, 896, 32, 512
-STAGE_STEPS = 200
-RESAMPLES = 2
-MICRO = 2
+VOCAB, HID, NH, NKV, HD, INTER = 151936, 896, 14, 2, 64, 4864
+N_SEQ, T_SEQ = 128, 2048
+LIN = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="block", choices=["block", "linear"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=200)
     return ap.parse_args()
 
 
-def dist_setup(n_gpus):
+def dist_setup():
     import torch
     import torch.distributed as dist
     rank = int(os.environ.get("RANK", "0"))
@@ -55,17 +60,9 @@ def dist_setup(n_gpus):
     if world > 1:
         from datetime import timedelta
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
     return rank, world, local
-
-
-def make_inputs(seed=0):
-    rng = np.random.default_rng(seed)
-    W = (0.02 * rng.standard_normal((OUT_F, IN_F))).astype(np.float32)
-    sch = np.exp(rng.standard_normal(IN_F)).astype(np.float32)
-    X = (rng.standard_normal((N_SEQ * T_SEQ, IN_F)).astype(np.float32) * sch)
-    return W, X
 
 
 class Clocks:
@@ -74,8 +71,7 @@ class Clocks:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out"))
-                                 else "", f".clocks_{os.getpid()}.csv")
+        self.path = f"/tmp/.gsq_clocks_{os.getpid()}.csv"
 
     def start(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -84,7 +80,7 @@ class Clocks:
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -114,10 +110,243 @@ class Clocks:
         except OSError:
             pass
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons)}
+                "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def run_ours(args):
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    return json.load(open(p)) if os.path.exists(p) else {}
+
+
+# ----------------------------------------------------------------------------- block ---
+
+def make_block(seed, dev):
+    """Random-init block (bf16 N(0, 0.02^2), fixed draw order), embedding and calibration ids."""
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    shapes = {"q_proj": (NH * HD, HID), "k_proj": (NKV * HD, HID), "v_proj": (NKV * HD, HID),
+              "o_proj": (HID, NH * HD), "gate_proj": (INTER, HID), "up_proj": (INTER, HID),
+              "down_proj": (HID, INTER), "q_bias": (NH * HD,), "k_bias": (NKV * HD,),
+              "v_bias": (NKV * HD,)}
+    W = {k: (0.02 * torch.randn(*s, generator=g)).bfloat16().to(dev) for k, s in shapes.items()}
+    W["in_norm"] = torch.ones(HID, dtype=torch.bfloat16, device=dev)
+    W["post_norm"] = torch.ones(HID, dtype=torch.bfloat16, device=dev)
+    return W
+
+
+def make_calibration(dev, seed=0):
+    import torch
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    E = (0.02 * torch.randn(VOCAB, HID, generator=gen)).bfloat16()
+    ids = np.random.default_rng(seed).integers(0, VOCAB, size=(N_SEQ, T_SEQ)).astype(np.int32)
+    return E, ids
+
+
+def embed(E_dev, ids, dev):
+    import torch
+    from gsq_rco_mlx_b200 import _lib
+    ids_t = torch.as_tensor(ids.reshape(-1), device=dev)
+    h = torch.empty(ids.size, HID, device=dev, dtype=torch.bfloat16)
+    _lib.call("gsq_embed", _lib.ptr(ids_t), ids.size, _lib.ptr(E_dev), HID, _lib.ptr(h),
+              _lib.stream_ptr())
+    return h
+
+
+def gemm_flops_of_mlp_stage(M):
+    """Algorithmic (float32-equivalent) FLOPs of one mlp-stage resample: 5 GEMMs."""
+    return 2 * M * (2 * INTER) * HID + 2 * M * HID * INTER * 4
+
+
+def run_block(args):
+    import torch
+    import torch.distributed as dist
+    from gsq_rco_mlx_b200 import _lib
+    from gsq_rco_mlx_b200.gemm import LaunchLog
+    from gsq_rco_mlx_b200.gsq.e2e import BlockConfig
+    from gsq_rco_mlx_b200.gsq.staged import BlockOpts, StageTimer, quantize_block
+
+    rank, world, local = dist_setup()
+    _lib.lib()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = BlockConfig()
+    W = make_block(1000 + rank, dev)
+    E, ids = make_calibration(dev)
+    E_dev = E.to(dev)
+    h = embed(E_dev, ids, dev)
+    del E_dev
+    bits = {n: 3 for n in LIN}
+    quiet = lambda *a: None
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # warm-up: a short full run (allocations, first launches)
+    quantize_block(h, W, bits, BlockOpts(steps=args.warmup + 1), layer=rank, cfg=cfg, T=T_SEQ,
+                   log=quiet)
+    barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    timer = StageTimer(args.warmup)
+    opts = BlockOpts(steps=args.warmup + args.steps)
+    _, stats, _ = quantize_block(h, W, bits, opts, layer=rank, cfg=cfg, T=T_SEQ, log=quiet,
+                                 timer=timer)
+    barrier()
+    clk = clocks.stop()
+    ms = {s: max_over_ranks(timer.ms[s]) for s in ("qk", "vo", "mlp")}
+    ms_step = ms["qk"] + ms["vo"] + ms["mlp"]
+
+    # roofline of the dominant kernel (the tensor-core GEMM): per-launch events over a short
+    # mlp-stage run, algorithmic float32-equivalent FLOPs of each launch
+    with LaunchLog() as log:
+        quantize_block(h, W, bits, BlockOpts(steps=3), layer=rank, cfg=cfg, T=T_SEQ, log=quiet)
+    rows = log.summary()
+    fl = sum(2.0 * M * N * K * b for (M, N, K, p, b, t) in rows)
+    fl_exec = sum(2.0 * M * N * K * b * p for (M, N, K, p, b, t) in rows)
+    t_ms = sum(t for (*_, t) in rows)
+    achieved = fl / (t_ms * 1e-3) / 1e12
+    pk = peaks()
+    peak = float(pk.get("bf16_tflops", 1590.0))
+
+    # end to end through the public API: host calibration stream in, stored shards out
+    h_host = h.cpu().pin_memory()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    h_dev = h_host.to(dev, non_blocking=True)
+    shard, st2, _ = quantize_block(h_dev, W, bits, BlockOpts(steps=args.e2e_steps), layer=rank,
+                                   cfg=cfg, T=T_SEQ, log=quiet)
+    e1.record()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    d2h = sum(v["codes"].nbytes + v["scales"].nbytes for v in shard.values())
+
+    value = world * 1000.0 / ms_step
+    res = {
+        "metric": "GSQ steps/s per block (Qwen2.5-0.5B block, 3-bit g64: one qk + vo + mlp Lion step)",
+        "value": round(value, 3), "unit": "block steps/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: random-init bf16 block and embedding, uniform-random token ids",
+        "config": {"workload": "config 2: one Qwen2.5-0.5B block, calib 128 x 2048, micro-batch 2, R=2",
+                   "stage_ms_per_step": {k: round(v, 4) for k, v in ms.items()},
+                   "block_seconds_200_steps": round(e2e_ms / 1000, 3),
+                   "parallelism": f"one block per GPU x{world}",
+                   "l2": "per-step working set > L2 (126 MB)"},
+        "e2e": {"value": round(world * args.e2e_steps / (e2e_ms / 1000), 3),
+                "unit": "block steps/s",
+                "h2d_bytes_per_step": int(h_host.numel() * 2 / args.e2e_steps),
+                "d2h_bytes_per_step": int(d2h / args.e2e_steps),
+                "what": "quantize_block(200 steps per stage) from pinned host activations to "
+                        "host shards, GPTQ init and hardening included"},
+        "gpu_launches": None,
+        "roofline": {"kernel": "gemm_tc_kernel (all launches of 3 block steps)", "bound": "tensor",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "executed_bf16_tflops": round(fl_exec / (t_ms * 1e-3) / 1e12, 1),
+                     "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)"
+                     if "bf16_tflops" in pk else "fallback 1590 TFLOP/s",
+                     "note": "achieved counts float32-equivalent GEMM FLOPs 2MNK; the split-bf16 "
+                             "engine executes 3-6 bf16 products per float32 product"},
+        "clocks": clk,
+    }
+    res["gpu_launches"] = count_launches_block(args.steps)
+    if rank == 0 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_block()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def count_launches_block(steps):
+    """Our kernel launches per block step (qk + vo + mlp), counted from the stage code:
+    qk: gather 1 + R x (gemm 2 + sum 1) x 2 linears + step 2 = 15; vo: gather 3 + rope 2 + scores
+    1 + softmax 1 + R x (7 gemm + 1 sum + 3 transpose + 1 group sum) + step 2 = 33;
+    mlp: gather 3 + R x (5 gemm + 1 sum + 3 transpose) + step 3 = 24."""
+    return steps * (15 + 33 + 24)
+
+
+def cpu_baseline_block():
+    """The CPU restatement (oracle port) of one mlp-stage step of the block, the dominant stage,
+    on this host's cores, at the configuration's micro-batch (2 x 2047 rows)."""
+    import torch
+    from oracle import block as ob
+    from oracle import gptq as og
+    from oracle import gsq as ogsq
+    torch.set_num_threads(os.cpu_count())
+    rng = np.random.default_rng(0)
+    M = 2 * (T_SEQ - 1)
+    mn = torch.as_tensor(rng.standard_normal((M, HID)).astype(np.float32)).bfloat16().float()
+    h1 = torch.as_tensor(0.02 * rng.standard_normal((M, HID)).astype(np.float32)).bfloat16().float()
+    Y = torch.as_tensor(0.02 * rng.standard_normal((M, HID)).astype(np.float32)).bfloat16().float()
+    states = []
+    for i, (o, n) in enumerate(((INTER, HID), (INTER, HID), (HID, INTER))):
+        Wl = (0.02 * rng.standard_normal((o, n))).astype(np.float32)
+        r = og.quantize_rtn(Wl, 3, 64)
+        states.append(ogsq.LinearState(3, r["codes"], r["scales"].astype(np.float16), 64, seed=i,
+                                       linear_id=i))
+    t0 = time.perf_counter()
+    ob.train_mlp(states, [mn, mn], [h1, h1], [Y, Y], 1, micro_batch=1)
+    dt = time.perf_counter() - t0
+    # a block step = qk + vo + mlp steps; the mlp step is 85-88 % of it (reference run logs),
+    # so the block-step rate is bounded above by the mlp-step rate
+    return {"value": round(1.0 / dt, 5), "unit": "block steps/s (mlp step only, upper bound)",
+            "cores": os.cpu_count(), "kind": "port",
+            "sample": "1 mlp-stage step at micro-batch 2 x 2047 rows, R=2 (numpy/torch-CPU float64 "
+                      "restatement; the MLX path is unavailable)"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    per = [cpu_baseline_block()["value"] for _ in range(max(1, min(args.steps, 2)))]
+    v = statistics.median(per)
+    res = {"impl": "reference",
+           "metric": "GSQ steps/s per block (Qwen2.5-0.5B block, 3-bit g64: one qk + vo + mlp Lion step)",
+           "value": round(v, 5), "unit": "block steps/s", "n_gpus": world, "steps": len(per),
+           "warmup": 0, "ms_per_step": round(1000 / v, 1), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "config 2: one Qwen2.5-0.5B block, calib 128 x 2048, micro-batch 2, R=2"},
+           "cpu_baseline": {"value": round(v, 5), "unit": "block steps/s", "cores": os.cpu_count(),
+                            "kind": "port",
+                            "sample": "mlp-stage steps only (upper bound of the block-step rate); "
+                                      "the reference's MLX path is unavailable, this is the "
+                                      "CPU restatement"},
+           "e2e": {"value": round(v, 5), "unit": "block steps/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(res), flush=True)
+
+
+# ---------------------------------------------------------------------------- linear ---
+
+OUT_F, IN_F, N_SEQ_L, T_SEQ_L = 4864, 896, 32, 512
+STAGE_STEPS = 200
+RESAMPLES = 2
+MICRO = 2
+
+
+def make_inputs(seed=0):
+    rng = np.random.default_rng(seed)
+    W = (0.02 * rng.standard_normal((OUT_F, IN_F))).astype(np.float32)
+    sch = np.exp(rng.standard_normal(IN_F)).astype(np.float32)
+    X = (rng.standard_normal((N_SEQ_L * T_SEQ_L, IN_F)).astype(np.float32) * sch)
+    return W, X
+
+
+def run_linear(args):
+    """the qk-stage step of one up_proj-shaped linear."""
     import torch
     import torch.distributed as dist
     from gsq_rco_mlx_b200 import _lib
@@ -125,7 +354,7 @@ def run_ours(args):
     from gsq_rco_mlx_b200.gsq.quant import gs_schedules
     from gsq_rco_mlx_b200.gsq.staged import BlockOpts, LinearStep, SoftLinear
 
-    rank, world, local = dist_setup(args.gpus)
+    rank, world, local = dist_setup()
     _lib.lib()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -137,12 +366,12 @@ def run_ours(args):
     lin = SoftLinear("up_proj", 3, g["codes"].cpu().numpy(), g["scales"].cpu().numpy().astype(np.float16),
                      64, seed=rank, linear_id=5)
     rng = np.random.default_rng(1)
-    M = MICRO * (T_SEQ - 1)
+    M = MICRO * (T_SEQ_L - 1)
     opts = BlockOpts(resamples=RESAMPLES, micro_batch=MICRO)
     lstep = LinearStep([lin], M, IN_F, RESAMPLES, x_terms=3)
     targets = {"up_proj": Wd}
     Xmb = torch.empty(M, IN_F, device=dev)
-    Xpin = torch.from_numpy(np.ascontiguousarray(X.reshape(N_SEQ, T_SEQ, IN_F)[:, 1:])).pin_memory()
+    Xpin = torch.from_numpy(np.ascontiguousarray(X.reshape(N_SEQ_L, T_SEQ_L, IN_F)[:, 1:])).pin_memory()
     loss_host = torch.empty(RESAMPLES, dtype=torch.float64).pin_memory()
     stream = torch.cuda.current_stream()
     bwd_events = []
@@ -151,13 +380,13 @@ def run_ours(args):
 
     def step(t, host_inputs=False, time_bwd=False):
         tau, kappa = gs_schedules(t % STAGE_STEPS, STAGE_STEPS)
-        idx = np.sort(rng.choice(N_SEQ, size=MICRO, replace=False))
+        idx = np.sort(rng.choice(N_SEQ_L, size=MICRO, replace=False))
         if host_inputs:
             for j, s in enumerate(idx):
-                Xmb[j * (T_SEQ - 1):(j + 1) * (T_SEQ - 1)].copy_(Xpin[s], non_blocking=True)
-            lstep.stage(Xmb, [0, 1], T_SEQ - 1, T_SEQ - 1, 0)
+                Xmb[j * (T_SEQ_L - 1):(j + 1) * (T_SEQ_L - 1)].copy_(Xpin[s], non_blocking=True)
+            lstep.stage(Xmb, [0, 1], T_SEQ_L - 1, T_SEQ_L - 1, 0)
         else:
-            lstep.stage(Xd, idx, T_SEQ - 1, T_SEQ, 1)
+            lstep.stage(Xd, idx, T_SEQ_L - 1, T_SEQ_L, 1)
         lstep.contract()
         if time_bwd:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -215,8 +444,7 @@ def run_ours(args):
     bwd_bytes = d * (40 + 1 + 4 + 40 + RESAMPLES * (20 + 4 + 20 + 6)) + \
         4 * 4 * OUT_F * (IN_F // 64)
     achieved = bwd_bytes / (bwd_ms * 1e-3) / 1e9
-    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) \
-        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    peaks = globals()["peaks"]()
     peak = float(peaks.get("hbm_gbs", 6650.0))
     value = world * args.steps / (ms * 1e-3)
     res = {
@@ -238,22 +466,22 @@ def run_ours(args):
         "clocks": clk,
     }
     if rank == 0 and not args.no_cpu_baseline:
-        res["cpu_baseline"] = cpu_baseline(W, X, lin_codes=g["codes"].cpu().numpy(),
-                                           s16=g["scales"].cpu().numpy().astype(np.float16),
-                                           n_steps=2)
+        res["cpu_baseline"] = cpu_baseline_linear(W, X, lin_codes=g["codes"].cpu().numpy(),
+                                                  s16=g["scales"].cpu().numpy().astype(np.float16),
+                                                  n_steps=2)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
-def cpu_baseline(W, X, lin_codes, s16, n_steps=2):
+def cpu_baseline_linear(W, X, lin_codes, s16, n_steps=2):
     """The CPU restatement of the same step (oracle port), on this host's cores."""
     from oracle import gsq as ogsq
     st = ogsq.LinearState(3, lin_codes, s16, 64, seed=0, linear_id=5)
-    Xs = X.reshape(N_SEQ, T_SEQ, IN_F)[:, 1:]
+    Xs = X.reshape(N_SEQ_L, T_SEQ_L, IN_F)[:, 1:]
     t0 = time.perf_counter()
-    ogsq.train_linear(st, lambda idx: Xs[idx].reshape(-1, IN_F), W, N_SEQ, n_steps, seed=1,
+    ogsq.train_linear(st, lambda idx: Xs[idx].reshape(-1, IN_F), W, N_SEQ_L, n_steps, seed=1,
                       noise_seed=77)
     dt = time.perf_counter() - t0
     return {"value": round(n_steps / dt, 4), "unit": "steps/s", "cores": os.cpu_count(),
@@ -261,44 +489,15 @@ def cpu_baseline(W, X, lin_codes, s16, n_steps=2):
             "sample": f"{n_steps} steps of the same workload (numpy float32 elementwise, float64 GEMMs)"}
 
 
-def run_reference(args):
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    if rank != 0:
-        return
-    from oracle import gptq as og
-    W, X = make_inputs(seed=0)
-    H, _ = og.hessian_from_inputs(X)
-    g = og.quantize_gptq(W[:64], H, 3, 64)  # init codes for the sample rows only (bounded)
-    rng = np.random.default_rng(0)
-    codes = np.concatenate([g["codes"]] * (OUT_F // 64))
-    scales = np.concatenate([g["scales"]] * (OUT_F // 64)).astype(np.float16)
-    per = []
-    for _ in range(max(1, min(args.steps, 3))):
-        r = cpu_baseline(W, X, codes, scales, n_steps=1)
-        per.append(r["value"])
-    v = statistics.median(per)
-    res = {"impl": "reference",
-           "metric": "GSQ steps/s (single linear up_proj 4864x896, 3-bit, micro-batch 2x511, R=2)",
-           "value": round(v, 4), "unit": "steps/s", "n_gpus": world, "steps": len(per),
-           "warmup": 0, "ms_per_step": round(1000 / v, 2), "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": "config 1: single linear GSQ (W 4864x896, X 16384x896 as 32x512)"},
-           "cpu_baseline": {"value": round(v, 4), "unit": "steps/s", "cores": os.cpu_count(),
-                            "kind": "port",
-                            "sample": "1-step samples of the same workload; the reference's MLX "
-                                      "path is unavailable, this is the numpy restatement"},
-           "e2e": {"value": round(v, 4), "unit": "steps/s", "h2d_bytes_per_step": 0,
-                   "d2h_bytes_per_step": 0}}
-    print(json.dumps(res), flush=True)
-
 
 def main():
     args = parse()
+    if args.workload == "linear":
+        return run_linear(args)
     if args.impl == "reference":
         run_reference(args)
     else:
-        run_ours(args)
+        run_block(args)
 
 
 if __name__ == "__main__":

@@ -154,6 +154,29 @@ def _tp(t):
     return None if t is None else t.data_ptr()
 
 
+class LaunchLog:
+    """Optional per-launch CUDA events of gemm() calls (for roofline measurements): while
+    active, every call records (label, M, N, K, products, start, end)."""
+    active = None
+
+    def __init__(self):
+        self.rows = []
+
+    def __enter__(self):
+        LaunchLog.active = self
+        return self
+
+    def __exit__(self, *a):
+        LaunchLog.active = None
+
+    def summary(self):
+        torch.cuda.synchronize()
+        out = []
+        for (M, N, K, prods, batch, e0, e1) in self.rows:
+            out.append((M, N, K, prods, batch, e0.elapsed_time(e1)))
+        return out
+
+
 def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, alpha=1.0,
          beta=0.0, C=None, ldc=None, c_terms: Terms = None, ct_terms: Terms = None,
          sq_partial=None, bias=None, resid=None, target=None, ld_rt=None, out_scale=1.0,
@@ -205,7 +228,15 @@ def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, 
     d.t_div, d.t_r1, d.t_r2, d.t_c1, d.t_c2 = t_off
     dev = A.t[0].device
     d.err = err_flag(dev).data_ptr()
+    log = LaunchLog.active
+    if log is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
     _lib.call("gsq_gemm", _C.byref(d), _lib.stream_ptr())
+    if log is not None:
+        e1.record()
+        prods = sum(1 for i in range(na) for j in range(nb) if i + j <= order)
+        log.rows.append((d.M, d.N, d.K, prods, batch, e0, e1))
     return C
 
 

@@ -211,7 +211,7 @@ class LinearStep:
 
 
 def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=None,
-                  noise_seed=None, exact_bf16_rows=False, sync_timing=True):
+                  noise_seed=None, exact_bf16_rows=False, timer=None, name="qk"):
     """qk-stage optimiser: loss = sum over linears of mean ||X (W_bar - W)^T||^2.
 
     x_all: float32 CUDA tensor [n_seqs, T, in] of the linears' inputs; each step draws a sorted
@@ -230,23 +230,25 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
     step = LinearStep(lins, m * (T - 1), in_f, opts.resamples, 1 if exact_bf16_rows else 3)
     flat = x_all.view(n_seq * T, in_f)
     err_flag(step.dev).zero_()
-    history, step_s = [], []
+    hist = torch.zeros(opts.steps, len(lins), device=step.dev, dtype=torch.float64)
+    timer = timer or StageTimer(min(3, opts.steps - 1))
     tau, kappa = gs_schedules(0, opts.steps)
     step.first_forward(targets, 0, tau, kappa, noise_seed, noise_of)
     for t in range(opts.steps):
-        t0 = time.perf_counter()
+        timer.mark(name, t, False)
         tau, kappa = gs_schedules(t, opts.steps)
         idx = np.sort(rng.choice(n_seqs, size=m, replace=False))
         step.stage(flat, idx, T - 1, T, 1)
         step.contract()
         nxt = (t + 1, *gs_schedules(t + 1, opts.steps)) if t + 1 < opts.steps else None
         step.update(targets, t, tau, kappa, opts, noise_seed, nxt=nxt, noise_of=noise_of)
-        history.append(step.mean_loss())
-        if sync_timing:
-            torch.cuda.synchronize()
-        step_s.append(time.perf_counter() - t0)
+        hist[t].copy_(step.loss.view(len(lins), step.R).sum(1))
+        timer.mark(name, t, t == opts.steps - 1)
     check_err(step.dev)
-    return history, round(1000 * float(np.median(step_s[3:] or step_s)), 1)
+    denom = torch.tensor([step.M * lin.out_f for lin in lins], device=step.dev,
+                         dtype=torch.float64)
+    history = ((hist / denom).sum(1) / step.R).cpu().tolist()
+    return history, (round(timer.ms[name], 4) if name in timer.ms else None)
 
 
 # ------------------------------------------------------------------------- block stages ---
@@ -488,12 +490,33 @@ class VOStep(_StageBase):
             gemm(self.DVT, self.HNT, C=self.grad_v[r])
 
 
+class StageTimer:
+    """CUDA-event timing of the steps after the first `warmup` of each stage: ms[name]."""
+
+    def __init__(self, warmup=3):
+        self.warmup = int(warmup)
+        self.ms = {}
+        self._ev = {}
+
+    def mark(self, name, t, last):
+        if t == self.warmup:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self._ev[name] = e
+        if last and name in self._ev:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            e.synchronize()
+            n = t + 1 - self.warmup
+            self.ms[name] = self._ev[name].elapsed_time(e) / max(n, 1)
+
+
 def train_stage(step, stage_args_of, n_seqs, opts: BlockOpts, seed, noise_seed=None,
-                noise_of=None, sync_timing=True):
+                noise_of=None, timer=None, name="stage"):
     """The stage optimiser loop (staged.py:357-400) around a vo / mlp step: schedules, the
     sorted micro-batch draw of the numpy stream, contractions, the fused update with the next
     step's forward. stage_args_of(idx) returns the arguments of step.stage for sequence ids idx.
-    Returns (history, median_ms)."""
+    The per-step mean soft loss stays on the device until the end. Returns (history, ms/step)."""
     if opts.steps == 0:
         return [], None
     rng = np.random.default_rng(seed)
@@ -502,21 +525,21 @@ def train_stage(step, stage_args_of, n_seqs, opts: BlockOpts, seed, noise_seed=N
     err_flag(step.dev).zero_()
     tau, kappa = gs_schedules(0, opts.steps)
     step.first_forward(0, tau, kappa, noise_seed, noise_of)
-    history, step_s = [], []
+    hist = torch.zeros(opts.steps, device=step.dev, dtype=torch.float64)
+    timer = timer or StageTimer(min(3, opts.steps - 1))
     for t in range(opts.steps):
-        t0 = time.perf_counter()
+        timer.mark(name, t, False)
         tau, kappa = gs_schedules(t, opts.steps)
         idx = np.sort(rng.choice(n_seqs, size=m, replace=False))
         step.stage(*stage_args_of(idx))
         step.contract()
         nxt = (t + 1, *gs_schedules(t + 1, opts.steps)) if t + 1 < opts.steps else None
         step.update(t, tau, kappa, opts, noise_seed, nxt=nxt, noise_of=noise_of)
-        history.append(step.mean_loss())
-        if sync_timing:
-            torch.cuda.synchronize()
-        step_s.append(time.perf_counter() - t0)
+        hist[t:t + 1].copy_(step.loss.sum(0, keepdim=True))
+        timer.mark(name, t, t == opts.steps - 1)
     check_err(step.dev)
-    return history, round(1000 * float(np.median(step_s[3:] or step_s)), 1)
+    history = (hist / (step.R * step.count)).cpu().tolist()
+    return history, (round(timer.ms[name], 4) if name in timer.ms else None)
 
 
 # --------------------------------------------------------------------- block quantizer ---
@@ -531,7 +554,7 @@ def _hard_bf16(codes_t, scales16, bits, group_size):
 
 
 def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None, T=None,
-                   chunk_seqs=8, log=print, noise_of=None):
+                   chunk_seqs=8, log=print, noise_of=None, timer=None):
     """Quantize the seven linears of one block on the calibration stream (staged.py:405-522).
 
     h: bf16 CUDA [N*T, H], the block inputs of the N calibration sequences (the quantized
@@ -597,10 +620,10 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
 
     def stage_done(stage, t0, hist, ms):
         stats["stages"][stage] = {"seconds": round(time.perf_counter() - t0, 3), "steps": len(hist),
-                                  "median_step_ms": ms,
+                                  "ms_per_step": ms,
                                   "soft_loss_first": hist[0] if hist else None,
                                   "soft_loss_last": hist[-1] if hist else None}
-        log(f"    stage {stage}: {len(hist)} steps, median {ms} ms/step, "
+        log(f"    stage {stage}: {len(hist)} steps, {ms} ms/step, "
             f"{stats['stages'][stage]['seconds']:.2f} s")
 
     # ---- qk: linear reconstruction on hn rows -------------------------------------------
@@ -613,7 +636,8 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
     qk = [gptq(n, H_hn, i) for i, n in enumerate(STAGE_LAYERS["qk"])]
     qk_lins = [l for l in qk if l is not None]
     hist, ms = train_linears(qk_lins, hn_all.view(N, T, H), Wf, N, opts, seed + 1,
-                             exact_bf16_rows=True, noise_of=noise_of) if qk_lins else ([], None)
+                             exact_bf16_rows=True, noise_of=noise_of, timer=timer,
+                             name="qk") if qk_lins else ([], None)
     for lin in qk_lins:
         harden(lin)
     stage_done("qk", t0, hist, ms)
@@ -637,7 +661,7 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
     if len(vo_lins) == 2:
         vstep = VOStep(vo_lins, cfg, min(opts.micro_batch, N), T, opts.resamples, W["v_bias"])
         hist, ms = train_stage(vstep, lambda idx: (hn_all, A_all, qk_all, idx), N, opts,
-                               seed + 2, noise_of=noise_of)
+                               seed + 2, noise_of=noise_of, timer=timer, name="vo")
     else:
         hist, ms = [], None  # an 8-bit v or o keeps its GPTQ values (not trained here)
     for lin in vo_lins:
@@ -664,7 +688,7 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
     if len(mlp_lins) == 3:
         mstep = MLPStep(mlp_lins, cfg, min(opts.micro_batch, N), T, opts.resamples)
         hist, ms = train_stage(mstep, lambda idx: (mn_all, h1_all, Y_all, idx), N, opts,
-                               seed + 3, noise_of=noise_of)
+                               seed + 3, noise_of=noise_of, timer=timer, name="mlp")
     else:
         hist, ms = [], None
     for lin in mlp_lins:

@@ -95,9 +95,13 @@ def test_vo_stage_matches_oracle():
         assert rl <= 1e-3 and rs <= 1e-3, (lin.name, rl, rs)
         assert (lin.hard_codes() == st.hard_codes()).mean() >= 0.999
     assert abs(hist[-1] - hist_o[-1]) <= 1e-3 * hist_o[-1]
-    # the GPU probabilities equal the oracle's from the same hn (bf16, rare last-bit flips)
-    P_ref = ob.attention_probs(hn[:T].float().cpu(), {k: v.float() for k, v in W.items()}, 2, 1)
-    blk2 = Qwen2Block(cfg, 1, T)
+    # the probabilities of the micro-batch equal the oracle's from the same hn (bf16; rare
+    # last-bit flips from the float32 scores)
+    rng = np.random.default_rng(6)
+    i0 = int(np.sort(rng.choice(N, size=2, replace=False))[0])
+    P_ref = ob.attention_probs(hn[i0 * T:(i0 + 1) * T].float().cpu(),
+                               {k: v.float() for k, v in W.items()}, 2, 1)
+    assert float((Ps[0][0] == P_ref).float().mean()) >= 0.97
 
 
 def test_quantize_block_runs_small():
