@@ -217,6 +217,11 @@ def run_block(args):
     pk = peaks()
     peak = float(pk.get("bf16_tflops", 1590.0))
 
+    if args.e2e_steps == 0:  # profiling runs: no end-to-end pass
+        res = {"ms_step": ms_step, "stage_ms": ms}
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
     # end to end through the public API: host calibration stream in, stored shards out
     h_host = h.cpu().pin_memory()
     barrier()

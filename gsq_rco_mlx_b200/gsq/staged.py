@@ -457,7 +457,9 @@ class VOStep(_StageBase):
              C=self.scores, ldc=T, a_off=(1, T, 0), b_off=(c.rep, T, 0), c_off=(1, T * T, 0),
              skip_upper=True)
         _lib.call("gsq_softmax_causal", _lib.ptr(self.scores), B, T, _lib.ptr(self.P.t[0]),
-                  _lib.ptr(self.PT.t[0]), st)
+                  None, st)
+        _lib.call("gsq_transpose_bf16", _lib.ptr(self.P.t[0]), T, T, T, T * T,
+                  _lib.ptr(self.PT.t[0]), T, T * T, B, st)
 
     def contract(self):
         c, T, m = self.cfg, self.T, self.m

@@ -122,7 +122,7 @@ def mlp_loss_and_grads(mn, h1, Y, Wg, Wu, Wd):
     r = h1.to(F64) + d_in @ wd.T - Y.to(F64)
     loss = (r * r).mean()
     loss.backward()
-    return float(loss), wg.grad.numpy(), wu.grad.numpy(), wd.grad.numpy()
+    return float(loss.detach()), wg.grad.numpy(), wu.grad.numpy(), wd.grad.numpy()
 
 
 def vo_loss_and_grads(hn_seqs, A_seqs, P_seqs, Wv, bv, Wo, n_heads=14, n_kv=2):
@@ -143,7 +143,7 @@ def vo_loss_and_grads(hn_seqs, A_seqs, P_seqs, Wv, bv, Wo, n_heads=14, n_kv=2):
         total = total + (r * r).mean()
     loss = total / S
     loss.backward()
-    return float(loss), wv.grad.numpy(), wo.grad.numpy()
+    return float(loss.detach()), wv.grad.numpy(), wo.grad.numpy()
 
 
 # ------------------------------------------------------------- stage optimisers ---
