@@ -127,42 +127,47 @@ __global__ void chol_trsm_kernel(double* __restrict__ A, int n, int p, int b) {
   }
 }
 
-// Inverse of the lower-triangular L, one warp per column j. Xc[j][i] = (L^-1)[i][j], i >= j.
-// Lane l owns the entries i with (i - j) % 32 == l, so each lane reads back only its own writes.
-__global__ void tri_inv_kernel(const double* __restrict__ L, int n, double* __restrict__ Xc) {
-  const int lane = threadIdx.x & 31;
-  const int j = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-  if (j >= n) return;
-  double* xc = Xc + (int64_t)j * n;
-  for (int i = j; i < n; ++i) {
-    double x;
-    if (i == j) {
-      x = 1.0 / L[(int64_t)j * n + j];
-    } else {
-      const double* li = L + (int64_t)i * n;
-      double dot = 0.0;
-      for (int k = j + lane; k < i; k += 32) dot = fma(li[k], xc[k], dot);
-      dot = warp_sum_d(dot);
-      x = -dot / li[i];
+// Inverse of each 64 x 64 diagonal block of the lower-triangular L (one CTA per block):
+// X[b][b] = L[b][b]^-1 by forward substitution, one thread per column of the block.
+constexpr int kInvNB = 64;
+
+__global__ void tri_inv_diag_kernel(const double* __restrict__ L, int n, double* __restrict__ X) {
+  __shared__ double Ls[kInvNB][kInvNB + 1];
+  const int p = blockIdx.x * kInvNB;
+  const int b = min(kInvNB, n - p);
+  for (int e = threadIdx.x; e < b * b; e += blockDim.x) {
+    const int r = e / b, c = e % b;
+    Ls[r][c] = (c <= r) ? L[(int64_t)(p + r) * n + p + c] : 0.0;
+  }
+  __syncthreads();
+  const int j = threadIdx.x;  // column of the inverse
+  if (j < b) {
+    double x[kInvNB];
+#pragma unroll
+    for (int i = 0; i < kInvNB; ++i) x[i] = 0.0;
+#pragma unroll
+    for (int i = 0; i < kInvNB; ++i) {
+      if (i >= b) break;
+      if (i < j) continue;
+      double dot = (i == j) ? 1.0 : 0.0;
+      for (int k = j; k < i; ++k) dot -= Ls[i][k] * x[k];
+      x[i] = dot / Ls[i][i];
     }
-    if (((i - j) & 31) == lane) xc[i] = x;
+#pragma unroll
+    for (int i = 0; i < kInvNB; ++i) {
+      if (i >= b) break;
+      X[(int64_t)(p + i) * n + p + j] = (i >= j) ? x[i] : 0.0;
+    }
   }
 }
 
-// U[a][b] = Xc[n-1-b][n-1-a] for b >= a, 0 below the diagonal (32 x 32 smem tiles).
-__global__ void reverse_transpose_kernel(const double* __restrict__ Xc, int n,
-                                         double* __restrict__ U) {
-  __shared__ double S[32][33];
-  const int a0 = blockIdx.y * 32, b0 = blockIdx.x * 32;
-  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
-  for (int bb = ty; bb < 32; bb += 8) {
-    const int b = b0 + bb, a = a0 + tx;
-    S[bb][tx] = (a < n && b < n && b >= a) ? Xc[(int64_t)(n - 1 - b) * n + (n - 1 - a)] : 0.0;
-  }
-  __syncthreads();
-  for (int aa = ty; aa < 32; aa += 8) {
-    const int a = a0 + aa, b = b0 + tx;
-    if (a < n && b < n) U[(int64_t)a * n + b] = S[tx][aa];
+// U = J X J (reversed rows and columns): X lower-triangular -> U upper-triangular.
+__global__ void reverse_both_kernel(const double* __restrict__ X, int n, double* __restrict__ U) {
+  const int64_t nn = (int64_t)n * n;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nn;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int a = (int)(e / n), c = (int)(e - (int64_t)a * n);
+    U[e] = (c >= a) ? X[(int64_t)(n - 1 - a) * n + (n - 1 - c)] : 0.0;
   }
 }
 
@@ -394,10 +399,28 @@ extern "C" int gptq_factor(const double* H, int n, double damp, double* U, uint8
       if (rc != GSQ_OK) return rc;
     }
   }
-  tri_inv_kernel<<<(unsigned)(((int64_t)n * 32 + 255) / 256), 256, 0, st>>>(A, n, Xc);
+  // X = L^-1, block lower-triangular: invert the 64 x 64 diagonal blocks, then merge pairs
+  // of neighbouring blocks of width w: [[A, 0], [B, C]]^-1 has lower-left block
+  // -C^-1 (B A^-1), two float64 GEMMs per pair (U serves as the temporary).
+  if (cudaMemsetAsync(Xc, 0, sizeof(double) * nn, st) != cudaSuccess) return GSQ_ECUDA;
+  tri_inv_diag_kernel<<<(n + kInvNB - 1) / kInvNB, kInvNB, 0, st>>>(A, n, Xc);
   GSQ_CHECK_LAUNCH();
-  dim3 tg((n + 31) / 32, (n + 31) / 32);
-  reverse_transpose_kernel<<<tg, dim3(32, 8), 0, st>>>(Xc, n, U);
+  for (int w = kInvNB; w < n; w *= 2) {
+    for (int p = 0; p + w < n; p += 2 * w) {
+      const int wa = w, wc = min(w, n - p - w);
+      const double* Bm = A + (int64_t)(p + w) * n + p;            // L21 [wc x wa]
+      const double* Ainv = Xc + (int64_t)p * n + p;               // [wa x wa]
+      const double* Cinv = Xc + (int64_t)(p + w) * n + p + w;     // [wc x wc]
+      double* Tm = U;                                             // [wc x wa], ld wa
+      double* X21 = Xc + (int64_t)(p + w) * n + p;                // [wc x wa]
+      int rc = gemm_simt<double, double>(wc, wa, wa, 1.0, Bm, n, 1, Ainv, n, 1, 0.0, Tm, wa, 0,
+                                         st);
+      if (rc != GSQ_OK) return rc;
+      rc = gemm_simt<double, double>(wc, wa, wc, -1.0, Cinv, n, 1, Tm, wa, 1, 0.0, X21, n, 0, st);
+      if (rc != GSQ_OK) return rc;
+    }
+  }
+  reverse_both_kernel<<<blocks_for(nn, 256), 256, 0, st>>>(Xc, n, U);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }
