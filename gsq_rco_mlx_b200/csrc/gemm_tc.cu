@@ -2,17 +2,25 @@
 //
 //   C[m, n] = alpha * sum_k A(m, k) B(n, k)        A, B given as 1..3 bf16 terms each,
 //                                                   A = sum_i A_i, B = sum_j B_j (K-major)
-// The products A_i B_j with i + j <= order are accumulated into one float32 TMEM accumulator
-// (order 2 with three terms per side reproduces float32 operands to 2^-24; an exactly-bf16
-// operand needs one term). One CTA computes one 128 x BN tile:
+// The products A_i B_j with i + j <= order are accumulated on the tensor cores (order 2 with
+// three terms per side reproduces float32 operands to 2^-24; an exactly-bf16 operand needs one
+// term). Persistent kernel: one CTA per SM walks the 128 x BN output tiles (batch z, row tile m,
+// column tile n; m fastest) in a static round-robin order. Roles:
 //   warp 0     TMA producer: for each 64-wide k-block, every term tile of A and B into one
 //              pipeline stage (128-byte swizzle), completion counted on the stage's mbarrier
-//   warp 1     TMEM allocator and MMA issuer: 4 UMMA K-steps x |products| per stage, then a
-//              commit that frees the stage; a final commit publishes the accumulator
-//   warps 2-5  epilogue: tcgen05.ld of their 32 TMEM lanes, then any of: float32 C
-//              (alpha acc + beta C), C as bf16 terms, C^T as bf16 terms (the K-major operand
-//              of a later reduction over m), and a per-tile sum of squares
-// Every mbarrier wait is bounded; a timeout sets *err and the CTA unwinds, freeing its TMEM.
+//   warp 1     TMEM allocator and MMA issuer
+//   warps 2-9  epilogue: fold the accumulators into float32 registers, then the fused outputs
+// Tensor-core accumulation into TMEM is not IEEE round-to-nearest. The hi x hi products ("big")
+// therefore go to a ring of chunk accumulators that the epilogue folds into registers with IEEE
+// adds after every chunk of k-blocks; the other products ("small", 2^8 smaller and less) stay in
+// one of two per-tile accumulators for the whole k-range. The ring lets the MMAs of the next tile
+// run while the epilogue is still writing the outputs of this one.
+// Outputs leave through a per-warp 32 x 32 shared-memory transpose: row-major outputs as
+// coalesced row segments, transposed outputs (C^T as bf16 terms: the K-major operand of a later
+// reduction over m) as coalesced column segments.
+// Every mbarrier wait is bounded; a timeout sets *err and every role winds down without further
+// waits on its partners, the MMA issuer waits (bounded) for its last MMAs and the producer for
+// its copies in flight, and the CTA frees its TMEM.
 #include "tc_common.cuh"
 
 namespace gsq {
@@ -22,7 +30,12 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kSmemBudget = 200 * 1024;
+constexpr int kStgLd = 33;                                   // staging row stride (floats)
+constexpr uint32_t kStgBytes = kEpiWarps * 32 * kStgLd * 4;  // one 32 x 32 tile per warp
+constexpr uint32_t kPipeBudget = 192 * 1024;                 // pipeline stages
+constexpr int kMaxStages = 8;
+constexpr int kMaxBig = 8;
+constexpr uint32_t kTmemCols = 512;
 
 enum Epi {
   EPI_PLAIN = 0,
@@ -50,7 +63,6 @@ struct GemmParams {
   float alpha, beta;
   float* C;
   int64_t ldc;
-  int c_vec;
   __nv_bfloat16* cs[3];
   int ncs;
   int64_t ldcs;
@@ -71,8 +83,13 @@ struct GemmParams {
   int* err;
   int stages;
   int kb_per_chunk;
+  int n_big;       // chunk accumulators in the TMEM ring
+  int tiles_m, tiles_n;
+  int64_t total_tiles;
   int skip_upper;  // output tiles entirely above the diagonal (n >= m) are not computed
   int row_period;  // epi 1: rows with (row % row_period) == 0 have a zero residual
+  // two-element (8-byte float / 4-byte bf16) accesses are aligned for these outputs
+  int pair_c, pair_cs, pair_ct, pair_aux, pair_rt;
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -89,53 +106,338 @@ __device__ __forceinline__ float sigmoid_f(float x) {
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// One 128 x BN output tile per CTA (grid z = batch). TMEM: two buffers of a "big" accumulator
-// (the hi x hi products) and a "small" one (every other product, 2^8 smaller); tensor-core
-// accumulation into TMEM is not IEEE round-to-nearest, so every chunk of k-blocks is folded into
-// float32 registers with IEEE adds. Eight epilogue warps fold and finish: warp w reads TMEM lanes
-// 32 (w % 4) .. + 31 (one output row per thread) and the 32-column chunks j with j % 2 == w / 4
-// of the tile (for the SwiGLU forward this pairs gate column c with up column c + 64).
+struct TileInfo {
+  int z, tile_m, tile_n, kb0, nkb;
+  int64_t part;  // index of the tile's sum-of-squares partial
+};
+
+// Tile L of the round-robin order; false for a tile that skip_upper leaves out. The k-block
+// range: causal 1 = lower-triangular A (k < end of this row tile), causal 2 = upper-triangular A
+// (k >= start of this row tile).
+template <int BN>
+__device__ __forceinline__ bool tile_at(const GemmParams& p, int64_t L, TileInfo& t) {
+  const int64_t per = (int64_t)p.tiles_m * p.tiles_n;
+  t.z = (int)(L / per);
+  const int rem = (int)(L - (int64_t)t.z * per);
+  const int my = rem % p.tiles_m, nx = rem / p.tiles_m;
+  t.tile_m = my * BM;
+  t.tile_n = nx * BN;
+  if (p.skip_upper && t.tile_n >= t.tile_m + BM) return false;
+  const int kb_total = (p.K + BK - 1) / BK;
+  t.kb0 = p.causal == 2 ? min(t.tile_m / BK, kb_total - 1) : 0;
+  const int kb1 = p.causal == 1 ? min(kb_total, (t.tile_m + BM + BK - 1) / BK) : kb_total;
+  t.nkb = kb1 - t.kb0;
+  t.part = ((int64_t)t.z * p.tiles_m + my) * p.tiles_n + nx;
+  return true;
+}
+
+// ------------------------------------------------------------- epilogue helpers ---
+
+// This lane's row of 32 values into row `lane` of the warp's staging tile.
+__device__ __forceinline__ void stage_put(float* stg, int lane, const float* v) {
+#pragma unroll
+  for (int t = 0; t < 32; ++t) stg[lane * kStgLd + t] = v[t];
+  __syncwarp();
+}
+
+__device__ __forceinline__ void load_bf2(const __nv_bfloat16* ptr, bool two, bool pair, float& a,
+                                         float& b) {
+  if (two && pair) {
+    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(ptr);
+    a = __low2float(v);
+    b = __high2float(v);
+  } else {
+    a = __bfloat162float(ptr[0]);
+    b = two ? __bfloat162float(ptr[1]) : 0.f;
+  }
+}
+
+__device__ __forceinline__ void load_f2(const float* ptr, bool two, bool pair, float& a,
+                                        float& b) {
+  if (two && pair) {
+    const float2 v = *reinterpret_cast<const float2*>(ptr);
+    a = v.x;
+    b = v.y;
+  } else {
+    a = ptr[0];
+    b = two ? ptr[1] : 0.f;
+  }
+}
+
+__device__ __forceinline__ void store_f2(float* ptr, float a, float b, bool two, bool pair) {
+  if (two && pair) {
+    *reinterpret_cast<float2*>(ptr) = make_float2(a, b);
+  } else {
+    ptr[0] = a;
+    if (two) ptr[1] = b;
+  }
+}
+
+// x0, x1 (consecutive elements) as n_terms bf16 terms at terms[i] + off
+__device__ __forceinline__ void store_terms2(__nv_bfloat16* const* terms, int n_terms, int64_t off,
+                                             float x0, float x1, bool two, bool pair) {
+  __nv_bfloat16 h0[3], h1[3];
+  split3_bf16(x0, h0[0], h0[1], h0[2]);
+  split3_bf16(x1, h1[0], h1[1], h1[2]);
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    if (i < n_terms) {
+      __nv_bfloat16* ptr = terms[i] + off;
+      if (two && pair) {
+        *reinterpret_cast<__nv_bfloat162*>(ptr) = __halves2bfloat162(h0[i], h1[i]);
+      } else {
+        ptr[0] = h0[i];
+        if (two) ptr[1] = h1[i];
+      }
+    }
+  }
+}
+
+// Columns c of the staging tile (rows m of the output band) as rows n0 + c of C^T:
+// ct[i][(r_base + up + n0 + c) * ldct + c_base + row0 + m], n0 + c < n_lim, row0 + m < M.
+__device__ __forceinline__ void transposed_pass(const GemmParams& p, const TileInfo& t,
+                                                const float* stg, int lane, int n0, int n_lim,
+                                                int row0, int64_t up) {
+  const int64_t r_base = p.t_row.at(t.z) + up, c_base = p.t_col.at(t.z);
+#pragma unroll 4
+  for (int i = 0; i < 16; ++i) {
+    const int c = 2 * i + (lane >> 4), m = 2 * (lane & 15);
+    const int n = n0 + c, row = row0 + m;
+    if (n < n_lim && row < p.M) {
+      const float x0 = stg[m * kStgLd + c], x1 = stg[(m + 1) * kStgLd + c];
+      store_terms2(p.ct, p.nct, (r_base + n) * p.ldct + c_base + row, x0, x1, row + 1 < p.M,
+                   p.pair_ct != 0);
+    }
+  }
+}
+
+// The fused outputs of one tile from the folded accumulator. Epilogue warp (q, h) holds rows
+// tile_m + 32 q + lane and the 32-column groups jc (columns tile_n + 64 jc + 32 h + t); for the
+// SwiGLU forward, slots [0, 32) are the gate and [32, 64) the up projection of the output
+// columns tile_n / 2 + 32 h + t.
+template <int BN, int EPI>
+__device__ __forceinline__ double epilogue_out(const GemmParams& p, const TileInfo& t, float* acc,
+                                               float* stg, int lane, int q, int h) {
+  constexpr int kNC = BN / 64;
+  const int64_t coff = p.c_off.at(t.z);
+  const int row0 = t.tile_m + 32 * q;
+  double sq = 0.0;
+#pragma unroll
+  for (int i = 0; i < BN / 2; ++i) acc[i] = __fmul_rn(p.alpha, acc[i]);
+
+  if (EPI == EPI_PLAIN || EPI == EPI_RESID || EPI == EPI_BF16) {
+#pragma unroll
+    for (int jc = 0; jc < kNC; ++jc) {
+      const int n0 = t.tile_n + 64 * jc + 32 * h;
+      float* a = acc + 32 * jc;
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int n = n0 + u;
+        float x = a[u];
+        if (EPI == EPI_BF16) {
+          x = bf16r(x);
+          if (p.bias && n < p.N) x = bf16r(__fadd_rn(x, p.bias[n]));
+        } else if (p.bias && n < p.N) {
+          x = __fadd_rn(x, p.bias[n]);
+        }
+        a[u] = x;
+      }
+      stage_put(stg, lane, a);
+#pragma unroll 2
+      for (int i = 0; i < 16; ++i) {
+        const int r = 2 * i + (lane >> 4), c = 2 * (lane & 15);
+        const int row = row0 + r, n = n0 + c;
+        float* sp = stg + r * kStgLd + c;
+        float x0 = sp[0], x1 = sp[1];
+        const bool in0 = row < p.M && n < p.N, in1 = in0 && n + 1 < p.N;
+        if (in0) {
+          if (EPI == EPI_PLAIN) {
+            if (p.beta != 0.f && p.C) {
+              float c0, c1;
+              load_f2(p.C + coff + (int64_t)row * p.ldc + n, in1, p.pair_c != 0, c0, c1);
+              x0 = __fadd_rn(x0, __fmul_rn(p.beta, c0));
+              x1 = __fadd_rn(x1, __fmul_rn(p.beta, c1));
+            }
+            if (p.sq_partial) {
+              sq += (double)x0 * (double)x0;
+              if (in1) sq += (double)x1 * (double)x1;
+            }
+          } else {
+            const int64_t o = coff + (int64_t)row * p.ld_rt + n;
+            float r0 = 0.f, r1 = 0.f;
+            if (p.resid) load_bf2(p.resid + o, in1, p.pair_rt != 0, r0, r1);
+            if (EPI == EPI_RESID) {
+              float t0, t1;
+              load_bf2(p.target + o, in1, p.pair_rt != 0, t0, t1);
+              if (p.resid) {
+                x0 = __fadd_rn(x0, r0);
+                x1 = __fadd_rn(x1, r1);
+              }
+              x0 = __fsub_rn(x0, t0);
+              x1 = __fsub_rn(x1, t1);
+              if (p.row_period > 0 && (row % p.row_period) == 0) {
+                x0 = 0.f;
+                x1 = 0.f;
+              }
+              sq += (double)x0 * (double)x0;
+              if (in1) sq += (double)x1 * (double)x1;
+              x0 = __fmul_rn(p.out_scale, x0);
+              x1 = __fmul_rn(p.out_scale, x1);
+            } else if (p.resid) {
+              x0 = bf16r(__fadd_rn(r0, x0));
+              x1 = bf16r(__fadd_rn(r1, x1));
+            }
+          }
+          if (p.C) store_f2(p.C + coff + (int64_t)row * p.ldc + n, x0, x1, in1, p.pair_c != 0);
+          if (p.ncs > 0)
+            store_terms2(p.cs, p.ncs, coff + (int64_t)row * p.ldcs + n, x0, x1, in1,
+                         p.pair_cs != 0);
+        }
+        if (p.nct > 0) {
+          sp[0] = x0;
+          sp[1] = x1;
+        }
+      }
+      if (p.nct > 0) {
+        __syncwarp();
+        transposed_pass(p, t, stg, lane, n0, p.N, row0, 0);
+      }
+      __syncwarp();
+    }
+  } else if (EPI == EPI_SWIGLU_FWD || EPI == EPI_SWIGLU_BF16) {
+    const int n0 = t.tile_n / 2 + 32 * h, nl = p.N / 2;
+    if (EPI == EPI_SWIGLU_FWD) {
+      // g and u (float32, row-major) for the backward
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        stage_put(stg, lane, acc + 32 * part);
+        float* dst = part ? p.aux1 : p.aux0;
+#pragma unroll 4
+        for (int i = 0; i < 16; ++i) {
+          const int r = 2 * i + (lane >> 4), c = 2 * (lane & 15);
+          const int row = row0 + r, j = n0 + c;
+          if (row < p.M && j < nl)
+            store_f2(dst + coff + (int64_t)row * p.ld_aux + j, stg[r * kStgLd + c],
+                     stg[r * kStgLd + c + 1], j + 1 < nl, p.pair_aux != 0);
+        }
+        __syncwarp();
+      }
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const float g = acc[u], uu = acc[32 + u];
+        acc[u] = __fmul_rn(__fmul_rn(g, sigmoid_f(g)), uu);  // silu(g) * u
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const float g = bf16r(acc[u]), uu = bf16r(acc[32 + u]);
+        acc[u] = bf16r(__fmul_rn(bf16r(__fmul_rn(g, bf16r(sigmoid_f(g)))), uu));
+      }
+    }
+    stage_put(stg, lane, acc);
+    if (p.ncs > 0) {
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const int r = 2 * i + (lane >> 4), c = 2 * (lane & 15);
+        const int row = row0 + r, j = n0 + c;
+        if (row < p.M && j < nl)
+          store_terms2(p.cs, p.ncs, coff + (int64_t)row * p.ldcs + j, stg[r * kStgLd + c],
+                       stg[r * kStgLd + c + 1], j + 1 < nl, p.pair_cs != 0);
+      }
+    }
+    if (p.nct > 0) transposed_pass(p, t, stg, lane, n0, nl, row0, 0);
+    __syncwarp();
+  } else {  // EPI_SWIGLU_BWD: slots hold dd = dL/d(silu(g) u) of column n; dL/dg and dL/du go
+            // out transposed (planes 0 and 1 of the C^T terms)
+#pragma unroll
+    for (int jc = 0; jc < kNC; ++jc) {
+      const int n0 = t.tile_n + 64 * jc + 32 * h;
+      stage_put(stg, lane, acc + 32 * jc);
+      float du_keep[32];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int r = 2 * i + (lane >> 4), c = 2 * (lane & 15);
+        const int row = row0 + r, n = n0 + c;
+        float* sp = stg + r * kStgLd + c;
+        float dg[2] = {0.f, 0.f}, du[2] = {0.f, 0.f};
+        const bool in0 = row < p.M && n < p.N, in1 = in0 && n + 1 < p.N;
+        if (in0) {
+          const int64_t o = coff + (int64_t)row * p.ld_aux + n;
+          float g[2], u[2];
+          load_f2(p.aux0 + o, in1, p.pair_aux != 0, g[0], g[1]);
+          load_f2(p.aux1 + o, in1, p.pair_aux != 0, u[0], u[1]);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float sg = sigmoid_f(g[e]);
+            const float dd = sp[e];
+            du[e] = __fmul_rn(dd, __fmul_rn(g[e], sg));
+            // d(g sigmoid(g))/dg = sigmoid(g) + g sigmoid(g) (1 - sigmoid(g))
+            const float dsil =
+                __fadd_rn(sg, __fmul_rn(g[e], __fmul_rn(sg, __fsub_rn(1.0f, sg))));
+            dg[e] = __fmul_rn(__fmul_rn(dd, u[e]), dsil);
+          }
+        }
+        sp[0] = dg[0];
+        sp[1] = dg[1];
+        du_keep[2 * i] = du[0];
+        du_keep[2 * i + 1] = du[1];
+      }
+      __syncwarp();
+      if (p.nct > 0) transposed_pass(p, t, stg, lane, n0, p.N, row0, 0);
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int r = 2 * i + (lane >> 4), c = 2 * (lane & 15);
+        stg[r * kStgLd + c] = du_keep[2 * i];
+        stg[r * kStgLd + c + 1] = du_keep[2 * i + 1];
+      }
+      __syncwarp();
+      if (p.nct > 0) transposed_pass(p, t, stg, lane, n0, p.N, row0, p.ct_up_rows);
+      __syncwarp();
+    }
+  }
+  return sq;
+}
+
+// --------------------------------------------------------------------------- kernel ---
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  __shared__ uint64_t full_bar[8];
-  __shared__ uint64_t empty_bar[8];
-  __shared__ uint64_t accf_bar[2];
-  __shared__ uint64_t acce_bar[2];
+  __shared__ uint64_t full_bar[kMaxStages];
+  __shared__ uint64_t empty_bar[kMaxStages];
+  __shared__ uint64_t bigf_bar[kMaxBig];   // chunk accumulator ready
+  __shared__ uint64_t bige_bar[kMaxBig];   // chunk accumulator folded
+  __shared__ uint64_t smf_bar[2];          // tile "small" accumulator ready
+  __shared__ uint64_t sme_bar[2];          // tile "small" accumulator folded
+  __shared__ uint64_t done_bar;
   __shared__ uint32_t tmem_base;
   __shared__ double red[kEpiWarps];
 
   constexpr uint32_t kTileA = BM * BK * 2;
   constexpr uint32_t kTileB = BN * BK * 2;
-  constexpr uint32_t kCols = 4 * BN;
-  constexpr int kAcc = BN / 2;   // accumulator columns per epilogue thread
-  constexpr int kNC = BN / 64;   // 32-column chunks per epilogue thread
+  constexpr int kAcc = BN / 2;  // accumulator columns per epilogue thread
+  constexpr int kNC = BN / 64;  // 32-column groups per epilogue thread
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int z = blockIdx.z;
-  const int tile_m = blockIdx.y * BM, tile_n = blockIdx.x * BN;
-  if (p.skip_upper && tile_n >= tile_m + BM) return;  // uniform across the CTA
-  const int S = p.stages;
+  const int S = p.stages, NB = p.n_big, P = p.kb_per_chunk;
   const uint32_t stage_bytes = p.na * kTileA + p.nb * kTileB;
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  // k-block range: causal 1 = lower-triangular A (k < end of this row tile), causal 2 =
-  // upper-triangular A (k >= start of this row tile)
-  const int kb_total = (p.K + BK - 1) / BK;
-  const int kb0 = p.causal == 2 ? min(tile_m / BK, kb_total - 1) : 0;
-  const int kb1 = p.causal == 1 ? min(kb_total, (tile_m + BM + BK - 1) / BK) : kb_total;
-  const int num_kb = kb1 - kb0;
-  const int P = p.kb_per_chunk;
-  const int n_chunks = (num_kb + P - 1) / P;
   const bool has_small = (p.na > 1 || p.nb > 1) && p.order > 0;
+  const uint32_t small_col = (uint32_t)(NB * BN);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&accf_bar[b], 1);
-      mbar_init(&acce_bar[b], kEpiWarps);
+    for (int b = 0; b < NB; ++b) {
+      mbar_init(&bigf_bar[b], 1);
+      mbar_init(&bige_bar[b], kEpiWarps);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&smf_bar[b], 1);
+      mbar_init(&sme_bar[b], kEpiWarps);
+    }
+    mbar_init(&done_bar, 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -145,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       if (p.dual_b) tma_prefetch_desc(&p.tma_b2[i]);
     }
   }
-  if (warp == 1) tmem_alloc(&tmem_base, kCols);
+  if (warp == 1) tmem_alloc(&tmem_base, kTmemCols);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
@@ -153,311 +455,208 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 
   if (warp == 0) {
     if (lane == 0) {
-      const int a_row = tile_m + (int)p.a_off.at(z);
-      const int b_row = (p.dual_b ? tile_n / 2 : tile_n) + (int)p.b_off.at(z);
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = (uint32_t)(kb / S) & 1u;
-        if (!mbar_wait(&empty_bar[s], ph ^ 1u, p.err, 1)) break;
-        uint8_t* st = smem + (size_t)s * stage_bytes;
-        mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
-        for (int i = 0; i < p.na; ++i)
-          tma_load_2d(st + i * kTileA, &p.tma_a[i], &full_bar[s], (kb0 + kb) * BK, a_row);
-        for (int j = 0; j < p.nb; ++j) {
-          uint8_t* bt = st + p.na * kTileA + j * kTileB;
-          if (p.dual_b) {
-            tma_load_2d(bt, &p.tma_b[j], &full_bar[s], (kb0 + kb) * BK, b_row);
-            tma_load_2d(bt + kTileB / 2, &p.tma_b2[j], &full_bar[s], (kb0 + kb) * BK, b_row);
-          } else {
-            tma_load_2d(bt, &p.tma_b[j], &full_bar[s], (kb0 + kb) * BK, b_row);
+      int s = 0;
+      uint32_t ph = 0, issued = 0;
+      bool ok = true;
+      for (int64_t L = blockIdx.x; L < p.total_tiles && ok; L += gridDim.x) {
+        TileInfo t;
+        if (!tile_at<BN>(p, L, t)) continue;
+        const int a_row = t.tile_m + (int)p.a_off.at(t.z);
+        const int b_row = (p.dual_b ? t.tile_n / 2 : t.tile_n) + (int)p.b_off.at(t.z);
+        for (int kb = 0; kb < t.nkb; ++kb) {
+          if (!mbar_wait(&empty_bar[s], ph ^ 1u, p.err, 1)) {
+            ok = false;
+            break;
           }
+          uint8_t* st = smem + (size_t)s * stage_bytes;
+          mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
+          const int kx = (t.kb0 + kb) * BK;
+          for (int i = 0; i < p.na; ++i)
+            tma_load_2d(st + i * kTileA, &p.tma_a[i], &full_bar[s], kx, a_row);
+          for (int j = 0; j < p.nb; ++j) {
+            uint8_t* bt = st + p.na * kTileA + j * kTileB;
+            if (p.dual_b) {
+              tma_load_2d(bt, &p.tma_b[j], &full_bar[s], kx, b_row);
+              tma_load_2d(bt + kTileB / 2, &p.tma_b2[j], &full_bar[s], kx, b_row);
+            } else {
+              tma_load_2d(bt, &p.tma_b[j], &full_bar[s], kx, b_row);
+            }
+          }
+          ++issued;
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // let the copies still in flight land before the CTA exits (bounded waits)
+        const uint32_t n = issued < (uint32_t)S ? issued : (uint32_t)S;
+        for (uint32_t j = 0; j < n; ++j) {
+          if (--s < 0) {
+            s = S - 1;
+            ph ^= 1u;
+          }
+          mbar_wait(&full_bar[s], ph, nullptr, 6);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(BM, BN);
-      bool ok = true;
-      for (int c = 0; c < n_chunks && ok; ++c) {
-        const int b = c & 1;
-        if (!mbar_wait(&acce_bar[b], ((uint32_t)(c >> 1) & 1u) ^ 1u, p.err, 4)) break;
-        fence_after_sync();
-        const uint32_t big = tmem + (uint32_t)(b * 2 * BN), small = big + BN;
-        bool big_init = false, small_init = false;
-        const int kb_end = min(num_kb, (c + 1) * P);
-        for (int kb = c * P; kb < kb_end; ++kb) {
-          const int s = kb % S;
-          const uint32_t ph = (uint32_t)(kb / S) & 1u;
-          if (!mbar_wait(&full_bar[s], ph, p.err, 2)) { ok = false; break; }
+      int s = 0, bs = 0;
+      uint32_t ph = 0, bph = 0, tcount = 0;
+      bool ok = true, any = false;
+      for (int64_t L = blockIdx.x; L < p.total_tiles && ok; L += gridDim.x) {
+        TileInfo t;
+        if (!tile_at<BN>(p, L, t)) continue;
+        const uint32_t tb = tcount & 1u, tph = (tcount >> 1) & 1u;
+        ++tcount;
+        const uint32_t small = tmem + small_col + tb * (uint32_t)BN;
+        if (has_small) {
+          if (!mbar_wait(&sme_bar[tb], tph ^ 1u, p.err, 5)) break;
           fence_after_sync();
-          const uint32_t st = smem_u32(smem + (size_t)s * stage_bytes);
-          for (int i = 0; i < p.na; ++i) {
-            for (int j = 0; j < p.nb; ++j) {
-              if (i + j > p.order) continue;
-              const uint32_t a0 = st + i * kTileA;
-              const uint32_t b0 = st + p.na * kTileA + j * kTileB;
-              const bool to_big = (i + j == 0);
-              const uint32_t d = to_big ? big : small;
+        }
+        bool small_init = false;
+        for (int c0 = 0; c0 < t.nkb && ok; c0 += P) {
+          if (!mbar_wait(&bige_bar[bs], bph ^ 1u, p.err, 4)) {
+            ok = false;
+            break;
+          }
+          fence_after_sync();
+          const uint32_t big = tmem + (uint32_t)(bs * BN);
+          bool big_init = false;
+          const int c1 = min(t.nkb, c0 + P);
+          for (int kb = c0; kb < c1; ++kb) {
+            if (!mbar_wait(&full_bar[s], ph, p.err, 2)) {
+              ok = false;
+              break;
+            }
+            fence_after_sync();
+            const uint32_t st = smem_u32(smem + (size_t)s * stage_bytes);
+            for (int i = 0; i < p.na; ++i) {
+              for (int j = 0; j < p.nb; ++j) {
+                if (i + j > p.order) continue;
+                const uint32_t a0 = st + i * kTileA;
+                const uint32_t b0 = st + p.na * kTileA + j * kTileB;
+                const bool to_big = (i + j == 0);
+                const uint32_t d = to_big ? big : small;
 #pragma unroll
-              for (int k = 0; k < BK / 16; ++k) {
-                const uint32_t acc = to_big ? (uint32_t)big_init : (uint32_t)small_init;
-                umma_bf16(d, umma_desc_k_sw128(a0 + k * 32), umma_desc_k_sw128(b0 + k * 32),
-                          idesc, acc);
-                if (to_big) big_init = true; else small_init = true;
+                for (int k = 0; k < BK / 16; ++k) {
+                  const uint32_t accum = to_big ? (uint32_t)big_init : (uint32_t)small_init;
+                  umma_bf16(d, umma_desc_k_sw128(a0 + k * 32), umma_desc_k_sw128(b0 + k * 32),
+                            idesc, accum);
+                  if (to_big) big_init = true; else small_init = true;
+                }
               }
             }
+            umma_commit(&empty_bar[s]);
+            any = true;
+            if (++s == S) {
+              s = 0;
+              ph ^= 1u;
+            }
           }
-          umma_commit(&empty_bar[s]);
+          if (!ok) break;
+          umma_commit(&bigf_bar[bs]);
+          if (++bs == NB) {
+            bs = 0;
+            bph ^= 1u;
+          }
         }
-        umma_commit(&accf_bar[b]);
+        if (ok && has_small) umma_commit(&smf_bar[tb]);
+      }
+      if (any) {  // every MMA issued here has completed before the TMEM is freed
+        umma_commit(&done_bar);
+        mbar_wait(&done_bar, 0, nullptr, 7);
       }
     }
   } else {
     const int ew = warp - 2;
-    const int q = warp & 3;
+    const int q = warp & 3;  // TMEM lane quadrant of this warp
     const int h = ew >> 2;
-    const int r_loc = q * 32 + lane;
-    const int row = tile_m + r_loc;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    float acc[kAcc];
-#pragma unroll
-    for (int t = 0; t < kAcc; ++t) acc[t] = 0.f;
+    float* stg = reinterpret_cast<float*>(smem + (size_t)S * stage_bytes) + ew * (32 * kStgLd);
+    int bs = 0;
+    uint32_t bph = 0, tcount = 0;
     bool ok = true;
-    for (int c = 0; c < n_chunks; ++c) {
-      const int b = c & 1;
-      ok = __all_sync(0xffffffffu, ok && mbar_wait(&accf_bar[b], (uint32_t)(c >> 1) & 1u,
-                                                   p.err, 3));
-      if (!ok) break;
-      fence_after_sync();
+    // after a timeout the loop still runs to the end (skipping every wait and output), so that
+    // all eight warps take the same named-barrier steps
+    for (int64_t L = blockIdx.x; L < p.total_tiles; L += gridDim.x) {
+      TileInfo t;
+      if (!tile_at<BN>(p, L, t)) continue;
+      const uint32_t tb = tcount & 1u, tph = (tcount >> 1) & 1u;
+      ++tcount;
+      float acc[kAcc];
 #pragma unroll
-      for (int jc = 0; jc < kNC; ++jc) {
-        const uint32_t col = (uint32_t)(64 * jc + 32 * h);
-        const uint32_t big = tmem + lane_off + (uint32_t)(b * 2 * BN) + col;
-        uint32_t v[32], w[32];
-        tmem_ld32_nowait(big, v);
-        if (has_small) tmem_ld32_nowait(big + BN, w);
-        tmem_wait_ld();
-        if (has_small) {
+      for (int u = 0; u < kAcc; ++u) acc[u] = 0.f;
+      for (int c0 = 0; c0 < t.nkb; c0 += P) {
+        if (ok) ok = mbar_wait(&bigf_bar[bs], bph, p.err, 3);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+          fence_after_sync();
+          uint32_t v[kNC][32];
 #pragma unroll
-          for (int t = 0; t < 32; ++t)
-            acc[32 * jc + t] = __fadd_rn(acc[32 * jc + t],
-                                         __fadd_rn(__uint_as_float(v[t]), __uint_as_float(w[t])));
-        } else {
+          for (int jc = 0; jc < kNC; ++jc)
+            tmem_ld32_nowait(tmem + lane_off + (uint32_t)(bs * BN + 64 * jc + 32 * h), v[jc]);
+          tmem_wait_ld();
 #pragma unroll
-          for (int t = 0; t < 32; ++t)
-            acc[32 * jc + t] = __fadd_rn(acc[32 * jc + t], __uint_as_float(v[t]));
+          for (int jc = 0; jc < kNC; ++jc)
+#pragma unroll
+            for (int u = 0; u < 32; ++u)
+              acc[32 * jc + u] = __fadd_rn(acc[32 * jc + u], __uint_as_float(v[jc][u]));
+          fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bige_bar[bs]);
+        }
+        if (++bs == NB) {
+          bs = 0;
+          bph ^= 1u;
         }
       }
-      fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acce_bar[b]);
-    }
-    // ---------------------------------------------------------------- outputs ---
-    // (the pipeline stages are idle: every MMA and every TMA load has completed)
-    const bool live = ok && row < p.M;
-    const int64_t coff = p.c_off.at(z);
-    double sq = 0.0;
-    // column of accumulator slot t: n_of(t) = tile_n + 64 (t / 32) + 32 h + t % 32
+      if (has_small) {
+        if (ok) ok = mbar_wait(&smf_bar[tb], tph, p.err, 3);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+          fence_after_sync();
+          uint32_t v[kNC][32];
 #pragma unroll
-    for (int t = 0; t < kAcc; ++t) acc[t] = __fmul_rn(p.alpha, acc[t]);
-    if (EPI == EPI_PLAIN || EPI == EPI_RESID || EPI == EPI_BF16) {
+          for (int jc = 0; jc < kNC; ++jc)
+            tmem_ld32_nowait(tmem + lane_off + small_col + tb * (uint32_t)BN +
+                                 (uint32_t)(64 * jc + 32 * h),
+                             v[jc]);
+          tmem_wait_ld();
 #pragma unroll
-      for (int jc = 0; jc < kNC; ++jc) {
-        const int n0 = tile_n + 64 * jc + 32 * h;
+          for (int jc = 0; jc < kNC; ++jc)
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int n = n0 + t;
-          float x = acc[32 * jc + t];
-          if (EPI == EPI_BF16) {
-            x = bf16r(x);
-            if (p.bias && n < p.N) x = bf16r(__fadd_rn(x, p.bias[n]));
-            if (p.resid && live && n < p.N)
-              x = bf16r(__fadd_rn(__bfloat162float(p.resid[coff + (int64_t)row * p.ld_rt + n]), x));
-            acc[32 * jc + t] = x;
-            continue;
-          }
-          if (p.bias && n < p.N) x = __fadd_rn(x, p.bias[n]);
-          if (EPI == EPI_RESID && live && n < p.N) {
-            const int64_t o = coff + (int64_t)row * p.ld_rt + n;
-            if (p.resid) x = __fadd_rn(x, __bfloat162float(p.resid[o]));
-            x = __fsub_rn(x, __bfloat162float(p.target[o]));
-            if (p.row_period > 0 && (row % p.row_period) == 0) x = 0.f;
-            sq += (double)x * (double)x;
-            x = __fmul_rn(p.out_scale, x);
-          }
-          acc[32 * jc + t] = x;
-        }
-        if (live && p.C) {
-          float* crow = p.C + coff + (int64_t)row * p.ldc + n0;
-          if (p.c_vec && n0 + 32 <= p.N) {
-#pragma unroll
-            for (int t = 0; t < 32; t += 4) {
-              float4 x = make_float4(acc[32 * jc + t], acc[32 * jc + t + 1], acc[32 * jc + t + 2],
-                                     acc[32 * jc + t + 3]);
-              if (EPI == EPI_PLAIN && p.beta != 0.f) {
-                const float4 o = *reinterpret_cast<const float4*>(crow + t);
-                x.x = __fadd_rn(x.x, __fmul_rn(p.beta, o.x));
-                x.y = __fadd_rn(x.y, __fmul_rn(p.beta, o.y));
-                x.z = __fadd_rn(x.z, __fmul_rn(p.beta, o.z));
-                x.w = __fadd_rn(x.w, __fmul_rn(p.beta, o.w));
-                acc[32 * jc + t] = x.x; acc[32 * jc + t + 1] = x.y;
-                acc[32 * jc + t + 2] = x.z; acc[32 * jc + t + 3] = x.w;
-              }
-              *reinterpret_cast<float4*>(crow + t) = x;
-            }
-          } else {
-#pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              if (n0 + t < p.N) {
-                float x = acc[32 * jc + t];
-                if (EPI == EPI_PLAIN && p.beta != 0.f) {
-                  x = __fadd_rn(x, __fmul_rn(p.beta, crow[t]));
-                  acc[32 * jc + t] = x;
-                }
-                crow[t] = x;
-              }
-            }
-          }
-        }
-        if (EPI == EPI_PLAIN && live && p.sq_partial) {
-#pragma unroll
-          for (int t = 0; t < 32; ++t)
-            if (n0 + t < p.N) sq += (double)acc[32 * jc + t] * (double)acc[32 * jc + t];
+            for (int u = 0; u < 32; ++u)
+              acc[32 * jc + u] = __fadd_rn(acc[32 * jc + u], __uint_as_float(v[jc][u]));
+          fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sme_bar[tb]);
         }
       }
-    } else if (EPI == EPI_SWIGLU_BF16) {
-#pragma unroll
-      for (int t = 0; t < 32; ++t) {
-        const float g = bf16r(acc[t]), u = bf16r(acc[32 + t]);
-        acc[t] = bf16r(__fmul_rn(bf16r(__fmul_rn(g, bf16r(sigmoid_f(g)))), u));
-      }
-    } else if (EPI == EPI_SWIGLU_FWD) {
-      // slots [0, 32): gate of column j = tile_n / 2 + 32 h + t; slots [32, 64): up of the same j
-#pragma unroll
-      for (int t = 0; t < 32; ++t) {
-        const int j = tile_n / 2 + 32 * h + t;
-        const float g = acc[t], u = acc[32 + t];
-        if (live && j < p.N / 2) {
-          const int64_t o = coff + (int64_t)row * p.ld_aux + j;
-          p.aux0[o] = g;
-          p.aux1[o] = u;
+      double sq = 0.0;
+      if (ok) sq = epilogue_out<BN, EPI>(p, t, acc, stg, lane, q, h);
+      if (p.sq_partial) {
+        sq = warp_sum_d(sq);
+        if (lane == 0) red[ew] = sq;
+        epi_sync();
+        if (ew == 0 && lane == 0 && ok) {
+          double tot = 0.0;
+          for (int i = 0; i < kEpiWarps; ++i) tot += red[i];
+          p.sq_partial[t.part] = tot;
         }
-        acc[t] = __fmul_rn(__fmul_rn(g, sigmoid_f(g)), u);  // silu(g) * u
+        epi_sync();
       }
-    } else {  // EPI_SWIGLU_BWD: slots hold dd = dL/d(silu(g) u) of column n
-#pragma unroll
-      for (int jc = 0; jc < kNC; ++jc) {
-#pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int n = tile_n + 64 * jc + 32 * h + t;
-          float dg = 0.f, du = 0.f;
-          if (live && n < p.N) {
-            const int64_t o = coff + (int64_t)row * p.ld_aux + n;
-            const float g = p.aux0[o], u = p.aux1[o];
-            const float sg = sigmoid_f(g);
-            const float dd = acc[32 * jc + t];
-            du = __fmul_rn(dd, __fmul_rn(g, sg));
-            // d(g sigmoid(g))/dg = sigmoid(g) + g sigmoid(g) (1 - sigmoid(g))
-            const float dsil = __fadd_rn(sg, __fmul_rn(g, __fmul_rn(sg, __fsub_rn(1.0f, sg))));
-            dg = __fmul_rn(__fmul_rn(dd, u), dsil);
-          }
-          acc[32 * jc + t] = dg;
-          // du is staged right away below (transposed); keep dg in acc
-          if (p.nct > 0) {
-            __nv_bfloat16 hv[3];
-            split3_bf16(du, hv[0], hv[1], hv[2]);
-            __nv_bfloat16* T = reinterpret_cast<__nv_bfloat16*>(smem);
-            const int n_loc = 64 * jc + 32 * h + t;
-            for (int i = 0; i < p.nct; ++i)
-              T[((p.nct + i) * BN + n_loc) * BM + r_loc] = live ? hv[i] : __float2bfloat16_rn(0.f);
-          }
-        }
-      }
-    }
-    // ---- bf16 term outputs
-    const int n_out_cols = EPI == EPI_SWIGLU_FWD ? 32 * kNC / 2 : 0;  // (unused marker)
-    (void)n_out_cols;
-    constexpr bool kHalfOut = (EPI == EPI_SWIGLU_FWD || EPI == EPI_SWIGLU_BF16);
-    if (EPI != EPI_SWIGLU_BWD) {
-      if (live && p.ncs > 0) {
-        const int nch = kHalfOut ? 1 : kNC;
-        for (int jc = 0; jc < nch; ++jc) {
-          const int n0 = kHalfOut ? tile_n / 2 + 32 * h : tile_n + 64 * jc + 32 * h;
-          const int n_lim = kHalfOut ? p.N / 2 : p.N;
-#pragma unroll
-          for (int t = 0; t < 32; t += 8) {
-            if (n0 + t >= n_lim) break;
-            __align__(16) __nv_bfloat16 hv[3][8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              split3_bf16(acc[32 * jc + t + u], hv[0][u], hv[1][u], hv[2][u]);
-            for (int i = 0; i < p.ncs; ++i)
-              *reinterpret_cast<uint4*>(p.cs[i] + coff + (int64_t)row * p.ldcs + n0 + t) =
-                  *reinterpret_cast<const uint4*>(hv[i]);
-          }
-        }
-      }
-    }
-    if (p.nct > 0) {
-      // transposed terms: stage [plane][term][n_loc][m_loc] bf16 in shared memory, then 16-byte
-      // coalesced row stores of C^T (plane 1: the up-gradient rows of the SwiGLU backward)
-      __nv_bfloat16* T = reinterpret_cast<__nv_bfloat16*>(smem);
-      const int rows_t = kHalfOut ? BN / 2 : BN;
-      const int planes = EPI == EPI_SWIGLU_BWD ? 2 : 1;
-      if (kHalfOut) {
-#pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          __nv_bfloat16 hv[3];
-          split3_bf16(live ? acc[t] : 0.f, hv[0], hv[1], hv[2]);
-          const int n_loc = 32 * h + t;
-          for (int i = 0; i < p.nct; ++i) T[(i * rows_t + n_loc) * BM + r_loc] = hv[i];
-        }
-      } else {
-#pragma unroll
-        for (int jc = 0; jc < kNC; ++jc) {
-#pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            __nv_bfloat16 hv[3];
-            split3_bf16(live ? acc[32 * jc + t] : 0.f, hv[0], hv[1], hv[2]);
-            const int n_loc = 64 * jc + 32 * h + t;
-            for (int i = 0; i < p.nct; ++i) T[(i * rows_t + n_loc) * BM + r_loc] = hv[i];
-          }
-        }
-      }
-      epi_sync();
-      const int tid = threadIdx.x - 64;
-      const int n_first = kHalfOut ? tile_n / 2 : tile_n;
-      const int n_lim = kHalfOut ? p.N / 2 : p.N;
-      const int64_t r_base = p.t_row.at(z), c_base = p.t_col.at(z);
-      const int per_plane = p.nct * rows_t * (BM / 8);
-      for (int e = tid; e < planes * per_plane; e += 32 * kEpiWarps) {
-        const int pl = e / per_plane;
-        const int rem0 = e - pl * per_plane;
-        const int i = rem0 / (rows_t * (BM / 8));
-        const int rem = rem0 - i * (rows_t * (BM / 8));
-        const int n_loc = rem / (BM / 8), m8 = (rem % (BM / 8)) * 8;
-        const int n = n_first + n_loc, m = tile_m + m8;
-        if (n < n_lim && m < p.M && ok)
-          *reinterpret_cast<uint4*>(p.ct[i] + (r_base + n + (pl ? p.ct_up_rows : 0)) * p.ldct +
-                                    c_base + m) =
-              *reinterpret_cast<const uint4*>(T + ((pl * p.nct + i) * rows_t + n_loc) * BM + m8);
-      }
-    }
-    if (p.sq_partial) {
-      sq = warp_sum_d(sq);
-      if (lane == 0) red[ew] = sq;
     }
   }
   fence_before_sync();
   __syncthreads();
-  if (p.sq_partial && threadIdx.x == 0) {
-    double t = 0.0;
-    for (int i = 0; i < kEpiWarps; ++i) t += red[i];
-    p.sq_partial[((int64_t)z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x] = t;
-  }
   if (warp == 1) {
+    __syncwarp();
     fence_after_sync();
-    tmem_dealloc(tmem, kCols);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -499,30 +698,32 @@ static bool make_map(CUtensorMap* m, const void* base, int64_t rows, int cols, i
 template <int BN, int EPI>
 static int launch(GemmParams& p, int batch, cudaStream_t st) {
   const uint32_t stage_bytes = p.na * BM * BK * 2 + p.nb * BN * BK * 2;
-  int S = (int)(kSmemBudget / stage_bytes);
-  if (S > 8) S = 8;
+  int S = (int)(kPipeBudget / stage_bytes);
+  if (S > kMaxStages) S = kMaxStages;
   if (S < 2) return GSQ_ENOTSUP;
   p.stages = S;
-  // the transposed-term staging reuses the pipeline stages
-  const int rows_t = (EPI == EPI_SWIGLU_FWD || EPI == EPI_SWIGLU_BF16) ? BN / 2 : BN;
-  const size_t stage_need = (size_t)(EPI == EPI_SWIGLU_BWD ? 2 : 1) * p.nct * rows_t * BM * 2;
-  if (stage_need > (size_t)S * stage_bytes) return GSQ_ENOTSUP;
   int products = 0;
   for (int i = 0; i < p.na; ++i)
     for (int j = 0; j < p.nb; ++j) products += (i + j <= p.order);
   p.kb_per_chunk = products >= 3 ? 1 : (products == 2 ? 2 : 4);
-  const size_t smem = (size_t)S * stage_bytes + 1024;
+  const bool has_small = (p.na > 1 || p.nb > 1) && p.order > 0;
+  int nbig = (int)((kTmemCols - (has_small ? 2u * BN : 0u)) / BN);
+  p.n_big = nbig > kMaxBig ? kMaxBig : nbig;
+  p.tiles_m = (p.M + BM - 1) / BM;
+  p.tiles_n = (p.N + BN - 1) / BN;
+  p.total_tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
+  const size_t smem = 1024 + (size_t)S * stage_bytes + kStgBytes;
   static bool attr_set[2][6] = {{false}};
   bool& done = attr_set[BN == 128][EPI];
   if (!done) {
     if (cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBudget + 1024) != cudaSuccess)
+                             (int)(1024 + kPipeBudget + kStgBytes)) != cudaSuccess)
       return GSQ_ECUDA;
     done = true;
   }
-  dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, batch);
-  gemm_tc_kernel<BN, EPI><<<grid, kThreads, smem, st>>>(p);
+  const int64_t g = p.total_tiles < num_sms() ? p.total_tiles : num_sms();
+  gemm_tc_kernel<BN, EPI><<<(unsigned)g, kThreads, smem, st>>>(p);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }
@@ -581,8 +782,6 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   p.row_period = d->row_period;
   p.alpha = d->alpha; p.beta = d->beta;
   p.C = d->C; p.ldc = d->ldc;
-  p.c_vec = (d->C && ((uintptr_t)d->C & 15) == 0 && (d->ldc & 3) == 0 &&
-             ((d->c_s1 | d->c_s2) & 3) == 0) ? 1 : 0;
   for (int i = 0; i < d->ncs; ++i) p.cs[i] = (__nv_bfloat16*)d->cs[i];
   p.ncs = d->ncs; p.ldcs = d->ldcs;
   for (int i = 0; i < d->nct; ++i) p.ct[i] = (__nv_bfloat16*)d->ct[i];
@@ -600,6 +799,14 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   p.t_row = to_aff(d->t_div, d->t_r1, d->t_r2);
   p.t_col = to_aff(d->t_div, d->t_c1, d->t_c2);
   p.err = d->err;
+  const bool c_even = ((d->c_s1 | d->c_s2) & 1) == 0;
+  p.pair_c = (d->C && ((uintptr_t)d->C & 7) == 0 && (d->ldc & 1) == 0 && c_even) ? 1 : 0;
+  p.pair_cs = ((d->ldcs & 1) == 0 && c_even) ? 1 : 0;
+  p.pair_ct = ((d->ldct & 1) == 0 && ((d->t_c1 | d->t_c2) & 1) == 0) ? 1 : 0;
+  p.pair_aux = (((uintptr_t)d->aux0 & 7) == 0 && ((uintptr_t)d->aux1 & 7) == 0 &&
+                (d->ld_aux & 1) == 0 && c_even) ? 1 : 0;
+  p.pair_rt = (((uintptr_t)d->resid & 3) == 0 && ((uintptr_t)d->target & 3) == 0 &&
+               (d->ld_rt & 1) == 0 && c_even) ? 1 : 0;
   cudaStream_t st = (cudaStream_t)stream;
   if (BN == 64) {
     if (epi == 0) return tc::launch<64, 0>(p, d->batch, st);
