@@ -122,3 +122,16 @@ def call(name: str, *args):
 
 def device():
     return torch.device("cuda", torch.cuda.current_device())
+
+
+_SMS = {}
+
+
+def num_sms(dev=None):
+    """Streaming multiprocessors of the device (148 on B200)."""
+    import torch
+    d = torch.device(dev) if dev is not None else device()
+    key = str(d)
+    if key not in _SMS:
+        _SMS[key] = torch.cuda.get_device_properties(d).multi_processor_count
+    return _SMS[key]

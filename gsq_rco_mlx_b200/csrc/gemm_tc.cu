@@ -90,6 +90,8 @@ struct GemmParams {
   int row_period;  // epi 1: rows with (row % row_period) == 0 have a zero residual
   // two-element (8-byte float / 4-byte bf16) accesses are aligned for these outputs
   int pair_c, pair_cs, pair_ct, pair_aux, pair_rt;
+  int splits, kb_split;  // split-K: parts of kb_split k-blocks, partials into ws [part][M][N]
+  float* ws;
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -107,7 +109,7 @@ __device__ __forceinline__ float sigmoid_f(float x) {
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 struct TileInfo {
-  int z, tile_m, tile_n, kb0, nkb;
+  int z, ks, tile_m, tile_n, kb0, nkb;
   int64_t part;  // index of the tile's sum-of-squares partial
 };
 
@@ -117,8 +119,10 @@ struct TileInfo {
 template <int BN>
 __device__ __forceinline__ bool tile_at(const GemmParams& p, int64_t L, TileInfo& t) {
   const int64_t per = (int64_t)p.tiles_m * p.tiles_n;
-  t.z = (int)(L / per);
-  const int rem = (int)(L - (int64_t)t.z * per);
+  const int64_t zk = L / per;
+  t.z = (int)(zk / p.splits);
+  t.ks = (int)(zk - (int64_t)t.z * p.splits);
+  const int rem = (int)(L - zk * per);
   const int my = rem % p.tiles_m, nx = rem / p.tiles_m;
   t.tile_m = my * BM;
   t.tile_n = nx * BN;
@@ -127,6 +131,10 @@ __device__ __forceinline__ bool tile_at(const GemmParams& p, int64_t L, TileInfo
   t.kb0 = p.causal == 2 ? min(t.tile_m / BK, kb_total - 1) : 0;
   const int kb1 = p.causal == 1 ? min(kb_total, (t.tile_m + BM + BK - 1) / BK) : kb_total;
   t.nkb = kb1 - t.kb0;
+  if (p.splits > 1) {
+    t.kb0 += t.ks * p.kb_split;
+    t.nkb = min(p.kb_split, t.nkb - t.ks * p.kb_split);
+  }
   t.part = ((int64_t)t.z * p.tiles_m + my) * p.tiles_n + nx;
   return true;
 }
@@ -222,6 +230,24 @@ __device__ __forceinline__ double epilogue_out(const GemmParams& p, const TileIn
   const int64_t coff = p.c_off.at(t.z);
   const int row0 = t.tile_m + 32 * q;
   double sq = 0.0;
+  if (EPI == EPI_PLAIN && p.splits > 1) {  // split-K partial: raw sums into the workspace
+    float* W = p.ws + (int64_t)t.ks * p.M * p.N;
+#pragma unroll
+    for (int jc = 0; jc < kNC; ++jc) {
+      const int n0 = t.tile_n + 64 * jc + 32 * h;
+      stage_put(stg, lane, acc + 32 * jc);
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const int r = 2 * i + (lane >> 4), c = 2 * (lane & 15);
+        const int row = row0 + r, n = n0 + c;
+        if (row < p.M && n < p.N)
+          store_f2(W + (int64_t)row * p.N + n, stg[r * kStgLd + c], stg[r * kStgLd + c + 1],
+                   n + 1 < p.N, (p.N & 1) == 0);
+      }
+      __syncwarp();
+    }
+    return 0.0;
+  }
 #pragma unroll
   for (int i = 0; i < BN / 2; ++i) acc[i] = __fmul_rn(p.alpha, acc[i]);
 
@@ -711,7 +737,7 @@ static int launch(GemmParams& p, int batch, cudaStream_t st) {
   p.n_big = nbig > kMaxBig ? kMaxBig : nbig;
   p.tiles_m = (p.M + BM - 1) / BM;
   p.tiles_n = (p.N + BN - 1) / BN;
-  p.total_tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
+  p.total_tiles = (int64_t)p.tiles_m * p.tiles_n * batch * p.splits;
   const size_t smem = 1024 + (size_t)S * stage_bytes + kStgBytes;
   static bool attr_set[2][6] = {{false}};
   bool& done = attr_set[BN == 128][EPI];
@@ -726,6 +752,22 @@ static int launch(GemmParams& p, int batch, cudaStream_t st) {
   gemm_tc_kernel<BN, EPI><<<(unsigned)g, kThreads, smem, st>>>(p);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
+}
+
+// C = alpha sum_s ws[s] + beta C (sum in part order), float32 [M][ldc]
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N,
+                                     float alpha, float beta, float* __restrict__ C, int64_t ldc) {
+  const int64_t n_el = (int64_t)M * N;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n_el;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    float v = ws[e];
+    for (int s = 1; s < splits; ++s) v = __fadd_rn(v, ws[(int64_t)s * n_el + e]);
+    const int r = (int)(e / N), c = (int)(e - (int64_t)r * N);
+    float* cp = C + (int64_t)r * ldc + c;
+    float x = __fmul_rn(alpha, v);
+    if (beta != 0.f) x = __fadd_rn(x, __fmul_rn(beta, *cp));
+    *cp = x;
+  }
 }
 
 }  // namespace tc
@@ -763,6 +805,10 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   if ((epi == 2 || epi == 3) && (!d->aux0 || !d->aux1 || d->bn != 128)) return GSQ_EINVAL;
   if ((epi == 2 || epi == 5) && (!d->b2[0] || (N % 128) != 0 || d->bn != 128)) return GSQ_EINVAL;
   if (d->causal < 0 || d->causal > 2 || (d->causal && d->K < M)) return GSQ_EINVAL;
+  const int splits = d->split_k > 1 ? d->split_k : 1;
+  if (splits > 1 && (epi != 0 || d->batch != 1 || d->causal || !d->C || d->bias || d->ncs ||
+                     d->nct || d->sq_partial || !d->workspace || ((uintptr_t)d->workspace & 7)))
+    return GSQ_EINVAL;
   tc::GemmParams p;
   memset(&p, 0, sizeof(p));
   const int BN = d->bn;
@@ -799,6 +845,13 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   p.t_row = to_aff(d->t_div, d->t_r1, d->t_r2);
   p.t_col = to_aff(d->t_div, d->t_c1, d->t_c2);
   p.err = d->err;
+  {
+    const int kb_total = (K + tc::BK - 1) / tc::BK;
+    const int per = (kb_total + splits - 1) / splits;
+    p.kb_split = per;
+    p.splits = (kb_total + per - 1) / per;  // every part non-empty
+    p.ws = d->workspace;
+  }
   const bool c_even = ((d->c_s1 | d->c_s2) & 1) == 0;
   p.pair_c = (d->C && ((uintptr_t)d->C & 7) == 0 && (d->ldc & 1) == 0 && c_even) ? 1 : 0;
   p.pair_cs = ((d->ldcs & 1) == 0 && c_even) ? 1 : 0;
@@ -808,6 +861,17 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   p.pair_rt = (((uintptr_t)d->resid & 3) == 0 && ((uintptr_t)d->target & 3) == 0 &&
                (d->ld_rt & 1) == 0 && c_even) ? 1 : 0;
   cudaStream_t st = (cudaStream_t)stream;
+  if (p.splits > 1) {
+    const int rc = BN == 64 ? tc::launch<64, 0>(p, 1, st) : tc::launch<128, 0>(p, 1, st);
+    if (rc != GSQ_OK) return rc;
+    const int64_t n_el = (int64_t)M * N;
+    int64_t blocks = (n_el + 255) / 256;
+    if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
+    tc::splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(p.ws, p.splits, M, N, d->alpha,
+                                                               d->beta, d->C, d->ldc);
+    GSQ_CHECK_LAUNCH();
+    return GSQ_OK;
+  }
   if (BN == 64) {
     if (epi == 0) return tc::launch<64, 0>(p, d->batch, st);
     if (epi == 1) return tc::launch<64, 1>(p, d->batch, st);

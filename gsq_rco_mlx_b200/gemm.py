@@ -147,7 +147,38 @@ class GemmDesc(_C.Structure):
         ("err", _C.c_void_p),
         ("skip_upper", _C.c_int),
         ("row_period", _C.c_int),
+        ("split_k", _C.c_int),
+        ("workspace", _C.c_void_p),
     ]
+
+
+_WS = {}
+
+
+def _workspace(dev, n_floats):
+    """A per-device float32 split-K workspace of at least n_floats (grown on demand)."""
+    key = str(dev)
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < n_floats:
+        ws = torch.empty(int(n_floats), device=dev, dtype=torch.float32)
+        _WS[key] = ws
+    return ws
+
+
+def auto_split(M, N, K, bn=128):
+    """Number of k-parts for an output of fewer tiles than SMs: the split s <= k-blocks / 3
+    that minimises ceil(tiles * s / SMs) / s (waves times the per-part k-length)."""
+    tiles = -(-M // 128) * -(-N // bn)
+    kb = -(-K // 64)
+    sms = _lib.num_sms()
+    if tiles >= sms:
+        return 1
+    best, best_cost = 1, None
+    for s in range(1, max(1, kb // 3) + 1):
+        cost = -(-tiles * s // sms) / s
+        if best_cost is None or cost < best_cost - 1e-9:
+            best, best_cost = s, cost
+    return best
 
 
 def _tp(t):
@@ -182,7 +213,7 @@ def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, 
          sq_partial=None, bias=None, resid=None, target=None, ld_rt=None, out_scale=1.0,
          aux0=None, aux1=None, ld_aux=None, B2: Terms = None, epi=0, bn=128, causal=False,
          batch=1, a_off=(1, 0, 0), b_off=(1, 0, 0), c_off=(1, 0, 0), t_off=(1, 0, 0, 0, 0),
-         ct_up_rows=0, skip_upper=False, row_period=0):
+         ct_up_rows=0, skip_upper=False, row_period=0, split_k="auto"):
     """One (batched) tensor-core GEMM with a fused epilogue; see gsq_gemm in the C header.
     M, N, K default to the operand shapes; a_off/b_off/c_off = (div, s1, s2),
     t_off = (div, row_s1, row_s2, col_s1, col_s2)."""
@@ -222,6 +253,13 @@ def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, 
     d.ld_aux = (d.N // 2 if epi == 2 else d.N) if ld_aux is None else ld_aux
     d.skip_upper = int(skip_upper)
     d.row_period = int(row_period)
+    splittable = (epi == 0 and batch == 1 and not causal and C is not None and bias is None
+                  and c_terms is None and ct_terms is None and sq_partial is None)
+    if split_k == "auto":
+        split_k = auto_split(d.M, d.N, d.K, bn) if splittable else 1
+    if split_k > 1:
+        d.split_k = int(split_k)
+        d.workspace = _workspace(A.t[0].device, split_k * d.M * d.N).data_ptr()
     d.a_div, d.a_s1, d.a_s2 = a_off
     d.b_div, d.b_s1, d.b_s2 = b_off
     d.c_div, d.c_s1, d.c_s2 = c_off

@@ -149,42 +149,63 @@ class Qwen2Block:
              c_off=(c.n_heads, T * c.hidden, c.head_dim), c_terms=Ot,
              ct_terms=o_tap, t_off=(c.n_heads, 0, c.head_dim, T, 0))
 
-    def forward(self, h, W: BlockWeights, S=None, out=None, taps=(), attn_out=None):
-        """Block forward of S sequences h bf16 [S*T, H] -> out bf16 [S*T, H] (or only the
-        attention output after o_proj into attn_out, the vo-stage target). taps: names of
-        TAPS to write transposed (self.tap(name)), position-0 columns zeroed."""
+    def forward(self, h, W: BlockWeights, S=None, out=None, taps=(), attn_out=None, upto=None,
+                mn=None):
+        """Block forward of S sequences h bf16 [S*T, H] -> out bf16 [S*T, H]. taps: names of
+        TAPS to write transposed (self.tap(name)), position-0 columns zeroed.
+        attn_out: also the attention output after o_proj (no residual; the vo-stage target);
+        without `out` the forward ends there. upto: end after the named site ("hn", "o", "mn",
+        "d_in") when only its tap is wanted. mn: bf16 [S*T, H] post-attention-norm rows of an
+        earlier pass; the forward then starts at the MLP, with h the attention block output h1
+        (unused for upto="d_in")."""
         c, T = self.cfg, self.T
         S = self.S if S is None else S
         R = S * T
         st = _lib.stream_ptr()
+        if mn is not None:
+            return self._mlp(h, mn, W, R, T, st, out, taps, upto)
         hn_tap = self.tap("hn") if "hn" in taps else None
         _lib.call("gsq_rmsnorm", _lib.ptr(h), c.hidden, _lib.ptr(W.W["in_norm"]), R, c.hidden,
                   float(c.eps), _lib.ptr(self.hn), c.hidden,
                   _lib.ptr(hn_tap.t[0] if hn_tap else None), hn_tap.ld if hn_tap else 0, T, 1, st)
+        if upto == "hn":
+            return None
         o_tap = self.tap("o") if "o" in taps else None
         self.attention(self.hn, W, S, self.o, o_tap=o_tap)
         if o_tap is not None:
             _lib.call("gsq_zero_cols", _lib.ptr(o_tap.t[0]), c.hidden, o_tap.ld, R, T, st)
+        if upto == "o":
+            return None
         Ot = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[self.o])
         if attn_out is not None:
             gemm(Ot, wterms(W.W["o_proj"]), epi=4,
                  c_terms=Terms(R, c.hidden, 1, ld=c.hidden, tensors=[attn_out]))
-            return attn_out
+            if out is None:
+                return attn_out
         gemm(Ot, wterms(W.W["o_proj"]), epi=4, resid=h, ld_rt=c.hidden,
              c_terms=Terms(R, c.hidden, 1, ld=c.hidden, tensors=[self.h1]))
         mn_tap = self.tap("mn") if "mn" in taps else None
         _lib.call("gsq_rmsnorm", _lib.ptr(self.h1), c.hidden, _lib.ptr(W.W["post_norm"]), R,
                   c.hidden, float(c.eps), _lib.ptr(self.mn), c.hidden,
                   _lib.ptr(mn_tap.t[0] if mn_tap else None), mn_tap.ld if mn_tap else 0, T, 1, st)
+        if upto == "mn":
+            return None
+        return self._mlp(self.h1, self.mn, W, R, T, st, out, taps, upto)
+
+    def _mlp(self, h1, mn, W: BlockWeights, R, T, st, out, taps, upto):
+        """out = h1 + down(SwiGLU(mn)) (bf16 chain); the d_in tap if asked."""
+        c = self.cfg
         d_tap = self.tap("d_in") if "d_in" in taps else None
-        MNt = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[self.mn])
+        MNt = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[mn])
         gemm(MNt, wterms(W.W["gate_proj"]), B2=wterms(W.W["up_proj"]), epi=5,
              c_terms=Terms(R, c.inter, 1, ld=c.inter, tensors=[self.d_in]), ct_terms=d_tap)
         if d_tap is not None:
             _lib.call("gsq_zero_cols", _lib.ptr(d_tap.t[0]), c.inter, d_tap.ld, R, T, st)
+        if upto == "d_in":
+            return None
         out = torch.empty(R, c.hidden, device=self.dev, dtype=torch.bfloat16) if out is None else out
         Dt = Terms(R, c.inter, 1, ld=c.inter, tensors=[self.d_in])
-        gemm(Dt, wterms(W.W["down_proj"]), epi=4, resid=self.h1, ld_rt=c.hidden,
+        gemm(Dt, wterms(W.W["down_proj"]), epi=4, resid=h1, ld_rt=c.hidden,
              c_terms=Terms(R, c.hidden, 1, ld=c.hidden, tensors=[out]))
         return out
 

@@ -50,10 +50,38 @@ class BlockOpts:
     seed: int = 0
 
 
+def _shift_init_t(d, seed):
+    """init_shift_logits(d, seed) transposed to the plane-major [K, d] layout."""
+    return np.ascontiguousarray(
+        init_shift_logits(d, alpha=ALPHA_SCALAR, std=INIT_STD, seed=seed).T)
+
+
+class ShiftInitPool:
+    """The initial local-shift logits of a block's soft linears, drawn on host threads while
+    the GPU runs the Hessian passes and the earlier stages. The draws are the reference's
+    (numpy default_rng(seed) normals, gptq.py:192-219), which are sequential per linear; the
+    linears run in parallel (numpy releases the GIL in its generators and ufunc loops)."""
+
+    def __init__(self, jobs):
+        from concurrent.futures import ThreadPoolExecutor
+        self._ex = ThreadPoolExecutor(max_workers=max(1, min(8, len(jobs))))
+        self._fut = {name: self._ex.submit(_shift_init_t, d, seed)
+                     for name, (d, seed) in jobs.items()}
+
+    def take(self, name):
+        fut = self._fut.pop(name, None)
+        return None if fut is None else fut.result()
+
+    def close(self):
+        self._ex.shutdown(wait=True, cancel_futures=True)
+
+
 class SoftLinear:
     """One linear under the stage optimiser: GPTQ codes and scales plus trainable logits."""
 
-    def __init__(self, name, bits, codes, scales16, group_size, seed, linear_id=0):
+    def __init__(self, name, bits, codes, scales16, group_size, seed, linear_id=0, logits0=None):
+        """logits0: the initial logits [K, d] float32 (init_shift_logits of (d, seed),
+        transposed) when computed ahead, e.g. by ShiftInitPool."""
         self.name, self.bits = name, int(bits)
         if not 2 <= self.bits <= 7:
             raise NotImplementedError(
@@ -67,12 +95,17 @@ class SoftLinear:
         dev = _lib.device()
         self.j0 = torch.as_tensor(codes.reshape(-1), device=dev)
         d = codes.size
-        if self.bits == 2:
-            l0 = init_logits_2bit_from_codes(codes, 4, alpha=ALPHA_SCALAR, std=INIT_STD, seed=seed)
+        if logits0 is not None:
+            lt = np.asarray(logits0, dtype=np.float32)
+            if self.bits == 2 or lt.shape[1] != d:
+                raise ValueError(f"{name}: precomputed logits {lt.shape} do not fit {d} weights")
+        elif self.bits == 2:
+            lt = init_logits_2bit_from_codes(codes, 4, alpha=ALPHA_SCALAR, std=INIT_STD,
+                                             seed=seed).T
         else:
-            l0 = init_shift_logits(d, alpha=ALPHA_SCALAR, std=INIT_STD, seed=seed)
-        self.K = l0.shape[1]
-        self.logits = torch.as_tensor(np.ascontiguousarray(l0.T), device=dev)
+            lt = _shift_init_t(d, seed)
+        self.K = lt.shape[0]
+        self.logits = torch.as_tensor(np.ascontiguousarray(lt), device=dev)
         self.mom = torch.zeros_like(self.logits)
         self.scales = torch.as_tensor(np.asarray(scales16, dtype=np.float32), device=dev).contiguous()
         self.mom_s = torch.zeros_like(self.scales)
@@ -580,18 +613,26 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
     Wcur = dict(W)
     shard, stats = {}, {"stages": {}, "linears": {}}
     factors = {}
+    pos_of = {name: i for i, name in enumerate(LIN_ORDER)}
+    inits = ShiftInitPool({name: (W[name].numel(), seed + 10 * pos_of[name])
+                           for name in LIN_ORDER if 3 <= bits[name] <= 7})
 
     def chunks():
         for a in range(0, N, cs):
             yield a, min(cs, N - a)
 
-    def hessian(site, Wb, extra=None):
-        """Hessian of the input of `site` over positions 1.., under block weights Wb."""
+    def hessian(site, Wb, extra=None, mn_src=None):
+        """Hessian of the input of `site` over positions 1.., under block weights Wb; the
+        forward ends at the site (and starts at the MLP from cached rows mn_src)."""
         width = cfg.inter if site == "d_in" else H
         Hs = torch.zeros(width, width, device=dev, dtype=torch.float64)
         n = 0
         for a, s in chunks():
-            eng.forward(h[a * T:(a + s) * T], Wb, S=s, taps=(site,))
+            rows = slice(a * T, (a + s) * T)
+            if mn_src is not None:
+                eng.forward(None, Wb, S=s, taps=(site,), upto=site, mn=mn_src[rows])
+            else:
+                eng.forward(h[rows], Wb, S=s, taps=(site,), upto=site)
             n = eng.hessian_add(site, Hs, n, S=s)
             if extra:
                 extra(a, s)
@@ -611,7 +652,7 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
             shard[name] = {"codes": codes, "scales": s16, "bits": 8}
             return None
         return SoftLinear(name, bits[name], codes, s16, gs, seed=seed + 10 * pos,
-                          linear_id=layer * 8 + pos)
+                          linear_id=layer * 8 + pos, logits0=inits.take(name))
 
     def harden(lin):
         codes = lin.hard_codes()
@@ -651,12 +692,16 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
     o_lin = gptq("o_proj", H_o, 3)
     vo_lins = [l for l in (v_lin, o_lin) if l is not None]
     A_all = torch.empty(N * T, H, device=dev, dtype=torch.bfloat16)
+    Y_all = torch.empty(N * T, H, device=dev, dtype=torch.bfloat16)
     qkw = (cfg.n_heads + cfg.n_kv) * cfg.head_dim
     qk_all = torch.empty(N * T, qkw, device=dev, dtype=torch.bfloat16)
     Wc = BlockWeights(Wcur)
     from .e2e import wterms
     for a, s in chunks():
-        eng.forward(h[a * T:(a + s) * T], W_fp, S=s, attn_out=A_all[a * T:(a + s) * T])
+        # full-precision targets: the attention output (vo stage) and the block output (mlp
+        # stage) from one pass
+        eng.forward(h[a * T:(a + s) * T], W_fp, S=s, attn_out=A_all[a * T:(a + s) * T],
+                    out=Y_all[a * T:(a + s) * T])
         # hard q|k rows under the trained q / k (the vo stage's fixed attention pattern)
         gemm(_bf16_rows(hn_all[a * T:(a + s) * T]), wterms(Wc.qk), epi=4, bias=Wc.qk_bias,
              c_terms=_bf16_rows(qk_all[a * T:(a + s) * T]))
@@ -681,12 +726,9 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
         h1_all[a * T:(a + s) * T].copy_(eng.h1[:s * T])
     H_gu = hessian("mn", BlockWeights(Wcur), keep_mn)
     gate, up = gptq("gate_proj", H_gu, 4), gptq("up_proj", H_gu, 5)
-    H_d = hessian("d_in", BlockWeights(Wcur))
+    H_d = hessian("d_in", BlockWeights(Wcur), mn_src=mn_all)
     down = gptq("down_proj", H_d, 6)
     mlp_lins = [l for l in (gate, up, down) if l is not None]
-    Y_all = torch.empty(N * T, H, device=dev, dtype=torch.bfloat16)
-    for a, s in chunks():
-        eng.forward(h[a * T:(a + s) * T], W_fp, S=s, out=Y_all[a * T:(a + s) * T])
     if len(mlp_lins) == 3:
         mstep = MLPStep(mlp_lins, cfg, min(opts.micro_batch, N), T, opts.resamples)
         hist, ms = train_stage(mstep, lambda idx: (mn_all, h1_all, Y_all, idx), N, opts,
@@ -696,4 +738,5 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
     for lin in mlp_lins:
         harden(lin)
     stage_done("mlp", t0, hist, ms)
+    inits.close()
     return shard, stats, Wcur

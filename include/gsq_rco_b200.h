@@ -153,6 +153,11 @@ typedef struct {
   int *err;
   int skip_upper; /* skip output tiles with n >= m (all above the diagonal): causal scores */
   int row_period; /* epi 1: rows m with m % row_period == 0 get a zero residual (position 0) */
+  /* split_k > 1 (epi 0, batch 1, C only: no bias / terms / sq_partial, not causal): the k-range
+   * is cut into split_k contiguous parts whose partial products land in workspace
+   * (float32, >= split_k * M * N) and are summed in part order, then C = alpha sum + beta C. */
+  int split_k;
+  float *workspace;
 } gsq_gemm_desc;
 
 /* Batched float32-faithful tensor-core GEMM with a fused epilogue (see gsq_gemm_tc for the
