@@ -196,7 +196,7 @@ def run_block(args):
     barrier()
     clocks = Clocks(local)
     clocks.start()
-    timer = StageTimer(args.warmup)
+    timer = StageTimer(args.warmup, nvtx=True)
     opts = BlockOpts(steps=args.warmup + args.steps)
     _, stats, _ = quantize_block(h, W, bits, opts, layer=rank, cfg=cfg, T=T_SEQ, log=quiet,
                                  timer=timer)

@@ -216,11 +216,11 @@ class LinearStep:
             RT, G = self.RT[lin.name], self.grads[lin.name]
             tiles = ((self.M + 127) // 128) * ((lin.out_f + 127) // 128)
             for r in range(self.R):
-                gemm_tc(self.X, self.D[lin.name][r], ct_terms=RT, sq_partial=self.sq)
+                gemm(self.X, self.D[lin.name][r], ct_terms=RT, sq_partial=self.sq)
                 slot = self.loss[li * self.R + r:li * self.R + r + 1]
                 _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(slot),
                           _lib.stream_ptr())
-                gemm_tc(RT, self.XT, alpha=2.0 / (self.M * lin.out_f), C=G[r])
+                gemm(RT, self.XT, alpha=2.0 / (self.M * lin.out_f), C=G[r])
 
     def update(self, targets, t, tau, kappa, opts, noise_seed, nxt=None, noise_of=None):
         """Fused backward + Lion of step t; nxt = (t1, tau1, kappa1) also runs step t1's forward."""
@@ -268,7 +268,7 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
     tau, kappa = gs_schedules(0, opts.steps)
     step.first_forward(targets, 0, tau, kappa, noise_seed, noise_of)
     for t in range(opts.steps):
-        timer.mark(name, t, False)
+        timer.begin(name, t)
         tau, kappa = gs_schedules(t, opts.steps)
         idx = np.sort(rng.choice(n_seqs, size=m, replace=False))
         step.stage(flat, idx, T - 1, T, 1)
@@ -276,7 +276,7 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
         nxt = (t + 1, *gs_schedules(t + 1, opts.steps)) if t + 1 < opts.steps else None
         step.update(targets, t, tau, kappa, opts, noise_seed, nxt=nxt, noise_of=noise_of)
         hist[t].copy_(step.loss.view(len(lins), step.R).sum(1))
-        timer.mark(name, t, t == opts.steps - 1)
+        timer.end(name, t, t == opts.steps - 1)
     check_err(step.dev)
     denom = torch.tensor([step.M * lin.out_f for lin in lins], device=step.dev,
                          dtype=torch.float64)
@@ -526,21 +526,32 @@ class VOStep(_StageBase):
 
 
 class StageTimer:
-    """CUDA-event timing of the steps after the first `warmup` of each stage: ms[name]."""
+    """CUDA-event timing of the steps after the first `warmup` of each stage: ms[name]. With
+    nvtx=True the timed steps of every stage also form an NVTX range "gsq_steps" (a profiler
+    filter for the launch list of the steps alone)."""
 
-    def __init__(self, warmup=3):
+    def __init__(self, warmup=3, nvtx=False):
         self.warmup = int(warmup)
+        self.nvtx = bool(nvtx)
         self.ms = {}
         self._ev = {}
 
-    def mark(self, name, t, last):
+    def begin(self, name, t):
+        """At the start of step t."""
         if t == self.warmup:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
             self._ev[name] = e
+            if self.nvtx:
+                torch.cuda.nvtx.range_push("gsq_steps")
+
+    def end(self, name, t, last):
+        """After step t; last closes the timed range: ms[name] = mean over steps warmup..t."""
         if last and name in self._ev:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
+            if self.nvtx:
+                torch.cuda.nvtx.range_pop()
             e.synchronize()
             n = t + 1 - self.warmup
             self.ms[name] = self._ev[name].elapsed_time(e) / max(n, 1)
@@ -563,7 +574,7 @@ def train_stage(step, stage_args_of, n_seqs, opts: BlockOpts, seed, noise_seed=N
     hist = torch.zeros(opts.steps, device=step.dev, dtype=torch.float64)
     timer = timer or StageTimer(min(3, opts.steps - 1))
     for t in range(opts.steps):
-        timer.mark(name, t, False)
+        timer.begin(name, t)
         tau, kappa = gs_schedules(t, opts.steps)
         idx = np.sort(rng.choice(n_seqs, size=m, replace=False))
         step.stage(*stage_args_of(idx))
@@ -571,7 +582,7 @@ def train_stage(step, stage_args_of, n_seqs, opts: BlockOpts, seed, noise_seed=N
         nxt = (t + 1, *gs_schedules(t + 1, opts.steps)) if t + 1 < opts.steps else None
         step.update(t, tau, kappa, opts, noise_seed, nxt=nxt, noise_of=noise_of)
         hist[t:t + 1].copy_(step.loss.sum(0, keepdim=True))
-        timer.mark(name, t, t == opts.steps - 1)
+        timer.end(name, t, t == opts.steps - 1)
     check_err(step.dev)
     history = (hist / (step.R * step.count)).cpu().tolist()
     return history, (round(timer.ms[name], 4) if name in timer.ms else None)

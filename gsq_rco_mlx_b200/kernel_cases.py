@@ -1,0 +1,145 @@
+"""Representative launches of the hot kernels at Qwen2.5-0.5B block shapes, for profilers and
+micro-timing (one process, one GPU, a few GB of device memory).
+
+  python -m gsq_rco_mlx_b200.kernel_cases [mlp_gemms|attn|soft_step|cublas] [--once]
+
+--once runs every case a single time (an ncu capture: `-k regex:<kernel> -c <n>`); otherwise
+each case is timed with CUDA events over 10 launches after 3 warm-up launches and printed with
+its executed bf16 TFLOP/s (GEMMs) or algorithmic GB/s (streams).
+
+mlp_gemms: the five GEMMs of one mlp-stage resample (micro-batch 2 x 2047 rows) and the hard
+  SwiGLU GEMM of the block forward (8 x 2048 rows):
+    F1 gate|up = mn [Wg|Wu]^T (1 x 3 terms, SwiGLU epilogue)   F3 residual loss (3 x 3)
+    B1 dL/dWd (3 x 3)   B2 SwiGLU backward (3 x 3)   B3 dL/dWg|Wu (3 x 1, batch 2)
+attn: the causal scores GEMM and softmax of 8 sequences x 14 heads x 2048 positions.
+soft_step: the fused backward + Lion + next forward of one up_proj-shaped soft linear (R = 2).
+cublas: library bf16 GEMMs of the mlp shapes, for context only (not on any product path).
+"""
+from __future__ import annotations
+
+import sys
+
+import torch
+
+from . import _lib
+from .gemm import Terms, check_err, gemm
+
+H, I, HEADS, KV, HD, T = 896, 4864, 14, 2, 64, 2048
+
+
+def _terms(rows, cols, n, dev, g):
+    t = Terms(rows, cols, n, dev)
+    for i, x in enumerate(t.t):
+        x.copy_((torch.randn(x.shape, device=dev, generator=g) * (0.05 * 2.0 ** (-8 * i)))
+                .bfloat16())
+    return t
+
+
+def mlp_gemms(dev, g):
+    M = 2 * (T - 1)
+    MN, MNT, H1, Y = (_terms(M, H, 1, dev, g), _terms(H, M, 1, dev, g), _terms(M, H, 1, dev, g),
+                      _terms(M, H, 1, dev, g))
+    Dg, Du, Dd, DdT = (_terms(I, H, 3, dev, g), _terms(I, H, 3, dev, g), _terms(H, I, 3, dev, g),
+                       _terms(I, H, 3, dev, g))
+    gg, uu = torch.empty(M, I, device=dev), torch.empty(M, I, device=dev)
+    DIN, DINT = Terms(M, I, 3, dev), Terms(I, M, 3, dev)
+    DR, DRT = Terms(M, H, 3, dev), Terms(H, M, 3, dev)
+    GUT = Terms(2 * I, M, 3, dev)
+    grad_gu, grad_d = torch.empty(2, I, H, device=dev), torch.empty(H, I, device=dev)
+    sq = torch.zeros(((M + 127) // 128) * 7, device=dev, dtype=torch.float64)
+    R = 8 * T
+    MNt = _terms(R, H, 1, dev, g)
+    Wg1, Wu1 = _terms(I, H, 1, dev, g), _terms(I, H, 1, dev, g)
+    d_in = torch.empty(R, I, device=dev, dtype=torch.bfloat16)
+    return {
+        "F1 swiglu fwd (1x3)": (3 * 2 * M * 2 * I * H, lambda: gemm(
+            MN, Dg, B2=Du, epi=2, aux0=gg, aux1=uu, c_terms=DIN, ct_terms=DINT)),
+        "F3 resid (3x3)": (6 * 2 * M * H * I, lambda: gemm(
+            DIN, Dd, epi=1, resid=H1.t[0], target=Y.t[0], ld_rt=H1.ld, out_scale=1e-3,
+            sq_partial=sq, c_terms=DR, ct_terms=DRT)),
+        "B1 gradWd (3x3)": (6 * 2 * H * I * M, lambda: gemm(DRT, DINT, C=grad_d)),
+        "B2 swiglu bwd (3x3)": (6 * 2 * M * I * H, lambda: gemm(
+            DR, DdT, epi=3, aux0=gg, aux1=uu, ct_terms=GUT, ct_up_rows=I)),
+        "B3 gradWgu (3x1)": (3 * 2 * 2 * I * H * M, lambda: gemm(
+            GUT, MNT, M=I, batch=2, C=grad_gu, ldc=H, a_off=(1, I, 0), c_off=(1, I * H, 0))),
+        "hard swiglu bf16 (1x1)": (2 * R * 2 * I * H, lambda: gemm(
+            MNt, Wg1, B2=Wu1, epi=5, c_terms=Terms(R, I, 1, ld=I, tensors=[d_in]))),
+    }
+
+
+def attn(dev, g):
+    B = 8 * HEADS
+    q, k = _terms(B * T, HD, 3, dev, g), _terms(8 * KV * T, HD, 3, dev, g)  # float32 after RoPE
+    scores = torch.empty(B, T, T, device=dev)
+    P = torch.empty(B * T, T, device=dev, dtype=torch.bfloat16)
+    st = _lib.stream_ptr()
+    return {
+        "scores (3x3) causal": (6 * 2 * B * T * T * HD // 2, lambda: gemm(
+            q, k, M=T, N=T, K=HD, batch=B, alpha=0.125, C=scores, ldc=T, a_off=(1, T, 0),
+            b_off=(HEADS // KV, T, 0), c_off=(1, T * T, 0), skip_upper=True)),
+        "softmax causal": (None, lambda: _lib.call(
+            "gsq_softmax_causal", _lib.ptr(scores), B, T, _lib.ptr(P), None, st)),
+    }
+
+
+def soft_step(dev, g):
+    from .gsq.staged import SoftLinear
+    import numpy as np
+    out_f, in_f, R = I, H, 2
+    rng = np.random.default_rng(0)
+    codes = rng.integers(0, 8, size=(out_f, in_f)).astype(np.uint8)
+    s16 = (0.01 + 0.001 * rng.random((out_f, in_f // 64))).astype(np.float16)
+    lin = SoftLinear("up_proj", 3, codes, s16, 64, seed=0)
+    probs = torch.rand(R, lin.K, lin.d, device=dev)
+    grad = torch.randn(R, out_f, in_f, device=dev) * 1e-3
+    terms = torch.empty(R, 3, out_f, in_f, device=dev, dtype=torch.bfloat16)
+    nxt = {"step": 1, "tau": 1.9, "kappa": 102.0, "seed": 5, "terms": terms}
+    return {"soft_step up_proj (R=2)": (None, lambda: lin.step(probs, grad, 2.0, 100.0, nxt=nxt))}
+
+
+def cublas(dev, g):
+    """Library bf16 GEMMs of the same shapes (context for the tile-level figures above)."""
+    M, R = 2 * (T - 1), 8 * T
+    a1, b1 = torch.randn(R, H, device=dev).bfloat16(), torch.randn(2 * I, H, device=dev).bfloat16()
+    a2, b2 = torch.randn(M, I, device=dev).bfloat16(), torch.randn(H, I, device=dev).bfloat16()
+    a3, b3 = torch.randn(H, M, device=dev).bfloat16(), torch.randn(I, M, device=dev).bfloat16()
+    return {
+        "cublas bf16 16384x9728x896": (2 * R * 2 * I * H, lambda: a1 @ b1.T),
+        "cublas bf16 4094x896x4864": (2 * M * H * I, lambda: a2 @ b2.T),
+        "cublas bf16 896x4864x4094": (2 * H * I * M, lambda: a3 @ b3.T),
+    }
+
+
+CASES = {"mlp_gemms": mlp_gemms, "attn": attn, "soft_step": soft_step, "cublas": cublas}
+
+
+def main(argv):
+    names = [a for a in argv if not a.startswith("--")] or list(CASES)
+    once = "--once" in argv
+    _lib.lib()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    for name in names:
+        for label, (flops, fn) in CASES[name](dev, g).items():
+            if once:
+                fn()
+                torch.cuda.synchronize()
+                continue
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(10):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / 10 * 1000
+            extra = f"  {flops / us / 1e6:8.1f} TFLOP/s executed bf16" if flops else ""
+            print(f"{label:28s} {us:9.1f} us{extra}", flush=True)
+    check_err(dev)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])
