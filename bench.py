@@ -13,7 +13,13 @@ weights, probabilities, momenta: > 1 GB) exceeds the 126 MB L2.
 Workload "linear": one up_proj-shaped linear (W 4864 x 896, X 16384 x 896 as 32 x 512), the
 qk-stage step of one linear.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload block|linear]
+Workload "gptq": GPTQ of the 168 linears of a random-init 24-layer stack at 2, 3 and 4 bits from
+Hessians over 128 x 2048 tokens; value = seconds per model (lower is
+better); under torchrun the windows and solves are sharded (strong scaling, NCCL all-reduce of
+the Hessians).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload block|linear|gptq]
 
 N > 1 runs under torchrun, one rank per GPU, each rank quantizing its own block (weak scaling,
 no collective). --impl reference times the CPU restatement of the same step on this host's cores
@@ -45,7 +51,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="block", choices=["block", "linear"])
+    ap.add_argument("--workload", default="block", choices=["block", "linear", "gptq"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=200)
     return ap.parse_args()
@@ -264,21 +270,13 @@ def run_block(args):
                              "engine executes 3-6 bf16 products per float32 product"},
         "clocks": clk,
     }
-    res["gpu_launches"] = count_launches_block(args.steps)
+    res["gpu_launches"] = int(sum(timer.launches.values()))
     if rank == 0 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_block()
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:
         dist.destroy_process_group()
-
-
-def count_launches_block(steps):
-    """Our kernel launches per block step (qk + vo + mlp), counted from the stage code:
-    qk: gather 1 + R x (gemm 2 + sum 1) x 2 linears + step 2 = 15; vo: gather 3 + rope 2 + scores
-    1 + softmax 1 + R x (7 gemm + 1 sum + 3 transpose + 1 group sum) + step 2 = 33;
-    mlp: gather 3 + R x (5 gemm + 1 sum + 3 transpose) + step 3 = 24."""
-    return steps * (15 + 33 + 24)
 
 
 def cpu_baseline_block():
@@ -330,6 +328,141 @@ def run_reference(args):
                                       "the reference's MLX path is unavailable, this is the "
                                       "CPU restatement"},
            "e2e": {"value": round(v, 5), "unit": "block steps/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(res), flush=True)
+
+
+# ------------------------------------------------------------------------------ gptq ---
+
+GPTQ_OPTIONS = (2, 3, 4)
+
+
+def run_gptq(args):
+    """Config 3: GPTQ of every linear of a random-init 24-layer Qwen2.5-0.5B stack at 2, 3 and 4
+    bits (504 solves) from Hessians over 128 x 2048 uniform-random tokens. A step is one full
+    build (Hessian forward of 24 layers + 504 solves); the metric is seconds per model. Under
+    torchrun the windows and the solves are shared over the ranks (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+    from gsq_rco_mlx_b200 import _lib
+    from gsq_rco_mlx_b200.rco.database import DBSpec, build_database, random_model
+
+    rank, world, local = dist_setup()
+    _lib.lib()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    n_layers = 24
+    model = random_model(n_layers=n_layers, seed=0, device=dev)
+    tokens = np.random.default_rng(0).integers(0, VOCAB, size=(N_SEQ, T_SEQ)).astype(np.int32)
+    quiet = lambda *a: None
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # warm-up: one layer (allocations, first launches)
+    for _ in range(max(1, args.warmup)):
+        build_database(model, tokens, DBSpec(options=GPTQ_OPTIONS, n_layers=1), log=quiet,
+                       keep="device")
+    barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    tm = {}
+    n0 = _lib.Launches.n
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for _ in range(max(1, args.steps)):
+        barrier()
+        e0.record()
+        man, res = build_database(model, tokens, DBSpec(options=GPTQ_OPTIONS, n_layers=n_layers),
+                                  log=quiet, keep="device", timings=tm)
+        e1.record()
+        barrier()
+        times.append(max_over_ranks(e0.elapsed_time(e1) / 1000))
+    clk = clocks.stop()
+    launches = (_lib.Launches.n - n0) // max(1, args.steps)
+    sec = statistics.median(times)
+    # end to end: host tokens in, host codes / scales / sensitivities out
+    barrier()
+    t0 = time.perf_counter()
+    man, res = build_database(model, tokens, DBSpec(options=GPTQ_OPTIONS, n_layers=n_layers),
+                              log=quiet, keep="host")
+    barrier()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    d2h = sum(c.nbytes + sc.nbytes for c, sc in res.values())
+    steps = max(1, args.steps)
+    phase = {k: round(v / steps, 3) for k, v in tm.items()}
+    out = {
+        "metric": "GPTQ s/model (24-layer Qwen2.5-0.5B architecture, 168 linears x {2,3,4} bits, "
+                  "Hessians over 128 x 2048 tokens)",
+        "value": round(sec, 3), "unit": "s/model", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(sec * 1000, 1), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f64 solves, bf16/f32 Hessians",
+        "data": "synthetic: random-init bf16 24-layer stack, uniform-random token ids",
+        "config": {"workload": "config 3: 24-layer GPTQ, options (2, 3, 4), g64, damp 0.01",
+                   "phase_seconds_per_model": phase,
+                   "parallelism": f"windows and solves sharded over {world} rank(s)",
+                   "l2": "per-layer working set (470 MB of hidden states) > L2"},
+        "e2e": {"value": round(e2e_s, 3), "unit": "s/model",
+                "h2d_bytes_per_step": int(tokens.nbytes), "d2h_bytes_per_step": int(d2h),
+                "what": "build_database from host token ids to host codes, scales, sensitivities"},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline_gptq()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_baseline_gptq():
+    """The numpy restatement of the reference GPTQ (float64, the reference's own CPU path) on a
+    bounded sample: one solve of each distinct shape at 3 bits on this host's cores, scaled to
+    the 504 solves of the model (the Hessian forward is not included: a lower bound)."""
+    from oracle import gptq as og
+    rng = np.random.default_rng(0)
+    per_shape = {}
+    for (o, i) in ((HID, HID), (NKV * HD, HID), (INTER, HID), (HID, INTER)):
+        X = rng.standard_normal((4096, i)).astype(np.float32)
+        H = 2.0 * (X.astype(np.float64).T @ X.astype(np.float64)) / X.shape[0]
+        W = (0.02 * rng.standard_normal((o, i))).astype(np.float32)
+        t0 = time.perf_counter()
+        og.quantize_gptq(W, H, 3, 64, 0.01)
+        per_shape[(o, i)] = time.perf_counter() - t0
+    per_layer = (2 * per_shape[(HID, HID)] + 2 * per_shape[(NKV * HD, HID)] +
+                 2 * per_shape[(INTER, HID)] + per_shape[(HID, INTER)])
+    total = per_layer * len(GPTQ_OPTIONS) * 24
+    return {"value": round(total, 1), "unit": "s/model (solves only, lower bound)",
+            "cores": os.cpu_count(), "kind": "port",
+            "sample": "one 3-bit solve per distinct linear shape (q/o, k/v, gate/up, down) with "
+                      "H from 4096 rows, scaled to 24 layers x 7 linears x 3 options"}
+
+
+def run_reference_gptq(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    cb = cpu_baseline_gptq()
+    res = {"impl": "reference",
+           "metric": "GPTQ s/model (24-layer Qwen2.5-0.5B architecture, 168 linears x {2,3,4} bits, "
+                     "Hessians over 128 x 2048 tokens)",
+           "value": cb["value"], "unit": "s/model", "n_gpus": world, "steps": 1, "warmup": 0,
+           "ms_per_step": round(cb["value"] * 1000, 1), "higher_is_better": False,
+           "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+           "config": {"workload": "config 3: 24-layer GPTQ, options (2, 3, 4), g64, damp 0.01"},
+           "cpu_baseline": cb,
+           "e2e": {"value": cb["value"], "unit": "s/model", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(res), flush=True)
 
@@ -499,6 +632,8 @@ def main():
     args = parse()
     if args.workload == "linear":
         return run_linear(args)
+    if args.workload == "gptq":
+        return run_reference_gptq(args) if args.impl == "reference" else run_gptq(args)
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -115,8 +115,15 @@ def stream_ptr(stream=None):
     return C.c_void_p(s.cuda_stream)
 
 
+class Launches:
+    """Count of entry-point calls (each launches one kernel; gemm() adds the split-K reduce):
+    the bench's `gpu_launches`. Increment is a Python add per call."""
+    n = 0
+
+
 def call(name: str, *args):
     """Call an entry point and raise on a nonzero status."""
+    Launches.n += 1
     check(getattr(lib(), name)(*args), name)
 
 

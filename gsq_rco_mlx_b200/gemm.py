@@ -271,6 +271,11 @@ def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, 
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
     _lib.call("gsq_gemm", _C.byref(d), _lib.stream_ptr())
+    if d.split_k > 1:
+        kb = -(-d.K // 64)
+        per = -(-kb // d.split_k)
+        if -(-kb // per) > 1:
+            _lib.Launches.n += 1  # the split-K reduction
     if log is not None:
         e1.record()
         prods = sum(1 for i in range(na) for j in range(nb) if i + j <= order)

@@ -120,7 +120,7 @@ class Qwen2Block:
         hnT = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[hn])
         # q | k in one GEMM, bf16 chain with bias
         gemm(hnT, wterms(W.qk), M=R, epi=4, bias=W.qk_bias,
-             c_terms=Terms(R, self.qk.shape[1], 1, ld=self.qk.shape[1], tensors=[self.qk]))
+             c_terms=Terms(R, self.qk.shape[1], 1, ld=self.qk.shape[1], tensors=[self.qk[:R]]))
         # v^T per sequence: [s][kv * 64 + d][t]
         nkvd = c.n_kv * c.head_dim
         gemm(hnT, wterms(W.W["v_proj"]), M=T, batch=S, epi=4, bias=W.v_bias,
@@ -171,26 +171,26 @@ class Qwen2Block:
         if upto == "hn":
             return None
         o_tap = self.tap("o") if "o" in taps else None
-        self.attention(self.hn, W, S, self.o, o_tap=o_tap)
+        self.attention(self.hn[:R], W, S, self.o[:R], o_tap=o_tap)
         if o_tap is not None:
             _lib.call("gsq_zero_cols", _lib.ptr(o_tap.t[0]), c.hidden, o_tap.ld, R, T, st)
         if upto == "o":
             return None
-        Ot = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[self.o])
+        Ot = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[self.o[:R]])
         if attn_out is not None:
             gemm(Ot, wterms(W.W["o_proj"]), epi=4,
                  c_terms=Terms(R, c.hidden, 1, ld=c.hidden, tensors=[attn_out]))
             if out is None:
                 return attn_out
         gemm(Ot, wterms(W.W["o_proj"]), epi=4, resid=h, ld_rt=c.hidden,
-             c_terms=Terms(R, c.hidden, 1, ld=c.hidden, tensors=[self.h1]))
+             c_terms=Terms(R, c.hidden, 1, ld=c.hidden, tensors=[self.h1[:R]]))
         mn_tap = self.tap("mn") if "mn" in taps else None
         _lib.call("gsq_rmsnorm", _lib.ptr(self.h1), c.hidden, _lib.ptr(W.W["post_norm"]), R,
                   c.hidden, float(c.eps), _lib.ptr(self.mn), c.hidden,
                   _lib.ptr(mn_tap.t[0] if mn_tap else None), mn_tap.ld if mn_tap else 0, T, 1, st)
         if upto == "mn":
             return None
-        return self._mlp(self.h1, self.mn, W, R, T, st, out, taps, upto)
+        return self._mlp(self.h1[:R], self.mn[:R], W, R, T, st, out, taps, upto)
 
     def _mlp(self, h1, mn, W: BlockWeights, R, T, st, out, taps, upto):
         """out = h1 + down(SwiGLU(mn)) (bf16 chain); the d_in tap if asked."""
@@ -198,13 +198,13 @@ class Qwen2Block:
         d_tap = self.tap("d_in") if "d_in" in taps else None
         MNt = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[mn])
         gemm(MNt, wterms(W.W["gate_proj"]), B2=wterms(W.W["up_proj"]), epi=5,
-             c_terms=Terms(R, c.inter, 1, ld=c.inter, tensors=[self.d_in]), ct_terms=d_tap)
+             c_terms=Terms(R, c.inter, 1, ld=c.inter, tensors=[self.d_in[:R]]), ct_terms=d_tap)
         if d_tap is not None:
             _lib.call("gsq_zero_cols", _lib.ptr(d_tap.t[0]), c.inter, d_tap.ld, R, T, st)
         if upto == "d_in":
             return None
         out = torch.empty(R, c.hidden, device=self.dev, dtype=torch.bfloat16) if out is None else out
-        Dt = Terms(R, c.inter, 1, ld=c.inter, tensors=[self.d_in])
+        Dt = Terms(R, c.inter, 1, ld=c.inter, tensors=[self.d_in[:R]])
         gemm(Dt, wterms(W.W["down_proj"]), epi=4, resid=h1, ld_rt=c.hidden,
              c_terms=Terms(R, c.hidden, 1, ld=c.hidden, tensors=[out]))
         return out

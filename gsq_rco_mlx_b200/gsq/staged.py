@@ -263,7 +263,7 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
     step = LinearStep(lins, m * (T - 1), in_f, opts.resamples, 1 if exact_bf16_rows else 3)
     flat = x_all.view(n_seq * T, in_f)
     err_flag(step.dev).zero_()
-    hist = torch.zeros(opts.steps, len(lins), device=step.dev, dtype=torch.float64)
+    hist = torch.zeros(opts.steps, len(lins) * step.R, device=step.dev, dtype=torch.float64)
     timer = timer or StageTimer(min(3, opts.steps - 1))
     tau, kappa = gs_schedules(0, opts.steps)
     step.first_forward(targets, 0, tau, kappa, noise_seed, noise_of)
@@ -275,12 +275,13 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
         step.contract()
         nxt = (t + 1, *gs_schedules(t + 1, opts.steps)) if t + 1 < opts.steps else None
         step.update(targets, t, tau, kappa, opts, noise_seed, nxt=nxt, noise_of=noise_of)
-        hist[t].copy_(step.loss.view(len(lins), step.R).sum(1))
+        hist[t].copy_(step.loss)  # a device copy; summed on the host at the end
         timer.end(name, t, t == opts.steps - 1)
     check_err(step.dev)
     denom = torch.tensor([step.M * lin.out_f for lin in lins], device=step.dev,
                          dtype=torch.float64)
-    history = ((hist / denom).sum(1) / step.R).cpu().tolist()
+    per_lin = hist.view(opts.steps, len(lins), step.R).sum(2)
+    history = ((per_lin / denom).sum(1) / step.R).cpu().tolist()
     return history, (round(timer.ms[name], 4) if name in timer.ms else None)
 
 
@@ -534,7 +535,9 @@ class StageTimer:
         self.warmup = int(warmup)
         self.nvtx = bool(nvtx)
         self.ms = {}
+        self.launches = {}  # our kernel launches inside each stage's timed steps
         self._ev = {}
+        self._n0 = {}
 
     def begin(self, name, t):
         """At the start of step t."""
@@ -542,6 +545,7 @@ class StageTimer:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
             self._ev[name] = e
+            self._n0[name] = _lib.Launches.n
             if self.nvtx:
                 torch.cuda.nvtx.range_push("gsq_steps")
 
@@ -550,6 +554,7 @@ class StageTimer:
         if last and name in self._ev:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
+            self.launches[name] = _lib.Launches.n - self._n0[name]
             if self.nvtx:
                 torch.cuda.nvtx.range_pop()
             e.synchronize()
@@ -571,7 +576,7 @@ def train_stage(step, stage_args_of, n_seqs, opts: BlockOpts, seed, noise_seed=N
     err_flag(step.dev).zero_()
     tau, kappa = gs_schedules(0, opts.steps)
     step.first_forward(0, tau, kappa, noise_seed, noise_of)
-    hist = torch.zeros(opts.steps, device=step.dev, dtype=torch.float64)
+    hist = torch.zeros(opts.steps, step.R, device=step.dev, dtype=torch.float64)
     timer = timer or StageTimer(min(3, opts.steps - 1))
     for t in range(opts.steps):
         timer.begin(name, t)
@@ -581,10 +586,10 @@ def train_stage(step, stage_args_of, n_seqs, opts: BlockOpts, seed, noise_seed=N
         step.contract()
         nxt = (t + 1, *gs_schedules(t + 1, opts.steps)) if t + 1 < opts.steps else None
         step.update(t, tau, kappa, opts, noise_seed, nxt=nxt, noise_of=noise_of)
-        hist[t:t + 1].copy_(step.loss.sum(0, keepdim=True))
+        hist[t].copy_(step.loss.view(-1))  # a device copy; summed on the host at the end
         timer.end(name, t, t == opts.steps - 1)
     check_err(step.dev)
-    history = (hist / (step.R * step.count)).cpu().tolist()
+    history = (hist.sum(1) / (step.R * step.count)).cpu().tolist()
     return history, (round(timer.ms[name], 4) if name in timer.ms else None)
 
 
