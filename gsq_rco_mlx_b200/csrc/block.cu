@@ -125,6 +125,36 @@ softmax_causal_kernel(const float* __restrict__ S, int B, int T, __nv_bfloat16* 
   }
 }
 
+// Row-windowed form: local row i of batch z is query position row0 + i; keys k <= row0 + i of
+// the cols stored ones are valid. S [B][rows][ld_s] float32 -> P [B][rows][ld_p] bf16 (zeros at
+// masked keys k < cols). One warp per row.
+__global__ void __launch_bounds__(256)
+softmax_causal_rows_kernel(const float* __restrict__ S, int B, int rows, int cols, int64_t ld_s,
+                           int row0, __nv_bfloat16* __restrict__ P, int64_t ld_p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n_rows = (int64_t)B * rows;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < n_rows;
+       row += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int i = (int)(row % rows);
+    const int last = min(row0 + i, cols - 1);  // last valid key
+    const float* s = S + row * ld_s;
+    __nv_bfloat16* p = P + row * ld_p;
+    float m = -INFINITY;
+    for (int k = lane; k <= last; k += 32) m = fmaxf(m, s[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    double sum = 0.0;
+    for (int k = lane; k <= last; k += 32) sum += (double)expf(__fsub_rn(s[k], m));
+    sum = warp_sum_d(sum);
+    const float inv = __frcp_rn((float)sum);
+    for (int k = lane; k < cols; k += 32) {
+      float v = 0.f;
+      if (k <= last) v = __fmul_rn(expf(__fsub_rn(s[k], m)), inv);
+      p[k] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
 __global__ void embed_kernel(const int32_t* __restrict__ ids, int64_t n, const __nv_bfloat16* __restrict__ E,
                              int H, __nv_bfloat16* __restrict__ out) {
   const int64_t total = n * H;
@@ -199,6 +229,18 @@ extern "C" int gsq_softmax_causal(const float* S, int B, int T, void* P, void* P
   if (!S || !P || B <= 0 || T <= 0) return GSQ_EINVAL;
   softmax_causal_kernel<<<blocks((int64_t)B * T * 32, 256), 256, 0, (cudaStream_t)stream>>>(
       S, B, T, (__nv_bfloat16*)P, (__nv_bfloat16*)PT);
+  GSQ_CHECK_LAUNCH();
+  return GSQ_OK;
+}
+
+extern "C" int gsq_softmax_causal_rows(const float* S, int B, int rows, int cols, int64_t ld_s,
+                                       int row0, void* P, int64_t ld_p, void* stream) {
+  if (!S || !P || B <= 0 || rows <= 0 || cols <= 0 || row0 < 0 || ld_s < cols || ld_p < cols ||
+      row0 + rows > cols)
+    return GSQ_EINVAL;
+  softmax_causal_rows_kernel<<<blocks((int64_t)B * rows * 32, 256), 256, 0,
+                                 (cudaStream_t)stream>>>(S, B, rows, cols, ld_s, row0,
+                                                         (__nv_bfloat16*)P, ld_p);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }

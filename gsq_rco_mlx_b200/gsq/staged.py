@@ -168,9 +168,12 @@ class LinearStep:
     the backward, the resample mean, Lion, and the next step's soft weights and probabilities.
     All GEMM operands are bf16 terms (three for float32 data, one for exactly-bf16 rows)."""
 
-    def __init__(self, lins, M, in_f, resamples, x_terms=3):
+    def __init__(self, lins, M, in_f, resamples, x_terms=3, M_total=None):
+        """M: rows of this rank's micro-batch share; M_total: rows of the whole micro-batch (the
+        loss normalisation), M when one process runs the stage."""
         dev = lins[0].logits.device
         self.lins, self.M, self.in_f, self.R = lins, int(M), int(in_f), int(resamples)
+        self.M_total = int(M if M_total is None else M_total)
         self.nx = int(x_terms)
         self.X = Terms(M, in_f, self.nx, dev)        # A of the residual GEMM
         self.XT = Terms(in_f, M, self.nx, dev)       # B of the weight-gradient GEMM
@@ -182,8 +185,8 @@ class LinearStep:
         self.probs = {l.name: torch.zeros(R, l.K, l.d, device=dev, dtype=torch.float32)
                       for l in lins}
         self.RT = {l.name: Terms(l.out_f, M, 3, dev) for l in lins}
-        self.grads = {l.name: torch.empty((R,) + l.shape, device=dev, dtype=torch.float32)
-                      for l in lins}
+        self.gflat, views = _flat_views(dev, [(R,) + l.shape for l in lins])
+        self.grads = {l.name: v for l, v in zip(lins, views)}
         tiles = max(((M + 127) // 128) * ((l.out_f + 127) // 128) for l in lins)
         self.sq = torch.zeros(tiles, device=dev, dtype=torch.float64)
         self.loss = torch.zeros(len(lins) * R, device=dev, dtype=torch.float64)
@@ -220,7 +223,7 @@ class LinearStep:
                 slot = self.loss[li * self.R + r:li * self.R + r + 1]
                 _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(slot),
                           _lib.stream_ptr())
-                gemm(RT, self.XT, alpha=2.0 / (self.M * lin.out_f), C=G[r])
+                gemm(RT, self.XT, alpha=2.0 / (self.M_total * lin.out_f), C=G[r])
 
     def update(self, targets, t, tau, kappa, opts, noise_seed, nxt=None, noise_of=None):
         """Fused backward + Lion of step t; nxt = (t1, tau1, kappa1) also runs step t1's forward."""
@@ -239,12 +242,13 @@ class LinearStep:
     def mean_loss(self):
         """sum over linears of mean R^2, averaged over resamples (staged.py:386-394)."""
         la = self.loss.view(len(self.lins), self.R).cpu().numpy()
-        denom = np.array([self.M * lin.out_f for lin in self.lins], dtype=np.float64)[:, None]
+        denom = np.array([self.M_total * lin.out_f for lin in self.lins],
+                         dtype=np.float64)[:, None]
         return float((la / denom).sum(axis=0).sum() / self.R)
 
 
 def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=None,
-                  noise_seed=None, exact_bf16_rows=False, timer=None, name="qk"):
+                  noise_seed=None, exact_bf16_rows=False, timer=None, name="qk", dp=None):
     """qk-stage optimiser: loss = sum over linears of mean ||X (W_bar - W)^T||^2.
 
     x_all: float32 CUDA tensor [n_seqs, T, in] of the linears' inputs; each step draws a sorted
@@ -260,7 +264,10 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
     m = min(opts.micro_batch, n_seqs)
     n_seq, T, in_f = x_all.shape
     noise_seed = seed if noise_seed is None else noise_seed
-    step = LinearStep(lins, m * (T - 1), in_f, opts.resamples, 1 if exact_bf16_rows else 3)
+    dp = dp or DataParallel()
+    p0, p1 = dp.window(1, T)
+    step = LinearStep(lins, m * (p1 - p0), in_f, opts.resamples, 1 if exact_bf16_rows else 3,
+                      M_total=m * (T - 1))
     flat = x_all.view(n_seq * T, in_f)
     err_flag(step.dev).zero_()
     hist = torch.zeros(opts.steps, len(lins) * step.R, device=step.dev, dtype=torch.float64)
@@ -271,14 +278,15 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
         timer.begin(name, t)
         tau, kappa = gs_schedules(t, opts.steps)
         idx = np.sort(rng.choice(n_seqs, size=m, replace=False))
-        step.stage(flat, idx, T - 1, T, 1)
+        step.stage(flat, idx, p1 - p0, T, p0)
         step.contract()
+        dp.allreduce(step.gflat, step.loss)
         nxt = (t + 1, *gs_schedules(t + 1, opts.steps)) if t + 1 < opts.steps else None
         step.update(targets, t, tau, kappa, opts, noise_seed, nxt=nxt, noise_of=noise_of)
         hist[t].copy_(step.loss)  # a device copy; summed on the host at the end
         timer.end(name, t, t == opts.steps - 1)
     check_err(step.dev)
-    denom = torch.tensor([step.M * lin.out_f for lin in lins], device=step.dev,
+    denom = torch.tensor([step.M_total * lin.out_f for lin in lins], device=step.dev,
                          dtype=torch.float64)
     per_lin = hist.view(opts.steps, len(lins), step.R).sum(2)
     history = ((per_lin / denom).sum(1) / step.R).cpu().tolist()
@@ -286,6 +294,45 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
 
 
 # ------------------------------------------------------------------------- block stages ---
+
+class DataParallel:
+    """Data parallelism of the GSQ stages over calibration tokens. Every rank draws the same
+    micro-batch (the numpy stream is replicated) and takes one window of positions of each of its
+    sequences; it computes dL/dw̄ of every resample on its rows, and one all-reduce per step sums
+    the weight gradients (4 B per weight per resample: the logit and scale gradients are linear
+    maps of them) and the loss partials. Every rank then runs the identical fused Lion update,
+    so the soft-weight states stay bit-identical across ranks. A single process is world 1."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        on = dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1
+        self.dist = dist if on else None
+        self.group = group
+        self.world = dist.get_world_size(group) if on else 1
+        self.rank = dist.get_rank(group) if on else 0
+
+    def window(self, lo, hi):
+        """This rank's contiguous share [a, b) of the positions [lo, hi)."""
+        base, extra = divmod(hi - lo, self.world)
+        a = lo + self.rank * base + min(self.rank, extra)
+        return a, a + base + (1 if self.rank < extra else 0)
+
+    def allreduce(self, *tensors):
+        if self.dist is not None:
+            for t in tensors:
+                self.dist.all_reduce(t, group=self.group)
+
+
+def _flat_views(dev, shapes):
+    """One float32 buffer with contiguous views of the given shapes (one all-reduce per step)."""
+    sizes = [int(np.prod(sh)) for sh in shapes]
+    flat = torch.empty(sum(sizes), device=dev, dtype=torch.float32)
+    views, off = [], 0
+    for sh, n in zip(shapes, sizes):
+        views.append(flat[off:off + n].view(sh))
+        off += n
+    return flat, views
+
 
 def _seq_ids(dev, ids):
     return torch.as_tensor(np.asarray(ids, dtype=np.int32)).to(dev, non_blocking=True)
@@ -356,13 +403,16 @@ class MLPStep(_StageBase):
       B3  [dL/dWg; dL/dWu] = [dg; du]^T mn
     """
 
-    def __init__(self, lins, cfg, m, T, R):
+    def __init__(self, lins, cfg, m, T, R, window=None):
+        """window: this rank's positions [p0, p1) of each sequence (default all of 1..T-1)."""
         gate, up, down = lins
         dev = gate.logits.device
         self._init_soft(lins, R, dev)
         H, I = cfg.hidden, cfg.inter
-        M = m * (T - 1)
-        self.cfg, self.m, self.T, self.M, self.count = cfg, m, T, M, M * H
+        self.p0, p1 = window or (1, T)
+        self.w = p1 - self.p0
+        M = m * self.w
+        self.cfg, self.m, self.T, self.M, self.count = cfg, m, T, M, m * (T - 1) * H
         bf = torch.bfloat16
         self.MN = Terms(M, H, 1, dev)
         self.MNT = Terms(H, M, 1, dev)
@@ -374,8 +424,7 @@ class MLPStep(_StageBase):
         self.DR, self.DRT = Terms(M, H, 3, dev), Terms(H, M, 3, dev)
         self.GUT = Terms(2 * I, M, 3, dev)
         self.DdT = Terms(I, H, 3, dev)
-        self.grad_gu = torch.empty(2, R, I, H, device=dev, dtype=torch.float32)
-        self.grad_d = torch.empty(R, H, I, device=dev, dtype=torch.float32)
+        self.gflat, (self.grad_gu, self.grad_d) = _flat_views(dev, [(2, R, I, H), (R, H, I)])
         tiles = ((M + 127) // 128) * ((H + 127) // 128)
         self.sq = torch.zeros(tiles, device=dev, dtype=torch.float64)
         self.names = (gate.name, up.name, down.name)
@@ -388,9 +437,9 @@ class MLPStep(_StageBase):
         """Positions 1.. of the chosen sequences of the caches (bf16 [N*T, H])."""
         H, T = self.cfg.hidden, self.T
         ids = _seq_ids(self.dev, seq_ids)
-        _gather(mn_all, ids, T - 1, T, 1, self.M, H, 1, self.MN, self.MNT)
-        _gather(h1_all, ids, T - 1, T, 1, self.M, H, 1, self.H1)
-        _gather(y_all, ids, T - 1, T, 1, self.M, H, 1, self.Y)
+        _gather(mn_all, ids, self.w, T, self.p0, self.M, H, 1, self.MN, self.MNT)
+        _gather(h1_all, ids, self.w, T, self.p0, self.M, H, 1, self.H1)
+        _gather(y_all, ids, self.w, T, self.p0, self.M, H, 1, self.Y)
 
     def contract(self):
         H, I, M = self.cfg.hidden, self.cfg.inter, self.M
@@ -417,10 +466,11 @@ class MLPStep(_StageBase):
 class VOStep(_StageBase):
     """The vo stage step (staged.py:332-342): A = (P v) Wo^T with soft v / o, loss
     mean((A - A_fp)^2) over positions 1.. per sequence, averaged over the micro-batch. q and k
-    are hard, so the probabilities P come from the cached q / k of the chosen sequences. Per
-    resample:
-      V     v^T = (hn Wv^T + bv)^T per sequence             bias epilogue, transposed terms
-      PV    o = P v per (sequence, head)                    causal k-range, row / transposed terms
+    are hard, so the probabilities P come from the cached q / k of the chosen sequences. This
+    rank takes the query positions [q0, q1) of every micro-batch sequence (all of them in one
+    process) and the keys 0..q1-1 they see. Per resample:
+      V     v^T = (hn Wv^T + bv)^T per sequence (keys)      bias epilogue, transposed terms
+      PV    o = P v per (sequence, head)                    causal k-range when q0 = 0
       Y     r = o Wo^T - A_fp (0 at position 0)             residual-loss epilogue: dY = 2 r / n
       Go    dL/dWo = dY^T o
       dO    dO^T = (dY Wo)^T per sequence
@@ -428,32 +478,33 @@ class VOStep(_StageBase):
       Gv    dL/dWv = dV^T hn
     """
 
-    def __init__(self, lins, cfg, m, T, R, v_bias):
+    def __init__(self, lins, cfg, m, T, R, v_bias, window=None):
         v, o = lins
         dev = v.logits.device
         self._init_soft(lins, R, dev)
         c = cfg
         H, nh, nkv, hd = c.hidden, c.n_heads, c.n_kv, c.head_dim
+        self.q0, q1 = window or (0, T)
+        self.Tq, self.Tk = q1 - self.q0, q1
+        Tq, Tk = self.Tq, self.Tk
         self.cfg, self.m, self.T, self.count = cfg, m, T, m * (T - 1) * H
-        RT = m * T
-        self.HN, self.HNT = Terms(RT, H, 1, dev), Terms(H, RT, 1, dev)
-        self.A = Terms(RT, H, 1, dev)
-        self.QK = torch.empty(RT, (nh + nkv) * hd, device=dev, dtype=torch.bfloat16)
-        self.q_rot = Terms(m * nh * T, hd, 3, dev)
-        self.k_rot = Terms(m * nkv * T, hd, 3, dev)
-        self.scores = torch.empty(m * nh, T, T, device=dev, dtype=torch.float32)
-        self.P = Terms(m * nh * T, T, 1, dev, ld=T)
-        self.PT = Terms(m * nh * T, T, 1, dev, ld=T)
-        self.VT = Terms(m * nkv * hd, T, 3, dev)
-        self.O, self.OT = Terms(RT, H, 3, dev), Terms(H, RT, 3, dev)
-        self.DY, self.DYT = Terms(RT, H, 3, dev), Terms(H, RT, 3, dev)
+        self.HN, self.HNT = Terms(m * Tk, H, 1, dev), Terms(H, m * Tk, 1, dev)
+        self.A = Terms(m * Tq, H, 1, dev)
+        self.QK = torch.empty(m * Tk, (nh + nkv) * hd, device=dev, dtype=torch.bfloat16)
+        self.q_rot = Terms(m * nh * Tk, hd, 3, dev)
+        self.k_rot = Terms(m * nkv * Tk, hd, 3, dev)
+        self.scores = torch.empty(m * nh, Tq, Tk, device=dev, dtype=torch.float32)
+        self.P = Terms(m * nh * Tq, Tk, 1, dev)
+        self.PT = Terms(m * nh * Tk, Tq, 1, dev)
+        self.VT = Terms(m * nkv * hd, Tk, 3, dev)
+        self.O, self.OT = Terms(m * Tq, H, 3, dev), Terms(H, m * Tq, 3, dev)
+        self.DY, self.DYT = Terms(m * Tq, H, 3, dev), Terms(H, m * Tq, 3, dev)
         self.DoT = Terms(H, H, 3, dev)
-        self.DOT = Terms(m * H, T, 3, dev)
-        self.dv = torch.empty(m * nh, T, hd, device=dev, dtype=torch.float32)
-        self.DVT = Terms(nkv * hd, RT, 3, dev)
-        self.grad_v = torch.empty(R, nkv * hd, H, device=dev, dtype=torch.float32)
-        self.grad_o = torch.empty(R, H, H, device=dev, dtype=torch.float32)
-        tiles = ((RT + 127) // 128) * ((H + 127) // 128)
+        self.DOT = Terms(m * H, Tq, 3, dev)
+        self.dv = torch.empty(m * nh, Tk, hd, device=dev, dtype=torch.float32)
+        self.DVT = Terms(nkv * hd, m * Tk, 3, dev)
+        self.gflat, (self.grad_v, self.grad_o) = _flat_views(dev, [(R, nkv * hd, H), (R, H, H)])
+        tiles = ((m * Tq + 127) // 128) * ((H + 127) // 128)
         self.sq = torch.zeros(tiles, device=dev, dtype=torch.float64)
         self.v_bias = v_bias.float().contiguous()
         self.names = (v.name, o.name)
@@ -466,62 +517,72 @@ class VOStep(_StageBase):
         return self.grad_v if lin.name == self.names[0] else self.grad_o
 
     def stage(self, hn_all, a_all, qk_all, seq_ids):
-        """All positions of the chosen sequences: hn, the target A_fp, the hard q|k rows; then
-        the causal probabilities P (and P^T) of the micro-batch."""
+        """Positions 0..q1-1 of the chosen sequences: hn and the hard q|k rows; the target A_fp
+        of the query positions q0..q1-1; then the causal probabilities P of the query rows over
+        their keys (and P^T)."""
         c, T, m = self.cfg, self.T, self.m
-        H = c.hidden
+        H, Tq, Tk, q0 = c.hidden, self.Tq, self.Tk, self.q0
         ids = _seq_ids(self.dev, seq_ids)
-        RT = m * T
-        _gather(hn_all, ids, T, T, 0, RT, H, 1, self.HN, self.HNT)
-        _gather(a_all, ids, T, T, 0, RT, H, 1, self.A)
+        _gather(hn_all, ids, Tk, T, 0, m * Tk, H, 1, self.HN, self.HNT)
+        _gather(a_all, ids, Tq, T, q0, m * Tq, H, 1, self.A)
         qkw = qk_all.shape[1]
-        QKt = Terms(RT, qkw, 1, ld=qkw, tensors=[self.QK])
-        _gather(qk_all, ids, T, T, 0, RT, qkw, 1, QKt)
+        QKt = Terms(m * Tk, qkw, 1, ld=qkw, tensors=[self.QK])
+        _gather(qk_all, ids, Tk, T, 0, m * Tk, qkw, 1, QKt)
         st = _lib.stream_ptr()
         qd = c.n_heads * c.head_dim
         t = self.q_rot.t
-        _lib.call("gsq_rope_split", _lib.ptr(self.QK), qkw, m, T, c.n_heads, _lib.ptr(self.cos),
+        _lib.call("gsq_rope_split", _lib.ptr(self.QK), qkw, m, Tk, c.n_heads, _lib.ptr(self.cos),
                   _lib.ptr(self.sin), _lib.ptr(t[0]), _lib.ptr(t[1]), _lib.ptr(t[2]), st)
         t = self.k_rot.t
         from .e2e import C_ptr
-        _lib.call("gsq_rope_split", C_ptr(self.QK[:, qd:]), qkw, m, T, c.n_kv, _lib.ptr(self.cos),
+        _lib.call("gsq_rope_split", C_ptr(self.QK[:, qd:]), qkw, m, Tk, c.n_kv, _lib.ptr(self.cos),
                   _lib.ptr(self.sin), _lib.ptr(t[0]), _lib.ptr(t[1]), _lib.ptr(t[2]), st)
         B = m * c.n_heads
-        gemm(self.q_rot, self.k_rot, M=T, N=T, K=c.head_dim, batch=B, alpha=1.0 / 8.0,
-             C=self.scores, ldc=T, a_off=(1, T, 0), b_off=(c.rep, T, 0), c_off=(1, T * T, 0),
-             skip_upper=True)
-        _lib.call("gsq_softmax_causal", _lib.ptr(self.scores), B, T, _lib.ptr(self.P.t[0]),
-                  None, st)
-        _lib.call("gsq_transpose_bf16", _lib.ptr(self.P.t[0]), T, T, T, T * T,
-                  _lib.ptr(self.PT.t[0]), T, T * T, B, st)
+        if q0 == 0:   # square: tiles above the diagonal are never read
+            gemm(self.q_rot, self.k_rot, M=Tk, N=Tk, K=c.head_dim, batch=B, alpha=1.0 / 8.0,
+                 C=self.scores, ldc=Tk, a_off=(1, Tk, 0), b_off=(c.rep, Tk, 0),
+                 c_off=(1, Tk * Tk, 0), skip_upper=True)
+        else:         # the query rows q0.. of each (sequence, head) block of q_rot
+            qv = Terms(self.q_rot.rows - q0, c.head_dim, 3, ld=self.q_rot.ld,
+                       tensors=[x[q0:] for x in self.q_rot.t])
+            gemm(qv, self.k_rot, M=Tq, N=Tk, K=c.head_dim, batch=B, alpha=1.0 / 8.0,
+                 C=self.scores, ldc=Tk, a_off=(1, Tk, 0), b_off=(c.rep, Tk, 0),
+                 c_off=(1, Tq * Tk, 0))
+        _lib.call("gsq_softmax_causal_rows", _lib.ptr(self.scores), B, Tq, Tk, Tk, q0,
+                  _lib.ptr(self.P.t[0]), self.P.ld, st)
+        _lib.call("gsq_transpose_bf16", _lib.ptr(self.P.t[0]), Tq, Tk, self.P.ld, Tq * self.P.ld,
+                  _lib.ptr(self.PT.t[0]), self.PT.ld, Tk * self.PT.ld, B, st)
 
     def contract(self):
-        c, T, m = self.cfg, self.T, self.m
-        H, nh, nkv, hd = c.hidden, c.n_heads, c.n_kv, c.head_dim
-        nkvd = nkv * hd
+        c, m = self.cfg, self.m
+        H, nh, hd = c.hidden, c.n_heads, c.head_dim
+        Tq, Tk, q0 = self.Tq, self.Tk, self.q0
+        nkvd = c.n_kv * hd
         vname, oname = self.names
         tiles = self.sq.numel()
         st = _lib.stream_ptr()
+        B = m * nh
         for r in range(self.R):
-            gemm(self.HN, self.D[vname][r], M=T, batch=m, bias=self.v_bias, a_off=(1, T, 0),
+            gemm(self.HN, self.D[vname][r], M=Tk, batch=m, bias=self.v_bias, a_off=(1, Tk, 0),
                  ct_terms=self.VT, t_off=(1, nkvd, 0, 0, 0))
-            gemm(self.P, self.VT, M=T, N=hd, K=T, batch=m * nh, bn=64, causal=1,
-                 a_off=(1, T, 0), b_off=(c.rep, hd, 0), c_off=(nh, T * H, hd),
-                 c_terms=self.O, ct_terms=self.OT, t_off=(nh, 0, hd, T, 0))
+            gemm(self.P, self.VT, M=Tq, N=hd, K=Tk, batch=B, bn=64, causal=int(q0 == 0),
+                 a_off=(1, Tq, 0), b_off=(c.rep, hd, 0), c_off=(nh, Tq * H, hd),
+                 c_terms=self.O, ct_terms=self.OT, t_off=(nh, 0, hd, Tq, 0))
             gemm(self.O, self.D[oname][r], epi=1, target=self.A.t[0], ld_rt=self.A.ld,
-                 row_period=T, out_scale=2.0 / self.count, sq_partial=self.sq,
-                 c_terms=self.DY, ct_terms=self.DYT)
+                 row_period=Tq if q0 == 0 else 0, out_scale=2.0 / self.count,
+                 sq_partial=self.sq, c_terms=self.DY, ct_terms=self.DYT)
             _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(self.loss[r:r + 1]), st)
             gemm(self.DYT, self.OT, C=self.grad_o[r])
             for i in range(3):
                 _lib.call("gsq_transpose_bf16", _lib.ptr(self.Dbuf[oname][r][i]), H, H, H, 0,
                           _lib.ptr(self.DoT.t[i]), self.DoT.ld, 0, 1, st)
-            gemm(self.DY, self.DoT, M=T, batch=m, a_off=(1, T, 0), ct_terms=self.DOT,
+            gemm(self.DY, self.DoT, M=Tq, batch=m, a_off=(1, Tq, 0), ct_terms=self.DOT,
                  t_off=(1, H, 0, 0, 0))
-            gemm(self.PT, self.DOT, M=T, N=hd, K=T, batch=m * nh, bn=64, causal=2,
-                 a_off=(1, T, 0), b_off=(1, hd, 0), C=self.dv, ldc=hd, c_off=(1, T * hd, 0))
+            gemm(self.PT, self.DOT, M=Tk, N=hd, K=Tq, batch=B, bn=64,
+                 causal=2 if q0 == 0 else 0, a_off=(1, Tk, 0), b_off=(1, hd, 0), C=self.dv,
+                 ldc=hd, c_off=(1, Tk * hd, 0))
             t = self.DVT.t
-            _lib.call("gsq_head_group_sum_t", _lib.ptr(self.dv), m, nh, c.rep, T, _lib.ptr(t[0]),
+            _lib.call("gsq_head_group_sum_t", _lib.ptr(self.dv), m, nh, c.rep, Tk, _lib.ptr(t[0]),
                       _lib.ptr(t[1]), _lib.ptr(t[2]), self.DVT.ld, st)
             gemm(self.DVT, self.HNT, C=self.grad_v[r])
 
@@ -563,7 +624,7 @@ class StageTimer:
 
 
 def train_stage(step, stage_args_of, n_seqs, opts: BlockOpts, seed, noise_seed=None,
-                noise_of=None, timer=None, name="stage"):
+                noise_of=None, timer=None, name="stage", dp=None):
     """The stage optimiser loop (staged.py:357-400) around a vo / mlp step: schedules, the
     sorted micro-batch draw of the numpy stream, contractions, the fused update with the next
     step's forward. stage_args_of(idx) returns the arguments of step.stage for sequence ids idx.
@@ -584,6 +645,8 @@ def train_stage(step, stage_args_of, n_seqs, opts: BlockOpts, seed, noise_seed=N
         idx = np.sort(rng.choice(n_seqs, size=m, replace=False))
         step.stage(*stage_args_of(idx))
         step.contract()
+        if dp is not None:
+            dp.allreduce(step.gflat, step.loss)
         nxt = (t + 1, *gs_schedules(t + 1, opts.steps)) if t + 1 < opts.steps else None
         step.update(t, tau, kappa, opts, noise_seed, nxt=nxt, noise_of=noise_of)
         hist[t].copy_(step.loss.view(-1))  # a device copy; summed on the host at the end
@@ -605,7 +668,7 @@ def _hard_bf16(codes_t, scales16, bits, group_size):
 
 
 def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None, T=None,
-                   chunk_seqs=8, log=print, noise_of=None, timer=None):
+                   chunk_seqs=8, log=print, noise_of=None, timer=None, dp=None):
     """Quantize the seven linears of one block on the calibration stream (staged.py:405-522).
 
     h: bf16 CUDA [N*T, H], the block inputs of the N calibration sequences (the quantized
@@ -613,6 +676,9 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
     Returns (shard, stats, Wq): shard[name] = {"codes" uint8 [out, in], "scales" float16, "bits"},
     Wq the bf16 hard weights of the block. Each stage: GPTQ warm start from the Hessian of its
     real input, Lion training of logits and group scales, hardening (argmax codes, fp16 scales).
+    dp: a DataParallel over the ranks of a process group (each rank computes its position
+    window of every micro-batch sequence; the stage gradients are summed over the ranks); the
+    Hessian passes and GPTQ run on every rank alike, so every rank returns the same result.
     """
     from .e2e import BlockConfig, BlockWeights, LIN_ORDER, Qwen2Block
     from .gptq import gptq_factor, quantize_gptq
@@ -694,7 +760,8 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
     H_hn = hessian("hn", W_fp, keep_hn)
     qk = [gptq(n, H_hn, i) for i, n in enumerate(STAGE_LAYERS["qk"])]
     qk_lins = [l for l in qk if l is not None]
-    hist, ms = train_linears(qk_lins, hn_all.view(N, T, H), Wf, N, opts, seed + 1,
+    dp = dp or DataParallel()
+    hist, ms = train_linears(qk_lins, hn_all.view(N, T, H), Wf, N, opts, seed + 1, dp=dp,
                              exact_bf16_rows=True, noise_of=noise_of, timer=timer,
                              name="qk") if qk_lins else ([], None)
     for lin in qk_lins:
@@ -722,9 +789,10 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
         gemm(_bf16_rows(hn_all[a * T:(a + s) * T]), wterms(Wc.qk), epi=4, bias=Wc.qk_bias,
              c_terms=_bf16_rows(qk_all[a * T:(a + s) * T]))
     if len(vo_lins) == 2:
-        vstep = VOStep(vo_lins, cfg, min(opts.micro_batch, N), T, opts.resamples, W["v_bias"])
+        vstep = VOStep(vo_lins, cfg, min(opts.micro_batch, N), T, opts.resamples, W["v_bias"],
+                       window=dp.window(0, T))
         hist, ms = train_stage(vstep, lambda idx: (hn_all, A_all, qk_all, idx), N, opts,
-                               seed + 2, noise_of=noise_of, timer=timer, name="vo")
+                               seed + 2, noise_of=noise_of, timer=timer, name="vo", dp=dp)
     else:
         hist, ms = [], None  # an 8-bit v or o keeps its GPTQ values (not trained here)
     for lin in vo_lins:
@@ -746,9 +814,10 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
     down = gptq("down_proj", H_d, 6)
     mlp_lins = [l for l in (gate, up, down) if l is not None]
     if len(mlp_lins) == 3:
-        mstep = MLPStep(mlp_lins, cfg, min(opts.micro_batch, N), T, opts.resamples)
+        mstep = MLPStep(mlp_lins, cfg, min(opts.micro_batch, N), T, opts.resamples,
+                        window=dp.window(1, T))
         hist, ms = train_stage(mstep, lambda idx: (mn_all, h1_all, Y_all, idx), N, opts,
-                               seed + 3, noise_of=noise_of, timer=timer, name="mlp")
+                               seed + 3, noise_of=noise_of, timer=timer, name="mlp", dp=dp)
     else:
         hist, ms = [], None
     for lin in mlp_lins:

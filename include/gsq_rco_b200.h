@@ -250,6 +250,13 @@ int gsq_rope_split(const void *x, int64_t ld_x, int S, int T, int nh, const floa
  * Replaces src/gsq_rco/gsq/e2e.py:149-154 (mask, softmax, cast to bf16). */
 int gsq_softmax_causal(const float *S, int B, int T, void *P, void *PT, void *stream);
 
+/* Row window of the causal softmax (data-parallel query rows): local row i of batch z is query
+ * position row0 + i and sees keys k <= row0 + i of the cols stored (row0 + rows <= cols).
+ * S float32 [B][rows][ld_s] -> P bf16 [B][rows][ld_p], masked keys k < cols written as 0.
+ * Same arithmetic as gsq_softmax_causal (src/gsq_rco/gsq/e2e.py:149-155). */
+int gsq_softmax_causal_rows(const float *S, int B, int rows, int cols, int64_t ld_s, int row0,
+                            void *P, int64_t ld_p, void *stream);
+
 /* out[r] = E[ids[r]] (bf16 rows of H). Replaces the embedding lookup of the calibration
  * stream (src/gsq_rco/gsq/pipeline.py's block inputs, e2e.py:64-74). */
 int gsq_embed(const int32_t *ids, int64_t n, const void *E, int H, void *out, void *stream);
