@@ -328,6 +328,31 @@ int mckp_dp_f64(const double *scores, const int64_t *step, int n_inst, int N, in
 int mckp_dp_f64_noalloc(const double *scores, const int64_t *step, int n_inst, int N, int K,
                         int64_t budget, int32_t *z_out, void *stream);
 
+/* ------------------------------------------------------------ RCO objective -------- */
+
+/* Row pass of the tied-embedding KL head (src/gsq_rco/common/evaluate.py:111-151,
+ * kl_value_and_grad_hidden / _kl_chunk_value_grad): zq, zr bf16 [n][ld] logits (bf16(h E^T) of the
+ * quantized and the reference stream, V = vocabulary, V % 8 == 0, 16-byte aligned rows). Per
+ * row: lse = logsumexp(z) (float32, float64 sum of exp), q = exp(zq - lse_q),
+ * p = exp(zr - lse_r), kl_rows[r] = sum p (zr - lse_r - zq + lse_q) (float64), D = bf16(q - p)
+ * [n][ld_d] (the logit gradient; dKL/dh_q = D E by a tensor-core GEMM). lse: optional float32
+ * [n][2] (lse_q, lse_r). The logit GEMMs and D E run through gsq_gemm (epi 4). */
+int gsq_kl_rows(const void *zq, const void *zr, int n, int V, int64_t ld, void *D, int64_t ld_d,
+                double *kl_rows, float *lse, void *stream);
+
+/* x = bf16(f32(x) / divisor) for n bf16 elements (the head gradient's mean over positions,
+ * evaluate.py:150). */
+int gsq_div_bf16(void *x, int64_t n, float divisor, void *stream);
+
+/* Straight-through upstream of one linear (src/gsq_rco/rco/allocate.py:169-174, _dots):
+ * out[k] = sum G * (f32(bf16(scales_k[r][c / gs] * grid_k[codes_k[r, c]])) - f32(W[r, c])) in
+ * float64 for the K <= 8 database options (codes_k uint8 [out][in], scales_k float32
+ * [out][ceil(in / gs)], bits_k in 1..8). G float32 [out][in] = dL/dW, W bf16 [out][in] the
+ * reference weight. partials: >= max_blocks * K doubles. */
+int ste_dots(const float *G, const void *W, int out_f, int in_f, int group_size, int K,
+             const uint8_t *const *codes, const float *const *scales, const int *bits,
+             double *partials, int max_blocks, double *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
