@@ -43,7 +43,8 @@ enum Epi {
   EPI_SWIGLU_FWD = 2,
   EPI_SWIGLU_BWD = 3,
   EPI_BF16 = 4,        // bf16 chain: x = bf16(acc); x = bf16(x + bias); x = bf16(resid + x)
-  EPI_SWIGLU_BF16 = 5  // bf16 SwiGLU: g, u = bf16(acc); bf16(bf16(g bf16(sigmoid(g))) u)
+  EPI_SWIGLU_BF16 = 5,  // bf16 SwiGLU: g, u = bf16(acc); bf16(bf16(g bf16(sigmoid(g))) u)
+  EPI_SWIGLU_BWD_BF16 = 6  // its backward with bf16 cotangents (dd = bf16(acc), g, u from aux)
 };
 
 struct Aff {
@@ -355,8 +356,27 @@ __device__ __forceinline__ double epilogue_out(const GemmParams& p, const TileIn
       }
     } else {
 #pragma unroll
+      for (int u = 0; u < 64; ++u) acc[u] = bf16r(acc[u]);
+      if (p.aux0) {
+        // bf16 g and u (float32 storage) for the backward
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          stage_put(stg, lane, acc + 32 * part);
+          float* dst = part ? p.aux1 : p.aux0;
+#pragma unroll 4
+          for (int i = 0; i < 16; ++i) {
+            const int r = 2 * i + (lane >> 4), c = 2 * (lane & 15);
+            const int row = row0 + r, j = n0 + c;
+            if (row < p.M && j < nl)
+              store_f2(dst + coff + (int64_t)row * p.ld_aux + j, stg[r * kStgLd + c],
+                       stg[r * kStgLd + c + 1], j + 1 < nl, p.pair_aux != 0);
+          }
+          __syncwarp();
+        }
+      }
+#pragma unroll
       for (int u = 0; u < 32; ++u) {
-        const float g = bf16r(acc[u]), uu = bf16r(acc[32 + u]);
+        const float g = acc[u], uu = acc[32 + u];
         acc[u] = bf16r(__fmul_rn(bf16r(__fmul_rn(g, bf16r(sigmoid_f(g)))), uu));
       }
     }
@@ -373,6 +393,64 @@ __device__ __forceinline__ double epilogue_out(const GemmParams& p, const TileIn
     }
     if (p.nct > 0) transposed_pass(p, t, stg, lane, n0, nl, row0, 0);
     __syncwarp();
+  } else if (EPI == EPI_SWIGLU_BWD_BF16) {
+    // slots hold the cotangent of d = bf16(a u) (a = bf16(g s), s = bf16(sigmoid g)) of column n;
+    // with g, u (bf16 values) from aux: du = bf16(dd a), da = bf16(dd u), ds = bf16(da g),
+    // dg = bf16(da s + ds sigmoid(g) (1 - sigmoid(g))). dg / du go out as row terms at columns n
+    // and n + ct_up_rows, and transposed at rows n and n + ct_up_rows.
+#pragma unroll
+    for (int jc = 0; jc < kNC; ++jc) {
+      const int n0 = t.tile_n + 64 * jc + 32 * h;
+      stage_put(stg, lane, acc + 32 * jc);
+      float du_keep[32];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int r = 2 * i + (lane >> 4), c = 2 * (lane & 15);
+        const int row = row0 + r, n = n0 + c;
+        float* sp = stg + r * kStgLd + c;
+        float dg[2] = {0.f, 0.f}, du[2] = {0.f, 0.f};
+        const bool in0 = row < p.M && n < p.N, in1 = in0 && n + 1 < p.N;
+        if (in0) {
+          const int64_t o = coff + (int64_t)row * p.ld_aux + n;
+          float g[2], u[2];
+          load_f2(p.aux0 + o, in1, p.pair_aux != 0, g[0], g[1]);
+          load_f2(p.aux1 + o, in1, p.pair_aux != 0, u[0], u[1]);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float dd = bf16r(sp[e]);
+            const float sf = sigmoid_f(g[e]);
+            const float sb = bf16r(sf);
+            const float a = bf16r(__fmul_rn(g[e], sb));
+            du[e] = bf16r(__fmul_rn(dd, a));
+            const float da = bf16r(__fmul_rn(dd, u[e]));
+            const float ds = bf16r(__fmul_rn(da, g[e]));
+            dg[e] = bf16r(__fadd_rn(__fmul_rn(da, sb),
+                                    __fmul_rn(ds, __fmul_rn(sf, __fsub_rn(1.0f, sf)))));
+          }
+          if (p.ncs > 0) {
+            const int64_t oc = coff + (int64_t)row * p.ldcs + n;
+            store_terms2(p.cs, 1, oc, dg[0], dg[1], in1, p.pair_cs != 0);
+            store_terms2(p.cs, 1, oc + p.ct_up_rows, du[0], du[1], in1, p.pair_cs != 0);
+          }
+        }
+        sp[0] = dg[0];
+        sp[1] = dg[1];
+        du_keep[2 * i] = du[0];
+        du_keep[2 * i + 1] = du[1];
+      }
+      __syncwarp();
+      if (p.nct > 0) transposed_pass(p, t, stg, lane, n0, p.N, row0, 0);
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int r = 2 * i + (lane >> 4), c = 2 * (lane & 15);
+        stg[r * kStgLd + c] = du_keep[2 * i];
+        stg[r * kStgLd + c + 1] = du_keep[2 * i + 1];
+      }
+      __syncwarp();
+      if (p.nct > 0) transposed_pass(p, t, stg, lane, n0, p.N, row0, p.ct_up_rows);
+      __syncwarp();
+    }
   } else {  // EPI_SWIGLU_BWD: slots hold dd = dL/d(silu(g) u) of column n; dL/dg and dL/du go
             // out transposed (planes 0 and 1 of the C^T terms)
 #pragma unroll
@@ -739,7 +817,7 @@ static int launch(GemmParams& p, int batch, cudaStream_t st) {
   p.tiles_n = (p.N + BN - 1) / BN;
   p.total_tiles = (int64_t)p.tiles_m * p.tiles_n * batch * p.splits;
   const size_t smem = 1024 + (size_t)S * stage_bytes + kStgBytes;
-  static bool attr_set[2][6] = {{false}};
+  static bool attr_set[2][7] = {{false}};
   bool& done = attr_set[BN == 128][EPI];
   if (!done) {
     if (cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>,
@@ -788,7 +866,7 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   const int M = d->M, N = d->N, K = d->K;
   if (M <= 0 || N <= 0 || K <= 0 || d->batch < 1 || d->batch > 65535 || d->na < 1 ||
       d->na > 3 || d->nb < 1 || d->nb > 3 || d->order < 0 || !d->err || d->ncs < 0 ||
-      d->ncs > 3 || d->nct < 0 || d->nct > 3 || d->epi < 0 || d->epi > 5)
+      d->ncs > 3 || d->nct < 0 || d->nct > 3 || d->epi < 0 || d->epi > 6)
     return GSQ_EINVAL;
   if (d->bn != 64 && d->bn != 128) return GSQ_EINVAL;
   const int epi = d->epi;
@@ -802,7 +880,10 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   for (int i = 0; i < d->nct; ++i)
     if (!d->ct[i] || ((uintptr_t)d->ct[i] & 15)) return GSQ_EINVAL;
   if (epi == 1 && !d->target) return GSQ_EINVAL;
-  if ((epi == 2 || epi == 3) && (!d->aux0 || !d->aux1 || d->bn != 128)) return GSQ_EINVAL;
+  if ((epi == 2 || epi == 3 || epi == 6) && (!d->aux0 || !d->aux1 || d->bn != 128))
+    return GSQ_EINVAL;
+  if (epi == 5 && (!d->aux0) != (!d->aux1)) return GSQ_EINVAL;
+  if (epi == 6 && (d->ncs > 1 || d->nct > 1)) return GSQ_EINVAL;
   if ((epi == 2 || epi == 5) && (!d->b2[0] || (N % 128) != 0 || d->bn != 128)) return GSQ_EINVAL;
   if (d->causal < 0 || d->causal > 2 || (d->causal && d->K < M)) return GSQ_EINVAL;
   const int splits = d->split_k > 1 ? d->split_k : 1;
@@ -884,7 +965,8 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
     case 2: return tc::launch<128, 2>(p, d->batch, st);
     case 3: return tc::launch<128, 3>(p, d->batch, st);
     case 4: return tc::launch<128, 4>(p, d->batch, st);
-    default: return tc::launch<128, 5>(p, d->batch, st);
+    case 5: return tc::launch<128, 5>(p, d->batch, st);
+    default: return tc::launch<128, 6>(p, d->batch, st);
   }
 }
 

@@ -250,7 +250,7 @@ def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, 
     d.ld_rt = (d.N if ld_rt is None else ld_rt)
     d.out_scale = out_scale
     d.aux0, d.aux1 = _tp(aux0), _tp(aux1)
-    d.ld_aux = (d.N // 2 if epi == 2 else d.N) if ld_aux is None else ld_aux
+    d.ld_aux = (d.N // 2 if epi in (2, 5) else d.N) if ld_aux is None else ld_aux
     d.skip_upper = int(skip_upper)
     d.row_period = int(row_period)
     splittable = (epi == 0 and batch == 1 and not causal and C is not None and bias is None

@@ -77,6 +77,23 @@ class BlockWeights:
         W.update(kw)
         return BlockWeights(W)
 
+    def transposed(self, key):
+        """K-major transposed copies for the backward GEMMs (made once, cached): "down" Wd^T
+        [I, H], "gate_up" [Wg; Wu]^T [H, 2I], "o" Wo^T [nh hd, H], "qkv" [Wq; Wk; Wv]^T
+        [H, (nh + 2 nkv) hd]."""
+        cache = self.__dict__.setdefault("_T", {})
+        if key not in cache:
+            w = self.W
+            src = {"down": w["down_proj"], "o": w["o_proj"],
+                   "gate_up": torch.cat([w["gate_proj"], w["up_proj"]]),
+                   "qkv": torch.cat([w["q_proj"], w["k_proj"], w["v_proj"]])}[key].contiguous()
+            r, c = src.shape
+            t = Terms(c, r, 1, src.device)
+            _lib.call("gsq_transpose_bf16", _lib.ptr(src), r, c, c, 0, _lib.ptr(t.t[0]), t.ld, 0,
+                      1, _lib.stream_ptr())
+            cache[key] = t
+        return cache[key]
+
 
 class Qwen2Block:
     """Buffers and launches of the block forward for chunks of up to S sequences of T."""
@@ -150,7 +167,7 @@ class Qwen2Block:
              ct_terms=o_tap, t_off=(c.n_heads, 0, c.head_dim, T, 0))
 
     def forward(self, h, W: BlockWeights, S=None, out=None, taps=(), attn_out=None, upto=None,
-                mn=None):
+                mn=None, gu=None):
         """Block forward of S sequences h bf16 [S*T, H] -> out bf16 [S*T, H]. taps: names of
         TAPS to write transposed (self.tap(name)), position-0 columns zeroed.
         attn_out: also the attention output after o_proj (no residual; the vo-stage target);
@@ -190,15 +207,18 @@ class Qwen2Block:
                   _lib.ptr(mn_tap.t[0] if mn_tap else None), mn_tap.ld if mn_tap else 0, T, 1, st)
         if upto == "mn":
             return None
-        return self._mlp(self.h1[:R], self.mn[:R], W, R, T, st, out, taps, upto)
+        return self._mlp(self.h1[:R], self.mn[:R], W, R, T, st, out, taps, upto, gu)
 
-    def _mlp(self, h1, mn, W: BlockWeights, R, T, st, out, taps, upto):
-        """out = h1 + down(SwiGLU(mn)) (bf16 chain); the d_in tap if asked."""
+    def _mlp(self, h1, mn, W: BlockWeights, R, T, st, out, taps, upto, gu=None):
+        """out = h1 + down(SwiGLU(mn)) (bf16 chain); the d_in tap if asked; gu = (g, u) float32
+        buffers receive the bf16 gate / up values (for the backward)."""
         c = self.cfg
         d_tap = self.tap("d_in") if "d_in" in taps else None
         MNt = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[mn])
         gemm(MNt, wterms(W.W["gate_proj"]), B2=wterms(W.W["up_proj"]), epi=5,
-             c_terms=Terms(R, c.inter, 1, ld=c.inter, tensors=[self.d_in[:R]]), ct_terms=d_tap)
+             c_terms=Terms(R, c.inter, 1, ld=c.inter, tensors=[self.d_in[:R]]), ct_terms=d_tap,
+             aux0=None if gu is None else gu[0], aux1=None if gu is None else gu[1],
+             ld_aux=c.inter)
         if d_tap is not None:
             _lib.call("gsq_zero_cols", _lib.ptr(d_tap.t[0]), c.inter, d_tap.ld, R, T, st)
         if upto == "d_in":
@@ -208,6 +228,153 @@ class Qwen2Block:
         gemm(Dt, wterms(W.W["down_proj"]), epi=4, resid=h1, ld_rt=c.hidden,
              c_terms=Terms(R, c.hidden, 1, ld=c.hidden, tensors=[out]))
         return out
+
+    # ------------------------------------------------------------------------ backward ---
+    def _bwd_buffers(self, S):
+        """Work buffers of vjp for S sequences (allocated on first use, reused)."""
+        key = ("bwd", S)
+        if getattr(self, "_bwd_key", None) == key:
+            return self._bwd
+        c, T, dev = self.cfg, self.T, self.dev
+        R, H, I, hd = S * T, c.hidden, c.inter, c.head_dim
+        QD, KD = c.n_heads * hd, c.n_kv * hd
+        B = S * c.n_heads
+        bf = torch.bfloat16
+        b = {
+            "g": torch.empty(R, I, device=dev), "u": torch.empty(R, I, device=dev),
+            "out": torch.empty(R, H, device=dev, dtype=bf),
+            "dGU": torch.empty(R, 2 * I, device=dev, dtype=bf), "dGUT": Terms(2 * I, R, 1, dev),
+            "dmn": torch.empty(R, H, device=dev, dtype=bf),
+            "dh1": torch.empty(R, H, device=dev, dtype=bf),
+            "doh": torch.empty(B * T, hd, device=dev, dtype=bf), "doT": Terms(B * hd, T, 1, dev),
+            "vrows": torch.empty(S * c.n_kv * T, hd, device=dev, dtype=bf),
+            "dP": torch.empty(B * T, T, device=dev, dtype=bf),
+            "dS": Terms(B * T, T, 3, dev), "dST": Terms(B * T, T, 3, dev),
+            "PT": Terms(B * T, T, 1, dev),
+            "qT": Terms(B * hd, T, 3, dev), "kT": Terms(S * c.n_kv * hd, T, 3, dev),
+            "dqr": torch.empty(B * T, hd, device=dev), "dkr": torch.empty(B * T, hd, device=dev),
+            "dvh": torch.empty(B * T, hd, device=dev),
+            "dk": torch.empty(S * c.n_kv * T, hd, device=dev),
+            "dQKV": torch.empty(R, QD + 2 * KD, device=dev, dtype=bf),
+            "dQKVT": Terms(QD + 2 * KD, R, 1, dev),
+            "dhn": torch.empty(R, H, device=dev, dtype=bf),
+            # transposed activations (K-major operands of the weight gradients)
+            "cotT": Terms(H, R, 1, dev), "dT": Terms(I, R, 1, dev), "mnT": Terms(H, R, 1, dev),
+            "dh1T": Terms(H, R, 1, dev), "oT": Terms(QD, R, 1, dev), "hnT": Terms(H, R, 1, dev),
+        }
+        self._bwd_key, self._bwd = key, b
+        return b
+
+    def _T(self, x, rows, cols, ld, out, ld_out=None, batch=1, bs_in=0, bs_out=0):
+        """out[z] = x[z]^T (bf16): out a Terms (term 0, its ld) or a tensor with ld_out."""
+        if isinstance(out, Terms):
+            out, ld_out = out.t[0], out.ld
+        _lib.call("gsq_transpose_bf16", _lib.ptr(x), rows, cols, ld, bs_in, _lib.ptr(out),
+                  ld_out, bs_out, batch, _lib.stream_ptr())
+
+    def new_grads(self, W: BlockWeights):
+        """Zeroed float32 weight gradients of the seven linears; gate / up and q / k / v are views
+        of one stacked buffer each (the layouts the weight-gradient GEMMs write)."""
+        c, dev = self.cfg, self.dev
+        H, I = c.hidden, c.inter
+        QD, KD = c.n_heads * c.head_dim, c.n_kv * c.head_dim
+        gu = torch.zeros(2 * I, H, device=dev)
+        qkv = torch.zeros(QD + 2 * KD, H, device=dev)
+        return {"_gu": gu, "_qkv": qkv, "gate_proj": gu[:I], "up_proj": gu[I:],
+                "q_proj": qkv[:QD], "k_proj": qkv[QD:QD + KD], "v_proj": qkv[QD + KD:],
+                "o_proj": torch.zeros(H, QD, device=dev),
+                "down_proj": torch.zeros(H, I, device=dev)}
+
+    def vjp(self, h, W: BlockWeights, cot, S=None, dh=None, grads=None, accumulate=False):
+        """Vector-Jacobian product of the block (the RCO objective's _layer_vjp,
+        src/gsq_rco/rco/allocate.py:156-167, of the block of e2e.py:160-174): h, cot bf16
+        [S*T, H] (block input, cotangent of the block output) -> dh bf16 [S*T, H] (cotangent of
+        the input) and the float32 weight gradients grads[name] [out, in] (added to when
+        accumulate, e.g. over chunks). Cotangents of bf16 forward tensors are rounded to bf16,
+        those of the float32 scores and RoPE'd q / k stay float32."""
+        c, T = self.cfg, self.T
+        S = self.S if S is None else S
+        R, H, I, hd = S * T, c.hidden, c.inter, c.head_dim
+        nh, nkv, rep = c.n_heads, c.n_kv, c.rep
+        QD, KD = nh * hd, nkv * hd
+        B = S * nh
+        st = _lib.stream_ptr()
+        b = self._bwd_buffers(S)
+        dev = self.dev
+        if grads is None:
+            grads = self.new_grads(W)
+        beta = 1.0 if accumulate else 0.0
+        dh = torch.empty(R, H, device=dev, dtype=torch.bfloat16) if dh is None else dh
+        # forward recompute, keeping the intermediates (and bf16 g, u)
+        self.forward(h, W, S=S, out=b["out"][:R], gu=(b["g"][:R], b["u"][:R]))
+        rows = lambda x, n=None: Terms(x.shape[0] if n is None else n, x.shape[1], 1,
+                                       ld=x.shape[1], tensors=[x if n is None else x[:n]])
+        # transposed activations
+        self._T(cot, R, H, H, b["cotT"])
+        self._T(self.d_in, R, I, I, b["dT"])
+        self._T(self.mn, R, H, H, b["mnT"])
+        self._T(self.o, R, QD, QD, b["oT"])
+        self._T(self.hn, R, H, H, b["hnT"])
+        # MLP: dd = bf16(cot Wd) with the SwiGLU backward in the epilogue
+        gemm(rows(cot), W.transposed("down"), epi=6, aux0=b["g"], aux1=b["u"], ld_aux=I,
+             c_terms=Terms(R, 2 * I, 1, ld=2 * I, tensors=[b["dGU"][:R]]), ct_terms=b["dGUT"],
+             ct_up_rows=I)
+        gemm(rows(b["dGU"], R), W.transposed("gate_up"), epi=4, c_terms=rows(b["dmn"], R))
+        gemm(b["dGUT"], b["mnT"], M=2 * I, N=H, K=R, C=grads["_gu"], beta=beta)
+        gemm(b["cotT"], b["dT"], M=H, N=I, K=R, C=grads["down_proj"], beta=beta)
+        _lib.call("gsq_rmsnorm_bwd", _lib.ptr(self.h1), H, _lib.ptr(W.W["post_norm"]),
+                  _lib.ptr(b["dmn"]), H, _lib.ptr(cot), H, _lib.ptr(b["dh1"]), H, R, H,
+                  float(c.eps), st)
+        # o_proj: do per (sequence, head) = bf16(dh1 Wo[:, h]) and its transpose
+        self._T(b["dh1"], R, H, H, b["dh1T"])
+        gemm(b["dh1T"], b["oT"], M=H, N=QD, K=R, C=grads["o_proj"], beta=beta)
+        gemm(rows(b["dh1"], R), W.transposed("o"), M=T, N=hd, K=H, batch=B, bn=64, epi=4,
+             a_off=(nh, T, 0), b_off=(nh, 0, hd),
+             c_terms=Terms(B * T, hd, 1, ld=hd, tensors=[b["doh"]]), c_off=(1, T * hd, 0),
+             ct_terms=b["doT"], t_off=(1, hd, 0, 0, 0))
+        # attention: dP = bf16(do v^T); dS; dq, dk (float32); dv
+        self._T(self.vT.t[0], hd, T, self.vT.ld, b["vrows"], hd, batch=S * nkv,
+                bs_in=hd * self.vT.ld, bs_out=T * hd)
+        gemm(Terms(B * T, hd, 1, ld=hd, tensors=[b["doh"]]),
+             Terms(S * nkv * T, hd, 1, ld=hd, tensors=[b["vrows"]]), M=T, N=T, K=hd, batch=B,
+             epi=4, a_off=(1, T, 0), b_off=(rep, T, 0),
+             c_terms=Terms(B * T, T, 1, ld=T, tensors=[b["dP"]]), c_off=(1, T * T, 0),
+             skip_upper=True)
+        dS, dST = b["dS"], b["dST"]
+        _lib.call("gsq_softmax_bwd", _lib.ptr(self.scores), _lib.ptr(b["dP"]), B, T, T,
+                  _lib.ptr(dS.t[0]), _lib.ptr(dS.t[1]), _lib.ptr(dS.t[2]), dS.ld, 0.125, st)
+        for i in range(3):
+            self._T(dS.t[i], T, T, dS.ld, dST.t[i], dST.ld, batch=B, bs_in=T * dS.ld,
+                    bs_out=T * dST.ld)
+            self._T(self.q_rot.t[i], T, hd, self.q_rot.ld, b["qT"].t[i], b["qT"].ld, batch=B,
+                    bs_in=T * self.q_rot.ld, bs_out=hd * b["qT"].ld)
+            self._T(self.k_rot.t[i], T, hd, self.k_rot.ld, b["kT"].t[i], b["kT"].ld,
+                    batch=S * nkv, bs_in=T * self.k_rot.ld, bs_out=hd * b["kT"].ld)
+        self._T(self.P.t[0], T, T, self.P.ld, b["PT"], batch=B, bs_in=T * self.P.ld,
+                bs_out=T * b["PT"].ld)
+        gemm(dS, b["kT"], M=T, N=hd, K=T, batch=B, bn=64, causal=1, a_off=(1, T, 0),
+             b_off=(rep, hd, 0), C=b["dqr"], ldc=hd, c_off=(1, T * hd, 0))
+        gemm(dST, b["qT"], M=T, N=hd, K=T, batch=B, bn=64, causal=2, a_off=(1, T, 0),
+             b_off=(1, hd, 0), C=b["dkr"], ldc=hd, c_off=(1, T * hd, 0))
+        gemm(b["PT"], b["doT"], M=T, N=hd, K=T, batch=B, bn=64, causal=2, a_off=(1, T, 0),
+             b_off=(1, hd, 0), C=b["dvh"], ldc=hd, c_off=(1, T * hd, 0))
+        QKV = QD + 2 * KD
+        dQKV = b["dQKV"]
+        _lib.call("gsq_rope_bwd", _lib.ptr(b["dqr"]), hd, S, T, nh, _lib.ptr(self.cos),
+                  _lib.ptr(self.sin), _lib.ptr(dQKV), QKV, 0, st)
+        _lib.call("gsq_group_sum", _lib.ptr(b["dkr"]), hd, S, nh, rep, T, _lib.ptr(b["dk"]),
+                  None, 0, 0, st)
+        _lib.call("gsq_rope_bwd", _lib.ptr(b["dk"]), hd, S, T, nkv, _lib.ptr(self.cos),
+                  _lib.ptr(self.sin), _lib.ptr(dQKV), QKV, QD, st)
+        _lib.call("gsq_group_sum", _lib.ptr(b["dvh"]), hd, S, nh, rep, T, None,
+                  _lib.ptr(dQKV), QKV, QD + KD, st)
+        # q / k / v projections and the input norm
+        self._T(dQKV, R, QKV, QKV, b["dQKVT"])
+        gemm(rows(dQKV, R), W.transposed("qkv"), epi=4, c_terms=rows(b["dhn"], R))
+        gemm(b["dQKVT"], b["hnT"], M=QKV, N=H, K=R, C=grads["_qkv"], beta=beta)
+        _lib.call("gsq_rmsnorm_bwd", _lib.ptr(h), H, _lib.ptr(W.W["in_norm"]), _lib.ptr(b["dhn"]),
+                  H, _lib.ptr(b["dh1"]), H, _lib.ptr(dh), H, R, H, float(c.eps), st)
+        return dh, grads
 
     def hessian_add(self, name, H, n, S=None):
         """Fold X^T X of tap `name` (positions 1.. of S sequences) into the float64 Hessian

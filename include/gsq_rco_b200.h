@@ -175,7 +175,11 @@ typedef struct {
  *        x = bf16(resid[m, n] + x) if resid -> C (float32 of the bf16 value), cs, ct (1 term
  *        each is the bf16 value itself).
  * epi 5: bf16 SwiGLU (b / b2 as in epi 2): g, u = bf16(acc); bf16(bf16(g bf16(sigmoid(g))) u)
- *        -> cs, ct.
+ *        -> cs, ct; with aux0 / aux1 also g, u (bf16 values, float32 [M][ld_aux]).
+ * epi 6: its backward with bf16 cotangents: dd = bf16(acc) of column n, g, u from aux0 / aux1;
+ *        s = bf16(sigmoid g), a = bf16(g s): du = bf16(dd a), da = bf16(dd u), ds = bf16(da g),
+ *        dg = bf16(da s + ds sigmoid(g)(1 - sigmoid(g))) -> cs (1 term) at columns n and
+ *        n + ct_up_rows, ct (1 term) at rows n and n + ct_up_rows.
  * Replaces the block matmuls of src/gsq_rco/gsq/e2e.py:132-134,155,166,170,173 in the stage
  * losses of src/gsq_rco/gsq/staged.py:332-354 and their MLX backward. */
 int gsq_gemm(const gsq_gemm_desc *desc, void *stream);
@@ -352,6 +356,33 @@ int gsq_div_bf16(void *x, int64_t n, float divisor, void *stream);
 int ste_dots(const float *G, const void *W, int out_f, int in_f, int group_size, int K,
              const uint8_t *const *codes, const float *const *scales, const int *bits,
              double *partials, int max_blocks, double *out, void *stream);
+
+/* ------------------------------------------------ decoder block backward (RCO) ------ */
+/* The per-layer vjp of the RCO objective (src/gsq_rco/rco/allocate.py:156-167): cotangents of
+ * bf16 forward tensors are rounded to bf16, float32 ones (scores, RoPE'd q / k) stay float32. */
+
+/* out = bf16(resid + bf16(dx)) with dx the cotangent of x for the RMSNorm y = (x inv) w
+ * (e2e.py:90-93), inv = 1 / sqrt(mean x^2 + eps) in float64; resid may be NULL. bf16 rows. */
+int gsq_rmsnorm_bwd(const void *x, int64_t ld_x, const void *w, const void *dy, int64_t ld_dy,
+                    const void *resid, int64_t ld_r, void *out, int64_t ld_o, int rows, int H,
+                    double eps, void *stream);
+
+/* dS = scale Pf (dP - sum_k dP Pf) of the causal softmax Pf = softmax(S) (recomputed from the
+ * float32 scores S [B*T][T] as gsq_softmax_causal does), dP bf16 [B*T][ld_p]; dS as three bf16
+ * terms [B*T][ld_o] (zeros for keys > query). e2e.py:149-155 backward. */
+int gsq_softmax_bwd(const float *S, const void *dP, int B, int T, int64_t ld_p, void *o0,
+                    void *o1, void *o2, int64_t ld_o, float scale, void *stream);
+
+/* RoPE backward (e2e.py:103-108): dy float32 [(s nh + h) T + t][ld_i] (64 per head) ->
+ * bf16(rotation^T dy) at out[s T + t][col0 + h 64 + d]. */
+int gsq_rope_bwd(const float *dy, int64_t ld_i, int S, int T, int nh, const float *cosv,
+                 const float *sinv, void *out, int64_t ld_o, int col0, void *stream);
+
+/* GQA cotangent sum (e2e.py:146-148 backward): in float32 [(s nh + h) T + t][ld_i] summed over
+ * the rep query heads of each kv head -> out_f float32 [(s nkv + kv) T + t][64] and / or out_b
+ * bf16 at [s T + t][col0 + kv 64 + d] (ld_o). */
+int gsq_group_sum(const float *in, int64_t ld_i, int S, int nh, int rep, int T, float *out_f,
+                  void *out_b, int64_t ld_o, int col0, void *stream);
 
 #ifdef __cplusplus
 }
