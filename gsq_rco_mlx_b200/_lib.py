@@ -43,6 +43,7 @@ SIGNATURES = {
     "gsq_softmax_causal_rows": [_vp, _i32, _i32, _i32, _i64, _i32, _vp, _i64, _vp],
     "gsq_kl_rows": [_vp, _vp, _i32, _i32, _i64, _vp, _i64, _vp, _vp, _vp],
     "gsq_div_bf16": [_vp, _i64, _f32, _vp],
+    "gsq_dequant_bf16": [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp],
     "gsq_rmsnorm_bwd": [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _f64, _vp],
     "gsq_softmax_bwd": [_vp, _vp, _i32, _i32, _i64, _vp, _vp, _vp, _i64, _f32, _vp],
     "gsq_rope_bwd": [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _i64, _i32, _vp],

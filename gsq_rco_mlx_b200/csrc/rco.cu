@@ -195,9 +195,37 @@ __global__ void div_bf16_kernel(__nv_bfloat16* __restrict__ x, int64_t n, float 
     x[i] = __float2bfloat16_rn(__fdiv_rn(__bfloat162float(x[i]), divisor));
 }
 
+// w = bf16(scales[r][c / gs] grid[codes[r, c]]): an assembled database weight in the model dtype
+// (database.py:244-256 dequant, then allocate.py:117 astype(bf16)).
+__global__ void dequant_bf16_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ sc,
+                                    int out_f, int in_f, int bits, int gs,
+                                    __nv_bfloat16* __restrict__ w) {
+  const int64_t d = (int64_t)out_f * in_f;
+  const int ng = (in_f + gs - 1) / gs;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < d;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(e / in_f), c = (int)(e - (int64_t)r * in_f);
+    w[e] = __float2bfloat16_rn(__fmul_rn(grid_value(bits, codes[e]), sc[(int64_t)r * ng + c / gs]));
+  }
+}
+
 }  // namespace gsq
 
 using namespace gsq;
+
+extern "C" int gsq_dequant_bf16(const uint8_t* codes, const float* scales, int out_f, int in_f,
+                                int bits, int group_size, void* w, void* stream) {
+  if (!codes || !scales || !w || out_f <= 0 || in_f <= 0 || bits < 1 || bits > 8 ||
+      group_size <= 0)
+    return GSQ_EINVAL;
+  const int64_t d = (int64_t)out_f * in_f;
+  int64_t b = (d + 255) / 256;
+  if (b > (int64_t)num_sms() * 16) b = (int64_t)num_sms() * 16;
+  dequant_bf16_kernel<<<(unsigned)b, 256, 0, (cudaStream_t)stream>>>(
+      codes, scales, out_f, in_f, bits, group_size, (__nv_bfloat16*)w);
+  GSQ_CHECK_LAUNCH();
+  return GSQ_OK;
+}
 
 extern "C" int gsq_div_bf16(void* x, int64_t n, float divisor, void* stream) {
   if (!x || n <= 0 || !(divisor != 0.f)) return GSQ_EINVAL;

@@ -65,11 +65,13 @@ class DBSpec:
 
 @dataclass
 class QwenModel:
-    """A Qwen2-architecture decoder stack on the GPU: the token embedding (bf16 [V, H]) and one
-    weight dict per block (the keys of gsq.e2e.BlockWeights)."""
+    """A Qwen2-architecture decoder stack on the GPU: the tied token embedding (bf16 [V, H]),
+    one weight dict per block (the keys of gsq.e2e.BlockWeights) and the final RMSNorm weight
+    (bf16 [H])."""
     cfg: BlockConfig
     embed: torch.Tensor
     layers: list
+    norm: torch.Tensor = None
 
 
 def _check_spec(spec: DBSpec, n_model_layers: int):
@@ -330,4 +332,4 @@ def random_model(n_layers=24, seed=0, device=None, cfg: BlockConfig = None, voca
         W["in_norm"] = torch.ones(H, dtype=torch.bfloat16, device=dev)
         W["post_norm"] = torch.ones(H, dtype=torch.bfloat16, device=dev)
         layers.append(W)
-    return QwenModel(cfg, embed, layers)
+    return QwenModel(cfg, embed, layers, torch.ones(H, dtype=torch.bfloat16, device=dev))

@@ -344,6 +344,11 @@ int mckp_dp_f64_noalloc(const double *scores, const int64_t *step, int n_inst, i
 int gsq_kl_rows(const void *zq, const void *zr, int n, int V, int64_t ld, void *D, int64_t ld_d,
                 double *kl_rows, float *lse, void *stream);
 
+/* w bf16 [out][in] = bf16(scales[r][c / gs] * grid[codes[r, c]]): a database candidate
+ * assembled in the model dtype (src/gsq_rco/rco/database.py:244-256, allocate.py:117). */
+int gsq_dequant_bf16(const uint8_t *codes, const float *scales, int out_f, int in_f, int bits,
+                     int group_size, void *w, void *stream);
+
 /* x = bf16(f32(x) / divisor) for n bf16 elements (the head gradient's mean over positions,
  * evaluate.py:150). */
 int gsq_div_bf16(void *x, int64_t n, float divisor, void *stream);
