@@ -18,8 +18,13 @@ Hessians over 128 x 2048 tokens; value = seconds per model (
 better); under torchrun the windows and solves are sharded (strong scaling, NCCL all-reduce of
 the Hessians).
 
+Workload "rco": RCO allocation on the same stack and a GPTQ database at
+2 / 3 / 4 bits: seconds per RCO step of 8 Gumbel samples x 32 windows x 2048 tokens (forward,
+KL head, backward through 24 blocks, straight-through dots); at most 2 timed steps after 3
+warm-up steps (a step takes seconds); windows sharded over ranks under torchrun.
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload block|linear|gptq]
+                  [--workload block|linear|gptq|rco]
 
 N > 1 runs under torchrun, one rank per GPU. Block: the ranks quantize one block together,
 data-parallel over the positions of each micro-batch sequence with one NCCL all-reduce of the
@@ -53,7 +58,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="block", choices=["block", "linear", "gptq"])
+    ap.add_argument("--workload", default="block", choices=["block", "linear", "gptq", "rco"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=200)
     return ap.parse_args()
@@ -473,6 +478,159 @@ def run_reference_gptq(args):
     print(json.dumps(res), flush=True)
 
 
+# ------------------------------------------------------------------------------- rco ---
+
+RCO_G, RCO_WINDOWS, RCO_WIN_PER_SAMPLE = 8, 32, 32
+
+
+def rco_setup(dev):
+    from gsq_rco_mlx_b200.rco.allocate import Bank, KLObjective
+    from gsq_rco_mlx_b200.rco.database import DBSpec, build_database, random_model
+    model = random_model(n_layers=24, seed=0, device=dev)
+    calib = np.random.default_rng(0).integers(0, VOCAB, size=(N_SEQ, T_SEQ)).astype(np.int32)
+    man, res = build_database(model, calib, DBSpec(options=GPTQ_OPTIONS, n_layers=24),
+                              log=lambda *a: None, keep="device")
+    windows = np.random.default_rng(1).integers(0, VOCAB, size=(RCO_WINDOWS, T_SEQ)).astype(
+        np.int32)
+    return model, Bank(man, res), windows, KLObjective
+
+
+def run_rco(args):
+    """Config 4: RCO allocation on the 24-layer stack (options 2 / 3 / 4, 3.0 bits exactly),
+    g = 8 Gumbel samples per step, each the mean token KL over 32 windows x 2048 with its
+    straight-through upstream (forward and backward through the 24 blocks). A step is one RCO
+    step (8 samples + DP + manifold Adam); the metric is seconds per step. Under torchrun each
+    sample's windows are shared over the ranks (one all-reduce of the upstream per sample)."""
+    import torch
+    import torch.distributed as dist
+    from gsq_rco_mlx_b200 import _lib
+    from gsq_rco_mlx_b200.rco.allocate import rco_allocate
+
+    rank, world, local = dist_setup()
+    _lib.lib()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    steps, warmup = max(1, min(args.steps, 2)), max(3, min(args.warmup, 3))
+    model, bank, windows, KLObjective = rco_setup(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    t_init = time.perf_counter()
+    obj = KLObjective(model, bank, windows, windows_per_sample=RCO_WIN_PER_SAMPLE, chunk_seqs=2)
+    barrier()
+    t_init = time.perf_counter() - t_init
+    rco_allocate(obj, bank, 3.0, steps=warmup, g=RCO_G, lr=0.1, seed=0)
+    barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    n0 = _lib.Launches.n
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    t0 = time.perf_counter()
+    e0.record()
+    res = rco_allocate(obj, bank, 3.0, steps=steps, g=RCO_G, lr=0.1, seed=1)
+    e1.record()
+    barrier()
+    wall = time.perf_counter() - t0
+    clk = clocks.stop()
+    sec = max_over_ranks(e0.elapsed_time(e1) / 1000 / steps)
+    launches = (_lib.Launches.n - n0) // steps
+    e2e = max_over_ranks((t_init + wall) / steps)
+    out = {
+        "metric": "RCO s per step (24-layer Qwen2.5-0.5B architecture, options {2,3,4}, 3.0 bits, "
+                  "g=8 samples x 32 windows x 2048 tokens)",
+        "value": round(sec, 3), "unit": "s/step", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(sec * 1000, 1), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 model, f32/f64 objective",
+        "data": "synthetic: random-init 24-layer stack, uniform-random token windows",
+        "config": {"workload": "config 4: RCO allocation, windows_per_sample 32, g 8, Adam lr 0.1",
+                   "decoded_avg_bits": res["decoded_avg_bits"],
+                   "parallelism": f"windows of each sample sharded over {world} rank(s)",
+                   "l2": "25 decoder states of 32 x 2048 tokens (3 GB) > L2"},
+        "e2e": {"value": round(e2e, 3), "unit": "s/step",
+                "h2d_bytes_per_step": int(RCO_G * RCO_WIN_PER_SAMPLE * T_SEQ * 4),
+                "d2h_bytes_per_step": int(RCO_G * 168 * len(GPTQ_OPTIONS) * 8),
+                "what": "KLObjective construction (reference states) amortised over the steps, "
+                        "plus rco_allocate steps from host token windows to the host allocation"},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline_rco()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_baseline_rco():
+    """The CPU restatement of the objective (oracle.block / oracle.block_vjp / oracle.kl) on a
+    bounded sample: one window of 2048 tokens forward + backward through 2 blocks plus its KL
+    head, scaled to 24 blocks x 32 windows x 8 samples per step."""
+    import torch
+    from oracle import block as ob
+    from oracle import block_vjp as ov
+    from oracle import kl as okl
+    torch.set_num_threads(os.cpu_count())
+    g = torch.Generator().manual_seed(0)
+    W = {"q_proj": (NH * HD, HID), "k_proj": (NKV * HD, HID), "v_proj": (NKV * HD, HID),
+         "o_proj": (HID, NH * HD), "gate_proj": (INTER, HID), "up_proj": (INTER, HID),
+         "down_proj": (HID, INTER), "q_bias": (NH * HD,), "k_bias": (NKV * HD,),
+         "v_bias": (NKV * HD,)}
+    W = {k: (0.02 * torch.randn(*s, generator=g)).bfloat16().float() for k, s in W.items()}
+    W["in_norm"] = torch.ones(HID)
+    W["post_norm"] = torch.ones(HID)
+    h = (0.02 * torch.randn(T_SEQ, HID, generator=g)).bfloat16().float()
+    t0 = time.perf_counter()
+    x = h
+    for _ in range(2):
+        x = ob.block_hard(x, W)[0]
+    cot = (1e-3 * torch.randn(T_SEQ, HID, generator=g)).bfloat16().float()
+    for _ in range(2):
+        cot = ov.block_vjp(h, W, cot)[0]
+    t_blocks = time.perf_counter() - t0
+    E = (0.02 * torch.randn(VOCAB // 16, HID, generator=g)).bfloat16().double()
+    t0 = time.perf_counter()
+    okl.kl_chunk_value_grad(x[:512].double(), h[:512].double(), E)
+    t_head = (time.perf_counter() - t0) * 16 * (T_SEQ / 512)
+    per_window = t_blocks * 12 + t_head
+    total = per_window * RCO_WIN_PER_SAMPLE * RCO_G
+    return {"value": round(total, 1), "unit": "s/step (extrapolated)", "cores": os.cpu_count(),
+            "kind": "port",
+            "sample": "one 2048-token window forward + backward through 2 blocks (x12 for 24) "
+                      "and 512 rows of the KL head over 1/16 of the vocabulary (scaled), "
+                      "x 32 windows x 8 samples"}
+
+
+def run_reference_rco(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    cb = cpu_baseline_rco()
+    res = {"impl": "reference",
+           "metric": "RCO s per step (24-layer Qwen2.5-0.5B architecture, options {2,3,4}, 3.0 "
+                     "bits, g=8 samples x 32 windows x 2048 tokens)",
+           "value": cb["value"], "unit": "s/step", "n_gpus": world, "steps": 1, "warmup": 0,
+           "ms_per_step": round(cb["value"] * 1000, 1), "higher_is_better": False,
+           "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+           "config": {"workload": "config 4: RCO allocation, windows_per_sample 32, g 8"},
+           "cpu_baseline": cb,
+           "e2e": {"value": cb["value"], "unit": "s/step", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(res), flush=True)
+
+
 # ---------------------------------------------------------------------------- linear ---
 
 OUT_F, IN_F, N_SEQ_L, T_SEQ_L = 4864, 896, 32, 512
@@ -640,6 +798,8 @@ def main():
         return run_linear(args)
     if args.workload == "gptq":
         return run_reference_gptq(args) if args.impl == "reference" else run_gptq(args)
+    if args.workload == "rco":
+        return run_reference_rco(args) if args.impl == "reference" else run_rco(args)
     if args.impl == "reference":
         run_reference(args)
     else:
