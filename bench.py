@@ -526,7 +526,7 @@ def run_rco(args):
         return float(t.item())
 
     t_init = time.perf_counter()
-    obj = KLObjective(model, bank, windows, windows_per_sample=RCO_WIN_PER_SAMPLE, chunk_seqs=2)
+    obj = KLObjective(model, bank, windows, windows_per_sample=RCO_WIN_PER_SAMPLE, chunk_seqs=8)
     barrier()
     t_init = time.perf_counter() - t_init
     rco_allocate(obj, bank, 3.0, steps=warmup, g=RCO_G, lr=0.1, seed=0)
