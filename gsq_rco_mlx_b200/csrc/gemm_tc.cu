@@ -503,6 +503,44 @@ __device__ __forceinline__ double epilogue_out(const GemmParams& p, const TileIn
   return sq;
 }
 
+// 4 K=16 steps of one 64-wide k-block into accumulator d: the shared-memory descriptors advance
+// by 32 bytes (2 in the start-address field) per step; the first step accumulates if acc_first.
+__device__ __forceinline__ void umma4(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                      uint32_t acc_first) {
+  asm volatile(
+      "{\n\t.reg .pred p0, p1;\n\t"
+      "setp.ne.b32 p0, %4, 0;\n\t"
+      "setp.eq.b32 p1, %3, %3;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %6, %3, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %7, %8, %3, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %9, %10, %3, p1;\n\t}"
+      ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc_first), "l"(a + 2), "l"(b + 2),
+        "l"(a + 4), "l"(b + 4), "l"(a + 6), "l"(b + 6));
+}
+
+// The products of one k-block for NA x NBT bf16 terms of order <= 2 (hi x hi into big, the rest
+// into small); A term i at +i*1024, B term j at +(NA*1024 + j*tb) in the descriptor field.
+template <int NA, int NBT>
+__device__ __forceinline__ void issue_kb(uint64_t ad, uint32_t tb, uint32_t big, uint32_t small,
+                                         uint32_t idesc, uint32_t big_acc, uint32_t small_acc) {
+  const uint64_t bd = ad + (uint64_t)(NA * 1024);
+  umma4(big, ad, bd, idesc, big_acc);
+  if (NA == 1 && NBT == 3) {
+    umma4(small, ad, bd + tb, idesc, small_acc);
+    umma4(small, ad, bd + 2 * tb, idesc, 1u);
+  } else if (NA == 3 && NBT == 1) {
+    umma4(small, ad + 1024, bd, idesc, small_acc);
+    umma4(small, ad + 2048, bd, idesc, 1u);
+  } else if (NA == 3 && NBT == 3) {
+    umma4(small, ad, bd + tb, idesc, small_acc);
+    umma4(small, ad + 1024, bd, idesc, 1u);
+    umma4(small, ad, bd + 2 * tb, idesc, 1u);
+    umma4(small, ad + 1024, bd + tb, idesc, 1u);
+    umma4(small, ad + 2048, bd, idesc, 1u);
+  }
+}
+
 // --------------------------------------------------------------------------- kernel ---
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
@@ -608,6 +646,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(BM, BN);
+      // term configurations with a compile-time product list (order 2); others: generic loop
+      const int cfg = (p.na == 1 && p.nb == 1) ? 1
+                    : (p.order != 2) ? 0
+                    : (p.na == 1 && p.nb == 3) ? 2 : (p.na == 3 && p.nb == 1) ? 3
+                    : (p.na == 3 && p.nb == 3) ? 4 : 0;
       int s = 0, bs = 0;
       uint32_t ph = 0, bph = 0, tcount = 0;
       bool ok = true, any = false;
@@ -638,6 +681,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             }
             fence_after_sync();
             const uint32_t st = smem_u32(smem + (size_t)s * stage_bytes);
+            if (cfg != 0) {  // compile-time product lists: few instructions between UMMAs
+              const uint64_t ad = umma_desc_k_sw128(st);
+              const uint32_t tb = kTileB >> 4;
+              const uint32_t ba = big_init ? 1u : 0u, sa = small_init ? 1u : 0u;
+              if (cfg == 1) issue_kb<1, 1>(ad, tb, big, small, idesc, ba, sa);
+              else if (cfg == 2) issue_kb<1, 3>(ad, tb, big, small, idesc, ba, sa);
+              else if (cfg == 3) issue_kb<3, 1>(ad, tb, big, small, idesc, ba, sa);
+              else issue_kb<3, 3>(ad, tb, big, small, idesc, ba, sa);
+              big_init = true;
+              if (cfg != 1) small_init = true;
+            } else
             for (int i = 0; i < p.na; ++i) {
               for (int j = 0; j < p.nb; ++j) {
                 if (i + j > p.order) continue;
