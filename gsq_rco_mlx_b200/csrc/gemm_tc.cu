@@ -863,7 +863,7 @@ static int launch(GemmParams& p, int batch, cudaStream_t st) {
   int products = 0;
   for (int i = 0; i < p.na; ++i)
     for (int j = 0; j < p.nb; ++j) products += (i + j <= p.order);
-  p.kb_per_chunk = products >= 3 ? 1 : (products == 2 ? 2 : 4);
+  p.kb_per_chunk = products >= 3 ? 2 : 4;
   const bool has_small = (p.na > 1 || p.nb > 1) && p.order > 0;
   int nbig = (int)((kTmemCols - (has_small ? 2u * BN : 0u)) / BN);
   p.n_big = nbig > kMaxBig ? kMaxBig : nbig;
