@@ -54,7 +54,7 @@ SIGNATURES = {
     "gsq_zero_cols": [_vp, _i32, _i64, _i32, _i32, _vp],
     "gsq_gather_split": [_vp, _i32, _i64, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _vp, _i64,
                          _vp, _i64, _vp],
-    "gsq_transpose_bf16": [_vp, _i32, _i32, _i64, _i64, _vp, _i64, _i64, _i32, _vp],
+    "gsq_transpose_bf16": [_vp, _i32, _i32, _i64, _i64, _vp, _i64, _i64, _i32, _i32, _vp],
     "gsq_head_group_sum_t": [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
     "gsq_sum_f64": [_vp, _i32, _vp, _vp],
     "hessian_accum": [_vp, _i64, _i32, _vp, _i64, _vp],

@@ -65,23 +65,53 @@ __global__ void sum_f64_kernel(const double* __restrict__ x, int n, double* out)
   }
 }
 
-// out[z][c][r] = in[z][r][c] for bf16 matrices [rows][ld_in] -> [cols][ld_out] (32 x 32 tiles)
-__global__ void transpose_bf16_kernel(const __nv_bfloat16* __restrict__ in, int rows, int cols,
-                                      int64_t ld_in, int64_t bs_in, __nv_bfloat16* __restrict__ out,
-                                      int64_t ld_out, int64_t bs_out) {
-  __shared__ __nv_bfloat16 S[32][34];
-  const int z = blockIdx.z;
-  const __nv_bfloat16* src = in + z * bs_in;
-  __nv_bfloat16* dst = out + z * bs_out;
-  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
-  for (int rr = threadIdx.y; rr < 32; rr += 8) {
-    const int r = r0 + rr, c = c0 + threadIdx.x;
-    S[rr][threadIdx.x] = (r < rows && c < cols) ? src[(int64_t)r * ld_in + c] : __float2bfloat16_rn(0.f);
+// out[z][c][r] = in[z][r][c] for bf16 matrices [rows][ld_in] -> [cols][ld_out]: 64 x 64 tiles
+// through shared memory, 16-byte row segments in and out when the strides allow (vec), single
+// elements otherwise. skip_upper: tiles whose 128-column block lies strictly above their 128-row
+// block (a causal matrix's zeros) are neither read nor written; a causal consumer that reduces
+// from the 128-aligned start of each 128-row tile never reads their transposed copies.
+__global__ void __launch_bounds__(256)
+transpose_bf16_kernel(const __nv_bfloat16* __restrict__ in, int rows, int cols, int64_t ld_in,
+                      int64_t bs_in, __nv_bfloat16* __restrict__ out, int64_t ld_out,
+                      int64_t bs_out, int vec_in, int vec_out, int skip_upper) {
+  __shared__ __align__(16) __nv_bfloat16 S[64][72];
+  const int r0 = blockIdx.y * 64, c0 = blockIdx.x * 64;
+  if (skip_upper && (c0 >> 7) > (r0 >> 7)) return;
+  const __nv_bfloat16* src = in + (int64_t)blockIdx.z * bs_in;
+  __nv_bfloat16* dst = out + (int64_t)blockIdx.z * bs_out;
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int r = (t >> 3) + 32 * p, c8 = (t & 7) * 8;
+    const int gr = r0 + r, gc = c0 + c8;
+    __align__(16) __nv_bfloat16 v[8];
+    if (vec_in && gr < rows && gc + 8 <= cols) {
+      *reinterpret_cast<uint4*>(v) = *reinterpret_cast<const uint4*>(src + (int64_t)gr * ld_in + gc);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        v[k] = (gr < rows && gc + k < cols) ? src[(int64_t)gr * ld_in + gc + k]
+                                            : __float2bfloat16_rn(0.f);
+    }
+    *reinterpret_cast<uint4*>(&S[r][c8]) = *reinterpret_cast<const uint4*>(v);
   }
   __syncthreads();
-  for (int cc = threadIdx.y; cc < 32; cc += 8) {
-    const int c = c0 + cc, r = r0 + threadIdx.x;
-    if (c < cols && r < rows) dst[(int64_t)c * ld_out + r] = S[threadIdx.x][cc];
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int c = (t >> 3) + 32 * p, r8 = (t & 7) * 8;
+    const int gc = c0 + c, gr = r0 + r8;
+    if (gc >= cols) continue;
+    __align__(16) __nv_bfloat16 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = S[r8 + k][c];
+    __nv_bfloat16* o = dst + (int64_t)gc * ld_out + gr;
+    if (vec_out && gr + 8 <= rows) {
+      *reinterpret_cast<uint4*>(o) = *reinterpret_cast<const uint4*>(v);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (gr + k < rows) o[k] = v[k];
+    }
   }
 }
 
@@ -123,12 +153,16 @@ using namespace gsq;
 
 extern "C" int gsq_transpose_bf16(const void* in, int rows, int cols, int64_t ld_in, int64_t bs_in,
                                   void* out, int64_t ld_out, int64_t bs_out, int batch,
-                                  void* stream) {
-  if (!in || !out || rows <= 0 || cols <= 0 || batch <= 0 || ld_in < cols || ld_out < rows)
+                                  int skip_upper, void* stream) {
+  if (!in || !out || rows <= 0 || cols <= 0 || batch <= 0 || ld_in < cols || ld_out < rows ||
+      batch > 65535)
     return GSQ_EINVAL;
-  dim3 g((cols + 31) / 32, (rows + 31) / 32, batch);
-  transpose_bf16_kernel<<<g, dim3(32, 8), 0, (cudaStream_t)stream>>>(
-      (const __nv_bfloat16*)in, rows, cols, ld_in, bs_in, (__nv_bfloat16*)out, ld_out, bs_out);
+  const int vec_in = ((uintptr_t)in % 16 == 0 && ld_in % 8 == 0 && bs_in % 8 == 0) ? 1 : 0;
+  const int vec_out = ((uintptr_t)out % 16 == 0 && ld_out % 8 == 0 && bs_out % 8 == 0) ? 1 : 0;
+  dim3 g((cols + 63) / 64, (rows + 63) / 64, batch);
+  transpose_bf16_kernel<<<g, 256, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)in, rows, cols, ld_in, bs_in, (__nv_bfloat16*)out, ld_out, bs_out,
+      vec_in, vec_out, skip_upper ? 1 : 0);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }

@@ -90,7 +90,7 @@ class BlockWeights:
             r, c = src.shape
             t = Terms(c, r, 1, src.device)
             _lib.call("gsq_transpose_bf16", _lib.ptr(src), r, c, c, 0, _lib.ptr(t.t[0]), t.ld, 0,
-                      1, _lib.stream_ptr())
+                      1, 0, _lib.stream_ptr())
             cache[key] = t
         return cache[key]
 
@@ -265,12 +265,14 @@ class Qwen2Block:
         self._bwd_key, self._bwd = key, b
         return b
 
-    def _T(self, x, rows, cols, ld, out, ld_out=None, batch=1, bs_in=0, bs_out=0):
-        """out[z] = x[z]^T (bf16): out a Terms (term 0, its ld) or a tensor with ld_out."""
+    def _T(self, x, rows, cols, ld, out, ld_out=None, batch=1, bs_in=0, bs_out=0,
+           skip_upper=False):
+        """out[z] = x[z]^T (bf16): out a Terms (term 0, its ld) or a tensor with ld_out;
+        skip_upper leaves the transposes of a causal block's zero tiles unwritten."""
         if isinstance(out, Terms):
             out, ld_out = out.t[0], out.ld
         _lib.call("gsq_transpose_bf16", _lib.ptr(x), rows, cols, ld, bs_in, _lib.ptr(out),
-                  ld_out, bs_out, batch, _lib.stream_ptr())
+                  ld_out, bs_out, batch, int(skip_upper), _lib.stream_ptr())
 
     def new_grads(self, W: BlockWeights):
         """Zeroed float32 weight gradients of the seven linears; gate / up and q / k / v are views
@@ -345,13 +347,13 @@ class Qwen2Block:
                   _lib.ptr(dS.t[0]), _lib.ptr(dS.t[1]), _lib.ptr(dS.t[2]), dS.ld, 0.125, st)
         for i in range(3):
             self._T(dS.t[i], T, T, dS.ld, dST.t[i], dST.ld, batch=B, bs_in=T * dS.ld,
-                    bs_out=T * dST.ld)
+                    bs_out=T * dST.ld, skip_upper=True)
             self._T(self.q_rot.t[i], T, hd, self.q_rot.ld, b["qT"].t[i], b["qT"].ld, batch=B,
                     bs_in=T * self.q_rot.ld, bs_out=hd * b["qT"].ld)
             self._T(self.k_rot.t[i], T, hd, self.k_rot.ld, b["kT"].t[i], b["kT"].ld,
                     batch=S * nkv, bs_in=T * self.k_rot.ld, bs_out=hd * b["kT"].ld)
         self._T(self.P.t[0], T, T, self.P.ld, b["PT"], batch=B, bs_in=T * self.P.ld,
-                bs_out=T * b["PT"].ld)
+                bs_out=T * b["PT"].ld, skip_upper=True)
         gemm(dS, b["kT"], M=T, N=hd, K=T, batch=B, bn=64, causal=1, a_off=(1, T, 0),
              b_off=(rep, hd, 0), C=b["dqr"], ldc=hd, c_off=(1, T * hd, 0))
         gemm(dST, b["qT"], M=T, N=hd, K=T, batch=B, bn=64, causal=2, a_off=(1, T, 0),

@@ -456,7 +456,7 @@ class MLPStep(_StageBase):
             gemm(self.DRT, self.DINT, C=self.grad_d[r])
             for i in range(3):
                 _lib.call("gsq_transpose_bf16", _lib.ptr(self.Dbuf[dname][r][i]), H, I, I, 0,
-                          _lib.ptr(self.DdT.t[i]), self.DdT.ld, 0, 1, _lib.stream_ptr())
+                          _lib.ptr(self.DdT.t[i]), self.DdT.ld, 0, 1, 0, _lib.stream_ptr())
             gemm(self.DR, self.DdT, epi=3, aux0=self.g, aux1=self.u, ct_terms=self.GUT,
                  ct_up_rows=I)
             gemm(self.GUT, self.MNT, M=I, batch=2, C=self.grad_gu[0, r], ldc=H,
@@ -550,8 +550,9 @@ class VOStep(_StageBase):
                  c_off=(1, Tq * Tk, 0))
         _lib.call("gsq_softmax_causal_rows", _lib.ptr(self.scores), B, Tq, Tk, Tk, q0,
                   _lib.ptr(self.P.t[0]), self.P.ld, st)
+        # P^T feeds the causal dV GEMM when q0 = 0: the transposes of P's zero tiles are unread
         _lib.call("gsq_transpose_bf16", _lib.ptr(self.P.t[0]), Tq, Tk, self.P.ld, Tq * self.P.ld,
-                  _lib.ptr(self.PT.t[0]), self.PT.ld, Tk * self.PT.ld, B, st)
+                  _lib.ptr(self.PT.t[0]), self.PT.ld, Tk * self.PT.ld, B, int(q0 == 0), st)
 
     def contract(self):
         c, m = self.cfg, self.m
@@ -575,7 +576,7 @@ class VOStep(_StageBase):
             gemm(self.DYT, self.OT, C=self.grad_o[r])
             for i in range(3):
                 _lib.call("gsq_transpose_bf16", _lib.ptr(self.Dbuf[oname][r][i]), H, H, H, 0,
-                          _lib.ptr(self.DoT.t[i]), self.DoT.ld, 0, 1, st)
+                          _lib.ptr(self.DoT.t[i]), self.DoT.ld, 0, 1, 0, st)
             gemm(self.DY, self.DoT, M=Tq, batch=m, a_off=(1, Tq, 0), ct_terms=self.DOT,
                  t_off=(1, H, 0, 0, 0))
             gemm(self.PT, self.DOT, M=Tk, N=hd, K=Tq, batch=B, bn=64,

@@ -39,7 +39,7 @@ class KLHead:
         self.Et = Terms(self.V, self.H, 1, ld=self.H, tensors=[self.E])
         self.ET = Terms(self.H, self.V, 1, dev)
         _lib.call("gsq_transpose_bf16", _lib.ptr(self.E), self.V, self.H, self.H, 0,
-                  _lib.ptr(self.ET.t[0]), self.ET.ld, 0, 1, _lib.stream_ptr())
+                  _lib.ptr(self.ET.t[0]), self.ET.ld, 0, 1, 0, _lib.stream_ptr())
         c = self.chunk
         self.zq = torch.empty(c, self.V, device=dev, dtype=torch.bfloat16)
         self.zr = torch.empty(c, self.V, device=dev, dtype=torch.bfloat16)

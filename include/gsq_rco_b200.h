@@ -217,9 +217,12 @@ int gsq_gather_split(const void *x, int src_bf16, int64_t ld_x, const int32_t *s
                      void *const *row_terms, int64_t ld_t, void *const *col_terms, int64_t ld_u,
                      void *stream);
 
-/* out[z] = in[z]^T for bf16 matrices [rows][ld_in] (batch stride bs_in) -> [cols][ld_out]. */
+/* out[z] = in[z]^T for bf16 matrices [rows][ld_in] (batch stride bs_in) -> [cols][ld_out].
+ * skip_upper: input tiles whose 128-column block lies strictly above their 128-row block (a
+ * causal matrix's zeros) are skipped and their transposed copies left unwritten (a causal
+ * consumer reducing from the 128-aligned start of each 128-row tile never reads them). */
 int gsq_transpose_bf16(const void *in, int rows, int cols, int64_t ld_in, int64_t bs_in, void *out,
-                       int64_t ld_out, int64_t bs_out, int batch, void *stream);
+                       int64_t ld_out, int64_t bs_out, int batch, int skip_upper, void *stream);
 
 /* The value gradient of each kv head, summed over its rep query heads (GQA repeat of
  * src/gsq_rco/gsq/e2e.py:146-148, backward), as three bf16 terms transposed:
