@@ -15,15 +15,37 @@
 namespace gsq {
 
 // ---------------------------------------------------------------- Philox4x32-10 ---
-// Salmon, Moraes, Dror, Shaw, SC'11. Ten rounds, Weyl key schedule.
-__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+// Salmon, Moraes, Dror, Shaw, SC'11. Ten rounds, Weyl key schedule. The ten round keys depend
+// only on (seed, linear id), so the host computes them once per launch and the kernels read
+// them from the parameter bank; a round is two 32x32->64 multiplies and two three-input XORs.
+struct PhiloxKey {
+  uint32_t k0[10], k1[10];
+};
+
+__host__ __device__ inline PhiloxKey philox_key(uint64_t seed, uint32_t linear_id) {
+  PhiloxKey k;
+  uint32_t a = (uint32_t)(seed & 0xFFFFFFFFull), b = (uint32_t)(seed >> 32) ^ linear_id;
+  for (int r = 0; r < 10; ++r) {
+    k.k0[r] = a;
+    k.k1[r] = b;
+    a += 0x9E3779B9u;
+    b += 0xBB67AE85u;
+  }
+  return k;
+}
+
+__device__ __forceinline__ uint64_t mul_wide_u32(uint32_t a, uint32_t b) {
+  uint64_t p;
+  asm("mul.wide.u32 %0, %1, %2;" : "=l"(p) : "r"(a), "r"(b));
+  return p;
+}
+
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, const PhiloxKey& k) {
 #pragma unroll
   for (int r = 0; r < 10; ++r) {
-    const uint32_t hi0 = __umulhi(0xD2511F53u, c.x), lo0 = 0xD2511F53u * c.x;
-    const uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z), lo1 = 0xCD9E8D57u * c.z;
-    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
-    k0 += 0x9E3779B9u;
-    k1 += 0xBB67AE85u;
+    const uint64_t p0 = mul_wide_u32(0xD2511F53u, c.x), p1 = mul_wide_u32(0xCD9E8D57u, c.z);
+    c = make_uint4((uint32_t)(p1 >> 32) ^ c.y ^ k.k0[r], (uint32_t)p1,
+                   (uint32_t)(p0 >> 32) ^ c.w ^ k.k1[r], (uint32_t)p0);
   }
   return c;
 }
@@ -31,28 +53,32 @@ __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1
 // Gumbel noise of one weight and draw: one Philox call (counter (i, 0, step, resample)),
 // planes 0..3 from the high 24 bits of x0..x3, plane 4 from their low bytes.
 struct NoiseKey {
-  uint32_t k0, k1, step, resample;
+  PhiloxKey key;
+  uint32_t step, resample;
 };
 
 __host__ __device__ inline NoiseKey make_noise_key(uint64_t seed, uint32_t linear_id,
                                                    uint32_t step, uint32_t resample) {
   NoiseKey k;
-  k.k0 = (uint32_t)(seed & 0xFFFFFFFFull);
-  k.k1 = (uint32_t)(seed >> 32) ^ linear_id;
+  k.key = philox_key(seed, linear_id);
   k.step = step;
   k.resample = resample;
   return k;
 }
 
+// u = (b + 0.5) 2^-24 as one fused multiply-add (b < 2^24 converts exactly; scaling by a power
+// of two commutes with rounding, so this equals rounding b + 0.5 and then scaling), clipped to
+// [1e-7, 1 - 1e-7]; g = -log(-log u).
 __device__ __forceinline__ float gumbel_from_24(uint32_t b) {
-  float u = __fmul_rn(__fadd_rn((float)b, 0.5f), 5.9604644775390625e-08f);
+  float u = __fmaf_rn((float)b, 5.9604644775390625e-08f, 2.98023223876953125e-08f);
   u = fminf(fmaxf(u, 1e-7f), 1.0f - 1e-7f);
   return -logf(-logf(u));
 }
 
 template <int K>
-__device__ __forceinline__ void gumbel_weight(const NoiseKey& nk, uint32_t i, float g[K]) {
-  const uint4 x = philox4x32_10(make_uint4(i, 0u, nk.step, nk.resample), nk.k0, nk.k1);
+__device__ __forceinline__ void gumbel_weight(const PhiloxKey& key, uint32_t i, uint32_t step,
+                                              uint32_t resample, float g[K]) {
+  const uint4 x = philox4x32_10(make_uint4(i, 0u, step, resample), key);
   g[0] = gumbel_from_24(x.x >> 8);
   g[1] = gumbel_from_24(x.y >> 8);
   g[2] = gumbel_from_24(x.z >> 8);

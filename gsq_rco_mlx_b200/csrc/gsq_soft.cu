@@ -48,12 +48,13 @@ struct SoftMath {
   }
 
   __device__ __forceinline__ static void noise(const float* __restrict__ noise_r, int64_t d,
-                                               int64_t i, const NoiseKey& nk, float g[K]) {
+                                               int64_t i, const PhiloxKey& key, uint32_t step,
+                                               uint32_t resample, float g[K]) {
     if (noise_r) {
 #pragma unroll
       for (int k = 0; k < K; ++k) g[k] = noise_r[k * d + i];
     } else {
-      gumbel_weight<K>(nk, (uint32_t)i, g);
+      gumbel_weight<K>(key, (uint32_t)i, step, resample, g);
     }
   }
 
@@ -91,7 +92,7 @@ soft_fwd_kernel(const float* __restrict__ logits, const uint8_t* __restrict__ j0
     float l[K], g[K], p[K], C[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) l[k] = logits[k * d + i];
-    SoftMath<K>::noise(noise, d, i, nk, g);
+    SoftMath<K>::noise(noise, d, i, nk.key, nk.step, nk.resample, g);
     SoftMath<K>::probs(l, g, inv_tau, kappa, p);
     SoftMath<K>::candidates(bits, K == 5 ? (int)j0[i] : 0, C);
     const int row = (int)(i / in_f), col = (int)(i - (int64_t)row * in_f);
@@ -120,6 +121,13 @@ __device__ __forceinline__ void lion1(float& p, float& m, float g, float lr, con
 
 constexpr int kMaxResamples = 8;
 
+// x / R correctly rounded for R = 1 or 2 (halving is exact up to the rounding the division does).
+template <int R>
+__device__ __forceinline__ float div_by(float x) {
+  static_assert(R == 1 || R == 2, "resample counts of the vectorised step");
+  return R == 1 ? x : __fmul_rn(x, 0.5f);
+}
+
 struct StepArgs {
   float* logits;
   float* mom;
@@ -134,8 +142,8 @@ struct StepArgs {
   LionConst lc;
   int next;              // run the forward of the next step
   const float* noise;    // [R][K][d] host-supplied noise of the next step, or NULL
-  uint64_t seed;
-  uint32_t linear_id, next_step;
+  PhiloxKey key;         // round keys of (seed, linear id)
+  uint32_t next_step;
   float inv_tau1, kappa1;
   const float* w_ref;
   float* w_out;          // [R][d]
@@ -226,8 +234,8 @@ __global__ void __launch_bounds__(256) soft_step_kernel(const StepArgs a) {
 #pragma unroll 1
       for (int r = 0; r < a.R; ++r) {
         float g[K], p[K];
-        const NoiseKey nk = make_noise_key(a.seed, a.linear_id, a.next_step, (uint32_t)r);
-        SoftMath<K>::noise(a.noise ? a.noise + (int64_t)r * K * d : nullptr, d, i, nk, g);
+        SoftMath<K>::noise(a.noise ? a.noise + (int64_t)r * K * d : nullptr, d, i, a.key,
+                           a.next_step, (uint32_t)r, g);
         SoftMath<K>::probs(l, g, a.inv_tau1, a.kappa1, p);
         float w = __fmul_rn(s_new, SoftMath<K>::value(p, C[t]));
         if (a.w_ref) w = __fsub_rn(w, wr);
@@ -246,11 +254,10 @@ __global__ void __launch_bounds__(256) soft_step_kernel(const StepArgs a) {
 // every 64-column chunk (8-byte loads and stores), and every input of a lane's two weights is
 // loaded before any arithmetic, so each lane keeps ~2 (2K + R(K + 1) + 2) loads in flight.
 template <int K, int R>
-__global__ void __launch_bounds__(256) soft_step_v2_kernel(const StepArgs a) {
+__global__ void __launch_bounds__(256, 3) soft_step_v2_kernel(const StepArgs a) {
   const int64_t d = (int64_t)a.out_f * a.in_f;
   const int lane = threadIdx.x & 31;
   const int64_t n_units = (int64_t)a.out_f * a.G;
-  const float fR = (float)R;
   const int n_chunks = a.gs / 64;
   for (int64_t unit = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; unit < n_units;
        unit += ((int64_t)gridDim.x * blockDim.x) >> 5) {
@@ -299,7 +306,7 @@ __global__ void __launch_bounds__(256) soft_step_v2_kernel(const StepArgs a) {
     float s_new = s;
     if (lane == 0) {
       float mv = a.mom_s[unit];
-      lion1(s_new, mv, __fdiv_rn(gsum, fR), a.lr_s, a.lc);
+      lion1(s_new, mv, div_by<R>(gsum), a.lr_s, a.lc);
       a.scales[unit] = s_new;
       a.mom_s[unit] = mv;
     }
@@ -354,15 +361,15 @@ __global__ void __launch_bounds__(256) soft_step_v2_kernel(const StepArgs a) {
         for (int k = 0; k < K; ++k) {
           l[k] = e ? lv[k].y : lv[k].x;
           m[k] = e ? mv[k].y : mv[k].x;
-          lion1(l[k], m[k], __fdiv_rn(acc[k], fR), a.lr_l, a.lc);
+          lion1(l[k], m[k], div_by<R>(acc[k]), a.lr_l, a.lc);
           if (e) { lv[k].y = l[k]; mv[k].y = m[k]; } else { lv[k].x = l[k]; mv[k].x = m[k]; }
         }
         if (a.next) {
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             float g[K], p[K];
-            const NoiseKey nk = make_noise_key(a.seed, a.linear_id, a.next_step, (uint32_t)r);
-            SoftMath<K>::noise(a.noise ? a.noise + (int64_t)r * K * d : nullptr, d, i + e, nk, g);
+            SoftMath<K>::noise(a.noise ? a.noise + (int64_t)r * K * d : nullptr, d, i + e, a.key,
+                               a.next_step, (uint32_t)r, g);
             SoftMath<K>::probs(l, g, a.inv_tau1, a.kappa1, p);
 #pragma unroll
             for (int k = 0; k < K; ++k) {
@@ -509,7 +516,7 @@ extern "C" int gsq_soft_step(float* logits, float* mom_logits, const uint8_t* j0
   a.kt = kappa / tau;
   a.lr_l = lr_logits; a.lr_s = lr_scales;
   a.lc = lion_const(wd, beta1, beta2);
-  a.next = next; a.noise = noise_next; a.seed = seed; a.linear_id = linear_id;
+  a.next = next; a.noise = noise_next; a.key = philox_key(seed, linear_id);
   a.next_step = next_step;
   a.inv_tau1 = next ? 1.0f / tau_next : 0.f;
   a.kappa1 = kappa_next;
