@@ -23,8 +23,14 @@ Workload "rco": RCO allocation on the same stack and a GPTQ 
 KL head, backward through 24 blocks, straight-through dots); at most 2 timed steps after 3
 warm-up steps (a step takes seconds); windows sharded over ranks under torchrun.
 
+Workload "eval": the quantized-model eval on the same stack: packed
+mixed 2 / 3 / 4-bit MLX-affine linears (a 3.0-bit allocation from the GPTQ database, fp16 g64
+scales), 146 windows x 2048 ids, next-token NLL; value = scored tokens per second of one pass
+over all windows (each window's 8-window batch dequantizes every layer into L2-resident bf16
+scratch, then runs the bf16 tensor-core forward and the head + NLL row pass).
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload block|linear|gptq|rco]
+                  [--workload block|linear|gptq|rco|eval]
 
 N > 1 runs under torchrun, one rank per GPU. Block: the ranks quantize one block together,
 data-parallel over the positions of each micro-batch sequence with one NCCL all-reduce of the
@@ -58,7 +64,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="block", choices=["block", "linear", "gptq", "rco"])
+    ap.add_argument("--workload", default="block",
+                    choices=["block", "linear", "gptq", "rco", "eval"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=200)
     return ap.parse_args()
@@ -631,6 +638,232 @@ def run_reference_rco(args):
     print(json.dumps(res), flush=True)
 
 
+# ------------------------------------------------------------------------------ eval ---
+
+EVAL_WINDOWS, EVAL_CHUNK = 146, 8
+
+
+def eval_setup(dev):
+    """The 24-layer stack, its GPTQ database at 2 / 3 / 4 bits (fp16-rounded scales as the
+    shards store them), a mixed allocation at exactly 3.0 bits (the DP on the database's
+    sensitivities) packed into MLX affine words, and 146 windows of 2048 ids (seed 2)."""
+    import torch
+    from gsq_rco_mlx_b200.common.evaluate import PackedModel
+    from gsq_rco_mlx_b200.gsq.export import module_path
+    from gsq_rco_mlx_b200.rco.allocate import Bank, decoded_cost, proxy_dp_choice
+    from gsq_rco_mlx_b200.rco.database import DBSpec, build_database, random_model
+    model = random_model(n_layers=24, seed=0, device=dev)
+    calib = np.random.default_rng(0).integers(0, VOCAB, size=(N_SEQ, T_SEQ)).astype(np.int32)
+    man, res = build_database(model, calib, DBSpec(options=GPTQ_OPTIONS, n_layers=24),
+                              log=lambda *a: None, keep="device")
+    bank = Bank(man, res)
+    choice = proxy_dp_choice(bank, 3.0)
+    quantized = {}
+    for i, (L, name) in enumerate(bank.groups):
+        codes, scales, bits = bank.cands(i)[int(choice[i])]
+        quantized[module_path(L, name)] = dict(
+            codes=codes.cpu().numpy(),
+            scales=scales.cpu().numpy().astype(np.float16).astype(np.float32),
+            bits=int(bits), group_size=64)
+    pm = PackedModel.from_quantized(model, quantized, scale_dtype="float16")
+    windows = np.random.default_rng(2).integers(0, VOCAB, size=(EVAL_WINDOWS, T_SEQ)).astype(
+        np.int32)
+    hist = {b: int(sum(1 for q in quantized.values() if q["bits"] == b)) for b in GPTQ_OPTIONS}
+    info = {"bits_histogram": hist, "avg_bits": round(decoded_cost(bank, choice)[1], 4),
+            "packed_mb": round(pm.packed_bytes() / 1e6, 1)}
+    return pm, windows, info
+
+
+def eval_flops_per_token(T):
+    """Algorithmic FLOPs per scored token: the 168 linears, the causal attention (q k^T and
+    P v over the average T / 2 keys), the tied head."""
+    lin = 2 * 24 * (HID * (NH + 2 * NKV) * HD + HID * NH * HD + 3 * HID * INTER)
+    attn = 24 * 2 * 2 * (T / 2) * HD * NH
+    head = 2 * HID * VOCAB
+    return lin + attn + head
+
+
+def run_eval(args):
+    """Config 5: the quantized-model eval: packed mixed 2 / 3 / 4-bit linears (fp16 group-64
+    scales), 146 windows x 2048 ids, next-token NLL. A step is one pass over all 146 windows;
+    the metric is scored tokens per second. Under torchrun the windows are sharded over the
+    ranks with one all-reduce of the NLL sum."""
+    import torch
+    import torch.distributed as dist
+    from gsq_rco_mlx_b200 import _lib
+    from gsq_rco_mlx_b200.common.evaluate import Evaluator, perplexity
+    from gsq_rco_mlx_b200.gemm import LaunchLog
+    from gsq_rco_mlx_b200.gsq.staged import DataParallel
+
+    rank, world, local = dist_setup()
+    _lib.lib()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    steps, warmup = max(1, min(args.steps, 5)), max(3, min(args.warmup, 5))
+    pm, windows, info = eval_setup(dev)
+    dp = DataParallel()
+    ev = Evaluator(pm, T_SEQ, EVAL_CHUNK)
+    a, b = dp.window(0, EVAL_WINDOWS)
+    # device-resident windows of this rank (the timed step reads no host memory)
+    mine = windows[a:b]
+    tok = torch.as_tensor(mine.reshape(-1)).to(dev)
+    tgt_h = np.full(mine.shape, -1, dtype=np.int32)
+    tgt_h[:, :-1] = mine[:, 1:]
+    tgt = torch.as_tensor(tgt_h.reshape(-1)).to(dev)
+    n_b = -(-(b - a) // EVAL_CHUNK)
+    sums = torch.zeros(max(1, n_b), device=dev, dtype=torch.float64)
+    total = torch.zeros(1, device=dev, dtype=torch.float64)
+
+    def step():
+        for j in range(n_b):
+            w0, w1 = j * EVAL_CHUNK, min(b - a, (j + 1) * EVAL_CHUNK)
+            ev.forward_nll(tok[w0 * T_SEQ:w1 * T_SEQ], tgt[w0 * T_SEQ:w1 * T_SEQ], w1 - w0,
+                           sums[j:j + 1])
+        _lib.call("gsq_sum_f64", _lib.ptr(sums), n_b, _lib.ptr(total), _lib.stream_ptr())
+        dp.allreduce(total)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(warmup):
+        step()
+    barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    n0 = _lib.Launches.n
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    barrier()
+    clk = clocks.stop()
+    sec = max_over_ranks(e0.elapsed_time(e1) / 1000 / steps)
+    launches = (_lib.Launches.n - n0) // steps
+    nll = float(total.item()) / (EVAL_WINDOWS * (T_SEQ - 1))
+    n_tok = EVAL_WINDOWS * (T_SEQ - 1)
+
+    # roofline of the dominant kernel (the tensor-core GEMM) over one batch's launches
+    with LaunchLog() as log:
+        ev.forward_nll(tok[:EVAL_CHUNK * T_SEQ], tgt[:EVAL_CHUNK * T_SEQ],
+                       min(EVAL_CHUNK, b - a), sums[:1])
+    rows = log.summary()
+    fl = sum(2.0 * M * N * K * bt for (M, N, K, p, bt, t) in rows)
+    t_ms = sum(t for (*_, t) in rows)
+    pk = peaks()
+    peak = float(pk.get("bf16_tflops", 1590.0))
+    achieved = fl / (t_ms * 1e-3) / 1e12
+
+    # end to end through the public API: host windows in, the perplexity dict out
+    barrier()
+    t0 = time.perf_counter()
+    r = perplexity(pm, windows, chunk_seqs=EVAL_CHUNK, dp=dp, evaluator=ev)
+    barrier()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    out = {
+        "metric": "eval tokens/s (24-layer Qwen2.5-0.5B architecture, packed mixed 2/3/4-bit "
+                  "g64 fp16 scales, 146 x 2048 windows, next-token NLL)",
+        "value": round(n_tok / sec, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(sec * 1000, 2), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: random-init 24-layer stack, GPTQ database, uniform-random windows",
+        "config": {"workload": "config 5: packed-model eval, 146 windows x 2048",
+                   **info, "nll_per_token": round(nll, 6), "windows_per_batch": EVAL_CHUNK,
+                   "parallelism": f"windows sharded over {world} rank(s), NCCL all-reduce of "
+                                  "the NLL sum",
+                   "l2": "per-batch activations (8 x 2048 x 896 bf16 per state, logits "
+                         "1024 x 151936) > L2",
+                   "algorithmic_tflops": round(eval_flops_per_token(T_SEQ) * n_tok / sec / 1e12,
+                                               1)},
+        "e2e": {"value": round(n_tok / e2e_s, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(windows.nbytes * 2),
+                "d2h_bytes_per_step": 8,
+                "what": "perplexity(): host windows copied per batch (ids and targets), "
+                        "NLL sum read back; ppl " + f"{r['ppl']:.3f}"},
+        "gpu_launches": int(launches),
+        "roofline": {"kernel": "gemm_tc_kernel (all launches of one 8-window batch)",
+                     "bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)"
+                     if "bf16_tflops" in pk else "fallback 1590 TFLOP/s",
+                     "note": "2MNK per launch (the attention scores' three bf16 terms counted "
+                             "once)"},
+        "clocks": clk,
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline_eval()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_baseline_eval(T=512):
+    """The CPU restatement of the dense bf16-dequantized eval (oracle.block / oracle.evaluate)
+    on a bounded sample: one window of T tokens through 2 blocks and the tied head over the
+    full vocabulary for its rows, scaled to 24 blocks; tokens per second."""
+    import torch
+    from oracle import block as ob
+    from oracle import evaluate as oe
+    torch.set_num_threads(os.cpu_count())
+    g = torch.Generator().manual_seed(0)
+    W = {"q_proj": (NH * HD, HID), "k_proj": (NKV * HD, HID), "v_proj": (NKV * HD, HID),
+         "o_proj": (HID, NH * HD), "gate_proj": (INTER, HID), "up_proj": (INTER, HID),
+         "down_proj": (HID, INTER), "q_bias": (NH * HD,), "k_bias": (NKV * HD,),
+         "v_bias": (NKV * HD,)}
+    W = {k: (0.02 * torch.randn(*s, generator=g)).bfloat16().float() for k, s in W.items()}
+    W["in_norm"] = torch.ones(HID)
+    W["post_norm"] = torch.ones(HID)
+    E = (0.02 * torch.randn(VOCAB, HID, generator=g)).bfloat16().float()
+    ids = torch.randint(0, VOCAB, (T + 1,), generator=g)
+    t0 = time.perf_counter()
+    h = E[ids[:-1]]
+    for _ in range(2):
+        h = ob.block_hard(h, W)[0]
+    t_blocks = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    hn = ob.rmsnorm(h, torch.ones(HID))
+    z = ob.bf(hn.double() @ E.double().T)
+    oe.nll_rows(z, ids[1:].numpy())
+    t_head = time.perf_counter() - t0
+    per_window = t_blocks * 12 + t_head
+    return {"value": round(T / per_window, 2), "unit": "tokens/s (extrapolated)",
+            "cores": os.cpu_count(), "kind": "port",
+            "sample": f"one {T}-token window through 2 blocks (x12 for 24) and the tied head over "
+                      "the full vocabulary (torch-CPU float64 restatement; the MLX path is "
+                      "unavailable)"}
+
+
+def run_reference_eval(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    cb = cpu_baseline_eval()
+    res = {"impl": "reference",
+           "metric": "eval tokens/s (24-layer Qwen2.5-0.5B architecture, packed mixed 2/3/4-bit "
+                     "g64 fp16 scales, 146 x 2048 windows, next-token NLL)",
+           "value": cb["value"], "unit": "tokens/s", "n_gpus": world, "steps": 1, "warmup": 0,
+           "ms_per_step": round(EVAL_WINDOWS * (T_SEQ - 1) / cb["value"] * 1000, 1),
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+           "data": "synthetic",
+           "config": {"workload": "config 5: packed-model eval, 146 windows x 2048"},
+           "cpu_baseline": cb,
+           "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(res), flush=True)
+
+
 # ---------------------------------------------------------------------------- linear ---
 
 OUT_F, IN_F, N_SEQ_L, T_SEQ_L = 4864, 896, 32, 512
@@ -800,6 +1033,8 @@ def main():
         return run_reference_gptq(args) if args.impl == "reference" else run_gptq(args)
     if args.workload == "rco":
         return run_reference_rco(args) if args.impl == "reference" else run_rco(args)
+    if args.workload == "eval":
+        return run_reference_eval(args) if args.impl == "reference" else run_eval(args)
     if args.impl == "reference":
         run_reference(args)
     else:

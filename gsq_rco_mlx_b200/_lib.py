@@ -64,6 +64,10 @@ SIGNATURES = {
     "gptq_err": [_vp, _vp, _vp, _i32, _i32, _vp, _vp, _vp],
     "mckp_dp_f64": [_vp, _vp, _i32, _i32, _i32, _i64, _vp, _vp, _vp, _vp],
     "mckp_dp_f64_noalloc": [_vp, _vp, _i32, _i32, _i32, _i64, _vp, _vp],
+    "qdequant_packed": [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _vp],
+    "qgemm_packed": [_vp, _i32, _i32, _i64, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64,
+                     _i32, _vp, _i64, _vp, _vp],
+    "gsq_nll_rows": [_vp, _i32, _i32, _i64, _vp, _vp, _vp],
 }
 
 _lib = None

@@ -129,6 +129,44 @@ kl_rows_kernel(const __nv_bfloat16* __restrict__ zq, const __nv_bfloat16* __rest
   }
 }
 
+// Next-token NLL of one logit row (evaluate.py:35-52): nll = logsumexp(z) - z[target] with z
+// the float32 value of the bf16 logits, the max and the float64 sum of exp(z - max) as in
+// kl_rows_kernel. target < 0 marks a row that is not scored (nll = 0). One CTA per row.
+__global__ void __launch_bounds__(kKlThreads)
+nll_rows_kernel(const __nv_bfloat16* __restrict__ z, int V, int64_t ld,
+                const int32_t* __restrict__ targets, double* __restrict__ nll) {
+  __shared__ float shf[32];
+  __shared__ double shd[32];
+  const int64_t row = blockIdx.x;
+  const int t = targets[row];
+  if (t < 0 || t >= V) {  // not scored, or an id outside the vocabulary (NaN)
+    if (threadIdx.x == 0) nll[row] = t < 0 ? 0.0 : (double)NAN;
+    return;
+  }
+  const __nv_bfloat16* a = z + row * ld;
+  const int nv = V / 8;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    float x[8];
+    load8(a + 8 * i, x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, x[j]);
+  }
+  m = block_max_f(m, shf);
+  double s = 0.0;
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    float x[8];
+    load8(a + 8 * i, x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += (double)expf(__fsub_rn(x[j], m));
+  }
+  s = block_sum_d(s, shd);
+  if (threadIdx.x == 0) {
+    const float lse = __fadd_rn(m, logf((float)s));
+    nll[row] = (double)__fsub_rn(lse, __bfloat162float(a[t]));
+  }
+}
+
 struct DotOpts {
   const uint8_t* codes[kMaxOptions];
   const float* scales[kMaxOptions];
@@ -273,6 +311,17 @@ extern "C" int ste_dots(const float* G, const void* W, int out_f, int in_f, int 
                                                 group_size, K, opt, partials);
   GSQ_CHECK_LAUNCH();
   dots_final_kernel<<<1, 256, 0, st>>>(partials, (int)nb, K, out);
+  GSQ_CHECK_LAUNCH();
+  return GSQ_OK;
+}
+
+extern "C" int gsq_nll_rows(const void* z, int n, int V, int64_t ld, const int32_t* targets,
+                            double* nll, void* stream) {
+  if (!z || !targets || !nll || n <= 0 || V <= 0 || (V & 7) || ld < V || (ld & 7) ||
+      ((uintptr_t)z & 15))
+    return GSQ_EINVAL;
+  nll_rows_kernel<<<n, kKlThreads, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)z, V, ld,
+                                                              targets, nll);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }

@@ -65,10 +65,12 @@ def wterms(W):
 class BlockWeights:
     """bf16 CUDA weights of one block plus the stacked forms the fused GEMMs read."""
 
-    def __init__(self, W: dict):
+    def __init__(self, W: dict, qk=None):
+        """qk: an existing [Wq; Wk] buffer whose row blocks are W["q_proj"] and W["k_proj"]
+        (weights dequantized in place); otherwise the stacked copy is made here."""
         self.W = {k: v.contiguous() for k, v in W.items()}
         w = self.W
-        self.qk = torch.cat([w["q_proj"], w["k_proj"]]).contiguous()
+        self.qk = torch.cat([w["q_proj"], w["k_proj"]]).contiguous() if qk is None else qk
         self.qk_bias = torch.cat([w["q_bias"], w["k_bias"]]).float().contiguous()
         self.v_bias = w["v_bias"].float().contiguous()
 

@@ -392,6 +392,36 @@ int gsq_rope_bwd(const float *dy, int64_t ld_i, int S, int T, int nh, const floa
 int gsq_group_sum(const float *in, int64_t ld_i, int S, int nh, int rep, int T, float *out_f,
                   void *out_b, int64_t ld_o, int col0, void *stream);
 
+/* ---- packed quantized-model eval (MLX affine export format) ----
+ * A packed linear W [N][K] (src/gsq_rco/gsq/export.py:60-90, pack_codes / to_mlx_affine):
+ * words u32 [N][K bits / 32], value k of row n at stream bits [k bits, (k + 1) bits), least
+ * significant bit first, little-endian words; scales and biases [N][K / group_size] of
+ * scale_dtype 0 = bf16, 1 = f16, 2 = f32; w = scale q + bias (float32, exact), rounded to bf16.
+ * bits in {2, 3, 4, 5, 6, 8}, group_size in {32, 64, 128} dividing K; words aligned to 16 bytes
+ * (bits 4, 8), 8 bytes (2, 6) or 4 bytes (3, 5). */
+
+/* out bf16 [N][ldw] = the bf16 dense weight (ldw % 8 == 0, 16-byte aligned): the dequant of
+ * mx.dequantize (export.py:87-90 inverse) as one HBM stream. */
+int qdequant_packed(const uint32_t *words, const void *scales, const void *biases,
+                    int scale_dtype, int N, int K, int bits, int group_size, void *out,
+                    int64_t ldw, void *stream);
+
+/* Y [M][ld_y] = X W^T (X bf16 [M][ld_x], 16-byte aligned, ld_x % 8 == 0; Y bf16 rounded once,
+ * or float32 if y_f32), float32 accumulation: the QuantizedLinear matmul of mlx-lm under
+ * evaluate.py:35-78. M <= 8: one fused kernel, the dequant inside the weight load (HBM stream
+ * of the packed words). M > 8: the weight is dequantized into workspace (>= N K 2 bytes,
+ * 16-byte aligned) and the tensor-core GEMM reads it (err: device int for its bounded waits). */
+int qgemm_packed(const void *X, int M, int K, int64_t ld_x, const uint32_t *words,
+                 const void *scales, const void *biases, int scale_dtype, int N, int bits,
+                 int group_size, void *Y, int64_t ld_y, int y_f32, void *workspace,
+                 int64_t workspace_bytes, int *err, void *stream);
+
+/* Next-token NLL rows (evaluate.py:35-52, nll_from_hidden): z bf16 [n][ld] logits (V % 8 == 0,
+ * 16-byte aligned rows), nll[r] = logsumexp(z_r) - z_r[targets[r]] (float32 logsumexp with a
+ * float64 sum of exp, as gsq_kl_rows); targets[r] < 0: row not scored (0); >= V: NaN. */
+int gsq_nll_rows(const void *z, int n, int V, int64_t ld, const int32_t *targets, double *nll,
+                 void *stream);
+
 #ifdef __cplusplus
 }
 #endif

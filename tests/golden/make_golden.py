@@ -237,12 +237,45 @@ def gen_gsq(gptq, quant, oracles):
     np.savez_compressed(OUT / "gsq.npz", **out)
 
 
+def gen_export():
+    """Packed words of the MLX affine export (gsq/export.py:61-73, pack_codes; mlx_bits :52-58;
+    bits_report :218-250 on the hand-made case of tests/test_export.py:139-150). export.py
+    imports mlx.core for its scale casts only; the stand-in module gains the dtype names its
+    module-level table reads (never called)."""
+    core = sys.modules["mlx.core"]
+    for name in ("bfloat16", "float16", "float32", "uint16", "uint32"):
+        if not hasattr(core, name):
+            setattr(core, name, object())
+    import gsq_rco.gsq.export as ex
+    out = {}
+    rng = np.random.default_rng(7)
+    for bits in (2, 3, 4, 5, 6, 8):
+        codes = rng.integers(0, 1 << bits, size=(5, 256), dtype=np.uint8)
+        codes[0] = 0
+        codes[1] = (1 << bits) - 1
+        codes[2, ::2] = (1 << bits) - 1
+        out[f"codes{bits}"] = codes
+        out[f"words{bits}"] = ex.pack_codes(codes, bits)
+    ternary = rng.integers(0, 3, size=(3, 128), dtype=np.uint8)
+    out["codes_t"], out["words_t"] = ternary, ex.pack_codes(ternary + np.uint8(1), ex.mlx_bits(1))
+    out["mlx_bits"] = np.array([ex.mlx_bits(b) for b in (1, 2, 3, 4, 5, 6, 8)])
+    hand = {"a": dict(codes=np.zeros((4, 128), np.uint8), scales=np.ones((4, 2), np.float16),
+                      bits=2, group_size=64),
+            "b": dict(codes=np.zeros((2, 64), np.uint8), scales=np.ones((2, 1), np.float16),
+                      bits=1, group_size=64)}
+    rep = ex.bits_report(hand, 640)
+    for k in ("code_bpp", "native_bpp", "mlx_bpp", "shard_bpp"):
+        out[f"report_{k}"] = np.float64(rep[k])
+    np.savez_compressed(OUT / "export.npz", **out)
+
+
 def main():
     gptq, quant, manifold, loop, oracles = _import_reference()
     gen_gptq(gptq)
     gen_dp(manifold, loop)
     gen_rco_host(manifold, loop)
     gen_gsq(gptq, quant, oracles)
+    gen_export()
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 
