@@ -78,7 +78,9 @@ class PackedLinear:
         return out
 
     def __call__(self, x, out=None, y_f32=False):
-        """y = x W^T for x bf16 [M, K] (QuantizedLinear's matmul): bf16 [M, N] (or float32)."""
+        """y = x W^T for x bf16 [M, K] (QuantizedLinear's matmul): bf16 [M, N] (or float32).
+        M <= 8: the fused matrix-vector kernel on the unrounded weight s q + bias; larger M: the
+        bf16-dequantized weight on the tensor cores (MLX's two forms)."""
         if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != self.K:
             raise ValueError(f"x must be bf16 [M, {self.K}]")
         x = x.contiguous()

@@ -12,8 +12,9 @@
 //   qdequant_kernel  packed -> bf16 [N][ldw]: one thread per 32 values (bits words), an HBM
 //                    stream; the prefill GEMM reads its output as the K-major B operand.
 //   qgemv_kernel     Y [M][N] = X W^T for M <= 8 rows with the dequant fused into the weight
-//                    load: a warp per output column n, lanes over 32-value blocks of the row,
-//                    X staged in shared memory, warp-shuffle reduction.
+//                    load (MLX's matrix-vector form: per 32-value block s sum(x q) + bias
+//                    sum(x), the weight never rounded): a warp per output column n, lanes over
+//                    blocks, X staged in shared memory, warp-shuffle reduction.
 #include <cuda_fp16.h>
 #include <string.h>
 
@@ -22,6 +23,7 @@
 namespace gsq {
 
 constexpr int kQgemvMaxRows = 8;
+constexpr size_t kQgemvSmemMax = 160 * 1024;
 
 __device__ __forceinline__ float load_scale(const void* p, int64_t i, int dtype) {
   if (dtype == 0) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
@@ -88,53 +90,123 @@ qdequant_kernel(const uint32_t* __restrict__ words, const void* __restrict__ sca
   }
 }
 
-// Y[m][n] = sum_k X[m][k] bf16(w[n][k]) for m < MR, float32 accumulation; out bf16 (rounded
-// once) or float32. Dynamic shared memory: X as bf16 [MR][K].
-template <int B, int MR>
+// Y[m][n] = sum over 32-value blocks b of the row: s_b (sum_j x[m][32 b + j] q_j) + bias_b
+// (sum_j x[m][32 b + j]), float32 -- MLX's quantized matrix-vector form (the weight s q + bias is
+// never rounded; the code sums are exact integers times x). A warp per output column n, lanes
+// over blocks (U blocks' words loaded before any arithmetic), codes turned into floats with the
+// 2^23 exponent trick (float(q) = bits(0x4B000000 | q) - 2^23, no conversion unit), X staged in
+// shared memory transposed per block position ([j / V][block][V], V values per vector load:
+// consecutive lanes read consecutive vectors) as float32 (XF) or bf16, with per-block sums of X.
+template <int B, int MR, int U, bool XF>
 __global__ void __launch_bounds__(256)
 qgemv_kernel(const __nv_bfloat16* __restrict__ X, int64_t ld_x, int M, int K,
              const uint32_t* __restrict__ words, const void* __restrict__ scales,
              const void* __restrict__ biases, int sdtype, int gs, int N, void* __restrict__ Y,
              int64_t ld_y, int y_f32) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);
-  const int nv = K / 8;
-  for (int i = threadIdx.x; i < MR * nv; i += blockDim.x) {
-    const int m = i / nv, c = i - m * nv;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (m < M) v = *reinterpret_cast<const uint4*>(X + (int64_t)m * ld_x + 8 * c);
-    *reinterpret_cast<uint4*>(xs + (int64_t)m * K + 8 * c) = v;
+  const int nblk = K / 32;
+  float* xsum = reinterpret_cast<float*>(smem_raw);                  // [MR][nblk]
+  unsigned char* xbase = smem_raw + (((size_t)MR * nblk * sizeof(float) + 15) & ~(size_t)15);
+  constexpr int V = XF ? 4 : 8;                                      // values per 16-byte vector
+  // staging: thread (m, b) moves block b of row m (32 values) and sums it
+  for (int i = threadIdx.x; i < MR * nblk; i += blockDim.x) {
+    const int m = i / nblk, b = i - m * nblk;
+    float sum = 0.f;
+#pragma unroll
+    for (int c = 0; c < 32 / 8; ++c) {
+      uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+      if (m < M) raw = *reinterpret_cast<const uint4*>(X + (int64_t)m * ld_x + 32 * b + 8 * c);
+      const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      float f[8];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 v = __bfloat1622float2(x2[t]);
+        f[2 * t] = v.x;
+        f[2 * t + 1] = v.y;
+      }
+#pragma unroll
+      for (int t = 0; t < 8; ++t) sum = __fadd_rn(sum, f[t]);
+      if constexpr (XF) {
+        float* xs = reinterpret_cast<float*>(xbase) + (size_t)m * K;
+        *reinterpret_cast<float4*>(xs + ((size_t)(2 * c) * nblk + b) * 4) =
+            make_float4(f[0], f[1], f[2], f[3]);
+        *reinterpret_cast<float4*>(xs + ((size_t)(2 * c + 1) * nblk + b) * 4) =
+            make_float4(f[4], f[5], f[6], f[7]);
+      } else {
+        __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(xbase) + (size_t)m * K;
+        *reinterpret_cast<uint4*>(xs + ((size_t)c * nblk + b) * 8) = raw;
+      }
+    }
+    xsum[m * nblk + b] = sum;
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int nblk = K / 32, wpr = nblk * B, G = K / gs;
+  const int wpr = nblk * B, G = K / gs;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int n = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; n < N; n += warps) {
     float acc[MR];
 #pragma unroll
     for (int m = 0; m < MR; ++m) acc[m] = 0.f;
-    for (int blk = lane; blk < nblk; blk += 32) {
-      uint32_t w[B];
-      load_words<B>(words + (int64_t)n * wpr + (int64_t)blk * B, w);
-      const int64_t gi = (int64_t)n * G + (blk * 32) / gs;
-      const float s = load_scale(scales, gi, sdtype), b = load_scale(biases, gi, sdtype);
+    const uint32_t* wrow = words + (int64_t)n * wpr;
+    for (int b0 = lane; b0 < nblk; b0 += 32 * U) {
+      uint32_t w[U][B];
+      float sc[U], bi[U];
 #pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        float wf[8];
+      for (int u = 0; u < U; ++u) {
+        const int b = b0 + 32 * u;
+        if (b < nblk) {
+          load_words<B>(wrow + (int64_t)b * B, w[u]);
+          const int64_t gi = (int64_t)n * G + (b * 32) / gs;
+          sc[u] = load_scale(scales, gi, sdtype);
+          bi[u] = load_scale(biases, gi, sdtype);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          wf[j] = bf16r_dev(__fadd_rn(__fmul_rn(s, (float)code_at<B>(w, 8 * v + j)), b));
+          for (int t = 0; t < B; ++t) w[u][t] = 0u;
+          sc[u] = 0.f;
+          bi[u] = 0.f;
+        }
+      }
 #pragma unroll
-        for (int m = 0; m < MR; ++m) {
-          const uint4 xv = *reinterpret_cast<const uint4*>(xs + (int64_t)m * K + blk * 32 + 8 * v);
-          const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
+      for (int u = 0; u < U; ++u) {
+        const int b = b0 + 32 * u;
+        if (b >= nblk) break;
+        float dot[MR];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 xf = __bfloat1622float2(x2[j]);
-            acc[m] = __fmaf_rn(xf.x, wf[2 * j], acc[m]);
-            acc[m] = __fmaf_rn(xf.y, wf[2 * j + 1], acc[m]);
+        for (int m = 0; m < MR; ++m) dot[m] = 0.f;
+#pragma unroll
+        for (int jv = 0; jv < 32 / V; ++jv) {
+          float q[V];
+#pragma unroll
+          for (int t = 0; t < V; ++t)
+            q[t] = __fsub_rn(__int_as_float(0x4B000000 | (int)code_at<B>(w[u], jv * V + t)),
+                             8388608.f);
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            float xv[V];
+            if constexpr (XF) {
+              const float4 v = *reinterpret_cast<const float4*>(
+                  reinterpret_cast<const float*>(xbase) + (size_t)m * K +
+                  ((size_t)jv * nblk + b) * 4);
+              xv[0] = v.x; xv[1] = v.y; xv[2] = v.z; xv[3] = v.w;
+            } else {
+              const uint4 raw = *reinterpret_cast<const uint4*>(
+                  reinterpret_cast<const __nv_bfloat16*>(xbase) + (size_t)m * K +
+                  ((size_t)jv * nblk + b) * 8);
+              const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+              for (int t = 0; t < V / 2; ++t) {
+                const float2 f = __bfloat1622float2(x2[t]);
+                xv[2 * t] = f.x;
+                xv[2 * t + 1] = f.y;
+              }
+            }
+#pragma unroll
+            for (int t = 0; t < V; ++t) dot[m] = __fmaf_rn(xv[t], q[t], dot[m]);
           }
         }
+#pragma unroll
+        for (int m = 0; m < MR; ++m)
+          acc[m] = __fmaf_rn(sc[u], dot[m], __fmaf_rn(bi[u], xsum[m * nblk + b], acc[m]));
       }
     }
 #pragma unroll
@@ -186,19 +258,26 @@ int qdequant_launch(const uint32_t* words, const void* scales, const void* biase
   return GSQ_OK;
 }
 
+inline size_t qgemv_smem(int MR, int K, bool xf) {
+  return (((size_t)MR * (K / 32) * sizeof(float) + 15) & ~(size_t)15) + (size_t)MR * K * (xf ? 4 : 2);
+}
+
 template <int B>
 int qgemv_launch_b(const __nv_bfloat16* X, int64_t ld_x, int M, int K, const uint32_t* words,
                    const void* scales, const void* biases, int sdtype, int gs, int N, void* Y,
                    int64_t ld_y, int y_f32, cudaStream_t st) {
+  constexpr int U = B <= 4 ? 4 : 2;
   const int MR = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
-  const size_t smem = (size_t)MR * K * sizeof(__nv_bfloat16);
+  const bool xf = qgemv_smem(MR, K, true) <= kQgemvSmemMax;
+  const size_t smem = qgemv_smem(MR, K, xf);
+  if (smem > kQgemvSmemMax) return GSQ_ENOTSUP;
   int64_t blocks = ((int64_t)N * 32 + 255) / 256;
   const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
   const unsigned g = (unsigned)(blocks < 1 ? 1 : blocks);
-#define GSQ_QGEMV(RR)                                                                        \
+#define GSQ_QGEMV(RR, XX)                                                                    \
   do {                                                                                       \
-    auto kern = qgemv_kernel<B, RR>;                                                         \
+    auto kern = qgemv_kernel<B, RR, U, XX>;                                                  \
     if (smem > 48 * 1024 &&                                                                  \
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != \
             cudaSuccess)                                                                     \
@@ -206,10 +285,17 @@ int qgemv_launch_b(const __nv_bfloat16* X, int64_t ld_x, int M, int K, const uin
     kern<<<g, 256, smem, st>>>(X, ld_x, M, K, words, scales, biases, sdtype, gs, N, Y, ld_y, \
                                y_f32);                                                       \
   } while (0)
-  if (MR == 1) GSQ_QGEMV(1);
-  else if (MR == 2) GSQ_QGEMV(2);
-  else if (MR == 4) GSQ_QGEMV(4);
-  else GSQ_QGEMV(8);
+  if (xf) {
+    if (MR == 1) GSQ_QGEMV(1, true);
+    else if (MR == 2) GSQ_QGEMV(2, true);
+    else if (MR == 4) GSQ_QGEMV(4, true);
+    else GSQ_QGEMV(8, true);
+  } else {
+    if (MR == 1) GSQ_QGEMV(1, false);
+    else if (MR == 2) GSQ_QGEMV(2, false);
+    else if (MR == 4) GSQ_QGEMV(4, false);
+    else GSQ_QGEMV(8, false);
+  }
 #undef GSQ_QGEMV
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
@@ -241,7 +327,6 @@ extern "C" int qgemm_packed(const void* X, int M, int K, int64_t ld_x, const uin
   cudaStream_t st = (cudaStream_t)stream;
   const auto* x = (const __nv_bfloat16*)X;
   if (M <= kQgemvMaxRows) {
-    if ((size_t)kQgemvMaxRows * K * sizeof(__nv_bfloat16) > 200 * 1024) return GSQ_ENOTSUP;
     switch (bits) {
       case 2: return qgemv_launch_b<2>(x, ld_x, M, K, words, scales, biases, scale_dtype,
                                        group_size, N, Y, ld_y, y_f32, st);

@@ -1,7 +1,8 @@
 """Representative launches of the hot kernels at Qwen2.5-0.5B block shapes, for profilers and
 micro-timing (one process, one GPU, a few GB of device memory).
 
-  python -m gsq_rco_mlx_b200.kernel_cases [mlp_gemms|attn|soft_step|cublas] [--once]
+  python -m gsq_rco_mlx_b200.kernel_cases [mlp_gemms|attn|soft_step|cublas|packed|eval_batch]
+                                          [--once]
 
 --once runs every case a single time (an ncu capture: `-k regex:<kernel> -c <n>`); otherwise
 each case is timed with CUDA events over 10 launches after 3 warm-up launches and printed with
@@ -14,6 +15,8 @@ mlp_gemms: the five GEMMs of one mlp-stage resample (micro-batch 2 x 2047 rows) 
 attn: the causal scores GEMM and softmax of 8 sequences x 14 heads x 2048 positions.
 soft_step: the fused backward + Lion + next forward of one up_proj-shaped soft linear (R = 2).
 cublas: library bf16 GEMMs of the mlp shapes, for context only (not on any product path).
+packed: the packed-weight dequant of one layer and the fused dequant-GEMV (HBM streams).
+eval_batch: one 8-window batch of the packed 24-layer eval (forward, head, NLL rows).
 """
 from __future__ import annotations
 
@@ -25,6 +28,10 @@ from . import _lib
 from .gemm import Terms, check_err, gemm
 
 H, I, HEADS, KV, HD, T = 896, 4864, 14, 2, 64, 2048
+
+
+class Bytes(int):
+    """A case's algorithmic byte count (printed as GB/s), where other cases give FLOPs."""
 
 
 def _terms(rows, cols, n, dev, g):
@@ -110,7 +117,73 @@ def cublas(dev, g):
     }
 
 
-CASES = {"mlp_gemms": mlp_gemms, "attn": attn, "soft_step": soft_step, "cublas": cublas}
+def _packed_linear(N, K, bits, dev, g):
+    """A packed linear with random words (every bit pattern is a valid code stream) and fp16
+    g64 scales, generated on the device."""
+    from .common.evaluate import PackedLinear
+    words = torch.randint(-2 ** 31, 2 ** 31, (N, K * bits // 32), device=dev, dtype=torch.int64,
+                          generator=g).to(torch.int32)
+    s = (0.01 * torch.randn(N, K // 64, device=dev, generator=g)).half()
+    return PackedLinear(words, s, (-(1 << (bits - 1)) * s.float()).half(), bits, 64, K)
+
+
+def packed(dev, g):
+    """Packed 3-bit weights (fp16 g64 scales): the dequant stream of one decoder layer's seven
+    linears into bf16, and the fused dequant-GEMV of a 65536 x 8192 weight (201 MB packed, more
+    than L2) at 1 and 8 rows. Figures are algorithmic bytes: packed words + scales + biases read,
+    bf16 weights written (dequant) or X read / Y written (GEMV)."""
+    shapes = [(1024, H), (128, H), (H, H), (I, H), (I, H), (H, I)]
+    lins = [_packed_linear(n, k, 3, dev, g) for n, k in shapes]
+    outs = [torch.empty(n, k, device=dev, dtype=torch.bfloat16) for n, k in shapes]
+    dq_bytes = sum(n * k * 3 // 8 + 2 * 2 * n * k // 64 + 2 * n * k for n, k in shapes)
+    big = _packed_linear(65536, 8192, 3, dev, g)
+    gv_bytes = 65536 * 8192 * 3 // 8 + 2 * 2 * 65536 * 8192 // 64
+    x1 = torch.randn(1, 8192, device=dev, generator=g).bfloat16()
+    x8 = torch.randn(8, 8192, device=dev, generator=g).bfloat16()
+    y1 = torch.empty(1, 65536, device=dev, dtype=torch.bfloat16)
+    y8 = torch.empty(8, 65536, device=dev, dtype=torch.bfloat16)
+
+    def dq():
+        for lin, o in zip(lins, outs):
+            lin.dequant(o)
+    return {
+        "qdequant layer (3-bit)": (Bytes(dq_bytes), dq),
+        "qgemv 65536x8192 M=1": (Bytes(gv_bytes), lambda: big(x1, out=y1)),
+        "qgemv 65536x8192 M=8": (Bytes(gv_bytes), lambda: big(x8, out=y8)),
+    }
+
+
+def eval_batch(dev, g):
+    """One 8-window x 2048 batch of the packed eval through 24 random 3-bit layers and the
+    tied head (next-token NLL): the launch mix of bench.py's eval step."""
+    import numpy as np
+    from .common.evaluate import Evaluator, PackedModel
+    from .gsq.e2e import LIN_ORDER, BlockConfig
+    from .rco.database import random_model
+    cfg = BlockConfig()
+    model = random_model(n_layers=24, seed=0, device=dev)
+    layers = []
+    for L, W in enumerate(model.layers):
+        d = {k: W[k] for k in ("q_bias", "k_bias", "v_bias", "in_norm", "post_norm")}
+        for name in LIN_ORDER:
+            n, k = W[name].shape
+            d[name] = _packed_linear(n, k, 3, dev, g)
+        layers.append(d)
+    del model.layers
+    pm = PackedModel(cfg, model.embed, model.norm, layers)
+    ev = Evaluator(pm, T, 8)
+    rng = np.random.default_rng(2)
+    win = rng.integers(0, model.embed.shape[0], size=(8, T))
+    tok = torch.as_tensor(win.reshape(-1).astype(np.int32)).to(dev)
+    tg = np.full(win.shape, -1, dtype=np.int32)
+    tg[:, :-1] = win[:, 1:]
+    tgt = torch.as_tensor(tg.reshape(-1)).to(dev)
+    out = torch.zeros(1, device=dev, dtype=torch.float64)
+    return {"eval batch 8 x 2048": (None, lambda: ev.forward_nll(tok, tgt, 8, out))}
+
+
+CASES = {"mlp_gemms": mlp_gemms, "attn": attn, "soft_step": soft_step, "cublas": cublas,
+         "packed": packed, "eval_batch": eval_batch}
 
 
 def main(argv):
@@ -136,7 +209,11 @@ def main(argv):
             e1.record()
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) / 10 * 1000
-            extra = f"  {flops / us / 1e6:8.1f} TFLOP/s executed bf16" if flops else ""
+            extra = ""
+            if isinstance(flops, Bytes):
+                extra = f"  {flops / us / 1e3:8.1f} GB/s algorithmic"
+            elif flops:
+                extra = f"  {flops / us / 1e6:8.1f} TFLOP/s executed bf16"
             print(f"{label:28s} {us:9.1f} us{extra}", flush=True)
     check_err(dev)
 

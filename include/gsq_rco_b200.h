@@ -408,9 +408,11 @@ int qdequant_packed(const uint32_t *words, const void *scales, const void *biase
 
 /* Y [M][ld_y] = X W^T (X bf16 [M][ld_x], 16-byte aligned, ld_x % 8 == 0; Y bf16 rounded once,
  * or float32 if y_f32), float32 accumulation: the QuantizedLinear matmul of mlx-lm under
- * evaluate.py:35-78. M <= 8: one fused kernel, the dequant inside the weight load (HBM stream
- * of the packed words). M > 8: the weight is dequantized into workspace (>= N K 2 bytes,
- * 16-byte aligned) and the tensor-core GEMM reads it (err: device int for its bounded waits). */
+ * evaluate.py:35-78, in MLX's two forms. M <= 8 (matrix-vector): one fused kernel reads the
+ * packed words once (HBM stream) and forms, per 32-value block, s sum(x q) + bias sum(x) -- the
+ * weight s q + bias is never rounded. M > 8 (matrix-matrix): the weight is dequantized to bf16
+ * into workspace (>= N K 2 bytes, 16-byte aligned) and the tensor-core GEMM reads it (err:
+ * device int for its bounded waits). */
 int qgemm_packed(const void *X, int M, int K, int64_t ld_x, const uint32_t *words,
                  const void *scales, const void *biases, int scale_dtype, int N, int bits,
                  int group_size, void *Y, int64_t ld_y, int y_f32, void *workspace,

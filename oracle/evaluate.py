@@ -69,6 +69,14 @@ def affine(codes, scales, bits, scale_dtype=torch.bfloat16):
     return q, s.to(scale_dtype).to(F64).numpy(), b.to(scale_dtype).to(F64).numpy()
 
 
+def affine_weight(codes, scales, bits, group_size=64, scale_dtype=torch.bfloat16):
+    """The unrounded weight scale q + bias (float64) with scale / bias in the export dtype: what
+    MLX's quantized matrix-vector product multiplies by (export.py:13-19)."""
+    q, s, b = affine(codes, scales, bits, scale_dtype)
+    gid = np.arange(q.shape[1]) // group_size
+    return torch.as_tensor(s[:, gid] * q + b[:, gid])
+
+
 def dequant(codes, scales, bits, group_size=64, scale_dtype=torch.bfloat16):
     """Dense bf16 weight (float32 values) of native codes / scales after the affine export:
     bf16(scale q + bias) with scale / bias in the export dtype."""

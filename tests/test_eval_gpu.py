@@ -14,7 +14,7 @@ DEV = "cuda"
 DT = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}
 
 
-def _linear(N, K, bits, gs, scale_dtype, seed):
+def _linear(N, K, bits, gs, scale_dtype, seed, unrounded=False):
     from gsq_rco_mlx_b200.common.evaluate import PackedLinear
     rng = np.random.default_rng(seed)
     codes = rng.integers(0, len(oe.grid(bits)), size=(N, K), dtype=np.uint8)
@@ -22,6 +22,8 @@ def _linear(N, K, bits, gs, scale_dtype, seed):
     codes[1] = len(oe.grid(bits)) - 1
     s = (0.02 * rng.standard_normal((N, K // gs))).astype(np.float32)
     lin = PackedLinear.from_native(codes, s, bits, gs, scale_dtype, device=DEV)
+    if unrounded:
+        return lin, oe.affine_weight(codes, s, bits, gs, DT[scale_dtype])
     return lin, oe.dequant(codes, s, bits, gs, DT[scale_dtype])
 
 
@@ -37,11 +39,14 @@ def test_dequant_is_bit_exact(bits, scale_dtype, gs):
 
 
 @pytest.mark.parametrize("M", [1, 3, 8, 9, 200])
-@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("bits", [2, 3, 4, 6])
 def test_packed_matmul_matches_dense(M, bits):
+    """M <= 8: the fused matrix-vector form multiplies by the unrounded weight s q + bias (MLX's
+    quantized matrix-vector product); M > 8: the tensor-core GEMM on the bf16-dequantized
+    weight."""
     from gsq_rco_mlx_b200.gemm import check_err
     N, K = 320, 896
-    lin, Wd = _linear(N, K, bits, 64, "float16", seed=10 + bits)
+    lin, Wd = _linear(N, K, bits, 64, "float16", seed=10 + bits, unrounded=M <= 8)
     g = torch.Generator().manual_seed(M)
     x = torch.randn(M, K, generator=g).bfloat16()
     ref = x.double() @ Wd.double().T
