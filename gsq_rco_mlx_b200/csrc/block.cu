@@ -125,6 +125,62 @@ softmax_causal_kernel(const float* __restrict__ S, int B, int T, __nv_bfloat16* 
   }
 }
 
+// Vectorised form of softmax_causal_kernel for T % 4 == 0: lanes take consecutive 16-byte
+// vectors of the row (512 bytes per warp access), over keys <= query only; the same max, float64
+// sum of exp and rounded reciprocal (identical probabilities up to the float64 sum's order
+// before its float32 rounding). P is written as 8-byte vectors up to the end of the row's
+// 128-key block only: the causal P V product reduces over keys below that end and the causal
+// transpose of the backward reads no block beyond it.
+__global__ void __launch_bounds__(256)
+softmax_causal_v2_kernel(const float* __restrict__ S, int B, int T, __nv_bfloat16* __restrict__ P) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n_rows = (int64_t)B * T;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < n_rows;
+       row += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int t = (int)(row % T);
+    const float4* s4 = reinterpret_cast<const float4*>(S + row * T);
+    const int nv = t / 4 + 1;  // vectors holding keys 0..t
+    float m = -INFINITY;
+#pragma unroll 4
+    for (int v = lane; v < nv; v += 32) {
+      const float4 q = s4[v];
+      const int k0 = 4 * v;
+      m = fmaxf(m, q.x);
+      if (k0 + 1 <= t) m = fmaxf(m, q.y);
+      if (k0 + 2 <= t) m = fmaxf(m, q.z);
+      if (k0 + 3 <= t) m = fmaxf(m, q.w);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    double sum = 0.0;
+#pragma unroll 2
+    for (int v = lane; v < nv; v += 32) {
+      const float4 q = s4[v];
+      const int k0 = 4 * v;
+      sum += (double)expf(__fsub_rn(q.x, m));
+      if (k0 + 1 <= t) sum += (double)expf(__fsub_rn(q.y, m));
+      if (k0 + 2 <= t) sum += (double)expf(__fsub_rn(q.z, m));
+      if (k0 + 3 <= t) sum += (double)expf(__fsub_rn(q.w, m));
+    }
+    sum = warp_sum_d(sum);
+    const float inv = __frcp_rn((float)sum);
+    const int end = min(T, (t / 128 + 1) * 128);
+    uint2* p2 = reinterpret_cast<uint2*>(P + row * T);
+#pragma unroll 2
+    for (int v = lane; v < end / 4; v += 32) {
+      const int k0 = 4 * v;
+      float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k0 <= t) q = s4[v];
+      const float x[4] = {q.x, q.y, q.z, q.w};
+      __align__(8) __nv_bfloat16 o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        o[j] = __float2bfloat16_rn(k0 + j <= t ? __fmul_rn(expf(__fsub_rn(x[j], m)), inv) : 0.f);
+      p2[v] = *reinterpret_cast<const uint2*>(o);
+    }
+  }
+}
+
 // Row-windowed form: local row i of batch z is query position row0 + i; keys k <= row0 + i of
 // the cols stored ones are valid. S [B][rows][ld_s] float32 -> P [B][rows][ld_p] bf16 (zeros at
 // masked keys k < cols). One warp per row.
@@ -227,8 +283,13 @@ extern "C" int gsq_rope_split(const void* x, int64_t ld_x, int S, int T, int nh,
 
 extern "C" int gsq_softmax_causal(const float* S, int B, int T, void* P, void* PT, void* stream) {
   if (!S || !P || B <= 0 || T <= 0) return GSQ_EINVAL;
-  softmax_causal_kernel<<<blocks((int64_t)B * T * 32, 256), 256, 0, (cudaStream_t)stream>>>(
-      S, B, T, (__nv_bfloat16*)P, (__nv_bfloat16*)PT);
+  const unsigned g = blocks((int64_t)B * T * 32, 256);
+  cudaStream_t st = (cudaStream_t)stream;
+  auto* Pb = (__nv_bfloat16*)P;
+  const bool vec = !PT && T % 4 == 0 && ((uintptr_t)S & 15) == 0 && ((uintptr_t)P & 7) == 0;
+  if (vec) softmax_causal_v2_kernel<<<g, 256, 0, st>>>(S, B, T, Pb);
+  else
+    softmax_causal_kernel<<<g, 256, 0, st>>>(S, B, T, Pb, (__nv_bfloat16*)PT);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }

@@ -32,6 +32,8 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kStgLd = 33;                                   // staging row stride (floats)
 constexpr uint32_t kStgBytes = kEpiWarps * 32 * kStgLd * 4;  // one 32 x 32 tile per warp
+constexpr uint32_t kTmaBuf = 4096;                           // one TMA-store staging buffer
+constexpr uint32_t kSmemMax = 232448 - 1024;  // dynamic opt-in: 227 KB less the static 1 KB
 constexpr uint32_t kPipeBudget = 192 * 1024;                 // pipeline stages
 constexpr int kMaxStages = 8;
 constexpr int kMaxBig = 8;
@@ -93,6 +95,12 @@ struct GemmParams {
   int pair_c, pair_cs, pair_ct, pair_aux, pair_rt;
   int splits, kb_split;  // split-K: parts of kb_split k-blocks, partials into ws [part][M][N]
   float* ws;
+  // row-major outputs through TMA stores (EPI_PLAIN / EPI_BF16 without transposed outputs):
+  // C float32 or the cs bf16 terms as 32 x 32 boxes, 3-D (x, y, batch) or 4-D (x, y, z % div,
+  // z / div) maps
+  CUtensorMap tma_c;
+  CUtensorMap tma_cs[2];
+  int tma_out, out_rank, tma_bufs;  // tma_bufs: 4 KB staging buffers per epilogue warp (1, 2)
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -218,6 +226,127 @@ __device__ __forceinline__ void transposed_pass(const GemmParams& p, const TileI
                    p.pair_ct != 0);
     }
   }
+}
+
+// Row-major outputs of one tile through TMA stores (tma_out): lane = row row0 + lane holds 32
+// consecutive columns per group jc; the values go through the epilogue arithmetic in registers,
+// into one of the warp's two 4 KB staging buffers in the store's swizzled layout (16-byte chunk
+// c of row r at c ^ (r % 8) for float32 rows of 128 B, c ^ ((r / 2) % 4) for bf16 rows of 64 B:
+// conflict-free 16-byte shared stores), then one lane issues the box stores. The TMA unit clips
+// rows >= M and columns >= N. pb: the warp's next buffer.
+template <int BN, int EPI>
+__device__ __forceinline__ double epilogue_tma(const GemmParams& p, const TileInfo& t, float* acc,
+                                               uint8_t* tbuf, int& pb, int lane, int q, int h) {
+  constexpr int kNC = BN / 64;
+  const int row0 = t.tile_m + 32 * q, row = row0 + lane;
+  const bool row_ok = row < p.M;
+  const int zr = t.z % p.c_off.div, zq = t.z / p.c_off.div;
+  double sq = 0.0;
+#pragma unroll
+  for (int i = 0; i < BN / 2; ++i) acc[i] = __fmul_rn(p.alpha, acc[i]);
+  if (EPI == EPI_SWIGLU_BF16) {
+    // gate slots [0, 32), up slots [32, 64) of output columns tile_n / 2 + 32 h + u
+#pragma unroll
+    for (int u = 0; u < 32; ++u) {
+      const float g = bf16r(acc[u]), uu = bf16r(acc[32 + u]);
+      acc[u] = bf16r(__fmul_rn(bf16r(__fmul_rn(g, bf16r(sigmoid_f(g)))), uu));
+    }
+  }
+  constexpr int kGroups = EPI == EPI_SWIGLU_BF16 ? 1 : kNC;
+  const int nlim = EPI == EPI_SWIGLU_BF16 ? p.N / 2 : p.N;
+#pragma unroll
+  for (int jc = 0; jc < kGroups; ++jc) {
+    const int n0 = EPI == EPI_SWIGLU_BF16 ? t.tile_n / 2 + 32 * h : t.tile_n + 64 * jc + 32 * h;
+    if (n0 >= nlim) continue;
+    float* a = acc + 32 * jc;
+    const bool full = n0 + 32 <= p.N;
+    if (EPI == EPI_BF16) {
+      float r[32];
+      if (p.resid) {
+        const __nv_bfloat16* rp = p.resid + p.c_off.at(t.z) + (int64_t)row * p.ld_rt + n0;
+        if (row_ok && full) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(rp + 8 * v);
+            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __bfloat1622float2(b2[j]);
+              r[8 * v + 2 * j] = f.x;
+              r[8 * v + 2 * j + 1] = f.y;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < 32; ++u)
+            r[u] = (row_ok && n0 + u < p.N) ? __bfloat162float(rp[u]) : 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        float x = bf16r(a[u]);
+        if (p.bias && n0 + u < p.N) x = bf16r(__fadd_rn(x, p.bias[n0 + u]));
+        if (p.resid) x = bf16r(__fadd_rn(r[u], x));
+        a[u] = x;
+      }
+    } else if (p.bias) {
+#pragma unroll
+      for (int u = 0; u < 32; ++u)
+        if (n0 + u < p.N) a[u] = __fadd_rn(a[u], p.bias[n0 + u]);
+    }
+    if (p.sq_partial && row_ok) {
+#pragma unroll
+      for (int u = 0; u < 32; ++u)
+        if (n0 + u < p.N) sq += (double)a[u] * (double)a[u];
+    }
+    uint8_t* buf = tbuf + pb * kTmaBuf;
+    if (lane == 0) {
+      if (p.tma_bufs == 2) bulk_wait_read<1>();
+      else bulk_wait_read<0>();
+    }
+    __syncwarp();
+    if (p.C) {
+      float* f = reinterpret_cast<float*>(buf) + lane * 32;
+#pragma unroll
+      for (int v = 0; v < 8; ++v)
+        *reinterpret_cast<float4*>(f + ((v ^ (lane & 7)) << 2)) =
+            make_float4(a[4 * v], a[4 * v + 1], a[4 * v + 2], a[4 * v + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        if (i >= p.ncs) break;
+        uint8_t* tb = buf + i * 2048 + lane * 64;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            __nv_bfloat16 h0, h1, h2;
+            split3_bf16(a[8 * c + j], h0, h1, h2);
+            o[j] = i == 0 ? h0 : h1;
+          }
+          *reinterpret_cast<uint4*>(tb + ((c ^ ((lane >> 1) & 3)) << 4)) =
+              *reinterpret_cast<const uint4*>(o);
+        }
+      }
+    }
+    fence_proxy_async_shared();
+    __syncwarp();
+    if (lane == 0 && row0 < p.M) {
+      if (p.C) {
+        if (p.out_rank == 3) tma_store_3d(&p.tma_c, buf, n0, row0, zq);
+        else tma_store_4d(&p.tma_c, buf, n0, row0, zr, zq);
+      } else {
+        for (int i = 0; i < p.ncs; ++i) {
+          if (p.out_rank == 3) tma_store_3d(&p.tma_cs[i], buf + i * 2048, n0, row0, zq);
+          else tma_store_4d(&p.tma_cs[i], buf + i * 2048, n0, row0, zr, zq);
+        }
+      }
+    }
+    if (lane == 0) bulk_commit();  // (an empty group when the box lies below the last row)
+    if (p.tma_bufs == 2) pb ^= 1;
+  }
+  return sq;
 }
 
 // The fused outputs of one tile from the folded accumulator. Epilogue warp (q, h) holds rows
@@ -735,6 +864,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     const int h = ew >> 2;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     float* stg = reinterpret_cast<float*>(smem + (size_t)S * stage_bytes) + ew * (32 * kStgLd);
+    uint8_t* tbuf = smem + (size_t)S * stage_bytes + (size_t)ew * p.tma_bufs * kTmaBuf;
+    int pb = 0;
     int bs = 0;
     uint32_t bph = 0, tcount = 0;
     bool ok = true;
@@ -795,7 +926,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         }
       }
       double sq = 0.0;
-      if (ok) sq = epilogue_out<BN, EPI>(p, t, acc, stg, lane, q, h);
+      if (ok) {
+        if ((EPI == EPI_PLAIN || EPI == EPI_BF16 || EPI == EPI_SWIGLU_BF16) && p.tma_out)
+          sq = epilogue_tma<BN, EPI>(p, t, acc, tbuf, pb, lane, q, h);
+        else
+          sq = epilogue_out<BN, EPI>(p, t, acc, stg, lane, q, h);
+      }
       if (p.sq_partial) {
         sq = warp_sum_d(sq);
         if (lane == 0) red[ew] = sq;
@@ -807,6 +943,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         }
         epi_sync();
       }
+    }
+    if (p.tma_out) {  // the boxes' global writes are done before the CTA exits
+      if (lane == 0) bulk_wait_all();
+      __syncwarp();
     }
   }
   fence_before_sync();
@@ -853,10 +993,54 @@ static bool make_map(CUtensorMap* m, const void* base, int64_t rows, int cols, i
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Output map of the TMA-store epilogue: [nz][div][M][ld] view (element strides ld, s2, s1) with
+// 32 x 32 boxes; float32 rows of 128 B (128-byte swizzle) or bf16 rows of 64 B (64-byte).
+static bool make_out_map(CUtensorMap* m, const void* base, bool f32, int N, int M, int64_t ld,
+                         int div, int64_t s1, int64_t s2, int batch, int* rank) {
+  EncodeTiledFn fn = encode_fn();
+  const int64_t e = f32 ? 4 : 2;
+  if (!fn || !base || ((uintptr_t)base & 15) || ((ld * e) & 15) || ((s1 * e) & 15) ||
+      ((s2 * e) & 15))
+    return false;
+  const int nz = (batch + div - 1) / div;
+  cuuint32_t box[4] = {32, 32, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                     : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapSwizzle sw = f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  if (div == 1) {
+    cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)nz};
+    cuuint64_t strides[2] = {(cuuint64_t)(ld * e),
+                             (cuuint64_t)((s1 > 0 ? s1 : ld * M) * e)};
+    *rank = 3;
+    return fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
+  if (s1 <= 0 || s2 <= 0) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)div, (cuuint64_t)nz};
+  cuuint64_t strides[3] = {(cuuint64_t)(ld * e), (cuuint64_t)(s2 * e), (cuuint64_t)(s1 * e)};
+  *rank = 4;
+  return fn(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, int EPI>
 static int launch(GemmParams& p, int batch, cudaStream_t st) {
   const uint32_t stage_bytes = p.na * BM * BK * 2 + p.nb * BN * BK * 2;
   int S = (int)(kPipeBudget / stage_bytes);
+  if (p.tma_out) {  // TMA-store staging: two buffers per warp where two stages still fit, else one
+    p.tma_bufs = 0;
+    for (int bufs = 2; bufs >= 1 && !p.tma_bufs; --bufs) {
+      const int sb = (int)((kSmemMax - 1024 - kEpiWarps * bufs * kTmaBuf) / stage_bytes);
+      if (sb >= 2) {
+        p.tma_bufs = bufs;
+        S = sb < S ? sb : S;
+      }
+    }
+    if (!p.tma_bufs) p.tma_out = 0;
+  }
   if (S > kMaxStages) S = kMaxStages;
   if (S < 2) return GSQ_ENOTSUP;
   p.stages = S;
@@ -870,16 +1054,18 @@ static int launch(GemmParams& p, int batch, cudaStream_t st) {
   p.tiles_m = (p.M + BM - 1) / BM;
   p.tiles_n = (p.N + BN - 1) / BN;
   p.total_tiles = (int64_t)p.tiles_m * p.tiles_n * batch * p.splits;
-  const size_t smem = 1024 + (size_t)S * stage_bytes + kStgBytes;
+  const size_t smem = 1024 + (size_t)S * stage_bytes +
+                      (p.tma_out ? (size_t)kEpiWarps * p.tma_bufs * kTmaBuf : (size_t)kStgBytes);
   static bool attr_set[2][7] = {{false}};
   bool& done = attr_set[BN == 128][EPI];
   if (!done) {
     if (cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(1024 + kPipeBudget + kStgBytes)) != cudaSuccess)
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemMax) !=
+        cudaSuccess)
       return GSQ_ECUDA;
     done = true;
   }
+  if (smem > kSmemMax) return GSQ_ENOTSUP;
   const int64_t g = p.total_tiles < num_sms() ? p.total_tiles : num_sms();
   gemm_tc_kernel<BN, EPI><<<(unsigned)g, kThreads, smem, st>>>(p);
   GSQ_CHECK_LAUNCH();
@@ -995,6 +1181,28 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
                 (d->ld_aux & 1) == 0 && c_even) ? 1 : 0;
   p.pair_rt = (((uintptr_t)d->resid & 3) == 0 && ((uintptr_t)d->target & 3) == 0 &&
                (d->ld_rt & 1) == 0 && c_even) ? 1 : 0;
+  // TMA-store epilogue: row-major C (float32) alone or one / two cs terms alone, no transposed
+  // outputs, no C read-back; the bf16 chain's residual read as 16-byte rows
+  if ((epi == 0 || epi == 4 || (epi == 5 && !d->aux0 && !d->C)) && p.splits == 1 &&
+      d->nct == 0 && !(epi == 0 && d->beta != 0.f) &&
+      ((d->C && d->ncs == 0) || (!d->C && (d->ncs == 1 || d->ncs == 2))) &&
+      (!d->resid || (((uintptr_t)d->resid & 15) == 0 && (d->ld_rt & 7) == 0 &&
+                     ((d->c_s1 | d->c_s2) & 7) == 0))) {
+    const int div = p.c_off.div;
+    int rank = 0;
+    bool ok = true;
+    if (d->C)
+      ok = tc::make_out_map(&p.tma_c, d->C, true, N, M, d->ldc, div, d->c_s1, d->c_s2,
+                            d->batch, &rank);
+    const int n_out = epi == 5 ? N / 2 : N;  // SwiGLU: one output column per gate / up pair
+    for (int i = 0; i < d->ncs && ok; ++i)
+      ok = tc::make_out_map(&p.tma_cs[i], d->cs[i], false, n_out, M, d->ldcs, div, d->c_s1,
+                            d->c_s2, d->batch, &rank);
+    if (ok) {
+      p.tma_out = 1;
+      p.out_rank = rank;
+    }
+  }
   cudaStream_t st = (cudaStream_t)stream;
   if (p.splits > 1) {
     const int rc = BN == 64 ? tc::launch<64, 0>(p, 1, st) : tc::launch<128, 0>(p, 1, st);

@@ -12,7 +12,8 @@ mlp_gemms: the five GEMMs of one mlp-stage resample (micro-batch 2 x 2047 rows) 
   SwiGLU GEMM of the block forward (8 x 2048 rows):
     F1 gate|up = mn [Wg|Wu]^T (1 x 3 terms, SwiGLU epilogue)   F3 residual loss (3 x 3)
     B1 dL/dWd (3 x 3)   B2 SwiGLU backward (3 x 3)   B3 dL/dWg|Wu (3 x 1, batch 2)
-attn: the causal scores GEMM and softmax of 8 sequences x 14 heads x 2048 positions.
+attn: the causal scores GEMM and softmax of 8 sequences x 14 heads x 2048 positions (attn1: one
+  sequence, 235 MB of scores: the profiler-sized case).
 soft_step: the fused backward + Lion + next forward of one up_proj-shaped soft linear (R = 2).
 cublas: library bf16 GEMMs of the mlp shapes, for context only (not on any product path).
 packed: the packed-weight dequant of one layer and the fused dequant-GEMV (HBM streams).
@@ -74,9 +75,9 @@ def mlp_gemms(dev, g):
     }
 
 
-def attn(dev, g):
-    B = 8 * HEADS
-    q, k = _terms(B * T, HD, 3, dev, g), _terms(8 * KV * T, HD, 3, dev, g)  # float32 after RoPE
+def attn(dev, g, seqs=8):
+    B = seqs * HEADS
+    q, k = _terms(B * T, HD, 3, dev, g), _terms(seqs * KV * T, HD, 3, dev, g)  # f32 after RoPE
     scores = torch.empty(B, T, T, device=dev)
     P = torch.empty(B * T, T, device=dev, dtype=torch.bfloat16)
     st = _lib.stream_ptr()
@@ -182,8 +183,8 @@ def eval_batch(dev, g):
     return {"eval batch 8 x 2048": (None, lambda: ev.forward_nll(tok, tgt, 8, out))}
 
 
-CASES = {"mlp_gemms": mlp_gemms, "attn": attn, "soft_step": soft_step, "cublas": cublas,
-         "packed": packed, "eval_batch": eval_batch}
+CASES = {"mlp_gemms": mlp_gemms, "attn": attn, "attn1": lambda dev, g: attn(dev, g, seqs=1),
+         "soft_step": soft_step, "cublas": cublas, "packed": packed, "eval_batch": eval_batch}
 
 
 def main(argv):

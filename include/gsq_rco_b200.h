@@ -253,7 +253,9 @@ int gsq_rope_split(const void *x, int64_t ld_x, int S, int T, int nh, const floa
                    const float *sinv, void *o0, void *o1, void *o2, void *stream);
 
 /* Causal softmax of score rows S float32 [B*T][T] (keys <= query): P bf16 [B*T][T] with zeros
- * above the diagonal, and optionally PT bf16 [B][T][T] (P transposed per batch).
+ * above the diagonal, and optionally PT bf16 [B][T][T] (P transposed per batch). Without PT
+ * (and T % 4 == 0, 16-byte aligned S, 8-byte aligned P) each row is written only up to the
+ * end of its 128-key block, the part the causal P V and transposed products read.
  * Replaces src/gsq_rco/gsq/e2e.py:149-154 (mask, softmax, cast to bf16). */
 int gsq_softmax_causal(const float *S, int B, int T, void *P, void *PT, void *stream);
 

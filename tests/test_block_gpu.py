@@ -101,3 +101,37 @@ def test_attention_output_target():
         hn = ob.rmsnorm(h[s * T:(s + 1) * T].float(), Wf["in_norm"])
         bad, eq = frac_diff(A[s * T:(s + 1) * T], ob.attn_out_hard(hn, Wf, 2, 1))
         assert bad < 2e-3 and eq > 0.95, (bad, eq)
+
+
+@pytest.mark.parametrize("T", [128, 384, 2048])
+def test_causal_softmax_vector_rows(T):
+    """gsq_softmax_causal (the vectorised row kernel when no transpose is asked) against the
+    oracle's float32 softmax with a float64 sum: P equal up to rare last-bit differences on keys
+    <= query, zeros from the query to the end of its 128-key block; the transposed-output form
+    (the reference kernel over whole rows) agrees on that region."""
+    from gsq_rco_mlx_b200 import _lib
+    B = 3
+    g = torch.Generator().manual_seed(T)
+    S = (4 * torch.randn(B, T, T, generator=g)).float()
+    Sd = S.to(DEV)
+    P = torch.full((B * T, T), 7.0, device=DEV, dtype=torch.bfloat16)
+    P2 = torch.empty(B * T, T, device=DEV, dtype=torch.bfloat16)
+    PT = torch.empty(B, T, T, device=DEV, dtype=torch.bfloat16)
+    st = _lib.stream_ptr()
+    _lib.call("gsq_softmax_causal", _lib.ptr(Sd), B, T, _lib.ptr(P), None, st)
+    _lib.call("gsq_softmax_causal", _lib.ptr(Sd), B, T, _lib.ptr(P2), _lib.ptr(PT), st)
+    torch.cuda.synchronize()
+    mask = torch.triu(torch.ones(T, T, dtype=torch.bool), 1)
+    Sm = S.masked_fill(mask, -torch.inf)
+    m = Sm.max(-1, keepdim=True).values
+    e = torch.exp(Sm - m)
+    ref = ob.bf(e * torch.reciprocal(e.double().sum(-1, keepdim=True).float()))
+    got = P.float().cpu().view(B, T, T)
+    t = torch.arange(T)[:, None]
+    k = torch.arange(T)[None, :]
+    inside = (k // 128) <= (t // 128)                 # the written region
+    assert torch.all(got[:, ~inside] == 7.0)           # beyond the block: untouched
+    region = inside.expand(B, T, T)
+    assert float((got[region] != ref[region]).float().mean()) < 1e-3
+    assert torch.equal(got[region], P2.float().cpu().view(B, T, T)[region])
+    assert torch.equal(PT.float().cpu(), P2.float().cpu().view(B, T, T).transpose(1, 2))
