@@ -99,8 +99,11 @@ struct GemmParams {
   // C float32 or the cs bf16 terms as 32 x 32 boxes, 3-D (x, y, batch) or 4-D (x, y, z % div,
   // z / div) maps
   CUtensorMap tma_c;
-  CUtensorMap tma_cs[2];
-  int tma_out, out_rank, tma_bufs;  // tma_bufs: 4 KB staging buffers per epilogue warp (1, 2)
+  CUtensorMap tma_cs[3];
+  CUtensorMap tma_ct[3];   // C^T terms, 3-D (x = row, y = output column, batch)
+  CUtensorMap tma_aux[2];  // SwiGLU g / u rows
+  int tma_out, out_rank, tma_bufs;  // tma_bufs: 4 KB staging buffers per epilogue warp (1..3)
+  int tma_bf16_only;                  // every box is bf16 (2 KB): no C / aux float32 boxes
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -228,123 +231,298 @@ __device__ __forceinline__ void transposed_pass(const GemmParams& p, const TileI
   }
 }
 
-// Row-major outputs of one tile through TMA stores (tma_out): lane = row row0 + lane holds 32
-// consecutive columns per group jc; the values go through the epilogue arithmetic in registers,
-// into one of the warp's two 4 KB staging buffers in the store's swizzled layout (16-byte chunk
-// c of row r at c ^ (r % 8) for float32 rows of 128 B, c ^ ((r / 2) % 4) for bf16 rows of 64 B:
-// conflict-free 16-byte shared stores), then one lane issues the box stores. The TMA unit clips
-// rows >= M and columns >= N. pb: the warp's next buffer.
+// ----------------------------------------------------------------- TMA box epilogue ---
+// The outputs of one tile as 32 x 32 boxes written by the TMA unit (tma_out). Epilogue warp
+// (q, h) holds, per 32-column group, rows row0 + lane (lane = row) and 32 consecutive columns in
+// registers; a box is staged in the warp's ring of 4 KB buffers in the store's swizzled layout
+// and stored by one lane, one bulk group per buffer. Row-major float32 boxes (128-byte rows:
+// 16-byte chunk c of row r at c ^ (r % 8)), row-major bf16 boxes (64-byte rows: chunk c at
+// c ^ ((r / 2) % 4)) and transposed bf16 boxes (box row = output column) are all written without
+// shared-memory bank conflicts. The TMA unit clips rows and columns outside the output.
+struct BoxRing {
+  uint8_t* base;
+  int nbuf, bsize, cur, used;  // nbuf buffers of bsize bytes (4096, or 2048 for bf16 boxes only)
+};
+
+__device__ __forceinline__ void ring_wait(int nbuf) {
+  if (nbuf >= 3) bulk_wait_read<2>();
+  else if (nbuf == 2) bulk_wait_read<1>();
+  else bulk_wait_read<0>();
+}
+
+// Room for a box of `bytes` (2048 or 4096): a full buffer is committed, and a fresh buffer is
+// used only once the group that last read it is done.
+__device__ __forceinline__ uint8_t* ring_slot(BoxRing& r, int bytes, int lane) {
+  if (r.used + bytes > r.bsize) {
+    if (lane == 0) bulk_commit();
+    r.cur = r.cur + 1 == r.nbuf ? 0 : r.cur + 1;
+    r.used = 0;
+  }
+  if (r.used == 0) {
+    if (lane == 0) ring_wait(r.nbuf);
+    __syncwarp();
+  }
+  uint8_t* b = r.base + r.cur * r.bsize + r.used;
+  r.used += bytes;
+  return b;
+}
+
+__device__ __forceinline__ void ring_flush(BoxRing& r, int lane) {
+  if (r.used) {
+    if (lane == 0) bulk_commit();
+    r.cur = r.cur + 1 == r.nbuf ? 0 : r.cur + 1;
+    r.used = 0;
+  }
+}
+
+// bf16 term i of x (x = t0 + t1 + t2 to float32 precision)
+__device__ __forceinline__ __nv_bfloat16 term_of(float x, int i) {
+  __nv_bfloat16 h0, h1, h2;
+  split3_bf16(x, h0, h1, h2);
+  return i == 0 ? h0 : (i == 1 ? h1 : h2);
+}
+
+__device__ __forceinline__ void box_put_f32(uint8_t* buf, int lane, const float* v) {
+  float* f = reinterpret_cast<float*>(buf) + lane * 32;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<float4*>(f + ((c ^ (lane & 7)) << 2)) =
+        make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+
+__device__ __forceinline__ void box_put_bf16(uint8_t* buf, int lane, const float* v, int term) {
+  uint8_t* row = buf + lane * 64;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = term_of(v[8 * c + j], term);
+    *reinterpret_cast<uint4*>(row + ((c ^ ((lane >> 1) & 3)) << 4)) =
+        *reinterpret_cast<const uint4*>(o);
+  }
+}
+
+// transposed: box row u (output column n0 + u), box column lane (output row row0 + lane)
+__device__ __forceinline__ void box_put_bf16_t(uint8_t* buf, int lane, const float* v, int term) {
+  const int c = lane >> 3, e = (lane & 7) * 2;
+#pragma unroll
+  for (int u = 0; u < 32; ++u)
+    *reinterpret_cast<__nv_bfloat16*>(buf + u * 64 + ((c ^ ((u >> 1) & 3)) << 4) + e) =
+        term_of(v[u], term);
+}
+
+__device__ __forceinline__ void box_store(const CUtensorMap* map, const uint8_t* buf, int rank,
+                                          int x, int y, int zr, int zq, int lane) {
+  fence_proxy_async_shared();
+  __syncwarp();
+  if (lane == 0) {
+    if (rank == 3) tma_store_3d(map, buf, x, y, zq);
+    else tma_store_4d(map, buf, x, y, zr, zq);
+  }
+}
+
+// Row-major output (map of the C layout) of the values v of columns col0 .. col0 + 31
+__device__ __forceinline__ void out_rows_f32(BoxRing& r, const GemmParams& p,
+                                             const CUtensorMap* map, const float* v, int col0,
+                                             int row0, int zr, int zq, int lane) {
+  uint8_t* b = ring_slot(r, 4096, lane);
+  box_put_f32(b, lane, v);
+  if (row0 < p.M) box_store(map, b, p.out_rank, col0, row0, zr, zq, lane);
+}
+
+__device__ __forceinline__ void out_rows_terms(BoxRing& r, const GemmParams& p, const float* v,
+                                               int nterms, int col0, int row0, int zr, int zq,
+                                               int lane) {
+  for (int i = 0; i < nterms; ++i) {
+    uint8_t* b = ring_slot(r, 2048, lane);
+    box_put_bf16(b, lane, v, i);
+    if (row0 < p.M) box_store(&p.tma_cs[i], b, p.out_rank, col0, row0, zr, zq, lane);
+  }
+}
+
+// C^T terms: output rows up + col0 .. (of batch z), columns row0 ..
+__device__ __forceinline__ void out_cols_terms(BoxRing& r, const GemmParams& p, const float* v,
+                                               int col0, int up, int row0, int z, int lane) {
+  for (int i = 0; i < p.nct; ++i) {
+    uint8_t* b = ring_slot(r, 2048, lane);
+    box_put_bf16_t(b, lane, v, i);
+    if (row0 < p.M) box_store(&p.tma_ct[i], b, 3, row0, up + col0, 0, z, lane);
+  }
+}
+
+// 8 consecutive values of a row segment (columns c .. c + 7 of 32): one 16-byte load where the
+// segment is whole, else per element; 0 outside the output.
+__device__ __forceinline__ void load8_bf16(const __nv_bfloat16* ptr, bool ok, int nvalid, int c,
+                                          float* r) {
+  if (ok && nvalid >= 32) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(ptr + c);
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(b2[j]);
+      r[2 * j] = f.x;
+      r[2 * j + 1] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = (ok && c + j < nvalid) ? __bfloat162float(ptr[c + j]) : 0.f;
+  }
+}
+
+__device__ __forceinline__ void load8_f32(const float* ptr, bool ok, int nvalid, int c, float* r) {
+  if (ok && nvalid >= 32) {
+    const float4 f0 = *reinterpret_cast<const float4*>(ptr + c);
+    const float4 f1 = *reinterpret_cast<const float4*>(ptr + c + 4);
+    r[0] = f0.x; r[1] = f0.y; r[2] = f0.z; r[3] = f0.w;
+    r[4] = f1.x; r[5] = f1.y; r[6] = f1.z; r[7] = f1.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = (ok && c + j < nvalid) ? ptr[c + j] : 0.f;
+  }
+}
+
 template <int BN, int EPI>
 __device__ __forceinline__ double epilogue_tma(const GemmParams& p, const TileInfo& t, float* acc,
-                                               uint8_t* tbuf, int& pb, int lane, int q, int h) {
+                                               BoxRing& ring, int lane, int q, int h) {
   constexpr int kNC = BN / 64;
+  constexpr bool kDual = EPI == EPI_SWIGLU_FWD || EPI == EPI_SWIGLU_BF16;
   const int row0 = t.tile_m + 32 * q, row = row0 + lane;
   const bool row_ok = row < p.M;
   const int zr = t.z % p.c_off.div, zq = t.z / p.c_off.div;
+  const int64_t coff = p.c_off.at(t.z);
   double sq = 0.0;
 #pragma unroll
   for (int i = 0; i < BN / 2; ++i) acc[i] = __fmul_rn(p.alpha, acc[i]);
-  if (EPI == EPI_SWIGLU_BF16) {
-    // gate slots [0, 32), up slots [32, 64) of output columns tile_n / 2 + 32 h + u
-#pragma unroll
-    for (int u = 0; u < 32; ++u) {
-      const float g = bf16r(acc[u]), uu = bf16r(acc[32 + u]);
-      acc[u] = bf16r(__fmul_rn(bf16r(__fmul_rn(g, bf16r(sigmoid_f(g)))), uu));
-    }
-  }
-  constexpr int kGroups = EPI == EPI_SWIGLU_BF16 ? 1 : kNC;
-  const int nlim = EPI == EPI_SWIGLU_BF16 ? p.N / 2 : p.N;
+  constexpr int kGroups = kDual ? 1 : kNC;
+  const int nlim = kDual ? p.N / 2 : p.N;
 #pragma unroll
   for (int jc = 0; jc < kGroups; ++jc) {
-    const int n0 = EPI == EPI_SWIGLU_BF16 ? t.tile_n / 2 + 32 * h : t.tile_n + 64 * jc + 32 * h;
+    const int n0 = kDual ? t.tile_n / 2 + 32 * h : t.tile_n + 64 * jc + 32 * h;
     if (n0 >= nlim) continue;
+    const int nvalid = nlim - n0;
     float* a = acc + 32 * jc;
-    const bool full = n0 + 32 <= p.N;
-    if (EPI == EPI_BF16) {
-      float r[32];
-      if (p.resid) {
-        const __nv_bfloat16* rp = p.resid + p.c_off.at(t.z) + (int64_t)row * p.ld_rt + n0;
-        if (row_ok && full) {
+    if (EPI == EPI_SWIGLU_FWD || EPI == EPI_SWIGLU_BF16) {
+      if (EPI == EPI_SWIGLU_BF16) {
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(rp + 8 * v);
-            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = __bfloat1622float2(b2[j]);
-              r[8 * v + 2 * j] = f.x;
-              r[8 * v + 2 * j + 1] = f.y;
-            }
-          }
-        } else {
-#pragma unroll
-          for (int u = 0; u < 32; ++u)
-            r[u] = (row_ok && n0 + u < p.N) ? __bfloat162float(rp[u]) : 0.f;
-        }
+        for (int u = 0; u < 64; ++u) a[u] = bf16r(a[u]);
+      }
+      if (p.aux0) {
+        out_rows_f32(ring, p, &p.tma_aux[0], a, n0, row0, zr, zq, lane);
+        out_rows_f32(ring, p, &p.tma_aux[1], a + 32, n0, row0, zr, zq, lane);
       }
 #pragma unroll
       for (int u = 0; u < 32; ++u) {
-        float x = bf16r(a[u]);
-        if (p.bias && n0 + u < p.N) x = bf16r(__fadd_rn(x, p.bias[n0 + u]));
-        if (p.resid) x = bf16r(__fadd_rn(r[u], x));
-        a[u] = x;
+        const float g = a[u], uu = a[32 + u];
+        a[u] = EPI == EPI_SWIGLU_FWD ? __fmul_rn(__fmul_rn(g, sigmoid_f(g)), uu)
+                                     : bf16r(__fmul_rn(bf16r(__fmul_rn(g, bf16r(sigmoid_f(g)))),
+                                                       uu));
       }
-    } else if (p.bias) {
+      if (p.ncs) out_rows_terms(ring, p, a, p.ncs, n0, row0, zr, zq, lane);
+      if (p.nct) out_cols_terms(ring, p, a, n0, 0, row0, t.z, lane);
+    } else if (EPI == EPI_SWIGLU_BWD || EPI == EPI_SWIGLU_BWD_BF16) {
+      const float* gp = p.aux0 + coff + (int64_t)row * p.ld_aux + n0;
+      const float* up = p.aux1 + coff + (int64_t)row * p.ld_aux + n0;
+      float du[32];
 #pragma unroll
-      for (int u = 0; u < 32; ++u)
-        if (n0 + u < p.N) a[u] = __fadd_rn(a[u], p.bias[n0 + u]);
-    }
-    if (p.sq_partial && row_ok) {
+      for (int c = 0; c < 32; c += 8) {
+        float g[8], u[8];
+        load8_f32(gp, row_ok, nvalid, c, g);
+        load8_f32(up, row_ok, nvalid, c, u);
 #pragma unroll
-      for (int u = 0; u < 32; ++u)
-        if (n0 + u < p.N) sq += (double)a[u] * (double)a[u];
-    }
-    uint8_t* buf = tbuf + pb * kTmaBuf;
-    if (lane == 0) {
-      if (p.tma_bufs == 2) bulk_wait_read<1>();
-      else bulk_wait_read<0>();
-    }
-    __syncwarp();
-    if (p.C) {
-      float* f = reinterpret_cast<float*>(buf) + lane * 32;
-#pragma unroll
-      for (int v = 0; v < 8; ++v)
-        *reinterpret_cast<float4*>(f + ((v ^ (lane & 7)) << 2)) =
-            make_float4(a[4 * v], a[4 * v + 1], a[4 * v + 2], a[4 * v + 3]);
+        for (int j = 0; j < 8; ++j) {
+          const int e = c + j;
+          if (EPI == EPI_SWIGLU_BWD) {
+            const float sg = sigmoid_f(g[j]);
+            const float dd = a[e];
+            du[e] = __fmul_rn(dd, __fmul_rn(g[j], sg));
+            const float dsil =
+                __fadd_rn(sg, __fmul_rn(g[j], __fmul_rn(sg, __fsub_rn(1.0f, sg))));
+            a[e] = __fmul_rn(__fmul_rn(dd, u[j]), dsil);
+          } else {
+            const float dd = bf16r(a[e]);
+            const float sf = sigmoid_f(g[j]);
+            const float sb = bf16r(sf);
+            const float av = bf16r(__fmul_rn(g[j], sb));
+            du[e] = bf16r(__fmul_rn(dd, av));
+            const float da = bf16r(__fmul_rn(dd, u[j]));
+            const float ds = bf16r(__fmul_rn(da, g[j]));
+            a[e] = bf16r(__fadd_rn(__fmul_rn(da, sb),
+                                   __fmul_rn(ds, __fmul_rn(sf, __fsub_rn(1.0f, sf)))));
+          }
+          if (!(row_ok && e < nvalid)) {
+            a[e] = 0.f;
+            du[e] = 0.f;
+          }
+        }
+      }
+      if (EPI == EPI_SWIGLU_BWD_BF16 && p.ncs) {
+        out_rows_terms(ring, p, a, 1, n0, row0, zr, zq, lane);
+        out_rows_terms(ring, p, du, 1, n0 + (int)p.ct_up_rows, row0, zr, zq, lane);
+      }
+      if (p.nct) {
+        out_cols_terms(ring, p, a, n0, 0, row0, t.z, lane);
+        out_cols_terms(ring, p, du, n0, (int)p.ct_up_rows, row0, t.z, lane);
+      }
     } else {
+      // EPI_PLAIN, EPI_RESID, EPI_BF16
+      if (EPI == EPI_BF16) {
+        const __nv_bfloat16* rp = p.resid + coff + (int64_t)row * p.ld_rt + n0;
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        if (i >= p.ncs) break;
-        uint8_t* tb = buf + i * 2048 + lane * 64;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          __align__(16) __nv_bfloat16 o[8];
+        for (int c = 0; c < 32; c += 8) {
+          float r[8];
+          if (p.resid) load8_bf16(rp, row_ok, nvalid, c, r);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            __nv_bfloat16 h0, h1, h2;
-            split3_bf16(a[8 * c + j], h0, h1, h2);
-            o[j] = i == 0 ? h0 : h1;
+            const int u = c + j;
+            float x = bf16r(a[u]);
+            if (p.bias && u < nvalid) x = bf16r(__fadd_rn(x, p.bias[n0 + u]));
+            if (p.resid) x = bf16r(__fadd_rn(r[j], x));
+            a[u] = x;
           }
-          *reinterpret_cast<uint4*>(tb + ((c ^ ((lane >> 1) & 3)) << 4)) =
-              *reinterpret_cast<const uint4*>(o);
         }
+      } else if (EPI == EPI_RESID) {
+        const __nv_bfloat16* rp = p.resid + coff + (int64_t)row * p.ld_rt + n0;
+        const __nv_bfloat16* tp = p.target + coff + (int64_t)row * p.ld_rt + n0;
+        const bool zero_row = p.row_period > 0 && (row % p.row_period) == 0;
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+          float r[8], tg[8];
+          if (p.resid) load8_bf16(rp, row_ok, nvalid, c, r);
+          load8_bf16(tp, row_ok, nvalid, c, tg);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int u = c + j;
+            float x = a[u];
+            if (p.bias && u < nvalid) x = __fadd_rn(x, p.bias[n0 + u]);
+            if (p.resid) x = __fadd_rn(x, r[j]);
+            x = __fsub_rn(x, tg[j]);
+            if (zero_row || !(row_ok && u < nvalid)) x = 0.f;
+            sq += (double)x * (double)x;
+            a[u] = __fmul_rn(p.out_scale, x);
+          }
+        }
+      } else if (p.bias) {
+#pragma unroll
+        for (int u = 0; u < 32; ++u)
+          if (u < nvalid) a[u] = __fadd_rn(a[u], p.bias[n0 + u]);
+      }
+      if (EPI != EPI_RESID && p.sq_partial && row_ok) {
+#pragma unroll
+        for (int u = 0; u < 32; ++u)
+          if (u < nvalid) sq += (double)a[u] * (double)a[u];
+      }
+      if (p.C) out_rows_f32(ring, p, &p.tma_c, a, n0, row0, zr, zq, lane);
+      if (p.ncs) out_rows_terms(ring, p, a, p.ncs, n0, row0, zr, zq, lane);
+      if (p.nct) {
+        // transposed values outside the output are zero (the consumer's padding rows)
+        if (!row_ok) {
+#pragma unroll
+          for (int u = 0; u < 32; ++u) a[u] = 0.f;
+        }
+        out_cols_terms(ring, p, a, n0, 0, row0, t.z, lane);
       }
     }
-    fence_proxy_async_shared();
-    __syncwarp();
-    if (lane == 0 && row0 < p.M) {
-      if (p.C) {
-        if (p.out_rank == 3) tma_store_3d(&p.tma_c, buf, n0, row0, zq);
-        else tma_store_4d(&p.tma_c, buf, n0, row0, zr, zq);
-      } else {
-        for (int i = 0; i < p.ncs; ++i) {
-          if (p.out_rank == 3) tma_store_3d(&p.tma_cs[i], buf + i * 2048, n0, row0, zq);
-          else tma_store_4d(&p.tma_cs[i], buf + i * 2048, n0, row0, zr, zq);
-        }
-      }
-    }
-    if (lane == 0) bulk_commit();  // (an empty group when the box lies below the last row)
-    if (p.tma_bufs == 2) pb ^= 1;
+    ring_flush(ring, lane);
   }
   return sq;
 }
@@ -864,8 +1042,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     const int h = ew >> 2;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     float* stg = reinterpret_cast<float*>(smem + (size_t)S * stage_bytes) + ew * (32 * kStgLd);
-    uint8_t* tbuf = smem + (size_t)S * stage_bytes + (size_t)ew * p.tma_bufs * kTmaBuf;
-    int pb = 0;
+    BoxRing ring;
+    ring.base = smem + (size_t)S * stage_bytes + (size_t)ew * p.tma_bufs * kTmaBuf;
+    ring.nbuf = p.tma_bufs;
+    ring.bsize = (int)kTmaBuf;
+    if (p.tma_bufs == 1 && p.tma_bf16_only) {  // one 4 KB area as two 2 KB buffers
+      ring.nbuf = 2;
+      ring.bsize = (int)kTmaBuf / 2;
+    }
+    ring.cur = 0;
+    ring.used = 0;
     int bs = 0;
     uint32_t bph = 0, tcount = 0;
     bool ok = true;
@@ -927,8 +1113,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       }
       double sq = 0.0;
       if (ok) {
-        if ((EPI == EPI_PLAIN || EPI == EPI_BF16 || EPI == EPI_SWIGLU_BF16) && p.tma_out)
-          sq = epilogue_tma<BN, EPI>(p, t, acc, tbuf, pb, lane, q, h);
+        if (p.tma_out)
+          sq = epilogue_tma<BN, EPI>(p, t, acc, ring, lane, q, h);
         else
           sq = epilogue_out<BN, EPI>(p, t, acc, stg, lane, q, h);
       }
@@ -1032,7 +1218,7 @@ static int launch(GemmParams& p, int batch, cudaStream_t st) {
   int S = (int)(kPipeBudget / stage_bytes);
   if (p.tma_out) {  // TMA-store staging: two buffers per warp where two stages still fit, else one
     p.tma_bufs = 0;
-    for (int bufs = 2; bufs >= 1 && !p.tma_bufs; --bufs) {
+    for (int bufs = 3; bufs >= 1 && !p.tma_bufs; --bufs) {
       const int sb = (int)((kSmemMax - 1024 - kEpiWarps * bufs * kTmaBuf) / stage_bytes);
       if (sb >= 2) {
         p.tma_bufs = bufs;
@@ -1181,26 +1367,47 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
                 (d->ld_aux & 1) == 0 && c_even) ? 1 : 0;
   p.pair_rt = (((uintptr_t)d->resid & 3) == 0 && ((uintptr_t)d->target & 3) == 0 &&
                (d->ld_rt & 1) == 0 && c_even) ? 1 : 0;
-  // TMA-store epilogue: row-major C (float32) alone or one / two cs terms alone, no transposed
-  // outputs, no C read-back; the bf16 chain's residual read as 16-byte rows
-  if ((epi == 0 || epi == 4 || (epi == 5 && !d->aux0 && !d->C)) && p.splits == 1 &&
-      d->nct == 0 && !(epi == 0 && d->beta != 0.f) &&
-      ((d->C && d->ncs == 0) || (!d->C && (d->ncs == 1 || d->ncs == 2))) &&
-      (!d->resid || (((uintptr_t)d->resid & 15) == 0 && (d->ld_rt & 7) == 0 &&
-                     ((d->c_s1 | d->c_s2) & 7) == 0))) {
+  // TMA box epilogue: every output of the tile as 32 x 32 boxes (row-major C / cs / aux, the
+  // transposed ct terms); falls back to the per-element stores where a layout does not fit.
+  if (p.splits == 1 && !(epi == 0 && d->beta != 0.f && d->C)) {
     const int div = p.c_off.div;
-    int rank = 0;
-    bool ok = true;
-    if (d->C)
+    const bool dual = (epi == 2 || epi == 5), bwd = (epi == 3 || epi == 6);
+    const int n_rows_out = dual ? N / 2 : (epi == 6 ? (int)d->ct_up_rows + N : N);
+    const bool c_ok = ((d->c_s1 | d->c_s2) & 7) == 0;
+    bool ok = c_ok;
+    int rank = 3;
+    if (ok && bwd && (N % 32) != 0) ok = false;
+    if (ok && (d->resid || d->target) &&
+        ((((uintptr_t)d->resid | (uintptr_t)d->target) & 15) || (d->ld_rt & 7)))
+      ok = false;
+    if (ok && bwd && ((((uintptr_t)d->aux0 | (uintptr_t)d->aux1) & 15) || (d->ld_aux & 3)))
+      ok = false;
+    if (ok && d->C && !dual && !bwd)
       ok = tc::make_out_map(&p.tma_c, d->C, true, N, M, d->ldc, div, d->c_s1, d->c_s2,
                             d->batch, &rank);
-    const int n_out = epi == 5 ? N / 2 : N;  // SwiGLU: one output column per gate / up pair
     for (int i = 0; i < d->ncs && ok; ++i)
-      ok = tc::make_out_map(&p.tma_cs[i], d->cs[i], false, n_out, M, d->ldcs, div, d->c_s1,
+      ok = tc::make_out_map(&p.tma_cs[i], d->cs[i], false, n_rows_out, M, d->ldcs, div,
+                            d->c_s1, d->c_s2, d->batch, &rank);
+    if (ok && dual && d->aux0)
+      ok = tc::make_out_map(&p.tma_aux[0], d->aux0, true, N / 2, M, d->ld_aux, div, d->c_s1,
+                            d->c_s2, d->batch, &rank) &&
+           tc::make_out_map(&p.tma_aux[1], d->aux1, true, N / 2, M, d->ld_aux, div, d->c_s1,
                             d->c_s2, d->batch, &rank);
+    if (ok && d->nct > 0) {
+      // C^T as [batch][rows][ldct] (x = output row m, y = output column): plain row offsets only
+      const bool t_ok = d->t_c1 == 0 && d->t_c2 == 0 && (d->batch == 1 || d->t_div <= 1);
+      const int ct_rows = bwd ? (int)d->ct_up_rows + N : (dual ? N / 2 : N);
+      const int64_t zs = d->batch > 1 ? d->t_r1 : (int64_t)ct_rows;
+      int r3 = 3;
+      ok = t_ok && zs > 0;
+      for (int i = 0; i < d->nct && ok; ++i)
+        ok = tc::make_out_map(&p.tma_ct[i], d->ct[i], false, M, ct_rows, d->ldct, 1,
+                              zs * d->ldct, 0, d->batch, &r3);
+    }
     if (ok) {
       p.tma_out = 1;
       p.out_rank = rank;
+      p.tma_bf16_only = !((d->C && !dual && !bwd) || (dual && d->aux0));
     }
   }
   cudaStream_t st = (cudaStream_t)stream;
