@@ -29,8 +29,12 @@ scales), 146 windows x 2048 ids, next-token NLL; value = scored tokens per secon
 over all windows (each window's 8-window batch dequantizes every layer into L2-resident bf16
 scratch, then runs the bf16 tensor-core forward and the head + NLL row pass).
 
+Workload "pipeline": the full 3-bit pipeline on the stack (build-db, RCO allocate, quantize the
+24 blocks on the quantized stream, export, eval), each phase timed; value = wall-clock seconds
+with the allocate phase extrapolated to 100 RCO steps from --rco-steps measured ones.
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload block|linear|gptq|rco|eval]
+                  [--workload block|linear|gptq|rco|eval|pipeline] [--rco-steps S]
 
 N > 1 runs under torchrun, one rank per GPU. Block: the ranks quantize one block together,
 data-parallel over the positions of each micro-batch sequence with one NCCL all-reduce of the
@@ -65,7 +69,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="block",
-                    choices=["block", "linear", "gptq", "rco", "eval"])
+                    choices=["block", "linear", "gptq", "rco", "eval", "pipeline"])
+    ap.add_argument("--rco-steps", type=int, default=2,
+                    help="pipeline: RCO steps run (the rest of the 100 extrapolated)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=200)
     return ap.parse_args()
@@ -864,6 +870,125 @@ def run_reference_eval(args):
     print(json.dumps(res), flush=True)
 
 
+# -------------------------------------------------------------------------- pipeline ---
+
+def run_pipeline(args):
+    """The full 3-bit pipeline on the 24-layer stack, each phase timed on the host clock:
+    build-db (Hessians + GPTQ at 2 / 3 / 4 bits over 128 x 2048 calibration ids), allocate (RCO,
+    3.0 bits, 8 samples x 32 windows x 2048; --rco-steps of the 100, the rest extrapolated
+    from their mean), quantize (24 blocks x qk / vo / mlp x 200 Lion steps on the quantized
+    stream, shards), export (MLX affine checkpoint), eval (packed model, 146 x 2048 windows).
+    value = the pipeline wall-clock in seconds with the allocate phase at 100 steps."""
+    import shutil
+    import tempfile
+    import torch
+    import torch.distributed as dist
+    from gsq_rco_mlx_b200 import _lib
+    from gsq_rco_mlx_b200.common.evaluate import PackedModel, perplexity
+    from gsq_rco_mlx_b200.gsq import pipeline as pl
+    from gsq_rco_mlx_b200.gsq.export import save_base_checkpoint
+    from gsq_rco_mlx_b200.gsq.staged import BlockOpts, DataParallel
+    from gsq_rco_mlx_b200.rco.allocate import Bank, KLObjective, rco_allocate
+    from gsq_rco_mlx_b200.rco.database import DBSpec, build_database, random_model
+
+    rank, world, local = dist_setup()
+    _lib.lib()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dp = DataParallel()
+    rco_steps = max(1, min(args.rco_steps, 100))
+
+    def sync():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    model = random_model(n_layers=24, seed=0, device=dev)
+    calib = np.random.default_rng(0).integers(0, VOCAB, size=(N_SEQ, T_SEQ)).astype(np.int32)
+    rco_win = np.random.default_rng(1).integers(0, VOCAB, size=(RCO_WINDOWS, T_SEQ)).astype(
+        np.int32)
+    ev_win = np.random.default_rng(2).integers(0, VOCAB, size=(EVAL_WINDOWS, T_SEQ)).astype(
+        np.int32)
+    work = tempfile.mkdtemp(prefix="gsq_pipeline_")
+    quiet = lambda *a: None
+    t = {}
+    clocks = Clocks(local)
+    clocks.start()
+    sync()
+    t0 = time.perf_counter()
+    man, res = build_database(model, calib, DBSpec(options=GPTQ_OPTIONS, n_layers=24), log=quiet,
+                              keep="device")
+    bank = Bank(man, res)
+    sync()
+    t["build_db"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    obj = KLObjective(model, bank, rco_win, windows_per_sample=RCO_WIN_PER_SAMPLE, chunk_seqs=8,
+                      dp=dp)
+    sync()
+    t["allocate_setup"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    alloc = rco_allocate(obj, bank, 3.0, steps=rco_steps, g=RCO_G, lr=0.1, seed=0)
+    sync()
+    t_rco = time.perf_counter() - t0
+    t["allocate_steps_measured"] = t_rco
+    t["allocate"] = t["allocate_setup"] + t_rco / rco_steps * 100
+    per_linear = {f"{L}.{n}": int(bank.options[int(k)])
+                  for (L, n), k in zip(bank.groups, alloc["choice"])}
+    del obj
+    torch.cuda.empty_cache()
+    bits = pl.load_bits(range(24), alloc={"per_linear_bits": per_linear})
+    t0 = time.perf_counter()
+    qres = pl.quantize_model(model, calib, bits, BlockOpts(steps=200), os.path.join(work, "q"),
+                             dp=dp, log=quiet)
+    sync()
+    t["quantize"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    if rank == 0:
+        save_base_checkpoint(model, os.path.join(work, "base"))
+        pl.export_quantized(os.path.join(work, "q"), os.path.join(work, "base"), range(24))
+    sync()
+    t["export"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    pm = PackedModel.load(os.path.join(work, "q", "mlx"), device=dev)
+    r = perplexity(pm, ev_win, chunk_seqs=EVAL_CHUNK, dp=dp)
+    sync()
+    t["eval"] = time.perf_counter() - t0
+    clk = clocks.stop()
+    total = t["build_db"] + t["allocate"] + t["quantize"] + t["export"] + t["eval"]
+    measured = total - t["allocate"] + t["allocate_setup"] + t_rco
+    out = {
+        "metric": "full 3-bit pipeline wall-clock (24-layer Qwen2.5-0.5B architecture: build-db, "
+                  "allocate, quantize, export, eval)",
+        "value": round(total, 2), "unit": "s", "n_gpus": world, "steps": 1, "warmup": 0,
+        "ms_per_step": round(total * 1000, 1), "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16 model, f32/f64 optimisation",
+        "data": "synthetic: random-init 24-layer stack, uniform-random calibration, RCO and "
+                "eval windows",
+        "config": {"workload": "full pipeline: 128 x 2048 calibration, RCO 100 steps (g 8, 32 "
+                               "windows), 24 blocks x 200 steps per stage, 146 eval windows",
+                   "phase_seconds": {k: round(v, 2) for k, v in t.items()},
+                   "rco_steps_measured": rco_steps,
+                   "measured_seconds": round(measured, 2),
+                   "decoded_avg_bits": round(alloc["decoded_avg_bits"], 4),
+                   "quantize_seconds_per_block": round(t["quantize"] / 24, 3),
+                   "eval_ppl": round(r["ppl"], 3),
+                   "parallelism": f"every phase data-parallel over {world} rank(s)"},
+        "e2e": {"value": round(total, 2), "unit": "s",
+                "h2d_bytes_per_step": int(calib.nbytes + rco_win.nbytes + ev_win.nbytes),
+                "d2h_bytes_per_step": int(sum(os.path.getsize(os.path.join(work, "q", f))
+                                              for f in os.listdir(os.path.join(work, "q"))
+                                              if f.endswith(".npz")) if rank == 0 else 0),
+                "what": "host ids in, shards and the checkpoint on disk, the eval dict out"},
+        "gpu_launches": None,
+        "clocks": clk,
+    }
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+        shutil.rmtree(work, ignore_errors=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 # ---------------------------------------------------------------------------- linear ---
 
 OUT_F, IN_F, N_SEQ_L, T_SEQ_L = 4864, 896, 32, 512
@@ -1035,6 +1160,12 @@ def main():
         return run_reference_rco(args) if args.impl == "reference" else run_rco(args)
     if args.workload == "eval":
         return run_reference_eval(args) if args.impl == "reference" else run_eval(args)
+    if args.workload == "pipeline":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the full pipeline's GSQ, RCO "
+                              "and eval phases are MLX-only in the reference (MLX absent)"}))
+            return None
+        return run_pipeline(args)
     if args.impl == "reference":
         run_reference(args)
     else:
