@@ -68,6 +68,7 @@ SIGNATURES = {
     "qgemm_packed": [_vp, _i32, _i32, _i64, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64,
                      _i32, _vp, _i64, _vp, _vp],
     "gsq_nll_rows": [_vp, _i32, _i32, _i64, _vp, _vp, _vp],
+    "gsq_scale_grad": [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp],
 }
 
 _lib = None

@@ -1234,6 +1234,12 @@ static int launch(GemmParams& p, int batch, cudaStream_t st) {
   for (int i = 0; i < p.na; ++i)
     for (int j = 0; j < p.nb; ++j) products += (i + j <= p.order);
   p.kb_per_chunk = products >= 3 ? 2 : 4;
+  // a bf16-output product of bf16 operands (the bf16 model's chain epilogues) folds its TMEM
+  // chunks every 8 k-blocks: its float32 sum is rounded to bf16 once, and K <= 512 (the
+  // attention products) needs no fold at all; the TMEM accumulation error grows with the
+  // chunk length, so long reductions (the head gradient over the vocabulary) keep folding
+  if (products == 1 && (EPI == EPI_BF16 || EPI == EPI_SWIGLU_BF16 || EPI == EPI_SWIGLU_BWD_BF16))
+    p.kb_per_chunk = 8;
   const bool has_small = (p.na > 1 || p.nb > 1) && p.order > 0;
   int nbig = (int)((kTmemCols - (has_small ? 2u * BN : 0u)) / BN);
   p.n_big = nbig > kMaxBig ? kMaxBig : nbig;

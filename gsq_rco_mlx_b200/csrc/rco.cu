@@ -167,6 +167,30 @@ nll_rows_kernel(const __nv_bfloat16* __restrict__ z, int V, int64_t ld,
   }
 }
 
+// Group-scale gradient of a stored-form linear W = bf16(s[r][c / gs] grid[code[r][c]]) with its
+// codes fixed (App-H scale fine-tune, staged.py:555-634, the mx.take backward): out[r][g] =
+// sum over the group's columns of G[r][c] grid[code[r][c]] (float64 sum, float32 out). One warp
+// per (row, group), lanes over the group's columns.
+__global__ void __launch_bounds__(256)
+scale_grad_kernel(const float* __restrict__ G, const uint8_t* __restrict__ codes, int out_f,
+                  int in_f, int bits, int gs, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int ng = (in_f + gs - 1) / gs;
+  const int64_t units = (int64_t)out_f * ng;
+  for (int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < units;
+       u += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int r = (int)(u / ng), g = (int)(u - (int64_t)r * ng);
+    const int c0 = g * gs, c1 = min(c0 + gs, in_f);
+    double acc = 0.0;
+    for (int c = c0 + lane; c < c1; c += 32) {
+      const int64_t i = (int64_t)r * in_f + c;
+      acc += (double)G[i] * (double)grid_value(bits, codes[i]);
+    }
+    acc = warp_sum_d(acc);
+    if (lane == 0) out[u] = (float)acc;
+  }
+}
+
 struct DotOpts {
   const uint8_t* codes[kMaxOptions];
   const float* scales[kMaxOptions];
@@ -322,6 +346,21 @@ extern "C" int gsq_nll_rows(const void* z, int n, int V, int64_t ld, const int32
     return GSQ_EINVAL;
   nll_rows_kernel<<<n, kKlThreads, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)z, V, ld,
                                                               targets, nll);
+  GSQ_CHECK_LAUNCH();
+  return GSQ_OK;
+}
+
+extern "C" int gsq_scale_grad(const float* G, const uint8_t* codes, int out_f, int in_f,
+                              int bits, int group_size, float* out, void* stream) {
+  if (!G || !codes || !out || out_f <= 0 || in_f <= 0 || group_size <= 0 || bits < 1 ||
+      bits > 8)
+    return GSQ_EINVAL;
+  const int ng = (in_f + group_size - 1) / group_size;
+  int64_t blocks = ((int64_t)out_f * ng * 32 + 255) / 256;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  scale_grad_kernel<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, (cudaStream_t)stream>>>(
+      G, codes, out_f, in_f, bits, group_size, out);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }

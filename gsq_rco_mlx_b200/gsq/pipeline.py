@@ -180,6 +180,31 @@ def quantize_model(model, cal_tokens, bits_by_layer: dict, opts: BlockOpts, out_
     return {"layers": stats_all, "seconds": round(time.perf_counter() - t_all, 3)}
 
 
+def finetune_shards(model, out_dir: str, layers, cal_tokens, steps: int, group_size: int = 64,
+                    log=print) -> dict:
+    """App-H on the written shards (pipeline.py:176-206): the group scales of every quantized
+    block fine-tuned end to end (gsq.finetune.scale_finetune, one calibration sequence per step)
+    and written back into the shards with the KL of the first and last steps in their stats."""
+    from .finetune import scale_finetune
+    from .lion import LR_SCALES
+    t0 = time.perf_counter()
+    shard_path = lambda i: os.path.join(out_dir, f"layer_{i:02d}.npz")
+    shards = {i: load_shard(shard_path(i)) for i in layers}
+    qblocks = {i: lins for i, (_, _, lins) in shards.items()}
+    new, kls = scale_finetune(model, qblocks, cal_tokens, steps, LR_SCALES, group_size, log)
+    w = max(1, min(10, len(kls) // 2))  # averaging window: at most half the steps
+    summary = {"steps": steps, "window": w, "kl_first": float(np.mean(kls[:w])),
+               "kl_last": float(np.mean(kls[-w:]))}
+    for i, (meta, stats, lins) in shards.items():
+        for name in LIN_ORDER:
+            lins[name]["scales"] = new[i][name]
+        stats["scale_finetune"] = dict(summary)
+        save_shard(shard_path(i), i, lins, {k: int(v) for k, v in meta["bits"].items()},
+                   meta["fingerprint"], stats)
+    summary["seconds"] = round(time.perf_counter() - t0, 1)
+    return summary
+
+
 def export_quantized(out_dir: str, base_dir: str, layers, group_size: int = 64,
                      scale_dtype: str = "bfloat16") -> str:
     """The mlx-lm checkpoint of the quantized blocks' shards (pipeline.py:256-266 with

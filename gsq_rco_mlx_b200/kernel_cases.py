@@ -183,7 +183,31 @@ def eval_batch(dev, g):
     return {"eval batch 8 x 2048": (None, lambda: ev.forward_nll(tok, tgt, 8, out))}
 
 
-CASES = {"mlp_gemms": mlp_gemms, "attn": attn, "attn1": lambda dev, g: attn(dev, g, seqs=1),
+def vjp_gemms(dev, g):
+    """Two GEMMs of the block vector-Jacobian product at one sequence (14 heads x 2048): the
+    probability cotangent dP = dO V^T per head (bf16 chain, causal tiles) and the MLP's
+    dd = cot Wd with the bf16 SwiGLU backward epilogue (rows and transposed outputs)."""
+    B, R = HEADS, T
+    do = _terms(B * T, HD, 1, dev, g)
+    vr = _terms(KV * T, HD, 1, dev, g)
+    dP = Terms(B * T, T, 1, dev, ld=T)
+    cot = _terms(R, H, 1, dev, g)
+    WdT = _terms(I, H, 1, dev, g)
+    gg = torch.randn(R, I, device=dev, generator=g)
+    uu = torch.randn(R, I, device=dev, generator=g)
+    dGU = Terms(R, 2 * I, 1, dev, ld=2 * I)
+    dGUT = Terms(2 * I, R, 1, dev)
+    return {
+        "dP = dO V^T (1x1, causal)": (2 * B * T * T * HD // 2, lambda: gemm(
+            do, vr, M=T, N=T, K=HD, batch=B, epi=4, a_off=(1, T, 0), b_off=(HEADS // KV, T, 0),
+            c_terms=dP, c_off=(1, T * T, 0), skip_upper=True)),
+        "dd SwiGLU bwd bf16 (1x1)": (2 * R * I * H, lambda: gemm(
+            cot, WdT, epi=6, aux0=gg, aux1=uu, ld_aux=I, c_terms=dGU, ct_terms=dGUT,
+            ct_up_rows=I)),
+    }
+
+
+CASES = {"mlp_gemms": mlp_gemms, "vjp_gemms": vjp_gemms, "attn": attn, "attn1": lambda dev, g: attn(dev, g, seqs=1),
          "soft_step": soft_step, "cublas": cublas, "packed": packed, "eval_batch": eval_batch}
 
 

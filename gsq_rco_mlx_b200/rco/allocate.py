@@ -103,7 +103,7 @@ class KLObjective:
         self.dev = model.embed.device
         self.cs = int(chunk_seqs)
         self.eng = Qwen2Block(cfg, self.cs, self.T, self.dev)
-        self.head = KLHead(model.embed)
+        self.head = KLHead(model.embed, chunk=8192)
         self.dots_ws = DotsWorkspace(self.dev)
         self.W_fp = [BlockWeights(W) for W in model.layers]
         # the reference hidden states (after the final norm) of every window, computed once

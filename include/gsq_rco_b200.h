@@ -394,6 +394,13 @@ int gsq_rope_bwd(const float *dy, int64_t ld_i, int S, int T, int nh, const floa
 int gsq_group_sum(const float *in, int64_t ld_i, int S, int nh, int rep, int T, float *out_f,
                   void *out_b, int64_t ld_o, int col0, void *stream);
 
+/* Group-scale gradient of a stored-form linear with fixed codes (App-H scale fine-tune,
+ * src/gsq_rco/gsq/staged.py:555-634): out[r][g] = sum over the columns c of group g of
+ * G[r][c] grid[code[r][c]], G float32 [out_f][in_f] the weight gradient, out float32
+ * [out_f][ceil(in_f / group_size)] (float64 sums). */
+int gsq_scale_grad(const float *G, const uint8_t *codes, int out_f, int in_f, int bits,
+                   int group_size, float *out, void *stream);
+
 /* ---- packed quantized-model eval (MLX affine export format) ----
  * A packed linear W [N][K] (src/gsq_rco/gsq/export.py:60-90, pack_codes / to_mlx_affine):
  * words u32 [N][K bits / 32], value k of row n at stream bits [k bits, (k + 1) bits), least
