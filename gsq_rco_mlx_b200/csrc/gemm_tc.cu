@@ -104,6 +104,7 @@ struct GemmParams {
   CUtensorMap tma_aux[2];  // SwiGLU g / u rows
   int tma_out, out_rank, tma_bufs;  // tma_bufs: 4 KB staging buffers per epilogue warp (1..3)
   int tma_bf16_only;                  // every box is bf16 (2 KB): no C / aux float32 boxes
+  int a_mn, b_mn;  // MN-major operands: 64 x 64 boxes (MN inner) at +8 KB per 64 MN indices
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -455,9 +456,10 @@ __device__ __forceinline__ double epilogue_tma(const GemmParams& p, const TileIn
           }
         }
       }
-      if (EPI == EPI_SWIGLU_BWD_BF16 && p.ncs) {
-        out_rows_terms(ring, p, a, 1, n0, row0, zr, zq, lane);
-        out_rows_terms(ring, p, du, 1, n0 + (int)p.ct_up_rows, row0, zr, zq, lane);
+      if (p.ncs) {  // row-major [dg | du]: columns n and n + ct_up_rows
+        const int nt = EPI == EPI_SWIGLU_BWD_BF16 ? 1 : p.ncs;
+        out_rows_terms(ring, p, a, nt, n0, row0, zr, zq, lane);
+        out_rows_terms(ring, p, du, nt, n0 + (int)p.ct_up_rows, row0, zr, zq, lane);
       }
       if (p.nct) {
         out_cols_terms(ring, p, a, n0, 0, row0, t.z, lane);
@@ -812,8 +814,8 @@ __device__ __forceinline__ double epilogue_out(const GemmParams& p, const TileIn
 
 // 4 K=16 steps of one 64-wide k-block into accumulator d: the shared-memory descriptors advance
 // by 32 bytes (2 in the start-address field) per step; the first step accumulates if acc_first.
-__device__ __forceinline__ void umma4(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                      uint32_t acc_first) {
+__device__ __forceinline__ void umma4(uint32_t d, uint64_t a, uint64_t b, uint64_t sa,
+                                      uint64_t sb, uint32_t idesc, uint32_t acc_first) {
   asm volatile(
       "{\n\t.reg .pred p0, p1;\n\t"
       "setp.ne.b32 p0, %4, 0;\n\t"
@@ -822,29 +824,30 @@ __device__ __forceinline__ void umma4(uint32_t d, uint64_t a, uint64_t b, uint32
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %6, %3, p1;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %7, %8, %3, p1;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %9, %10, %3, p1;\n\t}"
-      ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc_first), "l"(a + 2), "l"(b + 2),
-        "l"(a + 4), "l"(b + 4), "l"(a + 6), "l"(b + 6));
+      ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc_first), "l"(a + sa), "l"(b + sb),
+        "l"(a + 2 * sa), "l"(b + 2 * sb), "l"(a + 3 * sa), "l"(b + 3 * sb));
 }
 
 // The products of one k-block for NA x NBT bf16 terms of order <= 2 (hi x hi into big, the rest
-// into small); A term i at +i*1024, B term j at +(NA*1024 + j*tb) in the descriptor field.
+// into small); A term i at ad + i*1024, B term j at bd + j*tb in the descriptor's address field;
+// sa / sb: the address step of one K = 16 slice (32 B K-major, 2 KB MN-major).
 template <int NA, int NBT>
-__device__ __forceinline__ void issue_kb(uint64_t ad, uint32_t tb, uint32_t big, uint32_t small,
+__device__ __forceinline__ void issue_kb(uint64_t ad, uint64_t bd, uint32_t tb, uint64_t sa,
+                                         uint64_t sb, uint32_t big, uint32_t small,
                                          uint32_t idesc, uint32_t big_acc, uint32_t small_acc) {
-  const uint64_t bd = ad + (uint64_t)(NA * 1024);
-  umma4(big, ad, bd, idesc, big_acc);
+  umma4(big, ad, bd, sa, sb, idesc, big_acc);
   if (NA == 1 && NBT == 3) {
-    umma4(small, ad, bd + tb, idesc, small_acc);
-    umma4(small, ad, bd + 2 * tb, idesc, 1u);
+    umma4(small, ad, bd + tb, sa, sb, idesc, small_acc);
+    umma4(small, ad, bd + 2 * tb, sa, sb, idesc, 1u);
   } else if (NA == 3 && NBT == 1) {
-    umma4(small, ad + 1024, bd, idesc, small_acc);
-    umma4(small, ad + 2048, bd, idesc, 1u);
+    umma4(small, ad + 1024, bd, sa, sb, idesc, small_acc);
+    umma4(small, ad + 2048, bd, sa, sb, idesc, 1u);
   } else if (NA == 3 && NBT == 3) {
-    umma4(small, ad, bd + tb, idesc, small_acc);
-    umma4(small, ad + 1024, bd, idesc, 1u);
-    umma4(small, ad, bd + 2 * tb, idesc, 1u);
-    umma4(small, ad + 1024, bd + tb, idesc, 1u);
-    umma4(small, ad + 2048, bd, idesc, 1u);
+    umma4(small, ad, bd + tb, sa, sb, idesc, small_acc);
+    umma4(small, ad + 1024, bd, sa, sb, idesc, 1u);
+    umma4(small, ad, bd + 2 * tb, sa, sb, idesc, 1u);
+    umma4(small, ad + 1024, bd + tb, sa, sb, idesc, 1u);
+    umma4(small, ad + 2048, bd, sa, sb, idesc, 1u);
   }
 }
 
@@ -920,11 +923,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           uint8_t* st = smem + (size_t)s * stage_bytes;
           mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
           const int kx = (t.kb0 + kb) * BK;
-          for (int i = 0; i < p.na; ++i)
-            tma_load_2d(st + i * kTileA, &p.tma_a[i], &full_bar[s], kx, a_row);
+          for (int i = 0; i < p.na; ++i) {
+            if (p.a_mn) {  // two 64 (M) x 64 (K) boxes of the [K][M] operand
+              tma_load_2d(st + i * kTileA, &p.tma_a[i], &full_bar[s], t.tile_m, kx);
+              tma_load_2d(st + i * kTileA + 8192, &p.tma_a[i], &full_bar[s], t.tile_m + 64, kx);
+            } else {
+              tma_load_2d(st + i * kTileA, &p.tma_a[i], &full_bar[s], kx, a_row);
+            }
+          }
           for (int j = 0; j < p.nb; ++j) {
             uint8_t* bt = st + p.na * kTileA + j * kTileB;
-            if (p.dual_b) {
+            if (p.b_mn) {
+#pragma unroll
+              for (int bb = 0; bb < BN / 64; ++bb)
+                tma_load_2d(bt + bb * 8192, &p.tma_b[j], &full_bar[s], t.tile_n + 64 * bb, kx);
+            } else if (p.dual_b) {
               tma_load_2d(bt, &p.tma_b[j], &full_bar[s], kx, b_row);
               tma_load_2d(bt + kTileB / 2, &p.tma_b2[j], &full_bar[s], kx, b_row);
             } else {
@@ -952,7 +965,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(BM, BN);
+      const uint32_t idesc = idesc_bf16_f32(BM, BN) | ((uint32_t)p.a_mn << 15) |
+                             ((uint32_t)p.b_mn << 16);
+      const uint64_t sa = p.a_mn ? 128u : 2u, sb = p.b_mn ? 128u : 2u;
       // term configurations with a compile-time product list (order 2); others: generic loop
       const int cfg = (p.na == 1 && p.nb == 1) ? 1
                     : (p.order != 2) ? 0
@@ -989,13 +1004,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             fence_after_sync();
             const uint32_t st = smem_u32(smem + (size_t)s * stage_bytes);
             if (cfg != 0) {  // compile-time product lists: few instructions between UMMAs
-              const uint64_t ad = umma_desc_k_sw128(st);
+              const uint32_t sb_addr = st + p.na * kTileA;
+              const uint64_t ad = p.a_mn ? umma_desc_mn_sw128(st) : umma_desc_k_sw128(st);
+              const uint64_t bd = p.b_mn ? umma_desc_mn_sw128(sb_addr) : umma_desc_k_sw128(sb_addr);
               const uint32_t tb = kTileB >> 4;
-              const uint32_t ba = big_init ? 1u : 0u, sa = small_init ? 1u : 0u;
-              if (cfg == 1) issue_kb<1, 1>(ad, tb, big, small, idesc, ba, sa);
-              else if (cfg == 2) issue_kb<1, 3>(ad, tb, big, small, idesc, ba, sa);
-              else if (cfg == 3) issue_kb<3, 1>(ad, tb, big, small, idesc, ba, sa);
-              else issue_kb<3, 3>(ad, tb, big, small, idesc, ba, sa);
+              const uint32_t ba = big_init ? 1u : 0u, sm = small_init ? 1u : 0u;
+              if (cfg == 1) issue_kb<1, 1>(ad, bd, tb, sa, sb, big, small, idesc, ba, sm);
+              else if (cfg == 2) issue_kb<1, 3>(ad, bd, tb, sa, sb, big, small, idesc, ba, sm);
+              else if (cfg == 3) issue_kb<3, 1>(ad, bd, tb, sa, sb, big, small, idesc, ba, sm);
+              else issue_kb<3, 3>(ad, bd, tb, sa, sb, big, small, idesc, ba, sm);
               big_init = true;
               if (cfg != 1) small_init = true;
             } else
@@ -1009,8 +1026,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 #pragma unroll
                 for (int k = 0; k < BK / 16; ++k) {
                   const uint32_t accum = to_big ? (uint32_t)big_init : (uint32_t)small_init;
-                  umma_bf16(d, umma_desc_k_sw128(a0 + k * 32), umma_desc_k_sw128(b0 + k * 32),
-                            idesc, accum);
+                  const uint64_t da = p.a_mn ? umma_desc_mn_sw128(a0) + k * sa
+                                             : umma_desc_k_sw128(a0) + k * sa;
+                  const uint64_t db = p.b_mn ? umma_desc_mn_sw128(b0) + k * sb
+                                             : umma_desc_k_sw128(b0) + k * sb;
+                  umma_bf16(d, da, db, idesc, accum);
                   if (to_big) big_init = true; else small_init = true;
                 }
               }
@@ -1303,8 +1323,15 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   if (d->bn != 64 && d->bn != 128) return GSQ_EINVAL;
   const int epi = d->epi;
   if (!d->C && d->ncs == 0 && d->nct == 0 && !d->sq_partial) return GSQ_EINVAL;
-  if (d->lda < K || d->ldb < K || (d->C && d->ldc < ((epi == 2 || epi == 5) ? N / 2 : N)))
+  const int amn = d->a_major != 0, bmn = d->b_major != 0;
+  if (d->a_major < 0 || d->a_major > 1 || d->b_major < 0 || d->b_major > 1) return GSQ_EINVAL;
+  if ((amn ? (d->lda < M || d->a_rows < K) : d->lda < K) ||
+      (bmn ? (d->ldb < N || d->b_rows < K) : d->ldb < K) ||
+      (d->C && d->ldc < ((epi == 2 || epi == 5) ? N / 2 : N)))
     return GSQ_EINVAL;
+  // MN-major operands: one product (no batch offsets), B not paired with b2
+  if ((amn || bmn) && (d->batch != 1 || d->causal)) return GSQ_EINVAL;
+  if (bmn && (epi == 2 || epi == 5)) return GSQ_EINVAL;
   if (d->ncs > 0 && (d->ldcs & 7)) return GSQ_EINVAL;
   if (d->nct > 0 && (d->ldct & 7)) return GSQ_EINVAL;
   for (int i = 0; i < d->ncs; ++i)
@@ -1327,10 +1354,17 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   const int BN = d->bn;
   const bool dual = (epi == 2 || epi == 5);
   const int b_box = dual ? BN / 2 : BN;
-  for (int i = 0; i < d->na; ++i)
-    if (!tc::make_map(&p.tma_a[i], d->a[i], d->a_rows, K, d->lda, tc::BM)) return GSQ_EINVAL;
+  for (int i = 0; i < d->na; ++i) {
+    const bool ok = amn ? tc::make_map(&p.tma_a[i], d->a[i], d->a_rows, M, d->lda, 64)
+                        : tc::make_map(&p.tma_a[i], d->a[i], d->a_rows, K, d->lda, tc::BM);
+    if (!ok) return GSQ_EINVAL;
+  }
+  p.a_mn = amn;
+  p.b_mn = bmn;
   for (int j = 0; j < d->nb; ++j) {
-    if (!tc::make_map(&p.tma_b[j], d->b[j], d->b_rows, K, d->ldb, b_box)) return GSQ_EINVAL;
+    const bool ok = bmn ? tc::make_map(&p.tma_b[j], d->b[j], d->b_rows, N, d->ldb, 64)
+                        : tc::make_map(&p.tma_b[j], d->b[j], d->b_rows, K, d->ldb, b_box);
+    if (!ok) return GSQ_EINVAL;
     if (dual && !tc::make_map(&p.tma_b2[j], d->b2[j], d->b_rows, K, d->ldb, b_box))
       return GSQ_EINVAL;
   }
@@ -1378,7 +1412,7 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   if (p.splits == 1 && !(epi == 0 && d->beta != 0.f && d->C)) {
     const int div = p.c_off.div;
     const bool dual = (epi == 2 || epi == 5), bwd = (epi == 3 || epi == 6);
-    const int n_rows_out = dual ? N / 2 : (epi == 6 ? (int)d->ct_up_rows + N : N);
+    const int n_rows_out = dual ? N / 2 : (bwd ? (int)d->ct_up_rows + N : N);
     const bool c_ok = ((d->c_s1 | d->c_s2) & 7) == 0;
     bool ok = c_ok;
     int rank = 3;
@@ -1416,6 +1450,8 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
       p.tma_bf16_only = !((d->C && !dual && !bwd) || (dual && d->aux0));
     }
   }
+  // the row-major outputs of the float32 SwiGLU backward exist only in the box epilogue
+  if (epi == 3 && d->ncs > 0 && !p.tma_out) return GSQ_ENOTSUP;
   cudaStream_t st = (cudaStream_t)stream;
   if (p.splits > 1) {
     const int rc = BN == 64 ? tc::launch<64, 0>(p, 1, st) : tc::launch<128, 0>(p, 1, st);

@@ -144,7 +144,21 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
-// kind::f16 instruction descriptor: BF16 x BF16 -> F32, both K-major, M x N.
+// MN-major, 128-byte swizzled operand tile: 64 MN indices (128 B) per row, one row per k,
+// 8-row atoms of 1024 B (SBO = 1024 >> 4) along K, the next 64 MN indices 8 KB further
+// (LBO = 8192 >> 4: the 64 x 64 box of the next TMA load), version 1, SWIZZLE_128B.
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)(8192 >> 4) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// kind::f16 instruction descriptor: BF16 x BF16 -> F32, both K-major, M x N (bits 15 / 16 set
+// MN-major A / B).
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);

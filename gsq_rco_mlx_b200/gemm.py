@@ -149,6 +149,8 @@ class GemmDesc(_C.Structure):
         ("row_period", _C.c_int),
         ("split_k", _C.c_int),
         ("workspace", _C.c_void_p),
+        ("a_major", _C.c_int),
+        ("b_major", _C.c_int),
     ]
 
 
@@ -213,14 +215,17 @@ def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, 
          sq_partial=None, bias=None, resid=None, target=None, ld_rt=None, out_scale=1.0,
          aux0=None, aux1=None, ld_aux=None, B2: Terms = None, epi=0, bn=128, causal=False,
          batch=1, a_off=(1, 0, 0), b_off=(1, 0, 0), c_off=(1, 0, 0), t_off=(1, 0, 0, 0, 0),
-         ct_up_rows=0, skip_upper=False, row_period=0, split_k="auto"):
+         ct_up_rows=0, skip_upper=False, row_period=0, split_k="auto", a_major=0, b_major=0):
     """One (batched) tensor-core GEMM with a fused epilogue; see gsq_gemm in the C header.
     M, N, K default to the operand shapes; a_off/b_off/c_off = (div, s1, s2),
-    t_off = (div, row_s1, row_s2, col_s1, col_s2)."""
+    t_off = (div, row_s1, row_s2, col_s1, col_s2). a_major / b_major = 1: the operand's Terms
+    hold [K][M] / [K][N] (MN-major: a row-major activation read as its own transpose)."""
     d = GemmDesc()
-    d.M = A.rows if M is None else M
-    d.N = (B.rows if epi not in (2, 5) else 2 * B.rows) if N is None else N
-    d.K = A.cols if K is None else K
+    d.M = (A.cols if a_major else A.rows) if M is None else M
+    d.N = ((B.cols if b_major else B.rows) if epi not in (2, 5) else 2 * B.rows) if N is None \
+        else N
+    d.K = (A.rows if a_major else A.cols) if K is None else K
+    d.a_major, d.b_major = int(a_major), int(b_major)
     d.batch = batch
     na = A.n if na is None else na
     nb = B.n if nb is None else nb

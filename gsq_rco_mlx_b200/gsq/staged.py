@@ -349,6 +349,14 @@ def _gather(src, ids_t, per_seq, stride, offset, rows, cols, n_terms, row_terms=
               0 if col_terms is None else col_terms.ld, _lib.stream_ptr())
 
 
+def _col_terms(base: Terms, col0: int, cols: int) -> Terms:
+    """Columns [col0, col0 + cols) of a Terms operand as a Terms view (same rows and ld)."""
+    v = Terms.__new__(Terms)
+    v.rows, v.cols, v.n, v.ld = base.rows, int(cols), base.n, base.ld
+    v.t = [t[:, col0:] for t in base.t]
+    return v
+
+
 def _bf16_rows(x):
     """A bf16 tensor [rows, cols] as a one-term operand."""
     return Terms(x.shape[0], x.shape[1], 1, ld=x.shape[1], tensors=[x])
@@ -398,9 +406,12 @@ class MLPStep(_StageBase):
     from a cache. Per resample, five tensor-core GEMMs with fused epilogues:
       F1  gate | up = mn [Wg|Wu]^T       SwiGLU epilogue: g, u (float32), d = silu(g) u as terms
       F3  r = h1 + d Wd^T - Y_fp         residual-loss epilogue: loss partials, dR = 2 r / count
-      B1  dL/dWd = dR^T d
-      B2  dd = dR Wd                     SwiGLU-backward epilogue: dL/dg, dL/du (transposed)
-      B3  [dL/dWg; dL/dWu] = [dg; du]^T mn
+      B1  dL/dWd = dR^T d                dR and d read MN-major (row-major, as their transposes)
+      B2  dd = dR Wd                     Wd read MN-major; SwiGLU-backward epilogue: dL/dg and
+                                         dL/du as row-major terms [dg | du]
+      B3  dL/dWg = dg^T mn, dL/dWu = du^T mn    [dg | du] and mn read MN-major
+    No operand is transposed in memory: every reduction over the micro-batch rows reads the
+    row-major activations through MN-major tensor-core operands.
     """
 
     def __init__(self, lins, cfg, m, T, R, window=None):
@@ -415,15 +426,14 @@ class MLPStep(_StageBase):
         self.cfg, self.m, self.T, self.M, self.count = cfg, m, T, M, m * (T - 1) * H
         bf = torch.bfloat16
         self.MN = Terms(M, H, 1, dev)
-        self.MNT = Terms(H, M, 1, dev)
         self.H1 = Terms(M, H, 1, dev)
         self.Y = Terms(M, H, 1, dev)
         self.g = torch.empty(M, I, device=dev, dtype=torch.float32)
         self.u = torch.empty(M, I, device=dev, dtype=torch.float32)
-        self.DIN, self.DINT = Terms(M, I, 3, dev), Terms(I, M, 3, dev)
-        self.DR, self.DRT = Terms(M, H, 3, dev), Terms(H, M, 3, dev)
-        self.GUT = Terms(2 * I, M, 3, dev)
-        self.DdT = Terms(I, H, 3, dev)
+        self.DIN = Terms(M, I, 3, dev)
+        self.DR = Terms(M, H, 3, dev)
+        self.DGU = Terms(M, 2 * I, 3, dev)
+        self.DG, self.DU = _col_terms(self.DGU, 0, I), _col_terms(self.DGU, I, I)
         self.gflat, (self.grad_gu, self.grad_d) = _flat_views(dev, [(2, R, I, H), (R, H, I)])
         tiles = ((M + 127) // 128) * ((H + 127) // 128)
         self.sq = torch.zeros(tiles, device=dev, dtype=torch.float64)
@@ -437,7 +447,7 @@ class MLPStep(_StageBase):
         """Positions 1.. of the chosen sequences of the caches (bf16 [N*T, H])."""
         H, T = self.cfg.hidden, self.T
         ids = _seq_ids(self.dev, seq_ids)
-        _gather(mn_all, ids, self.w, T, self.p0, self.M, H, 1, self.MN, self.MNT)
+        _gather(mn_all, ids, self.w, T, self.p0, self.M, H, 1, self.MN)
         _gather(h1_all, ids, self.w, T, self.p0, self.M, H, 1, self.H1)
         _gather(y_all, ids, self.w, T, self.p0, self.M, H, 1, self.Y)
 
@@ -447,20 +457,17 @@ class MLPStep(_StageBase):
         tiles = self.sq.numel()
         for r in range(self.R):
             gemm(self.MN, self.D[gname][r], B2=self.D[uname][r], epi=2, aux0=self.g, aux1=self.u,
-                 c_terms=self.DIN, ct_terms=self.DINT)
+                 c_terms=self.DIN)
             gemm(self.DIN, self.D[dname][r], epi=1, resid=self.H1.t[0], target=self.Y.t[0],
                  ld_rt=self.H1.ld, out_scale=2.0 / self.count, sq_partial=self.sq,
-                 c_terms=self.DR, ct_terms=self.DRT)
+                 c_terms=self.DR)
             _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(self.loss[r:r + 1]),
                       _lib.stream_ptr())
-            gemm(self.DRT, self.DINT, C=self.grad_d[r])
-            for i in range(3):
-                _lib.call("gsq_transpose_bf16", _lib.ptr(self.Dbuf[dname][r][i]), H, I, I, 0,
-                          _lib.ptr(self.DdT.t[i]), self.DdT.ld, 0, 1, 0, _lib.stream_ptr())
-            gemm(self.DR, self.DdT, epi=3, aux0=self.g, aux1=self.u, ct_terms=self.GUT,
-                 ct_up_rows=I)
-            gemm(self.GUT, self.MNT, M=I, batch=2, C=self.grad_gu[0, r], ldc=H,
-                 a_off=(1, I, 0), c_off=(1, self.R * I * H, 0))
+            gemm(self.DR, self.DIN, C=self.grad_d[r], a_major=1, b_major=1)
+            gemm(self.DR, self.D[dname][r], b_major=1, epi=3, aux0=self.g, aux1=self.u,
+                 c_terms=self.DGU, ct_up_rows=I)
+            gemm(self.DG, self.MN, C=self.grad_gu[0, r], ldc=H, a_major=1, b_major=1)
+            gemm(self.DU, self.MN, C=self.grad_gu[1, r], ldc=H, a_major=1, b_major=1)
 
 
 class VOStep(_StageBase):

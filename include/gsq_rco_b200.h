@@ -158,6 +158,11 @@ typedef struct {
    * (float32, >= split_k * M * N) and are summed in part order, then C = alpha sum + beta C. */
   int split_k;
   float *workspace;
+  /* operand layout: 0 = K-major (A [M][lda], B [N][ldb], the reduction index contiguous);
+   * 1 = MN-major (A stored [K][lda] with the M index contiguous, B [K][ldb] with N contiguous:
+   * a row-major activation used as its own transpose). MN-major needs batch 1 (no row offsets)
+   * and, for B, no SwiGLU pairing (b2). */
+  int a_major, b_major;
 } gsq_gemm_desc;
 
 /* Batched float32-faithful tensor-core GEMM with a fused epilogue (see gsq_gemm_tc for the

@@ -92,3 +92,36 @@ def test_gemm_tc_exact_operand_three_products():
     gemm_tc(At, Bt, C=C)
     ref = A.double() @ B.double().T
     assert ((C.double() - ref).norm() / ref.norm()).item() < 2e-6
+
+
+@pytest.mark.parametrize("terms", [(1, 1), (3, 3), (1, 3)])
+@pytest.mark.parametrize("majors", [(1, 0), (0, 1), (1, 1)])
+@pytest.mark.parametrize("shape,bn", [((300, 200, 100), 128), ((256, 320, 640), 128),
+                                      ((200, 96, 1000), 64)])
+def test_mn_major_operands_equal_k_major(terms, majors, shape, bn):
+    """An MN-major operand (a row-major [K][M] / [K][N] matrix read as its own transpose) gives
+    bit-for-bit the product of the K-major copy: same products, same accumulation order."""
+    from gsq_rco_mlx_b200.gemm import Terms, gemm, check_err
+    M, N, K = shape
+    na, nb = terms
+    g = torch.Generator(device="cuda").manual_seed(M + N + K + 7 * na + nb)
+
+    def pair(rows, cols, n):
+        km = Terms(rows, cols, n, "cuda")
+        mn = Terms(cols, rows, n, "cuda")
+        for i in range(n):
+            x = (torch.randn(rows, cols, device="cuda", generator=g) * 2.0 ** (-8 * i)).bfloat16()
+            km.t[i][:, :cols] = x
+            mn.t[i][:, :rows] = x.T
+        return km, mn
+    A, Amn = pair(M, K, na)
+    B, Bmn = pair(N, K, nb)
+    ref = torch.empty(M, N, device="cuda")
+    out = torch.empty(M, N, device="cuda")
+    gemm(A, B, C=ref, bn=bn, split_k=1)
+    am, bm = majors
+    gemm(Amn if am else A, Bmn if bm else B, M=M, N=N, K=K, C=out, bn=bn, split_k=1,
+         a_major=am, b_major=bm)
+    torch.cuda.synchronize()
+    check_err(torch.device("cuda"))
+    assert torch.equal(out, ref)
