@@ -276,11 +276,23 @@ __device__ __forceinline__ void ring_flush(BoxRing& r, int lane) {
   }
 }
 
-// bf16 term i of x (x = t0 + t1 + t2 to float32 precision)
-__device__ __forceinline__ __nv_bfloat16 term_of(float x, int i) {
-  __nv_bfloat16 h0, h1, h2;
-  split3_bf16(x, h0, h1, h2);
-  return i == 0 ? h0 : (i == 1 ? h1 : h2);
+// The terms of x = t0 + t1 + t2 (to float32 precision) are peeled one at a time: the next term
+// is bf16(v) and v keeps the exact remainder v - t (split3_bf16 step by step). `last` skips the
+// remainder after the final term.
+__device__ __forceinline__ uint32_t peel2(float& v0, float& v1, bool last) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+  if (!last) {
+    const float2 f = __bfloat1622float2(h);
+    v0 = __fsub_rn(v0, f.x);
+    v1 = __fsub_rn(v1, f.y);
+  }
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ __nv_bfloat16 peel1(float& v, bool last) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(v);
+  if (!last) v = __fsub_rn(v, __bfloat162float(h));
+  return h;
 }
 
 __device__ __forceinline__ void box_put_f32(uint8_t* buf, int lane, const float* v) {
@@ -291,25 +303,49 @@ __device__ __forceinline__ void box_put_f32(uint8_t* buf, int lane, const float*
         make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
 }
 
-__device__ __forceinline__ void box_put_bf16(uint8_t* buf, int lane, const float* v, int term) {
+// the next bf16 term of v (peeled in place)
+__device__ __forceinline__ void box_put_bf16(uint8_t* buf, int lane, float* v, bool last) {
   uint8_t* row = buf + lane * 64;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    __align__(16) __nv_bfloat16 o[8];
+    uint4 o;
+    o.x = peel2(v[8 * c], v[8 * c + 1], last);
+    o.y = peel2(v[8 * c + 2], v[8 * c + 3], last);
+    o.z = peel2(v[8 * c + 4], v[8 * c + 5], last);
+    o.w = peel2(v[8 * c + 6], v[8 * c + 7], last);
+    *reinterpret_cast<uint4*>(row + ((c ^ ((lane >> 1) & 3)) << 4)) = o;
+  }
+}
+
+// bf16 term `term` of v, v unchanged (the earlier terms are peeled from a copy of each chunk)
+__device__ __forceinline__ void box_put_bf16_keep(uint8_t* buf, int lane, const float* v,
+                                                  int term) {
+  uint8_t* row = buf + lane * 64;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = term_of(v[8 * c + j], term);
-    *reinterpret_cast<uint4*>(row + ((c ^ ((lane >> 1) & 3)) << 4)) =
-        *reinterpret_cast<const uint4*>(o);
+  for (int c = 0; c < 4; ++c) {
+    float r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = v[8 * c + j];
+    for (int k = 0; k < term; ++k) {
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) peel2(r[j], r[j + 1], false);
+    }
+    uint4 o;
+    o.x = peel2(r[0], r[1], true);
+    o.y = peel2(r[2], r[3], true);
+    o.z = peel2(r[4], r[5], true);
+    o.w = peel2(r[6], r[7], true);
+    *reinterpret_cast<uint4*>(row + ((c ^ ((lane >> 1) & 3)) << 4)) = o;
   }
 }
 
 // transposed: box row u (output column n0 + u), box column lane (output row row0 + lane)
-__device__ __forceinline__ void box_put_bf16_t(uint8_t* buf, int lane, const float* v, int term) {
+__device__ __forceinline__ void box_put_bf16_t(uint8_t* buf, int lane, float* v, bool last) {
   const int c = lane >> 3, e = (lane & 7) * 2;
 #pragma unroll
   for (int u = 0; u < 32; ++u)
     *reinterpret_cast<__nv_bfloat16*>(buf + u * 64 + ((c ^ ((u >> 1) & 3)) << 4) + e) =
-        term_of(v[u], term);
+        peel1(v[u], last);
 }
 
 __device__ __forceinline__ void box_store(const CUtensorMap* map, const uint8_t* buf, int rank,
@@ -331,24 +367,42 @@ __device__ __forceinline__ void out_rows_f32(BoxRing& r, const GemmParams& p,
   if (row0 < p.M) box_store(map, b, p.out_rank, col0, row0, zr, zq, lane);
 }
 
-__device__ __forceinline__ void out_rows_terms(BoxRing& r, const GemmParams& p, const float* v,
+// Row-major bf16 terms of v (v is consumed: it holds the last remainder afterwards)
+__device__ __forceinline__ void out_rows_terms(BoxRing& r, const GemmParams& p, float* v,
                                                int nterms, int col0, int row0, int zr, int zq,
                                                int lane) {
   for (int i = 0; i < nterms; ++i) {
     uint8_t* b = ring_slot(r, 2048, lane);
-    box_put_bf16(b, lane, v, i);
+    box_put_bf16(b, lane, v, i + 1 == nterms);
     if (row0 < p.M) box_store(&p.tma_cs[i], b, p.out_rank, col0, row0, zr, zq, lane);
   }
 }
 
-// C^T terms: output rows up + col0 .. (of batch z), columns row0 ..
-__device__ __forceinline__ void out_cols_terms(BoxRing& r, const GemmParams& p, const float* v,
+// C^T terms: output rows up + col0 .. (of batch z), columns row0 .. (v is consumed)
+__device__ __forceinline__ void out_cols_terms(BoxRing& r, const GemmParams& p, float* v,
                                                int col0, int up, int row0, int z, int lane) {
   for (int i = 0; i < p.nct; ++i) {
     uint8_t* b = ring_slot(r, 2048, lane);
-    box_put_bf16_t(b, lane, v, i);
+    box_put_bf16_t(b, lane, v, i + 1 == p.nct);
     if (row0 < p.M) box_store(&p.tma_ct[i], b, 3, row0, up + col0, 0, z, lane);
   }
+}
+
+// Both term layouts of v: when the transposed terms follow, the row-major ones leave v as it is
+// (a single term never changes it)
+__device__ __forceinline__ void out_terms(BoxRing& r, const GemmParams& p, float* v, int nterms,
+                                          int col0, int up, int row0, int zr, int zq, int z,
+                                          int lane) {
+  if (p.nct && nterms > 1) {
+    for (int i = 0; i < nterms; ++i) {
+      uint8_t* b = ring_slot(r, 2048, lane);
+      box_put_bf16_keep(b, lane, v, i);
+      if (row0 < p.M) box_store(&p.tma_cs[i], b, p.out_rank, col0 + up, row0, zr, zq, lane);
+    }
+  } else if (nterms) {
+    out_rows_terms(r, p, v, nterms, col0 + up, row0, zr, zq, lane);
+  }
+  if (p.nct) out_cols_terms(r, p, v, col0, up, row0, z, lane);
 }
 
 // 8 consecutive values of a row segment (columns c .. c + 7 of 32): one 16-byte load where the
@@ -379,6 +433,43 @@ __device__ __forceinline__ void load8_f32(const float* ptr, bool ok, int nvalid,
   } else {
 #pragma unroll
     for (int j = 0; j < 8; ++j) r[j] = (ok && c + j < nvalid) ? ptr[c + j] : 0.f;
+  }
+}
+
+// The row inputs that the epilogue of this warp's part of tile t reads (SwiGLU-backward g and u,
+// residual and target rows), fetched into L2 while the tile's MMAs run: the epilogue's loads of
+// one 32-column group then wait on L2 rather than on HBM. Only addresses inside the inputs.
+template <int BN, int EPI>
+__device__ __forceinline__ void prefetch_row_inputs(const GemmParams& p, const TileInfo& t,
+                                                    int lane, int q, int h) {
+  constexpr bool kBwd = EPI == EPI_SWIGLU_BWD || EPI == EPI_SWIGLU_BWD_BF16;
+  if (!kBwd && EPI != EPI_RESID && EPI != EPI_BF16) return;
+  const int row = t.tile_m + 32 * q + lane;
+  if (row >= p.M) return;
+  const int64_t coff = p.c_off.at(t.z);
+#pragma unroll
+  for (int jc = 0; jc < BN / 64; ++jc) {
+    const int n0 = t.tile_n + 64 * jc + 32 * h;
+    if (n0 >= p.N) break;
+    const int last = min(31, p.N - 1 - n0);
+    if (kBwd) {
+      const float* gp = p.aux0 + coff + (int64_t)row * p.ld_aux + n0;
+      const float* up = p.aux1 + coff + (int64_t)row * p.ld_aux + n0;
+      prefetch_l2(gp);
+      prefetch_l2(gp + last);
+      prefetch_l2(up);
+      prefetch_l2(up + last);
+    } else {
+      const int64_t off = coff + (int64_t)row * p.ld_rt + n0;
+      if (p.resid) {
+        prefetch_l2(p.resid + off);
+        prefetch_l2(p.resid + off + last);
+      }
+      if (EPI == EPI_RESID) {
+        prefetch_l2(p.target + off);
+        prefetch_l2(p.target + off + last);
+      }
+    }
   }
 }
 
@@ -418,8 +509,7 @@ __device__ __forceinline__ double epilogue_tma(const GemmParams& p, const TileIn
                                      : bf16r(__fmul_rn(bf16r(__fmul_rn(g, bf16r(sigmoid_f(g)))),
                                                        uu));
       }
-      if (p.ncs) out_rows_terms(ring, p, a, p.ncs, n0, row0, zr, zq, lane);
-      if (p.nct) out_cols_terms(ring, p, a, n0, 0, row0, t.z, lane);
+      out_terms(ring, p, a, p.ncs, n0, 0, row0, zr, zq, t.z, lane);
     } else if (EPI == EPI_SWIGLU_BWD || EPI == EPI_SWIGLU_BWD_BF16) {
       const float* gp = p.aux0 + coff + (int64_t)row * p.ld_aux + n0;
       const float* up = p.aux1 + coff + (int64_t)row * p.ld_aux + n0;
@@ -456,15 +546,10 @@ __device__ __forceinline__ double epilogue_tma(const GemmParams& p, const TileIn
           }
         }
       }
-      if (p.ncs) {  // row-major [dg | du]: columns n and n + ct_up_rows
-        const int nt = EPI == EPI_SWIGLU_BWD_BF16 ? 1 : p.ncs;
-        out_rows_terms(ring, p, a, nt, n0, row0, zr, zq, lane);
-        out_rows_terms(ring, p, du, nt, n0 + (int)p.ct_up_rows, row0, zr, zq, lane);
-      }
-      if (p.nct) {
-        out_cols_terms(ring, p, a, n0, 0, row0, t.z, lane);
-        out_cols_terms(ring, p, du, n0, (int)p.ct_up_rows, row0, t.z, lane);
-      }
+      // row-major [dg | du]: columns n and n + ct_up_rows; transposed: rows n and n + ct_up_rows
+      const int nt = p.ncs == 0 ? 0 : (EPI == EPI_SWIGLU_BWD_BF16 ? 1 : p.ncs);
+      out_terms(ring, p, a, nt, n0, 0, row0, zr, zq, t.z, lane);
+      out_terms(ring, p, du, nt, n0, (int)p.ct_up_rows, row0, zr, zq, t.z, lane);
     } else {
       // EPI_PLAIN, EPI_RESID, EPI_BF16
       if (EPI == EPI_BF16) {
@@ -514,15 +599,13 @@ __device__ __forceinline__ double epilogue_tma(const GemmParams& p, const TileIn
           if (u < nvalid) sq += (double)a[u] * (double)a[u];
       }
       if (p.C) out_rows_f32(ring, p, &p.tma_c, a, n0, row0, zr, zq, lane);
-      if (p.ncs) out_rows_terms(ring, p, a, p.ncs, n0, row0, zr, zq, lane);
-      if (p.nct) {
-        // transposed values outside the output are zero (the consumer's padding rows)
-        if (!row_ok) {
+      if (p.nct && !row_ok) {
+        // transposed values outside the output are zero (the consumer's padding rows); the
+        // TMA unit clips these rows of the row-major boxes
 #pragma unroll
-          for (int u = 0; u < 32; ++u) a[u] = 0.f;
-        }
-        out_cols_terms(ring, p, a, n0, 0, row0, t.z, lane);
+        for (int u = 0; u < 32; ++u) a[u] = 0.f;
       }
+      out_terms(ring, p, a, p.ncs, n0, 0, row0, zr, zq, t.z, lane);
     }
     ring_flush(ring, lane);
   }
@@ -1082,6 +1165,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       if (!tile_at<BN>(p, L, t)) continue;
       const uint32_t tb = tcount & 1u, tph = (tcount >> 1) & 1u;
       ++tcount;
+      prefetch_row_inputs<BN, EPI>(p, t, lane, q, h);
       float acc[kAcc];
 #pragma unroll
       for (int u = 0; u < kAcc; ++u) acc[u] = 0.f;

@@ -245,7 +245,7 @@ class Qwen2Block:
         b = {
             "g": torch.empty(R, I, device=dev), "u": torch.empty(R, I, device=dev),
             "out": torch.empty(R, H, device=dev, dtype=bf),
-            "dGU": torch.empty(R, 2 * I, device=dev, dtype=bf), "dGUT": Terms(2 * I, R, 1, dev),
+            "dGU": torch.empty(R, 2 * I, device=dev, dtype=bf),
             "dmn": torch.empty(R, H, device=dev, dtype=bf),
             "dh1": torch.empty(R, H, device=dev, dtype=bf),
             "doh": torch.empty(B * T, hd, device=dev, dtype=bf), "doT": Terms(B * hd, T, 1, dev),
@@ -258,11 +258,7 @@ class Qwen2Block:
             "dvh": torch.empty(B * T, hd, device=dev),
             "dk": torch.empty(S * c.n_kv * T, hd, device=dev),
             "dQKV": torch.empty(R, QD + 2 * KD, device=dev, dtype=bf),
-            "dQKVT": Terms(QD + 2 * KD, R, 1, dev),
             "dhn": torch.empty(R, H, device=dev, dtype=bf),
-            # transposed activations (K-major operands of the weight gradients)
-            "cotT": Terms(H, R, 1, dev), "dT": Terms(I, R, 1, dev), "mnT": Terms(H, R, 1, dev),
-            "dh1T": Terms(H, R, 1, dev), "oT": Terms(QD, R, 1, dev), "hnT": Terms(H, R, 1, dev),
         }
         self._bwd_key, self._bwd = key, b
         return b
@@ -313,25 +309,21 @@ class Qwen2Block:
         self.forward(h, W, S=S, out=b["out"][:R], gu=(b["g"][:R], b["u"][:R]))
         rows = lambda x, n=None: Terms(x.shape[0] if n is None else n, x.shape[1], 1,
                                        ld=x.shape[1], tensors=[x if n is None else x[:n]])
-        # transposed activations
-        self._T(cot, R, H, H, b["cotT"])
-        self._T(self.d_in, R, I, I, b["dT"])
-        self._T(self.mn, R, H, H, b["mnT"])
-        self._T(self.o, R, QD, QD, b["oT"])
-        self._T(self.hn, R, H, H, b["hnT"])
-        # MLP: dd = bf16(cot Wd) with the SwiGLU backward in the epilogue
+        # weight gradients dW = dY^T X: both row-major [R, .] activations read as MN-major
+        # operands (the same products as their transposes)
+        wgrad = lambda dy, x, out: gemm(rows(dy, R), rows(x, R), M=dy.shape[1], N=x.shape[1],
+                                        K=R, C=out, beta=beta, a_major=1, b_major=1)
+        # MLP: dd = bf16(cot Wd) with the SwiGLU backward in the epilogue ([dg | du] rows)
         gemm(rows(cot), W.transposed("down"), epi=6, aux0=b["g"], aux1=b["u"], ld_aux=I,
-             c_terms=Terms(R, 2 * I, 1, ld=2 * I, tensors=[b["dGU"][:R]]), ct_terms=b["dGUT"],
-             ct_up_rows=I)
+             c_terms=Terms(R, 2 * I, 1, ld=2 * I, tensors=[b["dGU"][:R]]), ct_up_rows=I)
         gemm(rows(b["dGU"], R), W.transposed("gate_up"), epi=4, c_terms=rows(b["dmn"], R))
-        gemm(b["dGUT"], b["mnT"], M=2 * I, N=H, K=R, C=grads["_gu"], beta=beta)
-        gemm(b["cotT"], b["dT"], M=H, N=I, K=R, C=grads["down_proj"], beta=beta)
+        wgrad(b["dGU"], self.mn, grads["_gu"])
+        wgrad(cot, self.d_in, grads["down_proj"])
         _lib.call("gsq_rmsnorm_bwd", _lib.ptr(self.h1), H, _lib.ptr(W.W["post_norm"]),
                   _lib.ptr(b["dmn"]), H, _lib.ptr(cot), H, _lib.ptr(b["dh1"]), H, R, H,
                   float(c.eps), st)
         # o_proj: do per (sequence, head) = bf16(dh1 Wo[:, h]) and its transpose
-        self._T(b["dh1"], R, H, H, b["dh1T"])
-        gemm(b["dh1T"], b["oT"], M=H, N=QD, K=R, C=grads["o_proj"], beta=beta)
+        wgrad(b["dh1"], self.o, grads["o_proj"])
         gemm(rows(b["dh1"], R), W.transposed("o"), M=T, N=hd, K=H, batch=B, bn=64, epi=4,
              a_off=(nh, T, 0), b_off=(nh, 0, hd),
              c_terms=Terms(B * T, hd, 1, ld=hd, tensors=[b["doh"]]), c_off=(1, T * hd, 0),
@@ -373,9 +365,8 @@ class Qwen2Block:
         _lib.call("gsq_group_sum", _lib.ptr(b["dvh"]), hd, S, nh, rep, T, None,
                   _lib.ptr(dQKV), QKV, QD + KD, st)
         # q / k / v projections and the input norm
-        self._T(dQKV, R, QKV, QKV, b["dQKVT"])
         gemm(rows(dQKV, R), W.transposed("qkv"), epi=4, c_terms=rows(b["dhn"], R))
-        gemm(b["dQKVT"], b["hnT"], M=QKV, N=H, K=R, C=grads["_qkv"], beta=beta)
+        wgrad(dQKV, self.hn, grads["_qkv"])
         _lib.call("gsq_rmsnorm_bwd", _lib.ptr(h), H, _lib.ptr(W.W["in_norm"]), _lib.ptr(b["dhn"]),
                   H, _lib.ptr(b["dh1"]), H, _lib.ptr(dh), H, R, H, float(c.eps), st)
         return dh, grads

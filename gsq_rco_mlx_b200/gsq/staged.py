@@ -164,7 +164,8 @@ class SoftLinear:
 class LinearStep:
     """The qk-stage step of the linears that read the same rows X [M, in] (staged.py:322-329).
     Per resample r: R_r = X (w_bar_r - W)^T on the tensor cores (epilogue: loss partials and
-    R_r^T as bf16 terms), then G_r = 2 / (M out) R_r^T X. One fused pass per linear then runs
+    R_r as bf16 terms), then G_r = 2 / (M out) R_r^T X with R_r and X read as MN-major operands
+    (their transposes, never stored). One fused pass per linear then runs
     the backward, the resample mean, Lion, and the next step's soft weights and probabilities.
     All GEMM operands are bf16 terms (three for float32 data, one for exactly-bf16 rows)."""
 
@@ -175,8 +176,7 @@ class LinearStep:
         self.lins, self.M, self.in_f, self.R = lins, int(M), int(in_f), int(resamples)
         self.M_total = int(M if M_total is None else M_total)
         self.nx = int(x_terms)
-        self.X = Terms(M, in_f, self.nx, dev)        # A of the residual GEMM
-        self.XT = Terms(in_f, M, self.nx, dev)       # B of the weight-gradient GEMM
+        self.X = Terms(M, in_f, self.nx, dev)   # A of the residual GEMM, B of the gradient
         R = self.R
         self.Dbuf = {l.name: torch.zeros(R, 3, l.out_f, l.in_f, device=dev, dtype=torch.bfloat16)
                      for l in lins}
@@ -184,7 +184,7 @@ class LinearStep:
                            for r in range(R)] for l in lins}
         self.probs = {l.name: torch.zeros(R, l.K, l.d, device=dev, dtype=torch.float32)
                       for l in lins}
-        self.RT = {l.name: Terms(l.out_f, M, 3, dev) for l in lins}
+        self.Rres = {l.name: Terms(M, l.out_f, 3, dev) for l in lins}
         self.gflat, views = _flat_views(dev, [(R,) + l.shape for l in lins])
         self.grads = {l.name: v for l, v in zip(lins, views)}
         tiles = max(((M + 127) // 128) * ((l.out_f + 127) // 128) for l in lins)
@@ -194,7 +194,7 @@ class LinearStep:
         self.dev = dev
 
     def stage(self, x_all, seq_ids, per_seq, seq_stride, offset):
-        """Gather rows of x_all (float32 [n_rows, in]) into the X and X^T operand terms."""
+        """Gather rows of x_all (float32 [n_rows, in]) into the X operand terms."""
         ids = torch.as_tensor(np.asarray(seq_ids, dtype=np.int32))
         self.seq[:len(ids)].copy_(ids, non_blocking=True)
         rows = len(ids) * per_seq
@@ -203,7 +203,7 @@ class LinearStep:
         _lib.call("gsq_gather_split", _lib.ptr(x_all), int(x_all.dtype == torch.bfloat16),
                   x_all.shape[-1], _lib.ptr(self.seq),
                   int(per_seq), int(seq_stride), int(offset), self.M, self.in_f, self.nx,
-                  self.X.ptrs(), self.X.ld, self.XT.ptrs(), self.XT.ld, _lib.stream_ptr())
+                  self.X.ptrs(), self.X.ld, None, 0, _lib.stream_ptr())
 
     def first_forward(self, targets, t, tau, kappa, noise_seed, noise_of=None):
         """Soft weights and probabilities of the first step of the stage."""
@@ -216,14 +216,15 @@ class LinearStep:
     def contract(self):
         """Residuals, losses and weight gradients of every linear and resample."""
         for li, lin in enumerate(self.lins):
-            RT, G = self.RT[lin.name], self.grads[lin.name]
+            Rr, G = self.Rres[lin.name], self.grads[lin.name]
             tiles = ((self.M + 127) // 128) * ((lin.out_f + 127) // 128)
             for r in range(self.R):
-                gemm(self.X, self.D[lin.name][r], ct_terms=RT, sq_partial=self.sq)
+                gemm(self.X, self.D[lin.name][r], c_terms=Rr, sq_partial=self.sq)
                 slot = self.loss[li * self.R + r:li * self.R + r + 1]
                 _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(slot),
                           _lib.stream_ptr())
-                gemm(RT, self.XT, alpha=2.0 / (self.M_total * lin.out_f), C=G[r])
+                gemm(Rr, self.X, M=lin.out_f, N=self.in_f, K=self.M,
+                     alpha=2.0 / (self.M_total * lin.out_f), C=G[r], a_major=1, b_major=1)
 
     def update(self, targets, t, tau, kappa, opts, noise_seed, nxt=None, noise_of=None):
         """Fused backward + Lion of step t; nxt = (t1, tau1, kappa1) also runs step t1's forward."""
@@ -504,8 +505,8 @@ class VOStep(_StageBase):
         self.P = Terms(m * nh * Tq, Tk, 1, dev)
         self.PT = Terms(m * nh * Tk, Tq, 1, dev)
         self.VT = Terms(m * nkv * hd, Tk, 3, dev)
-        self.O, self.OT = Terms(m * Tq, H, 3, dev), Terms(H, m * Tq, 3, dev)
-        self.DY, self.DYT = Terms(m * Tq, H, 3, dev), Terms(H, m * Tq, 3, dev)
+        self.O = Terms(m * Tq, H, 3, dev)
+        self.DY = Terms(m * Tq, H, 3, dev)
         self.DoT = Terms(H, H, 3, dev)
         self.DOT = Terms(m * H, Tq, 3, dev)
         self.dv = torch.empty(m * nh, Tk, hd, device=dev, dtype=torch.float32)
@@ -575,12 +576,12 @@ class VOStep(_StageBase):
                  ct_terms=self.VT, t_off=(1, nkvd, 0, 0, 0))
             gemm(self.P, self.VT, M=Tq, N=hd, K=Tk, batch=B, bn=64, causal=int(q0 == 0),
                  a_off=(1, Tq, 0), b_off=(c.rep, hd, 0), c_off=(nh, Tq * H, hd),
-                 c_terms=self.O, ct_terms=self.OT, t_off=(nh, 0, hd, Tq, 0))
+                 c_terms=self.O)
             gemm(self.O, self.D[oname][r], epi=1, target=self.A.t[0], ld_rt=self.A.ld,
                  row_period=Tq if q0 == 0 else 0, out_scale=2.0 / self.count,
-                 sq_partial=self.sq, c_terms=self.DY, ct_terms=self.DYT)
+                 sq_partial=self.sq, c_terms=self.DY)
             _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(self.loss[r:r + 1]), st)
-            gemm(self.DYT, self.OT, C=self.grad_o[r])
+            gemm(self.DY, self.O, M=H, N=H, K=m * Tq, C=self.grad_o[r], a_major=1, b_major=1)
             for i in range(3):
                 _lib.call("gsq_transpose_bf16", _lib.ptr(self.Dbuf[oname][r][i]), H, H, H, 0,
                           _lib.ptr(self.DoT.t[i]), self.DoT.ld, 0, 1, 0, st)

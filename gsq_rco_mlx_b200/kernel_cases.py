@@ -8,10 +8,11 @@ micro-timing (one process, one GPU, a few GB of device memory).
 each case is timed with CUDA events over 10 launches after 3 warm-up launches and printed with
 its executed bf16 TFLOP/s (GEMMs) or algorithmic GB/s (streams).
 
-mlp_gemms: the five GEMMs of one mlp-stage resample (micro-batch 2 x 2047 rows) and the hard
+mlp_gemms: the six GEMMs of one mlp-stage resample (micro-batch 2 x 2047 rows) and the hard
   SwiGLU GEMM of the block forward (8 x 2048 rows):
     F1 gate|up = mn [Wg|Wu]^T (1 x 3 terms, SwiGLU epilogue)   F3 residual loss (3 x 3)
-    B1 dL/dWd (3 x 3)   B2 SwiGLU backward (3 x 3)   B3 dL/dWg|Wu (3 x 1, batch 2)
+    B1 dL/dWd (3 x 3, MN-major operands)   B2 SwiGLU backward (3 x 3, MN-major weight)
+    B3 dL/dWg, dL/dWu (3 x 1, two MN-major launches)
 attn: the causal scores GEMM and softmax of 8 sequences x 14 heads x 2048 positions (attn1: one
   sequence, 235 MB of scores: the profiler-sized case).
 soft_step: the fused backward + Lion + next forward of one up_proj-shaped soft linear (R = 2).
@@ -27,6 +28,7 @@ import torch
 
 from . import _lib
 from .gemm import Terms, check_err, gemm
+from .gsq.staged import _col_terms
 
 H, I, HEADS, KV, HD, T = 896, 4864, 14, 2, 64, 2048
 
@@ -44,32 +46,38 @@ def _terms(rows, cols, n, dev, g):
 
 
 def mlp_gemms(dev, g):
+    """The six GEMMs of one resample of the mlp stage step (one micro-batch of 2 x 2047
+    positions) as the stage runs them, plus the hard (bf16) SwiGLU forward of 8 sequences: F1
+    SwiGLU forward, F3 residual loss, B1 dWd, B2 SwiGLU backward, B3 dWg / dWu (the weight
+    gradients read row-major activations as MN-major operands)."""
     M = 2 * (T - 1)
-    MN, MNT, H1, Y = (_terms(M, H, 1, dev, g), _terms(H, M, 1, dev, g), _terms(M, H, 1, dev, g),
-                      _terms(M, H, 1, dev, g))
-    Dg, Du, Dd, DdT = (_terms(I, H, 3, dev, g), _terms(I, H, 3, dev, g), _terms(H, I, 3, dev, g),
-                       _terms(I, H, 3, dev, g))
+    MN, H1, Y = _terms(M, H, 1, dev, g), _terms(M, H, 1, dev, g), _terms(M, H, 1, dev, g)
+    Dg, Du, Dd = _terms(I, H, 3, dev, g), _terms(I, H, 3, dev, g), _terms(H, I, 3, dev, g)
     gg, uu = torch.empty(M, I, device=dev), torch.empty(M, I, device=dev)
-    DIN, DINT = Terms(M, I, 3, dev), Terms(I, M, 3, dev)
-    DR, DRT = Terms(M, H, 3, dev), Terms(H, M, 3, dev)
-    GUT = Terms(2 * I, M, 3, dev)
+    DIN, DR = Terms(M, I, 3, dev), Terms(M, H, 3, dev)
+    DGU = Terms(M, 2 * I, 3, dev)
+    DG, DU = _col_terms(DGU, 0, I), _col_terms(DGU, I, I)
     grad_gu, grad_d = torch.empty(2, I, H, device=dev), torch.empty(H, I, device=dev)
     sq = torch.zeros(((M + 127) // 128) * 7, device=dev, dtype=torch.float64)
     R = 8 * T
     MNt = _terms(R, H, 1, dev, g)
     Wg1, Wu1 = _terms(I, H, 1, dev, g), _terms(I, H, 1, dev, g)
     d_in = torch.empty(R, I, device=dev, dtype=torch.bfloat16)
+
+    def b3():
+        gemm(DG, MN, C=grad_gu[0], ldc=H, a_major=1, b_major=1)
+        gemm(DU, MN, C=grad_gu[1], ldc=H, a_major=1, b_major=1)
     return {
         "F1 swiglu fwd (1x3)": (3 * 2 * M * 2 * I * H, lambda: gemm(
-            MN, Dg, B2=Du, epi=2, aux0=gg, aux1=uu, c_terms=DIN, ct_terms=DINT)),
+            MN, Dg, B2=Du, epi=2, aux0=gg, aux1=uu, c_terms=DIN)),
         "F3 resid (3x3)": (6 * 2 * M * H * I, lambda: gemm(
             DIN, Dd, epi=1, resid=H1.t[0], target=Y.t[0], ld_rt=H1.ld, out_scale=1e-3,
-            sq_partial=sq, c_terms=DR, ct_terms=DRT)),
-        "B1 gradWd (3x3)": (6 * 2 * H * I * M, lambda: gemm(DRT, DINT, C=grad_d)),
+            sq_partial=sq, c_terms=DR)),
+        "B1 gradWd (3x3, MN-major)": (6 * 2 * H * I * M, lambda: gemm(
+            DR, DIN, C=grad_d, a_major=1, b_major=1)),
         "B2 swiglu bwd (3x3)": (6 * 2 * M * I * H, lambda: gemm(
-            DR, DdT, epi=3, aux0=gg, aux1=uu, ct_terms=GUT, ct_up_rows=I)),
-        "B3 gradWgu (3x1)": (3 * 2 * 2 * I * H * M, lambda: gemm(
-            GUT, MNT, M=I, batch=2, C=grad_gu, ldc=H, a_off=(1, I, 0), c_off=(1, I * H, 0))),
+            DR, Dd, b_major=1, epi=3, aux0=gg, aux1=uu, c_terms=DGU, ct_up_rows=I)),
+        "B3 gradWgu (3x1, MN-major)": (3 * 2 * 2 * I * H * M, b3),
         "hard swiglu bf16 (1x1)": (2 * R * 2 * I * H, lambda: gemm(
             MNt, Wg1, B2=Wu1, epi=5, c_terms=Terms(R, I, 1, ld=I, tensors=[d_in]))),
     }
@@ -186,7 +194,7 @@ def eval_batch(dev, g):
 def vjp_gemms(dev, g):
     """Two GEMMs of the block vector-Jacobian product at one sequence (14 heads x 2048): the
     probability cotangent dP = dO V^T per head (bf16 chain, causal tiles) and the MLP's
-    dd = cot Wd with the bf16 SwiGLU backward epilogue (rows and transposed outputs)."""
+    dd = cot Wd with the bf16 SwiGLU backward epilogue ([dg | du] rows)."""
     B, R = HEADS, T
     do = _terms(B * T, HD, 1, dev, g)
     vr = _terms(KV * T, HD, 1, dev, g)
@@ -196,14 +204,12 @@ def vjp_gemms(dev, g):
     gg = torch.randn(R, I, device=dev, generator=g)
     uu = torch.randn(R, I, device=dev, generator=g)
     dGU = Terms(R, 2 * I, 1, dev, ld=2 * I)
-    dGUT = Terms(2 * I, R, 1, dev)
     return {
         "dP = dO V^T (1x1, causal)": (2 * B * T * T * HD // 2, lambda: gemm(
             do, vr, M=T, N=T, K=HD, batch=B, epi=4, a_off=(1, T, 0), b_off=(HEADS // KV, T, 0),
             c_terms=dP, c_off=(1, T * T, 0), skip_upper=True)),
         "dd SwiGLU bwd bf16 (1x1)": (2 * R * I * H, lambda: gemm(
-            cot, WdT, epi=6, aux0=gg, aux1=uu, ld_aux=I, c_terms=dGU, ct_terms=dGUT,
-            ct_up_rows=I)),
+            cot, WdT, epi=6, aux0=gg, aux1=uu, ld_aux=I, c_terms=dGU, ct_up_rows=I)),
     }
 
 
