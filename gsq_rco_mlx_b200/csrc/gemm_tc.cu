@@ -473,6 +473,21 @@ __device__ __forceinline__ void prefetch_row_inputs(const GemmParams& p, const T
   }
 }
 
+// bias[n0 + c .. n0 + c + 7] (0 at columns >= n0 + nvalid); one float4 pair when the 32
+// columns are all inside and the bias is 16-byte aligned
+__device__ __forceinline__ void load8_bias(const float* bias, int n0, int nvalid, int c,
+                                           float* r) {
+  if (nvalid >= 32 && ((uintptr_t)bias & 15) == 0) {
+    const float4 f0 = *reinterpret_cast<const float4*>(bias + n0 + c);
+    const float4 f1 = *reinterpret_cast<const float4*>(bias + n0 + c + 4);
+    r[0] = f0.x; r[1] = f0.y; r[2] = f0.z; r[3] = f0.w;
+    r[4] = f1.x; r[5] = f1.y; r[6] = f1.z; r[7] = f1.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = c + j < nvalid ? bias[n0 + c + j] : 0.f;
+  }
+}
+
 template <int BN, int EPI>
 __device__ __forceinline__ double epilogue_tma(const GemmParams& p, const TileInfo& t, float* acc,
                                                BoxRing& ring, int lane, int q, int h) {
@@ -540,10 +555,9 @@ __device__ __forceinline__ double epilogue_tma(const GemmParams& p, const TileIn
             a[e] = bf16r(__fadd_rn(__fmul_rn(da, sb),
                                    __fmul_rn(ds, __fmul_rn(sf, __fsub_rn(1.0f, sf)))));
           }
-          if (!(row_ok && e < nvalid)) {
-            a[e] = 0.f;
-            du[e] = 0.f;
-          }
+          const bool live = row_ok && e < nvalid;
+          a[e] = live ? a[e] : 0.f;
+          du[e] = live ? du[e] : 0.f;
         }
       }
       // row-major [dg | du]: columns n and n + ct_up_rows; transposed: rows n and n + ct_up_rows
@@ -551,52 +565,85 @@ __device__ __forceinline__ double epilogue_tma(const GemmParams& p, const TileIn
       out_terms(ring, p, a, nt, n0, 0, row0, zr, zq, t.z, lane);
       out_terms(ring, p, du, nt, n0, (int)p.ct_up_rows, row0, zr, zq, t.z, lane);
     } else {
-      // EPI_PLAIN, EPI_RESID, EPI_BF16
+      // EPI_PLAIN, EPI_RESID, EPI_BF16. Every optional input is one uniform branch around a
+      // loop over the group (never a test per element): bias values arrive 8 at a time (0
+      // beyond the output's columns), residual and target rows through load8_bf16.
+      const bool hb = p.bias != nullptr, hr = p.resid != nullptr;
+      const __nv_bfloat16* rp = p.resid + coff + (int64_t)row * p.ld_rt + n0;
       if (EPI == EPI_BF16) {
-        const __nv_bfloat16* rp = p.resid + coff + (int64_t)row * p.ld_rt + n0;
+        // x = bf16(acc); x = bf16(x + bias); x = bf16(resid + x). With neither input and only
+        // single-term bf16 outputs the rounding is left to the output conversion, which rounds
+        // the same way.
+        if (hb || hr || p.C || p.sq_partial || p.ncs > 1 || p.nct > 1) {
 #pragma unroll
-        for (int c = 0; c < 32; c += 8) {
-          float r[8];
-          if (p.resid) load8_bf16(rp, row_ok, nvalid, c, r);
+          for (int u = 0; u < 32; ++u) a[u] = bf16r(a[u]);
+        }
+        if (hb) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int u = c + j;
-            float x = bf16r(a[u]);
-            if (p.bias && u < nvalid) x = bf16r(__fadd_rn(x, p.bias[n0 + u]));
-            if (p.resid) x = bf16r(__fadd_rn(r[j], x));
-            a[u] = x;
+          for (int c = 0; c < 32; c += 8) {
+            float b[8];
+            load8_bias(p.bias, n0, nvalid, c, b);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a[c + j] = bf16r(__fadd_rn(a[c + j], b[j]));
+          }
+        }
+        if (hr) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            float r[8];
+            load8_bf16(rp, row_ok, nvalid, c, r);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a[c + j] = bf16r(__fadd_rn(r[j], a[c + j]));
           }
         }
       } else if (EPI == EPI_RESID) {
-        const __nv_bfloat16* rp = p.resid + coff + (int64_t)row * p.ld_rt + n0;
         const __nv_bfloat16* tp = p.target + coff + (int64_t)row * p.ld_rt + n0;
-        const bool zero_row = p.row_period > 0 && (row % p.row_period) == 0;
+        const bool live = row_ok && !(p.row_period > 0 && (row % p.row_period) == 0);
+        if (hb) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            float b[8];
+            load8_bias(p.bias, n0, nvalid, c, b);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a[c + j] = __fadd_rn(a[c + j], b[j]);
+          }
+        }
+        if (hr) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            float r[8];
+            load8_bf16(rp, row_ok, nvalid, c, r);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a[c + j] = __fadd_rn(a[c + j], r[j]);
+          }
+        }
 #pragma unroll
         for (int c = 0; c < 32; c += 8) {
-          float r[8], tg[8];
-          if (p.resid) load8_bf16(rp, row_ok, nvalid, c, r);
+          float tg[8];
           load8_bf16(tp, row_ok, nvalid, c, tg);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const int u = c + j;
-            float x = a[u];
-            if (p.bias && u < nvalid) x = __fadd_rn(x, p.bias[n0 + u]);
-            if (p.resid) x = __fadd_rn(x, r[j]);
-            x = __fsub_rn(x, tg[j]);
-            if (zero_row || !(row_ok && u < nvalid)) x = 0.f;
-            sq += (double)x * (double)x;
+            const float x = (live && u < nvalid) ? __fsub_rn(a[u], tg[j]) : 0.f;
+            sq = fma((double)x, (double)x, sq);
             a[u] = __fmul_rn(p.out_scale, x);
           }
         }
-      } else if (p.bias) {
+      } else if (hb) {
 #pragma unroll
-        for (int u = 0; u < 32; ++u)
-          if (u < nvalid) a[u] = __fadd_rn(a[u], p.bias[n0 + u]);
+        for (int c = 0; c < 32; c += 8) {
+          float b[8];
+          load8_bias(p.bias, n0, nvalid, c, b);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) a[c + j] = __fadd_rn(a[c + j], b[j]);
+        }
       }
       if (EPI != EPI_RESID && p.sq_partial && row_ok) {
 #pragma unroll
-        for (int u = 0; u < 32; ++u)
-          if (u < nvalid) sq += (double)a[u] * (double)a[u];
+        for (int u = 0; u < 32; ++u) {
+          const double v = u < nvalid ? (double)a[u] : 0.0;
+          sq = fma(v, v, sq);
+        }
       }
       if (p.C) out_rows_f32(ring, p, &p.tma_c, a, n0, row0, zr, zq, lane);
       if (p.nct && !row_ok) {
