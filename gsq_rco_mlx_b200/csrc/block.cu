@@ -181,9 +181,67 @@ softmax_causal_v2_kernel(const float* __restrict__ S, int B, int T, __nv_bfloat1
   }
 }
 
-// Row-windowed form: local row i of batch z is query position row0 + i; keys k <= row0 + i of
-// the cols stored ones are valid. S [B][rows][ld_s] float32 -> P [B][rows][ld_p] bf16 (zeros at
-// masked keys k < cols). One warp per row.
+// Row-windowed and vectorised: local row i of batch z is query position t = row0 + i and sees
+// keys k <= t; the arithmetic of softmax_causal_v2_kernel (float4 reads, float64 sum, four bf16
+// per store). With row0 == 0 (a square causal block) the zeros stop at the end of the query's
+// 128-key block, the only keys that the causal P V product and the causal transpose read;
+// otherwise (a window of query rows over all keys) every masked key k < cols is written.
+// Needs cols, ld_s and ld_p multiples of 4, S 16-byte and P 8-byte aligned.
+__global__ void __launch_bounds__(256)
+softmax_causal_rows_v2_kernel(const float* __restrict__ S, int B, int rows, int cols,
+                              int64_t ld_s, int row0, __nv_bfloat16* __restrict__ P,
+                              int64_t ld_p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n_rows = (int64_t)B * rows;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < n_rows;
+       row += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int t = row0 + (int)(row % rows);
+    const float4* s4 = reinterpret_cast<const float4*>(S + row * ld_s);
+    const int nv = t / 4 + 1;  // vectors holding keys 0..t (t < cols, cols % 4 == 0)
+    float m = -INFINITY;
+#pragma unroll 4
+    for (int v = lane; v < nv; v += 32) {
+      const float4 q = s4[v];
+      const int k0 = 4 * v;
+      m = fmaxf(m, q.x);
+      if (k0 + 1 <= t) m = fmaxf(m, q.y);
+      if (k0 + 2 <= t) m = fmaxf(m, q.z);
+      if (k0 + 3 <= t) m = fmaxf(m, q.w);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    double sum = 0.0;
+#pragma unroll 2
+    for (int v = lane; v < nv; v += 32) {
+      const float4 q = s4[v];
+      const int k0 = 4 * v;
+      sum += (double)expf(__fsub_rn(q.x, m));
+      if (k0 + 1 <= t) sum += (double)expf(__fsub_rn(q.y, m));
+      if (k0 + 2 <= t) sum += (double)expf(__fsub_rn(q.z, m));
+      if (k0 + 3 <= t) sum += (double)expf(__fsub_rn(q.w, m));
+    }
+    sum = warp_sum_d(sum);
+    const float inv = __frcp_rn((float)sum);
+    const int end = row0 == 0 ? min(cols, (t / 128 + 1) * 128) : cols;
+    uint2* p2 = reinterpret_cast<uint2*>(P + row * ld_p);
+#pragma unroll 2
+    for (int v = lane; v < end / 4; v += 32) {
+      const int k0 = 4 * v;
+      float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k0 <= t) q = s4[v];
+      const float x[4] = {q.x, q.y, q.z, q.w};
+      __align__(8) __nv_bfloat16 o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        o[j] = __float2bfloat16_rn(k0 + j <= t ? __fmul_rn(expf(__fsub_rn(x[j], m)), inv) : 0.f);
+      p2[v] = *reinterpret_cast<const uint2*>(o);
+    }
+  }
+}
+
+// Row-windowed form, any layout: local row i of batch z is query position row0 + i; keys
+// k <= row0 + i of the cols stored ones are valid. S [B][rows][ld_s] float32 -> P [B][rows][ld_p]
+// bf16 (zeros at masked keys k < cols). One warp per row.
 __global__ void __launch_bounds__(256)
 softmax_causal_rows_kernel(const float* __restrict__ S, int B, int rows, int cols, int64_t ld_s,
                            int row0, __nv_bfloat16* __restrict__ P, int64_t ld_p) {
@@ -299,9 +357,16 @@ extern "C" int gsq_softmax_causal_rows(const float* S, int B, int rows, int cols
   if (!S || !P || B <= 0 || rows <= 0 || cols <= 0 || row0 < 0 || ld_s < cols || ld_p < cols ||
       row0 + rows > cols)
     return GSQ_EINVAL;
-  softmax_causal_rows_kernel<<<blocks((int64_t)B * rows * 32, 256), 256, 0,
-                                 (cudaStream_t)stream>>>(S, B, rows, cols, ld_s, row0,
-                                                         (__nv_bfloat16*)P, ld_p);
+  const unsigned g = blocks((int64_t)B * rows * 32, 256);
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool vec = cols % 4 == 0 && ld_s % 4 == 0 && ld_p % 4 == 0 && ((uintptr_t)S & 15) == 0 &&
+                   ((uintptr_t)P & 7) == 0;
+  if (vec)
+    softmax_causal_rows_v2_kernel<<<g, 256, 0, st>>>(S, B, rows, cols, ld_s, row0,
+                                                     (__nv_bfloat16*)P, ld_p);
+  else
+    softmax_causal_rows_kernel<<<g, 256, 0, st>>>(S, B, rows, cols, ld_s, row0,
+                                                  (__nv_bfloat16*)P, ld_p);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }

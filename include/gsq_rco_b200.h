@@ -266,8 +266,11 @@ int gsq_softmax_causal(const float *S, int B, int T, void *P, void *PT, void *st
 
 /* Row window of the causal softmax (data-parallel query rows): local row i of batch z is query
  * position row0 + i and sees keys k <= row0 + i of the cols stored (row0 + rows <= cols).
- * S float32 [B][rows][ld_s] -> P bf16 [B][rows][ld_p], masked keys k < cols written as 0.
- * Same arithmetic as gsq_softmax_causal (src/gsq_rco/gsq/e2e.py:149-155). */
+ * S float32 [B][rows][ld_s] -> P bf16 [B][rows][ld_p], masked keys k < cols written as 0; with
+ * row0 == 0 and cols, ld_s, ld_p multiples of 4 (S 16-byte, P 8-byte aligned) the zeros stop at
+ * the end of each query's 128-key block, as in gsq_softmax_causal (the causal P V product and
+ * the causal transpose read no key beyond it). Same arithmetic as gsq_softmax_causal
+ * (src/gsq_rco/gsq/e2e.py:149-155). */
 int gsq_softmax_causal_rows(const float *S, int B, int rows, int cols, int64_t ld_s, int row0,
                             void *P, int64_t ld_p, void *stream);
 

@@ -135,3 +135,31 @@ def test_causal_softmax_vector_rows(T):
     assert float((got[region] != ref[region]).float().mean()) < 1e-3
     assert torch.equal(got[region], P2.float().cpu().view(B, T, T)[region])
     assert torch.equal(PT.float().cpu(), P2.float().cpu().view(B, T, T).transpose(1, 2))
+
+
+@pytest.mark.parametrize("row0,rows,cols", [(0, 384, 384), (256, 128, 384), (1000, 1048, 2048)])
+def test_causal_softmax_row_window(row0, rows, cols):
+    """gsq_softmax_causal_rows (query rows row0 .. row0 + rows - 1 over cols keys) against the
+    oracle's float32 softmax with a float64 sum: equal up to rare last-bit differences on keys
+    <= query; masked keys are zero up to the end of the query's 128-key block when row0 == 0 (a
+    square causal block, whose consumers read no further) and up to cols otherwise."""
+    from gsq_rco_mlx_b200 import _lib
+    B = 2
+    g = torch.Generator().manual_seed(row0 + rows + cols)
+    S = (4 * torch.randn(B, rows, cols, generator=g)).float()
+    P = torch.full((B * rows, cols), 7.0, device=DEV, dtype=torch.bfloat16)
+    _lib.call("gsq_softmax_causal_rows", _lib.ptr(S.to(DEV)), B, rows, cols, cols, row0,
+              _lib.ptr(P), cols, _lib.stream_ptr())
+    torch.cuda.synchronize()
+    t = row0 + torch.arange(rows)[:, None]
+    k = torch.arange(cols)[None, :]
+    Sm = S.masked_fill(k > t, -torch.inf)
+    m = Sm.max(-1, keepdim=True).values
+    e = torch.exp(Sm - m)
+    ref = ob.bf(e * torch.reciprocal(e.double().sum(-1, keepdim=True).float()))
+    got = P.float().cpu().view(B, rows, cols)
+    inside = (k // 128) <= (t // 128) if row0 == 0 else torch.ones(rows, cols, dtype=torch.bool)
+    assert torch.all(got[:, ~inside] == 7.0)
+    region = inside.expand(B, rows, cols)
+    assert float((got[region] != ref[region]).float().mean()) < 1e-3
+    assert torch.all(got[:, (k > t) & inside] == 0)
