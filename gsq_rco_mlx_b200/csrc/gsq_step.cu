@@ -51,6 +51,48 @@ __global__ void gather_split_kernel(const TS* __restrict__ x, int64_t ld_x,
   }
 }
 
+// The row-major terms alone (no transposed copy): one thread per 8 consecutive columns of a
+// gathered row, 16-byte loads and stores. Needs cols, ld_x and ld_t multiples of 8 and 16-byte
+// aligned rows.
+template <typename TS>
+__global__ void gather_rows_kernel(const TS* __restrict__ x, int64_t ld_x,
+                                   const int32_t* __restrict__ seq, int per_seq,
+                                   int64_t seq_stride, int offset, int rows, int cols,
+                                   int n_terms, __nv_bfloat16* __restrict__ t0,
+                                   __nv_bfloat16* __restrict__ t1,
+                                   __nv_bfloat16* __restrict__ t2, int64_t ld_t) {
+  const int per_row = cols / 8;
+  const int64_t n = (int64_t)rows * per_row;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(e / per_row), c = (int)(e - (int64_t)r * per_row) * 8;
+    const int64_t src = (int64_t)seq[r / per_seq] * seq_stride + offset + (r % per_seq);
+    float v[8];
+    if (sizeof(TS) == 2) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(x + src * ld_x + c);
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(b2[j]);
+        v[2 * j] = f.x;
+        v[2 * j + 1] = f.y;
+      }
+    } else {
+      const float4* f4 = reinterpret_cast<const float4*>(x + src * ld_x + c);
+      const float4 a = f4[0], b = f4[1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    __align__(16) __nv_bfloat16 h[3][8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) split3_bf16(v[j], h[0][j], h[1][j], h[2][j]);
+    const int64_t o = (int64_t)r * ld_t + c;
+    *reinterpret_cast<uint4*>(t0 + o) = *reinterpret_cast<const uint4*>(h[0]);
+    if (n_terms > 1) *reinterpret_cast<uint4*>(t1 + o) = *reinterpret_cast<const uint4*>(h[1]);
+    if (n_terms > 2) *reinterpret_cast<uint4*>(t2 + o) = *reinterpret_cast<const uint4*>(h[2]);
+  }
+}
+
 __global__ void sum_f64_kernel(const double* __restrict__ x, int n, double* out) {
   __shared__ double sh[32];
   double s = 0.0;
@@ -192,6 +234,25 @@ extern "C" int gsq_gather_split(const void* x, int src_bf16, int64_t ld_x, const
   for (int i = 0; i < n_terms; ++i) {
     if (row_terms) t[i] = (__nv_bfloat16*)row_terms[i];
     if (col_terms) u[i] = (__nv_bfloat16*)col_terms[i];
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  bool vec = !col_terms && cols % 8 == 0 && ld_x % 8 == 0 && ld_t % 8 == 0 &&
+             ((uintptr_t)x & 15) == 0;
+  for (int i = 0; i < n_terms; ++i) vec = vec && ((uintptr_t)t[i] & 15) == 0;
+  if (vec) {
+    const int64_t n = (int64_t)rows * (cols / 8);
+    int64_t nb = (n + 255) / 256;
+    if (nb > 65535) nb = 65535;
+    if (src_bf16)
+      gather_rows_kernel<__nv_bfloat16><<<(unsigned)nb, 256, 0, st>>>(
+          (const __nv_bfloat16*)x, ld_x, seq, per_seq, seq_stride, offset, rows, cols, n_terms,
+          t[0], t[1], t[2], ld_t);
+    else
+      gather_rows_kernel<float><<<(unsigned)nb, 256, 0, st>>>(
+          (const float*)x, ld_x, seq, per_seq, seq_stride, offset, rows, cols, n_terms, t[0],
+          t[1], t[2], ld_t);
+    GSQ_CHECK_LAUNCH();
+    return GSQ_OK;
   }
   dim3 g((cols + 31) / 32, (rows + 31) / 32);
   if (src_bf16)

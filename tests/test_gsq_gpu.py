@@ -202,3 +202,34 @@ def test_qk_stage_exact_bf16_rows():
                       BlockOpts(steps=20), seed=3, exact_bf16_rows=exact)
         res.append(lin.logits.cpu().numpy())
     assert np.linalg.norm(res[0] - res[1]) / np.linalg.norm(res[0]) < 1e-4
+
+
+@pytest.mark.parametrize("src", ["bf16", "f32"])
+@pytest.mark.parametrize("n_terms", [1, 3])
+def test_gather_rows_vector_path_equals_tiled_path(src, n_terms):
+    """gsq_gather_split with row terms only (the 16-byte row kernel) writes the same bf16 terms
+    as the tiled kernel that also writes the transposed copy, and the terms are split3 of the
+    gathered rows (positions `offset ..` of the chosen sequences)."""
+    from gsq_rco_mlx_b200 import _lib
+    from gsq_rco_mlx_b200.gemm import Terms
+    T, N, H, per, off = 64, 5, 96, 40, 3
+    g = torch.Generator().manual_seed(n_terms + (src == "f32"))
+    x = torch.randn(N * T, H, generator=g) * 0.5
+    x = x.bfloat16() if src == "bf16" else x
+    xd = x.to(DEV)
+    seq = torch.tensor([4, 0, 2], dtype=torch.int32, device=DEV)
+    rows = 3 * per
+    A, B, BT = Terms(rows, H, n_terms, DEV), Terms(rows, H, n_terms, DEV), Terms(H, rows, n_terms, DEV)
+    st = _lib.stream_ptr()
+    args = (_lib.ptr(xd), int(src == "bf16"), H, _lib.ptr(seq), per, T, off, rows, H, n_terms)
+    _lib.call("gsq_gather_split", *args, A.ptrs(), A.ld, None, 0, st)
+    _lib.call("gsq_gather_split", *args, B.ptrs(), B.ld, BT.ptrs(), BT.ld, st)
+    torch.cuda.synchronize()
+    idx = torch.cat([s * T + off + torch.arange(per) for s in (4, 0, 2)])
+    want = x.float()[idx].double()
+    got = sum(A.t[i][:, :H].double().cpu() for i in range(n_terms))
+    for i in range(n_terms):
+        assert torch.equal(A.t[i][:, :H].cpu(), B.t[i][:, :H].cpu())
+        assert torch.equal(BT.t[i][:, :rows].cpu(), B.t[i][:, :H].cpu().T)
+    tol = 0.0 if (src == "bf16" or n_terms == 3) else 2.0 ** -8
+    assert float(((got - want).abs() / want.abs().clamp_min(1e-30)).max()) <= tol
