@@ -480,7 +480,7 @@ class VOStep(_StageBase):
       V     v^T = (hn Wv^T + bv)^T per sequence (keys)      bias epilogue, transposed terms
       PV    o = P v per (sequence, head)                    causal k-range when q0 = 0
       Y     r = o Wo^T - A_fp (0 at position 0)             residual-loss epilogue: dY = 2 r / n
-      Go    dL/dWo = dY^T o
+      Go    dL/dWo = dY^T o                                 dY, o read MN-major
       dO    dO^T = (dY Wo)^T per sequence
       dV    P^T dO per (sequence, head), summed over the heads of each kv head
       Gv    dL/dWv = dV^T hn
