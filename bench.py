@@ -344,7 +344,7 @@ def run_reference(args):
            "metric": "GSQ steps/s per block (Qwen2.5-0.5B block, 3-bit g64: one qk + vo + mlp Lion step)",
            "value": round(v, 5), "unit": "block steps/s", "n_gpus": world, "steps": len(per),
            "warmup": 0, "ms_per_step": round(1000 / v, 1), "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
            "config": {"workload": "config 2: one Qwen2.5-0.5B block, calib 128 x 2048, micro-batch 2, R=2"},
            "cpu_baseline": {"value": round(v, 5), "unit": "block steps/s", "cores": os.cpu_count(),
                             "kind": "port",
