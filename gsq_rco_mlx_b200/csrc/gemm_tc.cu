@@ -1054,9 +1054,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
           const int kx = (t.kb0 + kb) * BK;
           for (int i = 0; i < p.na; ++i) {
-            if (p.a_mn) {  // two 64 (M) x 64 (K) boxes of the [K][M] operand
-              tma_load_2d(st + i * kTileA, &p.tma_a[i], &full_bar[s], t.tile_m, kx);
-              tma_load_2d(st + i * kTileA + 8192, &p.tma_a[i], &full_bar[s], t.tile_m + 64, kx);
+            if (p.a_mn) {  // two 64 (M) x 64 (K) boxes of the [K][M] operand (batch rows at a_off)
+              const int ky = kx + (int)p.a_off.at(t.z);
+              tma_load_2d(st + i * kTileA, &p.tma_a[i], &full_bar[s], t.tile_m, ky);
+              tma_load_2d(st + i * kTileA + 8192, &p.tma_a[i], &full_bar[s], t.tile_m + 64, ky);
             } else {
               tma_load_2d(st + i * kTileA, &p.tma_a[i], &full_bar[s], kx, a_row);
             }
@@ -1460,8 +1461,11 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
       (bmn ? (d->ldb < N || d->b_rows < K) : d->ldb < K) ||
       (d->C && d->ldc < ((epi == 2 || epi == 5) ? N / 2 : N)))
     return GSQ_EINVAL;
-  // MN-major operands: one product (no batch offsets), B not paired with b2
-  if ((amn || bmn) && (d->batch != 1 || d->causal)) return GSQ_EINVAL;
+  // MN-major operands: B is one product (no batch offsets, no causal range) and not paired
+  // with b2; a batched or causal MN-major A moves its batch offsets along its K rows, so K is
+  // whole k-blocks there (no box reaches into the next batch's rows)
+  if (bmn && (d->batch != 1 || d->causal)) return GSQ_EINVAL;
+  if (amn && (d->batch != 1 || d->causal) && (K % tc::BK) != 0) return GSQ_EINVAL;
   if (bmn && (epi == 2 || epi == 5)) return GSQ_EINVAL;
   if (d->ncs > 0 && (d->ldcs & 7)) return GSQ_EINVAL;
   if (d->nct > 0 && (d->ldct & 7)) return GSQ_EINVAL;

@@ -482,7 +482,7 @@ class VOStep(_StageBase):
       Y     r = o Wo^T - A_fp (0 at position 0)             residual-loss epilogue: dY = 2 r / n
       Go    dL/dWo = dY^T o                                 dY, o read MN-major
       dO    dO^T = (dY Wo)^T per sequence
-      dV    P^T dO per (sequence, head), summed over the heads of each kv head
+      dV    P^T dO per (sequence, head), summed over the heads of each kv head (P MN-major)
       Gv    dL/dWv = dV^T hn
     """
 
@@ -503,7 +503,9 @@ class VOStep(_StageBase):
         self.k_rot = Terms(m * nkv * Tk, hd, 3, dev)
         self.scores = torch.empty(m * nh, Tq, Tk, device=dev, dtype=torch.float32)
         self.P = Terms(m * nh * Tq, Tk, 1, dev)
-        self.PT = Terms(m * nh * Tk, Tq, 1, dev)
+        # dV = P^T dO reads P as an MN-major operand when the query window is whole k-blocks;
+        # otherwise through a transposed copy
+        self.PT = None if Tq % 64 == 0 else Terms(m * nh * Tk, Tq, 1, dev)
         self.VT = Terms(m * nkv * hd, Tk, 3, dev)
         self.O = Terms(m * Tq, H, 3, dev)
         self.DY = Terms(m * Tq, H, 3, dev)
@@ -558,9 +560,11 @@ class VOStep(_StageBase):
                  c_off=(1, Tq * Tk, 0))
         _lib.call("gsq_softmax_causal_rows", _lib.ptr(self.scores), B, Tq, Tk, Tk, q0,
                   _lib.ptr(self.P.t[0]), self.P.ld, st)
-        # P^T feeds the causal dV GEMM when q0 = 0: the transposes of P's zero tiles are unread
-        _lib.call("gsq_transpose_bf16", _lib.ptr(self.P.t[0]), Tq, Tk, self.P.ld, Tq * self.P.ld,
-                  _lib.ptr(self.PT.t[0]), self.PT.ld, Tk * self.PT.ld, B, int(q0 == 0), st)
+        if self.PT is not None:
+            # P^T feeds the causal dV GEMM when q0 = 0: the transposes of P's zero tiles are unread
+            _lib.call("gsq_transpose_bf16", _lib.ptr(self.P.t[0]), Tq, Tk, self.P.ld,
+                      Tq * self.P.ld, _lib.ptr(self.PT.t[0]), self.PT.ld, Tk * self.PT.ld, B,
+                      int(q0 == 0), st)
 
     def contract(self):
         c, m = self.cfg, self.m
@@ -587,9 +591,14 @@ class VOStep(_StageBase):
                           _lib.ptr(self.DoT.t[i]), self.DoT.ld, 0, 1, 0, st)
             gemm(self.DY, self.DoT, M=Tq, batch=m, a_off=(1, Tq, 0), ct_terms=self.DOT,
                  t_off=(1, H, 0, 0, 0))
-            gemm(self.PT, self.DOT, M=Tk, N=hd, K=Tq, batch=B, bn=64,
-                 causal=2 if q0 == 0 else 0, a_off=(1, Tk, 0), b_off=(1, hd, 0), C=self.dv,
-                 ldc=hd, c_off=(1, Tk * hd, 0))
+            if self.PT is None:
+                gemm(self.P, self.DOT, M=Tk, N=hd, K=Tq, batch=B, bn=64,
+                     causal=2 if q0 == 0 else 0, a_off=(1, Tq, 0), b_off=(1, hd, 0), C=self.dv,
+                     ldc=hd, c_off=(1, Tk * hd, 0), a_major=1)
+            else:
+                gemm(self.PT, self.DOT, M=Tk, N=hd, K=Tq, batch=B, bn=64,
+                     causal=2 if q0 == 0 else 0, a_off=(1, Tk, 0), b_off=(1, hd, 0), C=self.dv,
+                     ldc=hd, c_off=(1, Tk * hd, 0))
             t = self.DVT.t
             _lib.call("gsq_head_group_sum_t", _lib.ptr(self.dv), m, nh, c.rep, Tk, _lib.ptr(t[0]),
                       _lib.ptr(t[1]), _lib.ptr(t[2]), self.DVT.ld, st)

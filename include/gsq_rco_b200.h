@@ -160,8 +160,9 @@ typedef struct {
   float *workspace;
   /* operand layout: 0 = K-major (A [M][lda], B [N][ldb], the reduction index contiguous);
    * 1 = MN-major (A stored [K][lda] with the M index contiguous, B [K][ldb] with N contiguous:
-   * a row-major activation used as its own transpose). MN-major needs batch 1 (no row offsets)
-   * and, for B, no SwiGLU pairing (b2). */
+   * a row-major activation used as its own transpose). An MN-major B needs batch 1, no causal
+   * range and no SwiGLU pairing (b2); an MN-major A may be batched (a_off then moves along its
+   * K rows) or causal when K is a multiple of 64. */
   int a_major, b_major;
 } gsq_gemm_desc;
 

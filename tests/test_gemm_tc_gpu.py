@@ -125,3 +125,33 @@ def test_mn_major_operands_equal_k_major(terms, majors, shape, bn):
     torch.cuda.synchronize()
     check_err(torch.device("cuda"))
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("causal", [0, 2])
+def test_mn_major_batched_a_equals_k_major(causal):
+    """A batched MN-major A (each batch's rows at a_off along K), with and without the causal
+    k-range, gives bit-for-bit the product of its K-major transposed copy: the vo stage's
+    dV = P^T dO reading P directly. K not a multiple of 64 is refused for a batched MN-major A."""
+    from gsq_rco_mlx_b200.gemm import Terms, gemm, check_err
+    B, T, hd = 3, 256, 64
+    g = torch.Generator(device="cuda").manual_seed(11 + causal)
+    P, PT = Terms(B * T, T, 1, "cuda"), Terms(B * T, T, 1, "cuda")
+    x = torch.randn(B, T, T, device="cuda", generator=g).bfloat16()
+    P.t[0][:, :T] = x.reshape(B * T, T)
+    PT.t[0][:, :T] = x.transpose(1, 2).reshape(B * T, T)
+    D = Terms(B * hd, T, 3, "cuda")
+    for i in range(3):
+        D.t[i][:, :T] = (torch.randn(B * hd, T, device="cuda", generator=g)
+                         * 2.0 ** (-8 * i)).bfloat16()
+    ref = torch.empty(B, T, hd, device="cuda")
+    out = torch.empty(B, T, hd, device="cuda")
+    kw = dict(M=T, N=hd, K=T, batch=B, bn=64, causal=causal, a_off=(1, T, 0),
+              b_off=(1, hd, 0), ldc=hd, c_off=(1, T * hd, 0))
+    gemm(PT, D, C=ref, **kw)
+    gemm(P, D, C=out, a_major=1, **kw)
+    torch.cuda.synchronize()
+    check_err(torch.device("cuda"))
+    assert torch.equal(out, ref)
+    kw["K"] = T - 32
+    with pytest.raises(ValueError):
+        gemm(P, D, C=out, a_major=1, **kw)
