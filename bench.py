@@ -304,33 +304,54 @@ def run_block(args):
 
 
 def cpu_baseline_block():
-    """The CPU restatement (oracle port) of one mlp-stage step of the block, the dominant stage,
-    on this host's cores, at the configuration's micro-batch (2 x 2047 rows)."""
+    """The CPU restatement (oracle port) of one block step — one Lion step each of the qk stage
+    (q_proj, k_proj on the normed rows), the vo stage (v_proj, o_proj through the hard
+    attention probabilities) and the mlp stage (gate, up, down) — at the configuration's
+    micro-batch (2 sequences x 2048 positions, R = 2), on this host's cores."""
     import torch
     from oracle import block as ob
     from oracle import gptq as og
     from oracle import gsq as ogsq
     torch.set_num_threads(os.cpu_count())
     rng = np.random.default_rng(0)
-    M = 2 * (T_SEQ - 1)
-    mn = torch.as_tensor(rng.standard_normal((M, HID)).astype(np.float32)).bfloat16().float()
-    h1 = torch.as_tensor(0.02 * rng.standard_normal((M, HID)).astype(np.float32)).bfloat16().float()
-    Y = torch.as_tensor(0.02 * rng.standard_normal((M, HID)).astype(np.float32)).bfloat16().float()
-    states = []
-    for i, (o, n) in enumerate(((INTER, HID), (INTER, HID), (HID, INTER))):
-        Wl = (0.02 * rng.standard_normal((o, n))).astype(np.float32)
-        r = og.quantize_rtn(Wl, 3, 64)
-        states.append(ogsq.LinearState(3, r["codes"], r["scales"].astype(np.float16), 64, seed=i,
-                                       linear_id=i))
+    T, M = T_SEQ, 2 * (T_SEQ - 1)
+
+    def rows(shape, scale=1.0):  # exactly-bf16 float32 activations
+        x = scale * rng.standard_normal(shape).astype(np.float32)
+        return torch.as_tensor(x).bfloat16().float()
+
+    def linear(out_f, in_f, i):
+        W = (0.02 * rng.standard_normal((out_f, in_f))).astype(np.float32)
+        r = og.quantize_rtn(W, 3, 64)
+        return W, ogsq.LinearState(3, r["codes"], r["scales"].astype(np.float16), 64, seed=i,
+                                   linear_id=i)
+
+    qk = [linear(NH * HD, HID, 0), linear(NKV * HD, HID, 1)]
+    hn_rows = rows((M, HID)).numpy()
+    vo = [linear(NKV * HD, HID, 2)[1], linear(HID, NH * HD, 3)[1]]
+    hn_seqs = [rows((T, HID)) for _ in range(2)]
+    A_seqs = [rows((T, HID), 0.02) for _ in range(2)]
+    bv = rows((NKV * HD,), 0.02)
+    scores = 4.0 * torch.randn(NH, T, T, generator=torch.Generator().manual_seed(0))
+    scores = scores.masked_fill(torch.triu(torch.ones(T, T, dtype=torch.bool), 1), -torch.inf)
+    P = torch.softmax(scores, dim=-1).bfloat16().float()
+    del scores
+    mlp = [linear(INTER, HID, 4)[1], linear(INTER, HID, 5)[1], linear(HID, INTER, 6)[1]]
+    mn, h1, Y = rows((T, HID)), rows((T, HID), 0.02), rows((T, HID), 0.02)
     t0 = time.perf_counter()
-    ob.train_mlp(states, [mn, mn], [h1, h1], [Y, Y], 1, micro_batch=1)
+    tau, kappa = ogsq.gs_schedules(0, 200)
+    for W, st in qk:
+        noises = [st.noise(0, 0, r) for r in range(2)]
+        _, glog, gs, _ = ogsq.linear_loss_and_grads(hn_rows, W, st.logits, st.Ckd, st.scales,
+                                                    noises, 64, tau, kappa)
+        ogsq.lion_step(st, glog, gs)
+    ob.train_vo(vo, hn_seqs, A_seqs, lambda t, idx: [P, P], bv, 1, NH, NKV, micro_batch=2)
+    ob.train_mlp(mlp, [mn, mn], [h1, h1], [Y, Y], 1, micro_batch=2)
     dt = time.perf_counter() - t0
-    # a block step = qk + vo + mlp steps; the mlp step is 85-88 % of it (reference run logs),
-    # so the block-step rate is bounded above by the mlp-step rate
-    return {"value": round(1.0 / dt, 5), "unit": "block steps/s (mlp step only, upper bound)",
+    return {"value": round(1.0 / dt, 5), "unit": "block steps/s",
             "cores": os.cpu_count(), "kind": "port",
-            "sample": "1 mlp-stage step at micro-batch 2 x 2047 rows, R=2 (numpy/torch-CPU float64 "
-                      "restatement; the MLX path is unavailable)"}
+            "sample": "1 block step (qk + vo + mlp Lion steps) at micro-batch 2 x 2048, R=2 "
+                      "(numpy/torch-CPU float64 restatement; the MLX path is unavailable)"}
 
 
 def run_reference(args):
@@ -348,7 +369,7 @@ def run_reference(args):
            "config": {"workload": "config 2: one Qwen2.5-0.5B block, calib 128 x 2048, micro-batch 2, R=2"},
            "cpu_baseline": {"value": round(v, 5), "unit": "block steps/s", "cores": os.cpu_count(),
                             "kind": "port",
-                            "sample": "mlp-stage steps only (upper bound of the block-step rate); "
+                            "sample": "1 block step (qk + vo + mlp Lion steps) per timed step; "
                                       "the reference's MLX path is unavailable, this is the "
                                       "CPU restatement"},
            "e2e": {"value": round(v, 5), "unit": "block steps/s", "h2d_bytes_per_step": 0,
