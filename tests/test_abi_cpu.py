@@ -121,3 +121,28 @@ def test_gemm_descriptor_layout_matches_header(tmp_path):
     vals = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
     assert vals[0] == ctypes.sizeof(GemmDesc)
     assert vals[1:] == [getattr(GemmDesc, n).offset for n in names]
+
+
+def declared_arities():
+    """{name: number of parameters} of every prototype in include/*.h."""
+    out = {}
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if not fn.endswith(".h"):
+            continue
+        text = open(os.path.join(ROOT, "include", fn)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"^(?:int|const char \*)\s*(\w+)\(([^;]*?)\)\s*;", text,
+                             flags=re.M | re.S):
+            params = " ".join(m.group(2).split())
+            out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_signatures_match_header_arity():
+    """Every ctypes binding in _lib.SIGNATURES has as many arguments as the header's
+    prototype, so the Python side cannot drift from the C ABI silently."""
+    arity = declared_arities()
+    assert len(arity) >= 14
+    for name, argtypes in _lib.SIGNATURES.items():
+        assert name in arity, name
+        assert len(argtypes) == arity[name], (name, len(argtypes), arity[name])
