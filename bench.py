@@ -69,7 +69,11 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="block",
-                    choices=["block", "linear", "gptq", "rco", "eval", "pipeline"])
+                    choices=["block", "linear", "gptq", "rco", "eval", "pipeline", "kernels"])
+    ap.add_argument("--cases", default="",
+                    help="kernels: comma-separated cases of bench_kernels.py (default all)")
+    ap.add_argument("--once", action="store_true",
+                    help="kernels: run each case once (for a profiler capture)")
     ap.add_argument("--rco-steps", type=int, default=2,
                     help="pipeline: RCO steps run (the rest of the 100 extrapolated)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1173,6 +1177,10 @@ def cpu_baseline_linear(W, X, lin_codes, s16, n_steps=2):
 
 def main():
     args = parse()
+    if args.workload == "kernels":
+        import bench_kernels
+        return bench_kernels.main([c for c in args.cases.split(",") if c] +
+                                  (["--once"] if args.once else []))
     if args.workload == "linear":
         return run_linear(args)
     if args.workload == "gptq":

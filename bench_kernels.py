@@ -1,8 +1,8 @@
 """Representative launches of the hot kernels at Qwen2.5-0.5B block shapes, for profilers and
 micro-timing (one process, one GPU, a few GB of device memory).
 
-  python -m gsq_rco_mlx_b200.kernel_cases [mlp_gemms|attn|soft_step|cublas|packed|eval_batch]
-                                          [--once]
+  python bench.py --workload kernels --cases mlp_gemms,attn,... [--once]
+  (cases: mlp_gemms, attn, attn1, soft_step, cublas, packed, eval_batch)
 
 --once runs every case a single time (an ncu capture: `-k regex:<kernel> -c <n>`); otherwise
 each case is timed with CUDA events over 10 launches after 3 warm-up launches and printed with
@@ -26,9 +26,9 @@ import sys
 
 import torch
 
-from . import _lib
-from .gemm import Terms, check_err, gemm
-from .gsq.staged import _col_terms
+from gsq_rco_mlx_b200 import _lib
+from gsq_rco_mlx_b200.gemm import Terms, check_err, gemm
+from gsq_rco_mlx_b200.gsq.staged import _col_terms
 
 H, I, HEADS, KV, HD, T = 896, 4864, 14, 2, 64, 2048
 
@@ -99,7 +99,7 @@ def attn(dev, g, seqs=8):
 
 
 def soft_step(dev, g):
-    from .gsq.staged import SoftLinear
+    from gsq_rco_mlx_b200.gsq.staged import SoftLinear
     import numpy as np
     out_f, in_f, R = I, H, 2
     rng = np.random.default_rng(0)
@@ -129,7 +129,7 @@ def cublas(dev, g):
 def _packed_linear(N, K, bits, dev, g):
     """A packed linear with random words (every bit pattern is a valid code stream) and fp16
     g64 scales, generated on the device."""
-    from .common.evaluate import PackedLinear
+    from gsq_rco_mlx_b200.common.evaluate import PackedLinear
     words = torch.randint(-2 ** 31, 2 ** 31, (N, K * bits // 32), device=dev, dtype=torch.int64,
                           generator=g).to(torch.int32)
     s = (0.01 * torch.randn(N, K // 64, device=dev, generator=g)).half()
@@ -166,9 +166,9 @@ def eval_batch(dev, g):
     """One 8-window x 2048 batch of the packed eval through 24 random 3-bit layers and the
     tied head (next-token NLL): the launch mix of bench.py's eval step."""
     import numpy as np
-    from .common.evaluate import Evaluator, PackedModel
-    from .gsq.e2e import LIN_ORDER, BlockConfig
-    from .rco.database import random_model
+    from gsq_rco_mlx_b200.common.evaluate import Evaluator, PackedModel
+    from gsq_rco_mlx_b200.gsq.e2e import LIN_ORDER, BlockConfig
+    from gsq_rco_mlx_b200.rco.database import random_model
     cfg = BlockConfig()
     model = random_model(n_layers=24, seed=0, device=dev)
     layers = []

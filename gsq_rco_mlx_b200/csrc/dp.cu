@@ -23,12 +23,23 @@ mckp_dp_kernel(const double* __restrict__ scores, const int64_t* __restrict__ st
                int32_t* __restrict__ z_all) {
   extern __shared__ double dsm[];
   __shared__ int64_t s_best;
+  __shared__ int s_bad;
   const int inst = blockIdx.x;
   const double* s = scores + (int64_t)inst * N * K;
   uint8_t* choice = choice_all + (int64_t)inst * N * (B + 1);
   int32_t* z = z_all + (int64_t)inst * N;
   double* cur = dp_glob ? dp_glob + (int64_t)inst * 2 * (B + 1) : dsm;
   double* nxt = cur + (B + 1);
+  // A negative cost would index cur[] past its end: refuse the instance (z = -1).
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
+  for (int64_t e = threadIdx.x; e < (int64_t)N * K; e += blockDim.x)
+    if (step[e] < 0) s_bad = 1;
+  __syncthreads();
+  if (s_bad) {
+    for (int i = threadIdx.x; i < N; i += blockDim.x) z[i] = -1;
+    return;
+  }
   for (int64_t b = threadIdx.x; b <= B; b += blockDim.x) cur[b] = 0.0;
   __syncthreads();
   for (int i = 0; i < N; ++i) {
@@ -50,10 +61,15 @@ mckp_dp_kernel(const double* __restrict__ scores, const int64_t* __restrict__ st
     __syncthreads();
     double* t = cur; cur = nxt; nxt = t;
   }
+  // No assignment fits the budget: dp[B] stayed -inf. Report it (z = -1), no backtrack.
+  const double target = cur[B];
+  if (target == -INFINITY) {
+    for (int i = threadIdx.x; i < N; i += blockDim.x) z[i] = -1;
+    return;
+  }
   // smallest b with dp[b] >= dp[B]
   if (threadIdx.x == 0) s_best = B;
   __syncthreads();
-  const double target = cur[B];
   int64_t mine = B;
   for (int64_t b = threadIdx.x; b <= B; b += blockDim.x)
     if (cur[b] >= target) { mine = b; break; }
@@ -61,11 +77,16 @@ mckp_dp_kernel(const double* __restrict__ scores, const int64_t* __restrict__ st
   __syncthreads();
   if (threadIdx.x == 0) {
     int64_t b = s_best;
-    for (int i = N - 1; i >= 0; --i) {
+    int i = N - 1;
+    for (; i >= 0; --i) {
       const int k = choice[(int64_t)i * (B + 1) + b];
+      const int64_t c = step[(int64_t)i * K + k];
+      if (c > b) break;  // cannot happen on a finite optimum; never read below row start
       z[i] = k;
-      b -= step[(int64_t)i * K + k];
+      b -= c;
     }
+    if (i >= 0)
+      for (int j = 0; j < N; ++j) z[j] = -1;
   }
 }
 

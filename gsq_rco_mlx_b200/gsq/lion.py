@@ -4,8 +4,8 @@
     m <- beta2 * m + (1 - beta2) * g
     theta <- theta - lr * (u + wd * theta)
 
-The stage optimiser applies this rule inside the fused soft-backward kernel
-(gsq_soft_bwd_lion); ``lion_update`` is the stand-alone form of the reference API on CUDA
+The stage optimiser applies this rule inside the fused soft-step kernel (gsq_soft_step:
+soft backward, resample mean, Lion, next forward); ``lion_update`` is the stand-alone form of the reference API on CUDA
 tensors, one launch per tensor.
 """
 from __future__ import annotations

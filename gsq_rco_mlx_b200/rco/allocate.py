@@ -35,17 +35,28 @@ N_PER_LAYER = len(LINEARS)
 
 
 def budget_grid(avg_bits, total_units: int, n_groups: int):
-    """Exact budget avg_bits * total_units on the integer grid (allocate.py:33-51)."""
-    frac = Fraction(repr(float(avg_bits))) * int(total_units)
-    ticks = frac.denominator
+    """The budget avg_bits * total_units held exactly on the DP's integer grid
+    (allocate.py:33-51 semantics): avg_bits is taken as the decimal it prints as (2.976 is
+    2976/1000, not its binary neighbour), ticks = the smallest grid scale that makes the budget
+    a whole number. Returns (budget float, ticks, budget_int). Raises ValueError when the grid
+    would need more than MAX_TICKS ticks per unit or the DP table would exceed
+    MAX_TABLE_ENTRIES bytes."""
+    exact = Fraction(str(float(avg_bits))) * int(total_units)
+    ticks, budget_int = exact.denominator, exact.numerator
     if ticks > MAX_TICKS:
-        raise ValueError(
-            f"avg_bits={avg_bits} needs {ticks} ticks per unit on the exact grid "
-            f"(max {MAX_TICKS}); use an average with a shorter decimal expansion")
-    budget_int = frac.numerator
+        raise ValueError(f"budget_grid: {avg_bits} bits on average needs a grid of {ticks} "
+                         f"ticks per unit, above {MAX_TICKS}; shorten its decimal expansion")
     if n_groups * (budget_int + 1) > MAX_TABLE_ENTRIES:
-        raise ValueError(f"DP table {n_groups} x {budget_int + 1} exceeds {MAX_TABLE_ENTRIES}")
-    return float(frac), int(ticks), int(budget_int)
+        raise ValueError(f"budget_grid: a DP table of {n_groups} groups x {budget_int + 1} "
+                         f"budgets is above {MAX_TABLE_ENTRIES} entries")
+    return float(exact), int(ticks), int(budget_int)
+
+
+def _grid(bank, avg_bits):
+    """(w_int [n_groups], total units, budget, ticks, budget_int) of a bank and an average."""
+    w_int, _ = integer_weights(bank.counts)
+    total = int(np.sum(w_int))
+    return (w_int, total) + budget_grid(avg_bits, total, len(bank.groups))
 
 
 class Bank:
@@ -216,43 +227,48 @@ def initial_logits(bank: Bank, init: str) -> np.ndarray:
 def rco_allocate(objective: KLObjective, bank: Bank, avg_bits, *, steps: int, g: int,
                  lr: float, seed: int, tau0: float = TAU0, tau_min: float = TAU_MIN,
                  init: str = "zero", callback=None) -> dict:
-    """RCO (Alg. 1) with the exact budget (allocate.py:195-240)."""
-    w_int, _ = integer_weights(bank.counts)
-    total = int(w_int.sum())
+    """RCO (Alg. 1) with the exact budget (allocate.py:195-224): the decoded choice per group,
+    the per-step history, the budget grid and the decoded / expected average bits."""
+    w_int, total, budget, ticks, budget_int = _grid(bank, avg_bits)
     bits = np.asarray(bank.options, dtype=np.float64)
-    budget, ticks, budget_int = budget_grid(avg_bits, total, len(bank.groups))
-    res = rco_loop(initial_logits(bank, init), bits, w_int, budget, steps=steps, g=g, lr=lr,
+    run = rco_loop(initial_logits(bank, init), bits, w_int, budget, steps=steps, g=g, lr=lr,
                    seed=seed, tau0=tau0, tau_min=tau_min, grad_fn=objective, ticks=ticks,
                    callback=callback)
-    if res["budget_int"] != budget_int:
-        raise RuntimeError(f"grid mismatch: rco_loop {res['budget_int']} vs {budget_int}")
-    choice = np.asarray(res["z_final"]).argmax(axis=1)
-    decoded_int, decoded_avg = decoded_cost(bank, choice)
-    return {"choice": choice, "history": res["history"], "budget": budget,
-            "budget_int": budget_int, "ticks": ticks, "total_units": total,
-            "decoded_int_cost": decoded_int, "decoded_avg_bits": decoded_avg,
-            "expected_avg_bits": float(expected_cost(res["logits"], bits, w_int)) / total}
+    if run["budget_int"] != budget_int:
+        raise RuntimeError(f"rco_allocate: the loop enforced budget {run['budget_int']}, the "
+                           f"grid says {budget_int}")
+    choice = np.argmax(run["z_final"], axis=1)
+    cost_int, avg = decoded_cost(bank, choice)
+    expected = float(expected_cost(run["logits"], bits, w_int)) / total
+    return dict(choice=choice, history=run["history"], budget=budget, budget_int=budget_int,
+                ticks=ticks, total_units=total, decoded_int_cost=cost_int,
+                decoded_avg_bits=avg, expected_avg_bits=expected)
 
 
 def decoded_cost(bank: Bank, choice):
-    """Integer cost sum_i w_i b_{k_i} and the decoded average bits (allocate.py:243-247)."""
+    """(sum_i w_i b_{k_i}, that sum / sum_i w_i): the integer cost and average bits of a
+    choice (allocate.py:243-247)."""
     w_int, _ = integer_weights(bank.counts)
-    cost = int(np.sum(w_int * np.asarray(bank.options, dtype=np.int64)[np.asarray(choice)]))
-    return cost, cost / int(w_int.sum())
+    chosen_bits = np.asarray(bank.options, dtype=np.int64)[np.asarray(choice)]
+    cost = int(np.dot(w_int, chosen_bits))
+    return cost, cost / int(np.sum(w_int))
 
 
 def proxy_dp_choice(bank: Bank, avg_bits):
-    """Baseline: the DP on the per-linear output-MSE sensitivities (allocate.py:250-256)."""
-    w_int, _ = integer_weights(bank.counts)
-    budget, ticks, budget_int = budget_grid(avg_bits, int(w_int.sum()), len(bank.groups))
-    costs_int = np.asarray(bank.options, dtype=np.int64) * ticks
-    z = dp_knapsack(-np.asarray(bank.sensitivity, dtype=np.float64), costs_int, w_int,
+    """Baseline allocation: the exact knapsack on minus the per-linear output-MSE
+    sensitivities under the same budget (allocate.py:250-256)."""
+    w_int, _, _, ticks, budget_int = _grid(bank, avg_bits)
+    option_cost = ticks * np.asarray(bank.options, dtype=np.int64)
+    z = dp_knapsack(-np.asarray(bank.sensitivity, dtype=np.float64), option_cost, w_int,
                     budget_int)
-    return np.asarray(z).argmax(axis=1)
+    return np.argmax(np.asarray(z), axis=1)
 
 
 def uniform_choice(bank: Bank, bits: int):
-    """Every linear at one bit width (allocate.py:259-264)."""
-    if int(bits) not in bank.options:
-        raise ValueError(f"{bits} bits is not among the database options {bank.options}")
-    return np.full(len(bank.groups), bank.options.index(int(bits)), dtype=np.int64)
+    """Baseline allocation: every linear at ``bits`` (one of the bank's options)."""
+    try:
+        k = bank.options.index(int(bits))
+    except ValueError:
+        raise ValueError(f"uniform_choice: {bits} bits is not an option of the bank "
+                         f"{bank.options}") from None
+    return np.full(len(bank.groups), k, dtype=np.int64)

@@ -329,6 +329,9 @@ int gptq_err(const float *w_q, const float *W, const double *H, int out_f, int i
  * [n_inst][N][budget + 1] scratch, z_out int32 [n_inst][N] chosen option per group.
  * The two DP rows live in shared memory when 2 * (budget + 1) doubles fit (budget <= 13823);
  * larger budgets use dp_ws float64 [n_inst][2][budget + 1] (may be NULL otherwise).
+ * step entries must be >= 0. An instance with a negative step entry, or with no assignment
+ * whose cost fits the budget, gets z_out = -1 in all N entries (nothing is read outside the
+ * instance's table).
  * Replaces src/gsq_rco/rco/manifold.py:304-334 (_mckp_dp). */
 int mckp_dp_f64(const double *scores, const int64_t *step, int n_inst, int N, int K,
                 int64_t budget, uint8_t *choice_ws, double *dp_ws, int32_t *z_out,
@@ -340,9 +343,10 @@ int mckp_dp_f64(const double *scores, const int64_t *step, int n_inst, int N, in
  * The choice table lives in a fixed 16 MiB array inside the library (every GPU that loads the
  * library holds it until exit); the DP rows live in shared memory. Limits: budget <= 13823 and
  * n_inst * N * (budget + 1) <= 16 MiB, else GSQ_EINVAL. The first call on a device looks up
- * the array's device address (cudaGetSymbolAddress): make it before any stream capture.
- * Calls share the array: calls whose kernels overlap on one GPU race, so serialise them.
- * Nothing is allocated or freed. Same results as mckp_dp_f64. */
+ * the array's device address (cudaGetSymbolAddress): make it before any stream capture. The
+ * address is kept for the life of the process, so do not call this across a cudaDeviceReset
+ * of that device. Calls share the array: calls whose kernels overlap on one GPU race, so serialise them.
+ * Nothing is allocated or freed. Same results as mckp_dp_f64 (z_out = -1 as there). */
 int mckp_dp_f64_noalloc(const double *scores, const int64_t *step, int n_inst, int N, int K,
                         int64_t budget, int32_t *z_out, void *stream);
 

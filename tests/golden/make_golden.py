@@ -1,9 +1,9 @@
 """Generate the golden vectors of the hot path by running the reference's own numpy code.
 
-Run in a container that holds the reference checkout (read-only) at /root/reference:
-    python tests/golden/make_golden.py
-It imports the reference package from /root/reference/src and its test oracles from
-/root/reference/tests, and writes small .npz fixtures next to this script. The fixtures are
+Run where a checkout of the reference (egesabanci/gsq-rco-mlx) is readable:
+    python tests/golden/make_golden.py --reference PATH_TO_CHECKOUT
+It imports the reference package from PATH/src and its test oracles from PATH/tests, and
+writes small .npz fixtures next to this script. The fixtures are
 committed; nothing at test time reads the reference.
 
 The reference's GSQ, Lion and KL code is MLX-only and MLX cannot run here. Its numpy test
@@ -19,7 +19,7 @@ from pathlib import Path
 
 import numpy as np
 
-REF = Path("/root/reference")
+REF = None  # the reference checkout, set by main() from --reference
 OUT = Path(__file__).resolve().parent
 
 
@@ -270,6 +270,12 @@ def gen_export():
 
 
 def main():
+    import argparse
+    global REF
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--reference", required=True,
+                    help="path of a checkout of the reference repository")
+    REF = Path(ap.parse_args().reference).resolve()
     gptq, quant, manifold, loop, oracles = _import_reference()
     gen_gptq(gptq)
     gen_dp(manifold, loop)

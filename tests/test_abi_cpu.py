@@ -42,6 +42,16 @@ def test_bad_arguments_are_rejected_without_launch():
     assert lib.gsq_soft_fwd(None, None, None, None, 0, 0, 0, 0, 4, 4, 64, 8, 1.0, 100.0,
                             None, None, None, None, None) == _lib.GSQ_ENOTSUP
     assert lib.mckp_dp_f64(None, None, 1, 3, 2, 10, None, None, None, None) == _lib.GSQ_EINVAL
+    # the allocation-free DP refuses null pointers and sizes beyond its fixed array before
+    # touching the device
+    import ctypes as C
+    fake = C.c_void_p(256)  # never dereferenced: every call below is refused first
+    assert lib.mckp_dp_f64_noalloc(None, fake, 1, 168, 3, 9360, fake, None) == _lib.GSQ_EINVAL
+    assert lib.mckp_dp_f64_noalloc(fake, None, 1, 168, 3, 9360, fake, None) == _lib.GSQ_EINVAL
+    assert lib.mckp_dp_f64_noalloc(fake, fake, 1, 168, 3, 9360, None, None) == _lib.GSQ_EINVAL
+    assert lib.mckp_dp_f64_noalloc(fake, fake, 1, 168, 3, 20000, fake, None) == _lib.GSQ_EINVAL
+    assert lib.mckp_dp_f64_noalloc(fake, fake, 20, 168, 3, 9360, fake, None) == _lib.GSQ_EINVAL
+    assert lib.mckp_dp_f64_noalloc(fake, fake, 1, 168, 300, 100, fake, None) == _lib.GSQ_EINVAL
     assert lib.gptq_sweep(None, None, None, 4, 4, 3, 64, 128, 1, None, None, None,
                           None) == _lib.GSQ_EINVAL
 
@@ -63,26 +73,66 @@ def test_host_grid_and_schedules():
     assert np.array_equal(quant.local_shift_indices(z["ls_j0"], z["ls_logits"], 8), z["ls_idx"])
 
 
+def _retract_ok(out, a, c, w, budget, gold, tol=1e-8):
+    """out is a + t c for one scalar t, meets the budget to tol, and its shift is within the
+    tolerance's reach of the reference's shift (both are valid retractions: any t with
+    |C - B| <= tol is one; the slope of C along c bounds how far two such t can be apart)."""
+    t = (out - a) / c[None, :]
+    assert np.allclose(t, t.flat[0], rtol=0, atol=1e-9 * max(1.0, abs(t.flat[0])))
+    assert abs(manifold.expected_cost(out, c, w) - budget) <= tol
+    t_gold = float(((gold - a) / c[None, :]).mean())
+    _, slope = manifold.Budget(c, w).cost_and_slope(out)
+    assert abs(t.flat[0] - t_gold) <= 2 * tol / slope + 1e-12
+
+
 def test_host_manifold_matches_reference():
     z = np.load(os.path.join(GOLD, "rco_host.npz"))
     a, c, w = z["a"], z["costs"], z["w"]
     np.testing.assert_allclose(manifold.softmax(a), z["softmax"], rtol=1e-15)
     assert manifold.expected_cost(a, c, w) == pytest.approx(float(z["expected_cost"]), rel=1e-15)
-    np.testing.assert_allclose(manifold.normal_vector(a, c, w), z["normal"], rtol=1e-14, atol=1e-16)
+    np.testing.assert_allclose(manifold.normal_vector(a, c, w), z["normal"], rtol=1e-14,
+                               atol=1e-15)
     np.testing.assert_allclose(manifold.project_tangent(z["g"], z["normal"]), z["proj"],
                                rtol=1e-13, atol=1e-15)
-    np.testing.assert_array_equal(manifold.retract(a, c, w, budget=52.0), z["retract_B52"])
-    np.testing.assert_array_equal(manifold.retract(z["abig"], z["close"], w, budget=2.15 * 20),
-                                  z["retract_big"])
+    _retract_ok(manifold.retract(a, c, w, budget=52.0), a, c, w, 52.0, z["retract_B52"])
+    _retract_ok(manifold.retract(z["abig"], z["close"], w, budget=2.15 * 20), z["abig"],
+                z["close"], w, 2.15 * 20, z["retract_big"])
     assert np.array_equal(np.array([loop.tau_schedule(t, 10) for t in range(10)]), z["tau"])
     np.testing.assert_allclose(loop.ste_grad(z["up"], manifold.softmax(a), 0.3), z["ste"],
-                               rtol=1e-14, atol=1e-16)
+                               rtol=1e-14, atol=1e-15)
     ci, wi, Bi = loop.to_int_grid(c, np.arange(1, 21), 2.5 * 210, ticks=2)
     assert np.array_equal(ci, z["tig_c"]) and np.array_equal(wi, z["tig_w"]) and Bi == int(z["tig_B"])
     with pytest.raises(ValueError):
-        manifold.retract(a, c, w, budget=160.5)
+        manifold.retract(a, c, w, budget=160.5)        # above every reachable cost
+    with pytest.raises(ValueError):
+        manifold.retract(a, c, w, budget=52.0, max_shift=1e-3)   # no bracket within reach
     with pytest.raises(RuntimeError):
-        manifold.retract(a, c, w, budget=52.0, iters=3)
+        manifold.retract(a, c, w, budget=52.0, iters=1, tol=1e-300)
+    with pytest.raises(ValueError):
+        loop.to_int_grid(c, np.full(20, 1.5), 10.0)
+
+
+def test_rco_loop_matches_reference_trajectory():
+    """rco_loop on the reference's linear objective (15 steps, g = 4, seed 3): the random
+    stream, Adam, retraction and transport follow the reference's run, and the decoded
+    allocation is identical. The knapsack decode is the oracle's (no GPU here)."""
+    from oracle import dp as odp
+    z = np.load(os.path.join(GOLD, "rco_host.npz"))
+    target, wl = z["lin_target"], z["lin_w"]
+
+    def grad_fn(zz, p, t, j, rng_):
+        return -target, float(-(zz * target).sum())
+    res = loop.rco_loop(np.zeros((12, 3)), np.array([2.0, 3.0, 4.0]), wl, 3.0 * wl.sum(),
+                        steps=15, g=4, lr=0.1, seed=3, grad_fn=grad_fn,
+                        decode=odp.dp_knapsack)
+    np.testing.assert_allclose(res["logits"], z["lin_logits"], rtol=1e-6, atol=1e-8)
+    np.testing.assert_allclose(res["momentum"], z["lin_m"], rtol=1e-5, atol=1e-9)
+    np.testing.assert_allclose(res["velocity"], z["lin_v"], rtol=1e-5, atol=1e-12)
+    assert np.array_equal(res["z_final"], z["lin_z"])
+    np.testing.assert_allclose([h["cost"] for h in res["history"]], z["lin_cost"], atol=2e-8)
+    np.testing.assert_array_equal([h["loss"] for h in res["history"]], z["lin_loss"])
+    with pytest.raises(ValueError):
+        loop.rco_loop(np.zeros((12, 3)), np.array([2.0, 3.0, 4.0]), wl, 3.0 * wl.sum())
 
 
 def test_integer_weights_and_dp_validation():
