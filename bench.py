@@ -77,6 +77,8 @@ def parse():
     ap.add_argument("--rco-steps", type=int, default=2,
                     help="pipeline: RCO steps run (the rest of the 100 extrapolated)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="block: skip the GPTQ s/model and RCO s/step fields")
     ap.add_argument("--e2e-steps", type=int, default=200)
     return ap.parse_args()
 
@@ -182,6 +184,14 @@ def embed(E_dev, ids, dev):
     return h
 
 
+# DRAM bytes (read + write) per gemm_tc_kernel launch, mean over the six GEMMs of one mlp-stage
+# resample, from the ncu capture summarised in profiles/gemm_tc_mlp_stage.md
+GEMM_TRAFFIC_PER_LAUNCH = int(round((60 + 227 + 297 + 18 + 161 + 11 + 335 + 219 + 246 + 14 +
+                                     246 + 13) / 6 * 1e6))
+GEMM_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum, mean per launch over "
+                       "the six GEMMs of one mlp-stage resample (profiles/gemm_tc_mlp_stage.md)")
+
+
 def gemm_flops_of_mlp_stage(M):
     """Algorithmic (float32-equivalent) FLOPs of one mlp-stage resample: 5 GEMMs."""
     return 2 * M * (2 * INTER) * HID + 2 * M * HID * INTER * 4
@@ -236,15 +246,29 @@ def run_block(args):
     ms = {s: max_over_ranks(timer.ms[s]) for s in ("qk", "vo", "mlp")}
     ms_step = ms["qk"] + ms["vo"] + ms["mlp"]
 
-    # roofline of the dominant kernel (the tensor-core GEMM): per-launch events over a short
-    # mlp-stage run, algorithmic float32-equivalent FLOPs of each launch
-    with LaunchLog() as log:
-        quantize_block(h, W, bits, BlockOpts(steps=3), layer=0, cfg=cfg, T=T_SEQ, log=quiet,
-                       dp=dp)
-    rows = log.summary()
-    fl = sum(2.0 * M * N * K * b for (M, N, K, p, b, t) in rows)
-    fl_exec = sum(2.0 * M * N * K * b * p for (M, N, K, p, b, t) in rows)
-    t_ms = sum(t for (*_, t) in rows)
+    # roofline of the dominant kernel (the tensor-core GEMM): CUDA events around every GEMM
+    # launch of 3 timed steps per stage (the log is active only inside the timed window), with
+    # the algorithmic float32-equivalent FLOPs 2 M N K of each launch
+    rl_log = LaunchLog()
+    rl_steps = 3
+    quantize_block(h, W, bits, BlockOpts(steps=args.warmup + rl_steps), layer=0, cfg=cfg,
+                   T=T_SEQ, log=quiet, dp=dp, timer=StageTimer(args.warmup, launch_log=rl_log))
+    by_stage = rl_log.by_tag()
+    stage_gemm = {}
+    fl = fl_exec = t_ms = 0.0
+    for stage in ("qk", "vo", "mlp"):
+        rows = by_stage.get(stage, [])
+        f = sum(2.0 * M * N * K * b for (M, N, K, p, b, t) in rows)
+        fe = sum(2.0 * M * N * K * b * p for (M, N, K, p, b, t) in rows)
+        tt = max_over_ranks(sum(t for (*_, t) in rows))
+        fl, fl_exec, t_ms = fl + f, fl_exec + fe, t_ms + tt
+        stage_gemm[stage] = {
+            "gemm_launches_per_step": len(rows) // rl_steps,
+            "gemm_ms_per_step": round(tt / rl_steps, 4),
+            "gemm_share_of_stage": round(tt / rl_steps / ms[stage], 3),
+            "f32eq_gflop_per_step": round(f / rl_steps / 1e9, 2),
+            "f32eq_tflops": round(f / (tt * 1e-3) / 1e12, 1) if tt else None,
+            "executed_bf16_tflops": round(fe / (tt * 1e-3) / 1e12, 1) if tt else None}
     achieved = fl / (t_ms * 1e-3) / 1e12
     pk = peaks()
     peak = float(pk.get("bf16_tflops", 1590.0))
@@ -288,17 +312,29 @@ def run_block(args):
                 "what": "quantize_block(200 steps per stage) from pinned host activations to "
                         "host shards, GPTQ init and hardening included"},
         "gpu_launches": None,
-        "roofline": {"kernel": "gemm_tc_kernel (all launches of 3 block steps)", "bound": "tensor",
+        "roofline": {"kernel": "gemm_tc_kernel: every launch of 3 timed block steps",
+                     "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "frac": round(achieved / peak, 4),
+                     "traffic": GEMM_TRAFFIC_PER_LAUNCH,
+                     "traffic_source": GEMM_TRAFFIC_SOURCE,
+                     "gemm_ms_per_step": round(t_ms / rl_steps, 4),
+                     "gemm_share_of_step": round(t_ms / rl_steps / ms_step, 3),
                      "executed_bf16_tflops": round(fl_exec / (t_ms * 1e-3) / 1e12, 1),
-                     "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)"
+                     "executed_frac": round(fl_exec / (t_ms * 1e-3) / 1e12 / peak, 4),
+                     "per_stage": stage_gemm,
+                     "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
                      if "bf16_tflops" in pk else "fallback 1590 TFLOP/s",
-                     "note": "achieved counts float32-equivalent GEMM FLOPs 2MNK; the split-bf16 "
-                             "engine executes 3-6 bf16 products per float32 product"},
+                     "note": "achieved = float32-equivalent GEMM FLOPs 2MNK of the timed steps / "
+                             "their GEMM time; the float32-faithful split engine executes 3-6 "
+                             "bf16 products per float32 product (executed_bf16_tflops)"},
         "clocks": clk,
     }
     res["gpu_launches"] = int(sum(timer.launches.values()))
+    if not args.no_secondary:
+        del h, h_dev, h_host
+        torch.cuda.empty_cache()
+        res["config"].update(measure_gptq_rco(dev, world, barrier, max_over_ranks))
     if rank == 0 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_block()
     if rank == 0:
@@ -307,18 +343,69 @@ def run_block(args):
         dist.destroy_process_group()
 
 
-def cpu_baseline_block():
-    """The CPU restatement (oracle port) of one block step — one Lion step each of the qk stage
-    (q_proj, k_proj on the normed rows), the vo stage (v_proj, o_proj through the hard
-    attention probabilities) and the mlp stage (gate, up, down) — at the configuration's
-    micro-batch (2 sequences x 2048 positions, R = 2), on this host's cores."""
+def measure_gptq_rco(dev, world, barrier, max_over_ranks, rco_steps=2):
+    """The other two parts of the metric, measured in the same run at the same N: GPTQ seconds
+    per model (the 24-layer stack at 2 / 3 / 4 bits from Hessians over 128 x 2048 tokens, after
+    a one-layer warm-up) and RCO seconds per step (g = 8 samples x 32 windows x 2048 tokens on
+    that database, ``rco_steps`` timed after one warm-up step). Windows, solves and samples'
+    windows are sharded over the ranks as in the gptq / rco workloads; CUDA events, max over
+    ranks."""
+    import torch
+    from gsq_rco_mlx_b200.rco.allocate import Bank, KLObjective, rco_allocate
+    from gsq_rco_mlx_b200.rco.database import DBSpec, build_database, random_model
+    quiet = lambda *a: None
+    model = random_model(n_layers=24, seed=0, device=dev)
+    tokens = np.random.default_rng(0).integers(0, VOCAB, size=(N_SEQ, T_SEQ)).astype(np.int32)
+    build_database(model, tokens, DBSpec(options=GPTQ_OPTIONS, n_layers=1), log=quiet,
+                   keep="device")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    tm = {}
+    barrier()
+    e0.record()
+    man, res = build_database(model, tokens, DBSpec(options=GPTQ_OPTIONS, n_layers=24),
+                              log=quiet, keep="device", timings=tm)
+    e1.record()
+    barrier()
+    gptq_s = max_over_ranks(e0.elapsed_time(e1) / 1000)
+    bank = Bank(man, res)
+    windows = np.random.default_rng(1).integers(0, VOCAB, size=(RCO_WINDOWS, T_SEQ)).astype(
+        np.int32)
+    obj = KLObjective(model, bank, windows, windows_per_sample=RCO_WIN_PER_SAMPLE, chunk_seqs=8)
+    rco_allocate(obj, bank, 3.0, steps=1, g=RCO_G, lr=0.1, seed=0)
+    barrier()
+    e0.record()
+    rco_allocate(obj, bank, 3.0, steps=rco_steps, g=RCO_G, lr=0.1, seed=1)
+    e1.record()
+    barrier()
+    rco_s = max_over_ranks(e0.elapsed_time(e1) / 1000 / rco_steps)
+    del obj, bank, man, res, model
+    torch.cuda.empty_cache()
+    return {"gptq_s_per_model": round(gptq_s, 3),
+            "gptq_phase_seconds": {k: round(v, 3) for k, v in tm.items()},
+            "rco_s_per_step": round(rco_s, 3),
+            "secondary_what": "gptq_s_per_model: 24-layer GPTQ database (168 linears x {2,3,4} "
+                              "bits, Hessians over 128 x 2048 tokens); rco_s_per_step: one RCO "
+                              f"step of g=8 samples x 32 windows x 2048 tokens ({rco_steps} "
+                              "timed after 1 warm-up); same N, CUDA events, max over ranks"}
+
+
+def cpu_baseline_block(steps=1, warmup=0):
+    """The CPU restatement (oracle port) of the block step in the reference's float32
+    arithmetic — one Lion step each of the qk stage (q_proj, k_proj on the normed rows), the vo
+    stage (v_proj, o_proj through the hard attention probabilities) and the mlp stage (gate,
+    up, down) — at the configuration's micro-batch (2 sequences x 2048 positions, R = 2), on
+    all of this host's cores: float32 GEMMs (torch / numpy BLAS) and the elementwise Gumbel /
+    softmax / backward / Lion passes in the oracle's C backend over every core. Returns the
+    block steps/s of ``steps`` timed steps after ``warmup`` untimed ones."""
     import torch
     from oracle import block as ob
     from oracle import gptq as og
     from oracle import gsq as ogsq
     torch.set_num_threads(os.cpu_count())
+    prev = ogsq.set_backend("c")
     rng = np.random.default_rng(0)
     T, M = T_SEQ, 2 * (T_SEQ - 1)
+    F32 = torch.float32
 
     def rows(shape, scale=1.0):  # exactly-bf16 float32 activations
         x = scale * rng.standard_normal(shape).astype(np.float32)
@@ -342,20 +429,33 @@ def cpu_baseline_block():
     del scores
     mlp = [linear(INTER, HID, 4)[1], linear(INTER, HID, 5)[1], linear(HID, INTER, 6)[1]]
     mn, h1, Y = rows((T, HID)), rows((T, HID), 0.02), rows((T, HID), 0.02)
-    t0 = time.perf_counter()
-    tau, kappa = ogsq.gs_schedules(0, 200)
-    for W, st in qk:
-        noises = [st.noise(0, 0, r) for r in range(2)]
-        _, glog, gs, _ = ogsq.linear_loss_and_grads(hn_rows, W, st.logits, st.Ckd, st.scales,
-                                                    noises, 64, tau, kappa)
-        ogsq.lion_step(st, glog, gs)
-    ob.train_vo(vo, hn_seqs, A_seqs, lambda t, idx: [P, P], bv, 1, NH, NKV, micro_batch=2)
-    ob.train_mlp(mlp, [mn, mn], [h1, h1], [Y, Y], 1, micro_batch=2)
-    dt = time.perf_counter() - t0
+
+    def block_step(t):
+        tau, kappa = ogsq.gs_schedules(t, 200)
+        for W, st in qk:
+            noises = [st.noise(0, t, r) for r in range(2)]
+            _, glog, gs, _ = ogsq.linear_loss_and_grads(hn_rows, W, st.logits, st.Ckd,
+                                                        st.scales, noises, 64, tau, kappa,
+                                                        gemm_dtype=np.float32)
+            ogsq.lion_step(st, glog, gs)
+        ob.train_vo(vo, hn_seqs, A_seqs, lambda t_, idx: [P, P], bv, 1, NH, NKV, micro_batch=2,
+                    dtype=F32)
+        ob.train_mlp(mlp, [mn, mn], [h1, h1], [Y, Y], 1, micro_batch=2, dtype=F32)
+
+    try:
+        for t in range(warmup):
+            block_step(t)
+        t0 = time.perf_counter()
+        for t in range(steps):
+            block_step(warmup + t)
+        dt = (time.perf_counter() - t0) / steps
+    finally:
+        ogsq.set_backend(prev)
     return {"value": round(1.0 / dt, 5), "unit": "block steps/s",
             "cores": os.cpu_count(), "kind": "port",
-            "sample": "1 block step (qk + vo + mlp Lion steps) at micro-batch 2 x 2048, R=2 "
-                      "(numpy/torch-CPU float64 restatement; the MLX path is unavailable)"}
+            "sample": f"{steps} block step(s) (qk + vo + mlp Lion steps) at micro-batch 2 x 2048, "
+                      f"R=2, after {warmup} warm-up: float32 restatement (the reference's "
+                      "arithmetic; its MLX path is unavailable), all host cores"}
 
 
 def run_reference(args):
@@ -363,19 +463,16 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    per = [cpu_baseline_block()["value"] for _ in range(max(1, min(args.steps, 2)))]
-    v = statistics.median(per)
+    steps, warmup = max(3, min(args.steps, 5)), 1
+    cb = cpu_baseline_block(steps=steps, warmup=warmup)
+    v = cb["value"]
     res = {"impl": "reference",
            "metric": "GSQ steps/s per block (Qwen2.5-0.5B block, 3-bit g64: one qk + vo + mlp Lion step)",
-           "value": round(v, 5), "unit": "block steps/s", "n_gpus": world, "steps": len(per),
-           "warmup": 0, "ms_per_step": round(1000 / v, 1), "higher_is_better": True,
+           "value": round(v, 5), "unit": "block steps/s", "n_gpus": world, "steps": steps,
+           "warmup": warmup, "ms_per_step": round(1000 / v, 1), "higher_is_better": True,
            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
            "config": {"workload": "config 2: one Qwen2.5-0.5B block, calib 128 x 2048, micro-batch 2, R=2"},
-           "cpu_baseline": {"value": round(v, 5), "unit": "block steps/s", "cores": os.cpu_count(),
-                            "kind": "port",
-                            "sample": "1 block step (qk + vo + mlp Lion steps) per timed step; "
-                                      "the reference's MLX path is unavailable, this is the "
-                                      "CPU restatement"},
+           "cpu_baseline": cb,
            "e2e": {"value": round(v, 5), "unit": "block steps/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(res), flush=True)

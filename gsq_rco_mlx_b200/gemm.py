@@ -189,11 +189,13 @@ def _tp(t):
 
 class LaunchLog:
     """Optional per-launch CUDA events of gemm() calls (for roofline measurements): while
-    active, every call records (label, M, N, K, products, start, end)."""
+    active, every call records (M, N, K, products, batch, start, end, tag); ``tag`` is the
+    log's current tag (a stage name) at the call."""
     active = None
 
     def __init__(self):
         self.rows = []
+        self.tag = None
 
     def __enter__(self):
         LaunchLog.active = self
@@ -205,8 +207,16 @@ class LaunchLog:
     def summary(self):
         torch.cuda.synchronize()
         out = []
-        for (M, N, K, prods, batch, e0, e1) in self.rows:
+        for (M, N, K, prods, batch, e0, e1, tag) in self.rows:
             out.append((M, N, K, prods, batch, e0.elapsed_time(e1)))
+        return out
+
+    def by_tag(self):
+        """{tag: [(M, N, K, products, batch, ms), ...]}."""
+        torch.cuda.synchronize()
+        out = {}
+        for (M, N, K, prods, batch, e0, e1, tag) in self.rows:
+            out.setdefault(tag, []).append((M, N, K, prods, batch, e0.elapsed_time(e1)))
         return out
 
 
@@ -284,7 +294,7 @@ def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, 
     if log is not None:
         e1.record()
         prods = sum(1 for i in range(na) for j in range(nb) if i + j <= order)
-        log.rows.append((d.M, d.N, d.K, prods, batch, e0, e1))
+        log.rows.append((d.M, d.N, d.K, prods, batch, e0, e1, log.tag))
     return C
 
 

@@ -608,11 +608,13 @@ class VOStep(_StageBase):
 class StageTimer:
     """CUDA-event timing of the steps after the first `warmup` of each stage: ms[name]. With
     nvtx=True the timed steps of every stage also form an NVTX range "gsq_steps" (a profiler
-    filter for the launch list of the steps alone)."""
+    filter for the launch list of the steps alone). With a gemm.LaunchLog, the log records the
+    GEMM launches of the timed steps only, tagged with the stage name."""
 
-    def __init__(self, warmup=3, nvtx=False):
+    def __init__(self, warmup=3, nvtx=False, launch_log=None):
         self.warmup = int(warmup)
         self.nvtx = bool(nvtx)
+        self.launch_log = launch_log
         self.ms = {}
         self.launches = {}  # our kernel launches inside each stage's timed steps
         self._ev = {}
@@ -627,6 +629,10 @@ class StageTimer:
             self._n0[name] = _lib.Launches.n
             if self.nvtx:
                 torch.cuda.nvtx.range_push("gsq_steps")
+            if self.launch_log is not None:
+                from ..gemm import LaunchLog
+                self.launch_log.tag = name
+                LaunchLog.active = self.launch_log
 
     def end(self, name, t, last):
         """After step t; last closes the timed range: ms[name] = mean over steps warmup..t."""
@@ -634,6 +640,9 @@ class StageTimer:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
             self.launches[name] = _lib.Launches.n - self._n0[name]
+            if self.launch_log is not None:
+                from ..gemm import LaunchLog
+                LaunchLog.active = None
             if self.nvtx:
                 torch.cuda.nvtx.range_pop()
             e.synchronize()

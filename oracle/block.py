@@ -109,41 +109,43 @@ def attn_out_hard(hn, W, n_heads=14, n_kv=2):
 
 # ------------------------------------------------------------- stage losses ---
 
-def mlp_loss_and_grads(mn, h1, Y, Wg, Wu, Wd):
+def mlp_loss_and_grads(mn, h1, Y, Wg, Wu, Wd, dtype=F64):
     """mlp stage (staged.py:345-354) on the micro-batch rows (positions 1..): mn, h1, Y bf16
-    [M, H]; soft float32 weights. Returns (loss, dL/dWg, dL/dWu, dL/dWd) in float64."""
-    wg = torch.as_tensor(Wg, dtype=F64).requires_grad_()
-    wu = torch.as_tensor(Wu, dtype=F64).requires_grad_()
-    wd = torch.as_tensor(Wd, dtype=F64).requires_grad_()
-    x = mn.to(F64)
+    [M, H]; soft float32 weights. Returns (loss, dL/dWg, dL/dWu, dL/dWd), computed in
+    ``dtype`` (float64 for parity; float32 is the reference's own arithmetic)."""
+    wg = torch.as_tensor(Wg, dtype=dtype).requires_grad_()
+    wu = torch.as_tensor(Wu, dtype=dtype).requires_grad_()
+    wd = torch.as_tensor(Wd, dtype=dtype).requires_grad_()
+    x = mn.to(dtype)
     g = x @ wg.T
     u = x @ wu.T
     d_in = g * torch.sigmoid(g) * u
-    r = h1.to(F64) + d_in @ wd.T - Y.to(F64)
+    r = h1.to(dtype) + d_in @ wd.T - Y.to(dtype)
     loss = (r * r).mean()
     loss.backward()
-    return float(loss.detach()), wg.grad.numpy(), wu.grad.numpy(), wd.grad.numpy()
+    return (float(loss.detach()), wg.grad.double().numpy(), wu.grad.double().numpy(),
+            wd.grad.double().numpy())
 
 
-def vo_loss_and_grads(hn_seqs, A_seqs, P_seqs, Wv, bv, Wo, n_heads=14, n_kv=2):
+def vo_loss_and_grads(hn_seqs, A_seqs, P_seqs, Wv, bv, Wo, n_heads=14, n_kv=2, dtype=F64):
     """vo stage (staged.py:332-342): per sequence R = (P v) Wo^T - A over positions 1..,
     v = hn Wv^T + bv (float32, soft Wv), P the bf16 probabilities of the hard q / k.
     Returns (loss averaged over sequences, dL/dWv, dL/dWo) in float64."""
-    wv = torch.as_tensor(Wv, dtype=F64).requires_grad_()
-    wo = torch.as_tensor(Wo, dtype=F64).requires_grad_()
+    wv = torch.as_tensor(Wv, dtype=dtype).requires_grad_()
+    wo = torch.as_tensor(Wo, dtype=dtype).requires_grad_()
     total = 0.0
     S = len(hn_seqs)
     for hn, A, P in zip(hn_seqs, A_seqs, P_seqs):
         T = hn.shape[0]
         hd = wv.shape[0] // n_kv
-        v = hn.to(F64) @ wv.T + bv.to(F64)
+        v = hn.to(dtype) @ wv.T + bv.to(dtype)
         v = v.view(T, n_kv, hd).transpose(0, 1).repeat_interleave(n_heads // n_kv, dim=0)
-        o = (P.to(F64) @ v).transpose(0, 1).reshape(T, n_heads * hd)
-        r = (o @ wo.T - A.to(F64))[1:]
+        o = (P.to(dtype) @ v).transpose(0, 1).reshape(T, n_heads * hd)
+        r = (o @ wo.T - A.to(dtype))[1:]
         total = total + (r * r).mean()
     loss = total / S
     loss.backward()
-    return float(loss.detach()), wv.grad.numpy(), wo.grad.numpy()
+    return float(loss.detach()), wv.grad.double().numpy(), wo.grad.double().numpy()
 
 
 # ------------------------------------------------------------- stage optimisers ---
@@ -158,22 +160,19 @@ def _soft(state, t, r, noise_seed, tau, kappa):
 
 def _apply(states, grads_per_r, soft_per_r, tau, kappa, lr_logits, lr_scales):
     """Resample mean of the soft backward and one Lion step per linear (staged.py:383-392)."""
-    from .gsq import lion_step, soft_backward
+    from .gsq import backward_accumulate, lion_step
     R = len(grads_per_r)
     for j, st in enumerate(states):
-        acc_g, acc_s = None, None
+        acc = [None, None]
         for r in range(R):
             _, p, c = soft_per_r[r][j]
-            gl, gsc = soft_backward(grads_per_r[r][j], p, st.Ckd, c, st.scales, st.group_size,
-                                    tau, kappa)
-            gl, gsc = gl.astype(np.float32), gsc.astype(np.float32)
-            acc_g = gl if acc_g is None else acc_g + gl
-            acc_s = gsc if acc_s is None else acc_s + gsc
-        lion_step(st, acc_g / np.float32(R), acc_s / np.float32(R), lr_logits, lr_scales)
+            backward_accumulate(acc, grads_per_r[r][j], p, st.Ckd, c, st.scales,
+                                st.group_size, tau, kappa)
+        lion_step(st, acc[0] / np.float32(R), acc[1] / np.float32(R), lr_logits, lr_scales)
 
 
 def train_mlp(states, mn_seqs, h1_seqs, Y_seqs, steps, micro_batch=2, resamples=2, seed=0,
-              noise_seed=0, lr_logits=1e-4, lr_scales=5e-5):
+              noise_seed=0, lr_logits=1e-4, lr_scales=5e-5, dtype=F64):
     """mlp-stage optimiser (staged.py:357-400 with _loss_block): states = gate, up, down
     LinearStates; per-sequence bf16 caches [T, H]. Returns the loss history."""
     from .gsq import gs_schedules
@@ -190,7 +189,7 @@ def train_mlp(states, mn_seqs, h1_seqs, Y_seqs, steps, micro_batch=2, resamples=
         grads, softs, loss = [], [], 0.0
         for r in range(resamples):
             sw = [_soft(st, t, r, noise_seed, tau, kappa) for st in states]
-            l, gg, gu, gd = mlp_loss_and_grads(mn, h1, Y, sw[0][0], sw[1][0], sw[2][0])
+            l, gg, gu, gd = mlp_loss_and_grads(mn, h1, Y, sw[0][0], sw[1][0], sw[2][0], dtype)
             loss += l
             grads.append([gg, gu, gd])
             softs.append(sw)
@@ -200,7 +199,7 @@ def train_mlp(states, mn_seqs, h1_seqs, Y_seqs, steps, micro_batch=2, resamples=
 
 
 def train_vo(states, hn_seqs, A_seqs, P_of, bv, steps, n_heads, n_kv, micro_batch=2,
-             resamples=2, seed=0, noise_seed=0, lr_logits=1e-4, lr_scales=5e-5):
+             resamples=2, seed=0, noise_seed=0, lr_logits=1e-4, lr_scales=5e-5, dtype=F64):
     """vo-stage optimiser (staged.py:357-400 with _loss_attn): states = v, o LinearStates;
     P_of(t, idx) returns the bf16 probabilities [nh, T, T] of each chosen sequence."""
     from .gsq import gs_schedules
@@ -216,10 +215,112 @@ def train_vo(states, hn_seqs, A_seqs, P_of, bv, steps, n_heads, n_kv, micro_batc
         for r in range(resamples):
             sw = [_soft(st, t, r, noise_seed, tau, kappa) for st in states]
             l, gv, go = vo_loss_and_grads([hn_seqs[i] for i in idx], [A_seqs[i] for i in idx],
-                                          Ps, sw[0][0], bv, sw[1][0], n_heads, n_kv)
+                                          Ps, sw[0][0], bv, sw[1][0], n_heads, n_kv, dtype)
             loss += l
             grads.append([gv, go])
             softs.append(sw)
         _apply(states, grads, softs, tau, kappa, lr_logits, lr_scales)
         hist.append(loss / resamples)
     return hist
+
+
+# ------------------------------------------------------------- block quantizer chain ---
+
+STAGE_LINEARS = {"qk": ("q_proj", "k_proj"), "vo": ("v_proj", "o_proj"),
+                 "mlp": ("gate_proj", "up_proj", "down_proj")}
+LIN_ORDER = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+
+
+def _hessian(rows):
+    """Running-mean Hessian 2 X^T X / n over the rows (positions 1..) of every sequence
+    (staged.py:143-163), float64."""
+    from .gptq import hessian_from_inputs
+    H, n = None, 0
+    for x in rows:
+        H, n = hessian_from_inputs(x.to(F64).numpy(), H, n)
+    return H
+
+
+def _hard_weight(codes, s16, bits, group_size):
+    """staged.py:194-196: dequantized with the fp16 scales, stored as bf16."""
+    from .gptq import dequantize
+    w = dequantize(codes, np.asarray(s16, dtype=np.float32), bits, group_size)
+    return torch.as_tensor(np.asarray(w, dtype=np.float32)).bfloat16()
+
+
+def quantize_block(h_seqs, W, bits, steps, layer=0, opt_seed=0, n_heads=14, n_kv=2,
+                   group_size=64, damp=0.01, block_size=128, micro_batch=2, resamples=2,
+                   eps=1e-6):
+    """The block quantizer of staged.py:405-522 on the CPU: for each stage, Hessians of the
+    linears' inputs under the weights hardened so far, GPTQ warm starts (fp16 scales), 200
+    Lion steps with Philox noise keyed as the CUDA path keys it, hardening (argmax codes, fp16
+    scales). h_seqs: bf16 [T, H] inputs of the calibration sequences; W: bf16 block weights.
+    Returns (shard {name: {codes, scales, bits}}, {stage: loss history}, {name: GPTQ codes})."""
+    from .gptq import quantize_gptq
+    from .gsq import LinearState, train_linear
+    Wf = {k: v.float() for k, v in W.items()}
+    Wcur = {k: v.clone() for k, v in W.items()}
+    seed = opt_seed * 1_000_003 + layer * 1_009
+    shard, hist, gptq_codes = {}, {}, {}
+    states = {}
+
+    def gptq(name, H, pos):
+        g = quantize_gptq(Wf[name].numpy(), H, bits[name], group_size, damp, block_size)
+        s16 = g["scales"].astype(np.float16)
+        gptq_codes[name] = g["codes"]
+        Wcur[name] = _hard_weight(g["codes"], s16, bits[name], group_size)
+        states[name] = LinearState(bits[name], g["codes"], s16, group_size, seed=seed + 10 * pos,
+                                   linear_id=layer * 8 + pos)
+        return states[name]
+
+    def harden(name):
+        st = states[name]
+        codes, s16 = st.hard_codes(), st.stored_scales()
+        Wcur[name] = _hard_weight(codes, s16, st.bits, group_size)
+        shard[name] = {"codes": codes, "scales": s16, "bits": st.bits}
+
+    def fwd(Wb):
+        return [block_hard(h, {k: v.float() for k, v in Wb.items()}, n_heads, n_kv, eps)
+                for h in h_seqs]
+
+    n = len(h_seqs)
+    # qk: linear reconstruction on hn rows (positions 1..)
+    hn = [rmsnorm(h, Wf["in_norm"], eps) for h in h_seqs]
+    H_hn = _hessian([x[1:] for x in hn])
+    qk = [gptq(name, H_hn, i) for i, name in enumerate(STAGE_LINEARS["qk"])]
+    Xs = torch.stack([x[1:] for x in hn]).numpy()
+    in_f = Xs.shape[-1]
+    per = []
+    for st, name in zip(qk, STAGE_LINEARS["qk"]):
+        per.append(train_linear(st, lambda idx: Xs[idx].reshape(-1, in_f), Wf[name].numpy(), n,
+                                steps, micro_batch, resamples, seed=seed + 1,
+                                noise_seed=seed + 1))
+    hist["qk"] = list(np.sum(per, axis=0))
+    for name in STAGE_LINEARS["qk"]:
+        harden(name)
+    # vo: attention output with q and k hard
+    v_st = gptq("v_proj", H_hn, 2)
+    taps = fwd(Wcur)
+    H_o = _hessian([tp["o"][1:] for _, tp in taps])
+    o_st = gptq("o_proj", H_o, 3)
+    A = [attn_out_hard(x, Wf, n_heads, n_kv) for x in hn]
+    Ps = [attention_probs(x, {k: v.float() for k, v in Wcur.items()}, n_heads, n_kv) for x in hn]
+    hist["vo"] = train_vo([v_st, o_st], hn, A, lambda t, idx: [Ps[i] for i in idx],
+                          Wf["v_bias"], steps, n_heads, n_kv, micro_batch, resamples,
+                          seed=seed + 2, noise_seed=seed + 2)
+    for name in STAGE_LINEARS["vo"]:
+        harden(name)
+    # mlp: block output with the attention hard
+    taps = fwd(Wcur)
+    H_gu = _hessian([tp["mn"][1:] for _, tp in taps])
+    g_st, u_st = gptq("gate_proj", H_gu, 4), gptq("up_proj", H_gu, 5)
+    taps_d = fwd(Wcur)
+    H_d = _hessian([tp["d_in"][1:] for _, tp in taps_d])
+    d_st = gptq("down_proj", H_d, 6)
+    Y = [block_hard(h, Wf, n_heads, n_kv, eps)[0] for h in h_seqs]
+    hist["mlp"] = train_mlp([g_st, u_st, d_st], [tp["mn"] for _, tp in taps],
+                            [tp["h1"] for _, tp in taps], Y, steps, micro_batch, resamples,
+                            seed=seed + 3, noise_seed=seed + 3)
+    for name in STAGE_LINEARS["mlp"]:
+        harden(name)
+    return shard, hist, gptq_codes

@@ -28,6 +28,23 @@ import numpy as np
 
 from .philox import gumbel_planes
 
+_BACKEND = "numpy"
+
+
+def set_backend(name: str) -> str:
+    """Select the elementwise passes of the training loops: "numpy" (this file, pinned to the
+    reference's golden vectors) or "c" (oracle/gsq_c.c, the same arithmetic split over the
+    host's cores, checked against numpy). Returns the previous backend."""
+    global _BACKEND
+    if name not in ("numpy", "c"):
+        raise ValueError(name)
+    prev, _BACKEND = _BACKEND, name
+    return prev
+
+
+def fast() -> bool:
+    return _BACKEND == "c"
+
 TAU_START, TAU_END = 2.0, 0.05        # quant.py:22-23
 KAPPA_START, KAPPA_END = 100.0, 500.0  # quant.py:24
 LR_LOGITS = 1e-4                       # lion.py:18
@@ -156,6 +173,10 @@ def group_sum(A, group_size):
 def soft_weight(logits_kd, noise_kd, Ckd, scales, shape, group_size, tau, kappa):
     """staged.py:271-298: w_bar = s[:, col // gs] * sum_k p_k C_k, float32 [out, in].
     Returns (w_bar, p [K, d], c [out, in])."""
+    if fast():
+        from . import gsq_fast
+        return gsq_fast.soft_weight(logits_kd, noise_kd, Ckd, scales, shape, group_size, tau,
+                                    kappa)
     p = gs_probs(logits_kd, noise_kd, tau, kappa)
     c = (p * Ckd).sum(axis=0).astype(np.float32).reshape(shape)
     w = expand_scales(scales, shape[1], group_size) * c
@@ -177,6 +198,23 @@ def soft_backward(G, p, Ckd, c, scales, group_size, tau, kappa):
     return glog, gs
 
 
+def backward_accumulate(acc, G, p, Ckd, c, scales, group_size, tau, kappa):
+    """Add one draw's float32 logit and scale gradients to acc = [glog, gscale] (None entries
+    start the sums), the resample accumulation of staged.py:386."""
+    if fast():
+        from . import gsq_fast
+        if acc[0] is None:
+            acc[0] = np.zeros(p.shape, dtype=np.float32)
+            acc[1] = np.zeros((G.shape[0], -(-G.shape[1] // group_size)), dtype=np.float32)
+        gsq_fast.soft_backward_acc(G, p, Ckd, c, scales, group_size, tau, kappa, acc[0], acc[1])
+        return acc
+    glog, gs = soft_backward(G, p, Ckd, c, scales, group_size, tau, kappa)
+    glog, gs = glog.astype(np.float32), gs.astype(np.float32)
+    acc[0] = glog if acc[0] is None else acc[0] + glog
+    acc[1] = gs if acc[1] is None else acc[1] + gs
+    return acc
+
+
 def lion(P, M, G, lr, wd=WEIGHT_DECAY, betas=BETAS):
     """lion.py:44-56 in float32: u = sign(b1 m + (1-b1) g); m <- b2 m + (1-b2) g;
     p <- p - lr (u + wd p)."""
@@ -192,35 +230,31 @@ def lion(P, M, G, lr, wd=WEIGHT_DECAY, betas=BETAS):
 
 # ------------------------------------------------------------ qk stage ---
 
-def linear_loss_and_grads(X, W, logits_kd, Ckd, scales, noises, group_size, tau, kappa):
+def linear_loss_and_grads(X, W, logits_kd, Ckd, scales, noises, group_size, tau, kappa,
+                          gemm_dtype=np.float64):
     """qk-stage loss of one linear (staged.py:322-329), averaged over the resamples in
     ``noises`` (staged.py:383-390): mean((X (w_bar - W)^T)^2), its logit and scale grads.
 
     X [M, in], W [out, in], noises: list of [K, d] Gumbel planes, one per resample.
     Returns (mean loss, glog [K, d], gscale [out, G], list of G_r = dL/dw_bar).
     """
-    X = np.asarray(X, dtype=np.float64)
-    Wd = np.asarray(W, dtype=np.float64)
+    X = np.asarray(X, dtype=gemm_dtype)
+    Wd = np.asarray(W, dtype=gemm_dtype)
     M = X.shape[0]
     out_f = Wd.shape[0]
     acc_l = 0.0
-    acc_glog = None
-    acc_gs = None
+    acc = [None, None]
     Gs = []
     for noise in noises:
         w, p, c = soft_weight(logits_kd, noise, Ckd, scales, Wd.shape, group_size, tau, kappa)
-        R = X @ (w.astype(np.float64) - Wd).T
-        acc_l += float((R * R).mean())
-        G = (2.0 / (M * out_f)) * (R.T @ X)
+        R = X @ (w.astype(gemm_dtype) - Wd).T
+        acc_l += float((R * R).mean(dtype=np.float64))
+        G = ((2.0 / (M * out_f)) * (R.T @ X)).astype(np.float64)
         Gs.append(G)
-        glog, gs = soft_backward(G, p, Ckd, c, scales, group_size, tau, kappa)
         # the reference accumulates float32 gradients (staged.py:386), then divides by R
-        glog = glog.astype(np.float32)
-        gs = gs.astype(np.float32)
-        acc_glog = glog if acc_glog is None else acc_glog + glog
-        acc_gs = gs if acc_gs is None else acc_gs + gs
+        backward_accumulate(acc, G, p, Ckd, c, scales, group_size, tau, kappa)
     n = np.float32(len(noises))
-    return acc_l / len(noises), acc_glog / n, acc_gs / n, Gs
+    return acc_l / len(noises), acc[0] / n, acc[1] / n, Gs
 
 
 class LinearState:
@@ -254,11 +288,21 @@ class LinearState:
         return self.scales.astype(np.float16)
 
     def noise(self, seed, step, resample):
+        if fast():
+            from . import gsq_fast
+            return gsq_fast.gumbel_planes(seed, self.linear_id, step, resample,
+                                          self.codes0.size, self.K)
         return gumbel_planes(seed, self.linear_id, step, resample, self.codes0.size, self.K)
 
 
 def lion_step(state: LinearState, glog, gs, lr_logits=LR_LOGITS, lr_scales=LR_SCALES):
     """One Lion step on logits and scales (staged.py:389-392; scale lr per lion.py:27-41)."""
+    if fast():
+        from . import gsq_fast
+        gsq_fast.lion_(state.logits, state.mom_logits, glog, lr_logits, WEIGHT_DECAY, BETAS)
+        gsq_fast.lion_(state.scales, state.mom_scales, gs, scale_lr(lr_scales, state.bits),
+                       WEIGHT_DECAY, BETAS)
+        return
     state.logits, state.mom_logits = lion(state.logits, state.mom_logits, glog, lr_logits)
     state.scales, state.mom_scales = lion(state.scales, state.mom_scales, gs,
                                           scale_lr(lr_scales, state.bits))

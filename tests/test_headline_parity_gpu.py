@@ -1,0 +1,121 @@
+"""Parity at the shapes the benchmark runs (Qwen2.5-0.5B block widths), GPU against the oracle.
+
+* The single-linear workload: up_proj W [4864 x 896] ~ N(0, 0.02^2), calibration X [16384 x 896]
+  ~ N(0, 1) times per-channel lognormal(0, 1) scales, GPTQ 3 bits g64 (fp16 scales), then 200
+  qk-stage Lion steps on 32 sequences x 512 (position 0 dropped, micro-batch 2: 1022 rows per
+  step) with host-supplied Gumbel noise: logits, scales and loss within 1e-3 relative, hard codes
+  equal on >= 99.9 % of the weights (src/gsq_rco/gsq/staged.py:322-329, 357-400).
+* GPTQ of the largest solve, down_proj W [896 x 4864] (a 4864 x 4864 Hessian): codes >= 99.9 %
+  equal, reconstruction error within 1e-3 (src/gsq_rco/gsq/gptq.py:123-187).
+* quantize_block end to end at the block's widths (hidden 896, 14 / 2 heads, SwiGLU 4864):
+  Hessians, GPTQ warm starts, the qk, vo and mlp stages at 200 steps each, hardening; against
+  the oracle's chain of the same steps (oracle.block.quantize_block), each side feeding its own
+  results forward (the vo stage's probabilities come from each side's own forward). Shorter
+  sequences (4 x 128) than the benchmark's 128 x 2048 keep the CPU oracle to minutes.
+The oracle's elementwise passes run on its C backend (checked against the numpy restatement in
+tests/test_oracle_golden.py); its contractions are float64.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import block as ob
+from oracle import gptq as og
+from oracle import gsq as ogsq
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture
+def c_oracle():
+    prev = ogsq.set_backend("c")
+    yield
+    ogsq.set_backend(prev)
+
+
+def _rel(a, b):
+    return float(np.linalg.norm(np.asarray(a, np.float64) - b) / np.linalg.norm(b))
+
+
+def test_up_proj_200_steps_parity(c_oracle):
+    from oracle import gsq_fast
+    from gsq_rco_mlx_b200.gsq import gptq
+    from gsq_rco_mlx_b200.gsq.staged import BlockOpts, SoftLinear, train_linears
+    rng = np.random.default_rng(0)
+    out_f, in_f, n_seq, T = 4864, 896, 32, 512
+    W = (0.02 * rng.standard_normal((out_f, in_f))).astype(np.float32)
+    sch = np.exp(rng.standard_normal(in_f)).astype(np.float32)
+    X = rng.standard_normal((n_seq * T, in_f)).astype(np.float32) * sch
+    H, _ = og.hessian_from_inputs(X)
+    go = og.quantize_gptq(W, H, 3, 64)
+    g = gptq.quantize_gptq(W, H, 3, 64)
+    assert (g["codes"] == go["codes"]).mean() >= 0.999
+    assert abs(g["err"] - go["err"]) <= 1e-3 * go["err"]
+    codes, s16 = go["codes"], go["scales"].astype(np.float16)
+    Xs = X.reshape(n_seq, T, in_f)[:, 1:]
+    st = ogsq.LinearState(3, codes, s16, 64, seed=0, linear_id=5)
+    hist_o = ogsq.train_linear(st, lambda idx: Xs[idx].reshape(-1, in_f), W, n_seq, 200,
+                               seed=1, noise_seed=77)
+    lin = SoftLinear("up_proj", 3, codes, s16, 64, seed=0, linear_id=5)
+    noise_of = lambda t, r, l: torch.as_tensor(gsq_fast.gumbel_planes(77, 5, t, r, W.size, 5),
+                                               device=DEV)
+    hist, _ = train_linears([lin], torch.as_tensor(X.reshape(n_seq, T, in_f), device=DEV),
+                            {"up_proj": torch.as_tensor(W, device=DEV)}, n_seq,
+                            BlockOpts(steps=200), seed=1, noise_of=noise_of, noise_seed=77)
+    rl = _rel(lin.logits.cpu().numpy(), st.logits)
+    rs = _rel(lin.scales.cpu().numpy(), st.scales)
+    rloss = abs(hist[-1] - hist_o[-1]) / hist_o[-1]
+    codes_eq = (lin.hard_codes() == st.hard_codes()).mean()
+    print(f"up_proj 200 steps: logits {rl:.2e} scales {rs:.2e} loss {rloss:.2e} "
+          f"codes {codes_eq:.6f}")
+    assert rl <= 1e-3 and rs <= 1e-3 and rloss <= 1e-3, (rl, rs, rloss)
+    assert codes_eq >= 0.999, codes_eq
+
+
+def test_down_proj_gptq_parity():
+    from gsq_rco_mlx_b200.gsq import gptq
+    rng = np.random.default_rng(1)
+    out_f, in_f = 896, 4864
+    W = (0.02 * rng.standard_normal((out_f, in_f))).astype(np.float32)
+    # SwiGLU-like inputs: heavy-tailed, correlated through a low-rank part
+    base = rng.standard_normal((8192, 64)).astype(np.float32)
+    mix = rng.standard_normal((64, in_f)).astype(np.float32) / 8.0
+    X = (base @ mix + 0.5 * rng.standard_normal((8192, in_f)).astype(np.float32))
+    X *= np.exp(0.5 * rng.standard_normal(in_f)).astype(np.float32)
+    H, _ = og.hessian_from_inputs(X)
+    for bits in (2, 3, 4):
+        r = gptq.quantize_gptq(W, H, bits, 64)
+        ro = og.quantize_gptq(W, H, bits, 64)
+        eq = (r["codes"] == ro["codes"]).mean()
+        print(f"down_proj {bits}-bit: codes {eq:.6f} err {r['err']:.6e} vs {ro['err']:.6e}")
+        assert eq >= 0.999, (bits, eq)
+        assert abs(r["err"] - ro["err"]) <= 1e-3 * ro["err"], bits
+
+
+def test_quantize_block_end_to_end_parity(c_oracle):
+    from tests.test_block_gpu import small_block
+    from gsq_rco_mlx_b200.gsq.e2e import BlockConfig, LIN_ORDER
+    from gsq_rco_mlx_b200.gsq.staged import BlockOpts, quantize_block
+    cfg = BlockConfig(hidden=896, n_heads=14, n_kv=2, inter=4864)
+    W = small_block(0, H=896, nh=14, nkv=2, inter=4864, scale=0.02)
+    N, T, steps = 4, 128, 200
+    g = torch.Generator().manual_seed(11)
+    h = (0.02 * torch.randn(N * T, cfg.hidden, generator=g)).bfloat16()
+    bits = {n: 3 for n in LIN_ORDER}
+    shard, stats, _ = quantize_block(h.to(DEV), {k: v.to(DEV) for k, v in W.items()}, bits,
+                                     BlockOpts(steps=steps), layer=0, cfg=cfg, T=T, chunk_seqs=2,
+                                     log=lambda *a: None)
+    shard_o, hist_o, _ = ob.quantize_block([h[i * T:(i + 1) * T] for i in range(N)], W, bits,
+                                           steps, layer=0)
+    for stage, names in ob.STAGE_LINEARS.items():
+        loss = stats["stages"][stage]["soft_loss_last"]
+        rloss = abs(loss - hist_o[stage][-1]) / hist_o[stage][-1]
+        for n in names:
+            eq = (shard[n]["codes"] == shard_o[n]["codes"]).mean()
+            rs = _rel(shard[n]["scales"].astype(np.float32),
+                      shard_o[n]["scales"].astype(np.float32))
+            print(f"{stage} {n}: codes {eq:.6f} scales {rs:.2e} loss {rloss:.2e}")
+            assert eq >= 0.999, (n, eq)
+            assert rs <= 1e-3, (n, rs)
+        assert rloss <= 1e-3, (stage, rloss)

@@ -186,3 +186,56 @@ def test_dp_c_matches_reference():
                                 zi.ctypes.data_as(ctypes.c_void_p))
         assert rc == 0
         assert np.array_equal(zref.argmax(axis=1), zi)
+
+
+@pytest.mark.parametrize("bits", [2, 3])
+def test_c_backend_matches_numpy_oracle(bits):
+    """The C backend of the GSQ oracle (oracle/gsq_c.c, used by the full-size parity runs)
+    against the numpy restatement that the golden vectors pin: the Philox noise, soft weight,
+    backward and Lion agree to float32 rounding, and a short training run stays together."""
+    from oracle import gsq as ogsq
+    from oracle import gsq_fast
+    from oracle.philox import gumbel_planes
+    rng = np.random.default_rng(bits)
+    out_f, in_f = 48, 200                       # ragged last group
+    codes = rng.integers(0, 2 ** bits, size=(out_f, in_f)).astype(np.uint8)
+    s16 = (0.01 + 0.02 * rng.random((out_f, 4))).astype(np.float16)
+    st = ogsq.LinearState(bits, codes, s16, 64, seed=1, linear_id=3)
+    d, K = codes.size, st.K
+    nz = gumbel_planes(5, 3, 7, 1, d, K)
+    nz_c = gsq_fast.gumbel_planes(5, 3, 7, 1, d, K)
+    assert np.abs(nz_c - nz).max() <= 4e-7 * np.abs(nz).max()
+    w, p, c = ogsq.soft_weight(st.logits, nz, st.Ckd, st.scales, (out_f, in_f), 64, 0.7, 180.0)
+    w2, p2, c2 = gsq_fast.soft_weight(st.logits, nz, st.Ckd, st.scales, (out_f, in_f), 64,
+                                      0.7, 180.0)
+    np.testing.assert_allclose(p2, p, rtol=2e-6, atol=1e-7)
+    np.testing.assert_allclose(w2, w, rtol=2e-6, atol=1e-8)
+    G = rng.standard_normal((out_f, in_f)) * 1e-3
+    gl, gsc = ogsq.soft_backward(G, p, st.Ckd, c, st.scales, 64, 0.7, 180.0)
+    acc = [np.zeros((K, d), np.float32), np.zeros((out_f, 4), np.float32)]
+    gsq_fast.soft_backward_acc(G, p, st.Ckd, c, st.scales, 64, 0.7, 180.0, acc[0], acc[1])
+    np.testing.assert_array_equal(acc[0], gl.astype(np.float32))
+    np.testing.assert_allclose(acc[1], gsc.astype(np.float32), rtol=1e-6, atol=1e-12)
+    P, M = st.logits.copy(), (0.1 * rng.standard_normal(st.logits.shape)).astype(np.float32)
+    Pn, Mn = ogsq.lion(P, M, gl, 1e-4)
+    gsq_fast.lion_(P, M, gl, 1e-4, ogsq.WEIGHT_DECAY, ogsq.BETAS)
+    np.testing.assert_array_equal(P, Pn)
+    np.testing.assert_array_equal(M, Mn)
+    # a short qk-stage run with each backend
+    X = rng.standard_normal((8 * 33, in_f)).astype(np.float32)
+    Wf = (0.02 * rng.standard_normal((out_f, in_f))).astype(np.float32)
+    Xs = X.reshape(8, 33, in_f)[:, 1:]
+    runs = []
+    for backend in ("numpy", "c"):
+        prev = ogsq.set_backend(backend)
+        try:
+            s = ogsq.LinearState(bits, codes, s16, 64, seed=1, linear_id=3)
+            h = ogsq.train_linear(s, lambda idx: Xs[idx].reshape(-1, in_f), Wf, 8, 6, seed=2,
+                                  noise_seed=9)
+            runs.append((s.logits.copy(), s.scales.copy(), h))
+        finally:
+            ogsq.set_backend(prev)
+    (l0, s0, h0), (l1, s1, h1) = runs
+    assert np.linalg.norm(l1 - l0) <= 1e-5 * np.linalg.norm(l0)
+    assert np.linalg.norm(s1 - s0) <= 1e-5 * np.linalg.norm(s0)
+    np.testing.assert_allclose(h1, h0, rtol=1e-5)
