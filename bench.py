@@ -77,6 +77,10 @@ def parse():
     ap.add_argument("--rco-steps", type=int, default=2,
                     help="pipeline: RCO steps run (the rest of the 100 extrapolated)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--split", default="sequences", choices=["sequences", "positions"],
+                    help="block, N > 1: each rank its own micro-batch of 2 sequences (weak "
+                         "scaling; global micro-batch 2N) or the positions of one shared "
+                         "micro-batch (strong scaling)")
     ap.add_argument("--no-secondary", action="store_true",
                     help="block: skip the GPTQ s/model and RCO s/step fields")
     ap.add_argument("--e2e-steps", type=int, default=200)
@@ -211,7 +215,7 @@ def run_block(args):
     torch.cuda.set_device(dev)
     cfg = BlockConfig()
     W = make_block(1000, dev)
-    dp = DataParallel()
+    dp = DataParallel(split=args.split)
     E, ids = make_calibration(dev)
     E_dev = E.to(dev)
     h = embed(E_dev, ids, dev)
@@ -291,21 +295,29 @@ def run_block(args):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     d2h = sum(v["codes"].nbytes + v["scales"].nbytes for v in shard.values())
 
-    value = 1000.0 / ms_step
+    # weak scaling: a step of the N ranks trains on N micro-batches of 2 sequences, so the
+    # whole job's throughput is N micro-batch steps per step time
+    per_step = dp.total(1)
+    value = 1000.0 / ms_step * per_step
     res = {
         "metric": "GSQ steps/s per block (Qwen2.5-0.5B block, 3-bit g64: one qk + vo + mlp Lion step)",
         "value": round(value, 3), "unit": "block steps/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "weak" if args.split == "sequences" else "strong",
+        "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: random-init bf16 block and embedding, uniform-random token ids",
         "config": {"workload": "config 2: one Qwen2.5-0.5B block, calib 128 x 2048, micro-batch 2, R=2",
                    "stage_ms_per_step": {k: round(v, 4) for k, v in ms.items()},
                    "block_seconds_200_steps": round(e2e_ms / 1000, 3),
-                   "parallelism": f"one block, data-parallel over {world} GPU(s): position "
-                                  "windows of each micro-batch sequence, NCCL all-reduce of "
-                                  "dL/dw per step",
+                   "parallelism": (f"one block, data-parallel over {world} GPU(s): each rank "
+                                   "its own micro-batch of 2 sequences of one global sorted "
+                                   f"draw of {2 * per_step} (value = {per_step} micro-batch "
+                                   "steps per step), NCCL all-reduce of dL/dw per step")
+                   if args.split == "sequences" else
+                   (f"one block, data-parallel over {world} GPU(s): position windows of each "
+                    "micro-batch sequence, NCCL all-reduce of dL/dw per step"),
                    "l2": "per-step working set > L2 (126 MB)"},
-        "e2e": {"value": round(args.e2e_steps / (e2e_ms / 1000), 3),
+        "e2e": {"value": round(args.e2e_steps * per_step / (e2e_ms / 1000), 3),
                 "unit": "block steps/s",
                 "h2d_bytes_per_step": int(h_host.numel() * 2 / args.e2e_steps),
                 "d2h_bytes_per_step": int(d2h / args.e2e_steps),
@@ -831,7 +843,7 @@ def run_eval(args):
     pm, windows, info = eval_setup(dev)
     dp = DataParallel()
     ev = Evaluator(pm, T_SEQ, EVAL_CHUNK)
-    a, b = dp.window(0, EVAL_WINDOWS)
+    a, b = dp.share(0, EVAL_WINDOWS)
     # device-resident windows of this rank (the timed step reads no host memory)
     mine = windows[a:b]
     tok = torch.as_tensor(mine.reshape(-1)).to(dev)

@@ -332,7 +332,7 @@ def perplexity(model: PackedModel, windows, chunk_seqs: int = 4, progress: bool 
     ev = evaluator or Evaluator(model, seq_len, chunk_seqs)
     if ev.S != seq_len:
         raise ValueError(f"evaluator built for windows of {ev.S}, got {seq_len}")
-    a, b = dp.window(0, n_windows)
+    a, b = dp.share(0, n_windows)
     dev = model.dev
     n_batches = max(1, -(-(b - a) // ev.cs))
     sums = torch.zeros(n_batches, device=dev, dtype=torch.float64)

@@ -262,13 +262,13 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
     if not lins or opts.steps == 0:
         return [], None
     rng = np.random.default_rng(seed)
-    m = min(opts.micro_batch, n_seqs)
     n_seq, T, in_f = x_all.shape
     noise_seed = seed if noise_seed is None else noise_seed
     dp = dp or DataParallel()
+    m = min(opts.micro_batch, n_seqs // dp.total(1))
     p0, p1 = dp.window(1, T)
     step = LinearStep(lins, m * (p1 - p0), in_f, opts.resamples, 1 if exact_bf16_rows else 3,
-                      M_total=m * (T - 1))
+                      M_total=dp.total(m) * (T - 1))
     flat = x_all.view(n_seq * T, in_f)
     err_flag(step.dev).zero_()
     hist = torch.zeros(opts.steps, len(lins) * step.R, device=step.dev, dtype=torch.float64)
@@ -278,7 +278,7 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
     for t in range(opts.steps):
         timer.begin(name, t)
         tau, kappa = gs_schedules(t, opts.steps)
-        idx = np.sort(rng.choice(n_seqs, size=m, replace=False))
+        idx = dp.draw(rng, n_seqs, m)
         step.stage(flat, idx, p1 - p0, T, p0)
         step.contract()
         dp.allreduce(step.gflat, step.loss)
@@ -297,26 +297,59 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
 # ------------------------------------------------------------------------- block stages ---
 
 class DataParallel:
-    """Data parallelism of the GSQ stages over calibration tokens. Every rank draws the same
-    micro-batch (the numpy stream is replicated) and takes one window of positions of each of its
-    sequences; it computes dL/dw̄ of every resample on its rows, and one all-reduce per step sums
-    the weight gradients (4 B per weight per resample: the logit and scale gradients are linear
-    maps of them) and the loss partials. Every rank then runs the identical fused Lion update,
-    so the soft-weight states stay bit-identical across ranks. A single process is world 1."""
+    """Data parallelism of the GSQ stages over calibration tokens, one of two splits:
 
-    def __init__(self, group=None):
+    * "sequences" (weak scaling): every rank draws the same global micro-batch of
+      m x world sequences from the replicated numpy stream (the reference's sorted draw,
+      staged.py:373,380) and takes its own m of them; the loss is the mean over the whole
+      global micro-batch, so one rank's gradients are a share of the global ones.
+    * "positions" (strong scaling): every rank draws the same m sequences and takes one
+      window of positions of each.
+
+    Either way each rank computes dL/dw_bar of every resample on its rows, one all-reduce per
+    step sums the weight gradients (4 B per weight per resample: the logit and scale
+    gradients are linear maps of them) and the loss partials, and every rank runs the
+    identical fused Lion update, so the soft-weight states stay bit-identical across ranks. A
+    single process is world 1, where both splits are the reference's step."""
+
+    def __init__(self, group=None, split="sequences"):
         import torch.distributed as dist
+        if split not in ("sequences", "positions"):
+            raise ValueError(f"split must be 'sequences' or 'positions', got {split!r}")
         on = dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1
         self.dist = dist if on else None
         self.group = group
         self.world = dist.get_world_size(group) if on else 1
         self.rank = dist.get_rank(group) if on else 0
+        self.split = split
 
     def window(self, lo, hi):
-        """This rank's contiguous share [a, b) of the positions [lo, hi)."""
+        """This rank's contiguous share [a, b) of the positions [lo, hi) (all of them when
+        the ranks split sequences)."""
+        if self.split == "sequences":
+            return lo, hi
+        return self.share(lo, hi)
+
+    def share(self, lo, hi):
+        """This rank's contiguous share [a, b) of the range [lo, hi)."""
         base, extra = divmod(hi - lo, self.world)
         a = lo + self.rank * base + min(self.rank, extra)
         return a, a + base + (1 if self.rank < extra else 0)
+
+    def total(self, m):
+        """Sequences of the global micro-batch when each rank takes m."""
+        return m * self.world if self.split == "sequences" else m
+
+    def draw(self, rng, n_seqs, m):
+        """This rank's sorted sequence ids of one step's micro-batch (m of them)."""
+        g = self.total(m)
+        if g > n_seqs:
+            raise ValueError(f"a global micro-batch of {g} sequences needs at least {g} "
+                             f"calibration sequences, got {n_seqs}")
+        idx = np.sort(rng.choice(n_seqs, size=g, replace=False))
+        if self.split == "sequences":
+            return idx[self.rank * m:(self.rank + 1) * m]
+        return idx
 
     def allreduce(self, *tensors):
         if self.dist is not None:
@@ -415,8 +448,9 @@ class MLPStep(_StageBase):
     row-major activations through MN-major tensor-core operands.
     """
 
-    def __init__(self, lins, cfg, m, T, R, window=None):
-        """window: this rank's positions [p0, p1) of each sequence (default all of 1..T-1)."""
+    def __init__(self, lins, cfg, m, T, R, window=None, m_total=None):
+        """window: this rank's positions [p0, p1) of each sequence (default all of 1..T-1);
+        m_total: sequences of the global micro-batch (the loss normalisation; default m)."""
         gate, up, down = lins
         dev = gate.logits.device
         self._init_soft(lins, R, dev)
@@ -424,7 +458,9 @@ class MLPStep(_StageBase):
         self.p0, p1 = window or (1, T)
         self.w = p1 - self.p0
         M = m * self.w
-        self.cfg, self.m, self.T, self.M, self.count = cfg, m, T, M, m * (T - 1) * H
+        self.m_total = int(m if m_total is None else m_total)
+        self.cfg, self.m, self.T, self.M = cfg, m, T, M
+        self.count = self.m_total * (T - 1) * H
         bf = torch.bfloat16
         self.MN = Terms(M, H, 1, dev)
         self.H1 = Terms(M, H, 1, dev)
@@ -486,7 +522,9 @@ class VOStep(_StageBase):
       Gv    dL/dWv = dV^T hn
     """
 
-    def __init__(self, lins, cfg, m, T, R, v_bias, window=None):
+    def __init__(self, lins, cfg, m, T, R, v_bias, window=None, m_total=None):
+        """window: this rank's query positions [q0, q1) (default all); m_total: sequences of the
+        global micro-batch (the loss normalisation; default m)."""
         v, o = lins
         dev = v.logits.device
         self._init_soft(lins, R, dev)
@@ -495,7 +533,9 @@ class VOStep(_StageBase):
         self.q0, q1 = window or (0, T)
         self.Tq, self.Tk = q1 - self.q0, q1
         Tq, Tk = self.Tq, self.Tk
-        self.cfg, self.m, self.T, self.count = cfg, m, T, m * (T - 1) * H
+        self.m_total = int(m if m_total is None else m_total)
+        self.cfg, self.m, self.T = cfg, m, T
+        self.count = self.m_total * (T - 1) * H
         self.HN, self.HNT = Terms(m * Tk, H, 1, dev), Terms(H, m * Tk, 1, dev)
         self.A = Terms(m * Tq, H, 1, dev)
         self.QK = torch.empty(m * Tk, (nh + nkv) * hd, device=dev, dtype=torch.bfloat16)
@@ -659,8 +699,9 @@ def train_stage(step, stage_args_of, n_seqs, opts: BlockOpts, seed, noise_seed=N
     if opts.steps == 0:
         return [], None
     rng = np.random.default_rng(seed)
-    m = min(opts.micro_batch, n_seqs)
+    m = step.m
     noise_seed = seed if noise_seed is None else noise_seed
+    draw = (dp or DataParallel()).draw
     err_flag(step.dev).zero_()
     tau, kappa = gs_schedules(0, opts.steps)
     step.first_forward(0, tau, kappa, noise_seed, noise_of)
@@ -669,7 +710,7 @@ def train_stage(step, stage_args_of, n_seqs, opts: BlockOpts, seed, noise_seed=N
     for t in range(opts.steps):
         timer.begin(name, t)
         tau, kappa = gs_schedules(t, opts.steps)
-        idx = np.sort(rng.choice(n_seqs, size=m, replace=False))
+        idx = draw(rng, n_seqs, m)
         step.stage(*stage_args_of(idx))
         step.contract()
         if dp is not None:
@@ -816,8 +857,9 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
         gemm(_bf16_rows(hn_all[a * T:(a + s) * T]), wterms(Wc.qk), epi=4, bias=Wc.qk_bias,
              c_terms=_bf16_rows(qk_all[a * T:(a + s) * T]))
     if len(vo_lins) == 2:
-        vstep = VOStep(vo_lins, cfg, min(opts.micro_batch, N), T, opts.resamples, W["v_bias"],
-                       window=dp.window(0, T))
+        m = min(opts.micro_batch, N // dp.total(1))
+        vstep = VOStep(vo_lins, cfg, m, T, opts.resamples, W["v_bias"],
+                       window=dp.window(0, T), m_total=dp.total(m))
         hist, ms = train_stage(vstep, lambda idx: (hn_all, A_all, qk_all, idx), N, opts,
                                seed + 2, noise_of=noise_of, timer=timer, name="vo", dp=dp)
     else:
@@ -841,8 +883,9 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
     down = gptq("down_proj", H_d, 6)
     mlp_lins = [l for l in (gate, up, down) if l is not None]
     if len(mlp_lins) == 3:
-        mstep = MLPStep(mlp_lins, cfg, min(opts.micro_batch, N), T, opts.resamples,
-                        window=dp.window(1, T))
+        m = min(opts.micro_batch, N // dp.total(1))
+        mstep = MLPStep(mlp_lins, cfg, m, T, opts.resamples, window=dp.window(1, T),
+                        m_total=dp.total(m))
         hist, ms = train_stage(mstep, lambda idx: (mn_all, h1_all, Y_all, idx), N, opts,
                                seed + 3, noise_of=noise_of, timer=timer, name="mlp", dp=dp)
     else:

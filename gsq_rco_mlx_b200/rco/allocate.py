@@ -128,7 +128,7 @@ class KLObjective:
 
     def _my_ids(self, ids):
         """This rank's share of a sample's windows (contiguous)."""
-        a, b = self.dp.window(0, len(ids))
+        a, b = self.dp.share(0, len(ids))
         return ids[a:b]
 
     def _states(self, ids, weights_of):

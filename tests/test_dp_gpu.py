@@ -110,7 +110,7 @@ def _dp_worker(rank, world, port, q):
         mn, h1 = blk.mn.clone(), blk.h1.clone()
         lins = [_pair(n, W[n].float().numpy(), 3, i + 4)[0] for i, n in
                 enumerate(("gate_proj", "up_proj", "down_proj"))]
-        dp = DataParallel()
+        dp = DataParallel(split="positions")
         step = MLPStep(lins, cfg, 2, T, 2, window=dp.window(1, T))
         hist = train_stage(step, lambda idx: (mn, h1, Y, idx), N, BlockOpts(steps=6), seed=5,
                            noise_seed=9, dp=dp)[0]
@@ -149,3 +149,24 @@ def test_mlp_stage_two_ranks_matches_one():
     one = torch.cat([l.logits.flatten() for l in lins]).cpu()
     assert _rel(logits[0], one) < 1e-5
     assert abs(hist2[-1] - hist1[-1]) <= 1e-5 * abs(hist1[-1])
+
+
+def test_mlp_sequence_shares_sum_to_global_step():
+    """The "sequences" split: two ranks' steps over their halves of a global micro-batch of 4
+    sequences (loss normalised by the global count) sum to one step over all 4."""
+    from gsq_rco_mlx_b200.gsq.staged import MLPStep
+    cfg, W, Wd, blk, h, N, T, _pair = _setup(3)
+    Y = blk.forward(h, Wd).clone()
+    mn, h1 = blk.mn.clone(), blk.h1.clone()
+    lins = [_pair(n, W[n].float().numpy(), 3, i + 4)[0] for i, n in
+            enumerate(("gate_proj", "up_proj", "down_proj"))]
+    full = MLPStep(lins, cfg, 4, T, 2)
+    parts = [MLPStep(lins, cfg, 2, T, 2, m_total=4) for _ in range(2)]
+    ids = [0, 1, 2, 3]
+    for st, idx in ((full, ids), (parts[0], ids[:2]), (parts[1], ids[2:])):
+        st.first_forward(0, 2.0, 100.0, 9)
+        st.stage(mn, h1, Y, idx)
+        st.contract()
+    torch.cuda.synchronize()
+    assert _rel(parts[0].gflat + parts[1].gflat, full.gflat) < 2e-6
+    assert _rel(parts[0].loss + parts[1].loss, full.loss) < 1e-9
