@@ -213,7 +213,35 @@ def vjp_gemms(dev, g):
     }
 
 
-CASES = {"mlp_gemms": mlp_gemms, "vjp_gemms": vjp_gemms, "attn": attn, "attn1": lambda dev, g: attn(dev, g, seqs=1),
+def vo_step(dev, g):
+    """The vo stage step at the block's widths on one micro-batch of 2 sequences x 2048 (R = 2):
+    stage() gathers the rows, RoPEs q / k, runs the causal scores GEMM and the windowed softmax;
+    contract() runs both resamples' GEMMs (V, P V, Y, dWo, dO, P^T dO, dWv) with the
+    transposes and head sums between them. Times only (the products mix 1, 3 and 6 bf16
+    products per float32 product)."""
+    import numpy as np
+    from gsq_rco_mlx_b200.gsq.e2e import BlockConfig
+    from gsq_rco_mlx_b200.gsq.staged import SoftLinear, VOStep
+    cfg = BlockConfig()
+    rng = np.random.default_rng(0)
+
+    def lin(name, out_f, in_f, i):
+        codes = rng.integers(0, 8, size=(out_f, in_f)).astype(np.uint8)
+        s16 = (0.01 + 0.001 * rng.random((out_f, in_f // 64))).astype(np.float16)
+        return SoftLinear(name, 3, codes, s16, 64, seed=i, linear_id=i)
+    v, o = lin("v_proj", KV * HD, H, 2), lin("o_proj", H, HEADS * HD, 3)
+    bv = (0.02 * torch.randn(KV * HD, device=dev, generator=g)).bfloat16()
+    step = VOStep([v, o], cfg, 2, T, 2, bv)
+    hn = torch.randn(4 * T, H, device=dev, generator=g).bfloat16()
+    a = (0.02 * torch.randn(4 * T, H, device=dev, generator=g)).bfloat16()
+    qk = torch.randn(4 * T, (HEADS + KV) * HD, device=dev, generator=g).bfloat16()
+    step.first_forward(0, 2.0, 100.0, 5)
+    return {"vo stage(): gathers, RoPE, scores, softmax": (None, lambda: step.stage(hn, a, qk,
+                                                                                    [1, 3])),
+            "vo contract(): 2 resamples": (None, step.contract)}
+
+
+CASES = {"mlp_gemms": mlp_gemms, "vo_step": vo_step, "vjp_gemms": vjp_gemms, "attn": attn, "attn1": lambda dev, g: attn(dev, g, seqs=1),
          "soft_step": soft_step, "cublas": cublas, "packed": packed, "eval_batch": eval_batch}
 
 

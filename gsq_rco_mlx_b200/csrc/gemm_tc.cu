@@ -5,7 +5,10 @@
 // The products A_i B_j with i + j <= order are accumulated on the tensor cores (order 2 with
 // three terms per side reproduces float32 operands to 2^-24; an exactly-bf16 operand needs one
 // term). Persistent kernel: one CTA per SM walks the 128 x BN output tiles (batch z, row tile m,
-// column tile n; m fastest) in a static round-robin order. Roles:
+// column tile n) in a static round-robin order. Within a batch the tile index runs along the
+// dimension of the smaller operand first (m fastest when B is the larger operand, n fastest
+// when A is): the CTAs that run at the same time then share the tiles of the larger operand,
+// so it crosses from DRAM once while the smaller one stays in L2. Roles:
 //   warp 0     TMA producer: for each 64-wide k-block, every term tile of A and B into one
 //              pipeline stage (128-byte swizzle), completion counted on the stage's mbarrier
 //   warp 1     TMEM allocator and MMA issuer
@@ -88,6 +91,7 @@ struct GemmParams {
   int kb_per_chunk;
   int n_big;       // chunk accumulators in the TMEM ring
   int tiles_m, tiles_n;
+  int n_fast;  // tile order: n fastest (A the larger operand) instead of m fastest
   int64_t total_tiles;
   int skip_upper;  // output tiles entirely above the diagonal (n >= m) are not computed
   int row_period;  // epi 1: rows with (row % row_period) == 0 have a zero residual
@@ -136,7 +140,8 @@ __device__ __forceinline__ bool tile_at(const GemmParams& p, int64_t L, TileInfo
   t.z = (int)(zk / p.splits);
   t.ks = (int)(zk - (int64_t)t.z * p.splits);
   const int rem = (int)(L - zk * per);
-  const int my = rem % p.tiles_m, nx = rem / p.tiles_m;
+  const int my = p.n_fast ? rem / p.tiles_n : rem % p.tiles_m;
+  const int nx = p.n_fast ? rem % p.tiles_n : rem / p.tiles_m;
   t.tile_m = my * BM;
   t.tile_n = nx * BN;
   if (p.skip_upper && t.tile_n >= t.tile_m + BM) return false;
@@ -1398,6 +1403,9 @@ static int launch(GemmParams& p, int batch, cudaStream_t st) {
   p.tiles_m = (p.M + BM - 1) / BM;
   p.tiles_n = (p.N + BN - 1) / BN;
   p.total_tiles = (int64_t)p.tiles_m * p.tiles_n * batch * p.splits;
+  // single products: walk along the smaller operand first (its bytes M x K x na vs N x K x nb)
+  p.n_fast = (batch == 1 && p.splits == 1 && !p.skip_upper && p.causal == 0 &&
+              (int64_t)p.M * p.na > (int64_t)p.N * p.nb) ? 1 : 0;
   const size_t smem = 1024 + (size_t)S * stage_bytes +
                       (p.tma_out ? (size_t)kEpiWarps * p.tma_bufs * kTmaBuf : (size_t)kStgBytes);
   static bool attr_set[2][7] = {{false}};

@@ -190,7 +190,8 @@ def _tp(t):
 class LaunchLog:
     """Optional per-launch CUDA events of gemm() calls (for roofline measurements): while
     active, every call records (M, N, K, products, batch, start, end, tag); ``tag`` is the
-    log's current tag (a stage name) at the call."""
+    log's current tag (a stage name) at the call. ``batch`` is the work in M x N x K boxes:
+    the batch count, halved for causal and skip-upper (triangular) products."""
     active = None
 
     def __init__(self):
@@ -294,7 +295,10 @@ def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, 
     if log is not None:
         e1.record()
         prods = sum(1 for i in range(na) for j in range(nb) if i + j <= order)
-        log.rows.append((d.M, d.N, d.K, prods, batch, e0, e1, log.tag))
+        # a causal product (or a square one whose upper tiles are skipped) does half the work
+        # of its M x N x K box: count batch x 1/2
+        eff = batch * (0.5 if (causal or skip_upper) else 1.0)
+        log.rows.append((d.M, d.N, d.K, prods, eff, e0, e1, log.tag))
     return C
 
 

@@ -798,6 +798,7 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
         codes = g["codes"].cpu().numpy()
         Wcur[name] = _hard_bf16(g["codes"], s16, bits[name], gs)
         stats["linears"].setdefault(name, {"bits": bits[name]})["err_gptq"] = float(g["err"].item())
+        stats.setdefault("warm_start", {})[name] = {"codes": codes, "scales": s16}
         if bits[name] == 8:
             shard[name] = {"codes": codes, "scales": s16, "bits": 8}
             return None

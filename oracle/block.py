@@ -250,12 +250,16 @@ def _hard_weight(codes, s16, bits, group_size):
 
 def quantize_block(h_seqs, W, bits, steps, layer=0, opt_seed=0, n_heads=14, n_kv=2,
                    group_size=64, damp=0.01, block_size=128, micro_batch=2, resamples=2,
-                   eps=1e-6):
+                   eps=1e-6, warm_start=None):
     """The block quantizer of staged.py:405-522 on the CPU: for each stage, Hessians of the
     linears' inputs under the weights hardened so far, GPTQ warm starts (fp16 scales), 200
     Lion steps with Philox noise keyed as the CUDA path keys it, hardening (argmax codes, fp16
     scales). h_seqs: bf16 [T, H] inputs of the calibration sequences; W: bf16 block weights.
-    Returns (shard {name: {codes, scales, bits}}, {stage: loss history}, {name: GPTQ codes})."""
+    warm_start {name: {codes, scales}}: continue from these GPTQ results instead of this chain's
+    own (which are still computed and returned), so that a comparison of the training stages
+    does not count a GPTQ near-tie twice.
+    Returns (shard {name: {codes, scales, bits}}, {stage: loss history},
+    {name: this chain's own GPTQ (codes, float16 scales)})."""
     from .gptq import quantize_gptq
     from .gsq import LinearState, train_linear
     Wf = {k: v.float() for k, v in W.items()}
@@ -266,10 +270,13 @@ def quantize_block(h_seqs, W, bits, steps, layer=0, opt_seed=0, n_heads=14, n_kv
 
     def gptq(name, H, pos):
         g = quantize_gptq(Wf[name].numpy(), H, bits[name], group_size, damp, block_size)
-        s16 = g["scales"].astype(np.float16)
-        gptq_codes[name] = g["codes"]
-        Wcur[name] = _hard_weight(g["codes"], s16, bits[name], group_size)
-        states[name] = LinearState(bits[name], g["codes"], s16, group_size, seed=seed + 10 * pos,
+        codes, s16 = g["codes"], g["scales"].astype(np.float16)
+        gptq_codes[name] = (codes, s16)
+        if warm_start is not None:
+            codes = np.asarray(warm_start[name]["codes"], dtype=np.uint8)
+            s16 = np.asarray(warm_start[name]["scales"], dtype=np.float16)
+        Wcur[name] = _hard_weight(codes, s16, bits[name], group_size)
+        states[name] = LinearState(bits[name], codes, s16, group_size, seed=seed + 10 * pos,
                                    linear_id=layer * 8 + pos)
         return states[name]
 

@@ -94,6 +94,13 @@ def test_down_proj_gptq_parity():
 
 
 def test_quantize_block_end_to_end_parity(c_oracle):
+    """quantize_block against the oracle's chain of the same steps. The GPTQ warm starts are
+    compared with the oracle's own solves on the oracle's own Hessians (codes >= 99.9 %); the
+    oracle chain then continues from the GPU's warm starts, so that the stages (training,
+    hardening, the forwards under the hardened weights that build the next stage's inputs and
+    targets) are compared without counting a GPTQ near-tie twice: the signed-scale choice of a
+    group whose two errors are within rounding of each other may go either way, and flips the
+    whole group's codes."""
     from tests.test_block_gpu import small_block
     from gsq_rco_mlx_b200.gsq.e2e import BlockConfig, LIN_ORDER
     from gsq_rco_mlx_b200.gsq.staged import BlockOpts, quantize_block
@@ -106,16 +113,22 @@ def test_quantize_block_end_to_end_parity(c_oracle):
     shard, stats, _ = quantize_block(h.to(DEV), {k: v.to(DEV) for k, v in W.items()}, bits,
                                      BlockOpts(steps=steps), layer=0, cfg=cfg, T=T, chunk_seqs=2,
                                      log=lambda *a: None)
-    shard_o, hist_o, _ = ob.quantize_block([h[i * T:(i + 1) * T] for i in range(N)], W, bits,
-                                           steps, layer=0)
+    warm = stats["warm_start"]
+    shard_o, hist_o, own = ob.quantize_block([h[i * T:(i + 1) * T] for i in range(N)], W, bits,
+                                             steps, layer=0, warm_start=warm)
+    fails = []
     for stage, names in ob.STAGE_LINEARS.items():
         loss = stats["stages"][stage]["soft_loss_last"]
         rloss = abs(loss - hist_o[stage][-1]) / hist_o[stage][-1]
         for n in names:
+            g_eq = (warm[n]["codes"] == own[n][0]).mean()
             eq = (shard[n]["codes"] == shard_o[n]["codes"]).mean()
             rs = _rel(shard[n]["scales"].astype(np.float32),
                       shard_o[n]["scales"].astype(np.float32))
-            print(f"{stage} {n}: codes {eq:.6f} scales {rs:.2e} loss {rloss:.2e}")
-            assert eq >= 0.999, (n, eq)
-            assert rs <= 1e-3, (n, rs)
-        assert rloss <= 1e-3, (stage, rloss)
+            print(f"{stage} {n}: gptq codes {g_eq:.6f}  final codes {eq:.6f} scales {rs:.2e} "
+                  f"loss {rloss:.2e}")
+            if g_eq < 0.999 or eq < 0.999 or rs > 1e-3:
+                fails.append((n, g_eq, eq, rs))
+        if rloss > 1e-3:
+            fails.append((stage, rloss))
+    assert not fails, fails
