@@ -92,6 +92,7 @@ struct GemmParams {
   int n_big;       // chunk accumulators in the TMEM ring
   int tiles_m, tiles_n;
   int n_fast;  // tile order: n fastest (A the larger operand) instead of m fastest
+  int causal_order;  // causal products: longest k-ranges first, in a snake over the CTAs
   int64_t total_tiles;
   int skip_upper;  // output tiles entirely above the diagonal (n >= m) are not computed
   int row_period;  // epi 1: rows with (row % row_period) == 0 have a zero residual
@@ -133,15 +134,36 @@ struct TileInfo {
 // Tile L of the round-robin order; false for a tile that skip_upper leaves out. The k-block
 // range: causal 1 = lower-triangular A (k < end of this row tile), causal 2 = upper-triangular A
 // (k >= start of this row tile).
+// Causal products (causal_order): the tiles of a row level (one row tile of every batch and
+// column tile) have the same k-range, so the order takes the levels from the longest k-range
+// to the shortest, and the CTAs walk the rounds of gridDim.x tiles alternately forwards and
+// backwards (a snake): a CTA that took a long tile in one round takes a short one in the next,
+// which bounds the causal tail (static round-robin otherwise leaves some CTAs 40 % above the
+// mean at the attention products' 16 row tiles).
 template <int BN>
 __device__ __forceinline__ bool tile_at(const GemmParams& p, int64_t L, TileInfo& t) {
-  const int64_t per = (int64_t)p.tiles_m * p.tiles_n;
-  const int64_t zk = L / per;
-  t.z = (int)(zk / p.splits);
-  t.ks = (int)(zk - (int64_t)t.z * p.splits);
-  const int rem = (int)(L - zk * per);
-  const int my = p.n_fast ? rem / p.tiles_n : rem % p.tiles_m;
-  const int nx = p.n_fast ? rem % p.tiles_n : rem / p.tiles_m;
+  int my, nx;
+  if (p.causal_order) {
+    const int64_t G = gridDim.x;
+    const int64_t r = L / G, pos = L - r * G;
+    const int64_t c = min(G, p.total_tiles - r * G);
+    const int64_t idx = r * G + ((r & 1) ? c - 1 - pos : pos);
+    const int64_t width = p.total_tiles / p.tiles_m;  // batch x tiles_n tiles per level
+    const int level = (int)(idx / width);
+    const int64_t rem = idx - (int64_t)level * width;
+    t.z = (int)(rem / p.tiles_n);
+    t.ks = 0;
+    nx = (int)(rem - (int64_t)t.z * p.tiles_n);
+    my = p.causal == 1 ? p.tiles_m - 1 - level : level;
+  } else {
+    const int64_t per = (int64_t)p.tiles_m * p.tiles_n;
+    const int64_t zk = L / per;
+    t.z = (int)(zk / p.splits);
+    t.ks = (int)(zk - (int64_t)t.z * p.splits);
+    const int rem = (int)(L - zk * per);
+    my = p.n_fast ? rem / p.tiles_n : rem % p.tiles_m;
+    nx = p.n_fast ? rem % p.tiles_n : rem / p.tiles_m;
+  }
   t.tile_m = my * BM;
   t.tile_n = nx * BN;
   if (p.skip_upper && t.tile_n >= t.tile_m + BM) return false;
@@ -1406,6 +1428,7 @@ static int launch(GemmParams& p, int batch, cudaStream_t st) {
   // single products: walk along the smaller operand first (its bytes M x K x na vs N x K x nb)
   p.n_fast = (batch == 1 && p.splits == 1 && !p.skip_upper && p.causal == 0 &&
               (int64_t)p.M * p.na > (int64_t)p.N * p.nb) ? 1 : 0;
+  p.causal_order = (p.causal != 0 && p.splits == 1 && !p.skip_upper) ? 1 : 0;
   const size_t smem = 1024 + (size_t)S * stage_bytes +
                       (p.tma_out ? (size_t)kEpiWarps * p.tma_bufs * kTmaBuf : (size_t)kStgBytes);
   static bool attr_set[2][7] = {{false}};

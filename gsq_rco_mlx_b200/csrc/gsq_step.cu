@@ -107,6 +107,50 @@ __global__ void sum_f64_kernel(const double* __restrict__ x, int n, double* out)
   }
 }
 
+// Block partials of sum (t0 + t1 + t2)[r, c] * G[r, c] over a [rows][cols] matrix held as bf16
+// terms (t1 / t2 may be null), products and sums in float64; one partial per block.
+__global__ void __launch_bounds__(256)
+dot_terms_kernel(const __nv_bfloat16* __restrict__ t0, const __nv_bfloat16* __restrict__ t1,
+                 const __nv_bfloat16* __restrict__ t2, int64_t ld_t, const float* __restrict__ G,
+                 int64_t ld_g, int rows, int cols, double* __restrict__ partials) {
+  __shared__ double sh[8];
+  const int64_t n = (int64_t)rows * cols;
+  double s = 0.0;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = e / cols, c = e - r * cols;
+    const int64_t it = r * ld_t + c;
+    float d = __bfloat162float(t0[it]);
+    if (t1) d = __fadd_rn(d, __bfloat162float(t1[it]));
+    if (t2) d = __fadd_rn(d, __bfloat162float(t2[it]));
+    s += (double)d * (double)G[r * ld_g + c];
+  }
+  s = warp_sum_d(s);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.0;
+    v = warp_sum_d(v);
+    if (threadIdx.x == 0) partials[blockIdx.x] = v;
+  }
+}
+
+// out[0] = scale * sum of partials[0..n) (one block, fixed order: deterministic)
+__global__ void scaled_sum_f64_kernel(const double* __restrict__ x, int n, double scale,
+                                      double* out) {
+  __shared__ double sh[32];
+  double s = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+  s = warp_sum_d(s);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.0;
+    v = warp_sum_d(v);
+    if (threadIdx.x == 0) out[0] = scale * v;
+  }
+}
+
 // out[z][c][r] = in[z][r][c] for bf16 matrices [rows][ld_in] -> [cols][ld_out]: 64 x 64 tiles
 // through shared memory, 16-byte row segments in and out when the strides allow (vec), single
 // elements otherwise. skip_upper: tiles whose 128-column block lies strictly above their 128-row
@@ -263,6 +307,25 @@ extern "C" int gsq_gather_split(const void* x, int src_bf16, int64_t ld_x, const
     gather_split_kernel<float><<<g, dim3(32, 8), 0, (cudaStream_t)stream>>>(
         (const float*)x, ld_x, seq, per_seq, seq_stride, offset, rows, cols, n_terms, t[0], t[1],
         t[2], ld_t, u[0], u[1], u[2], ld_u);
+  GSQ_CHECK_LAUNCH();
+  return GSQ_OK;
+}
+
+extern "C" int gsq_dot_terms(const void* t0, const void* t1, const void* t2, int64_t ld_t,
+                             const float* G, int64_t ld_g, int rows, int cols, double scale,
+                             double* partials, double* out, void* stream) {
+  if (!t0 || !G || !partials || !out || rows <= 0 || cols <= 0 || ld_t < cols || ld_g < cols)
+    return GSQ_EINVAL;
+  const int64_t n = (int64_t)rows * cols;
+  int64_t blocks = (n + 256 * 16 - 1) / (256 * 16);
+  if (blocks > 1024) blocks = 1024;
+  if (blocks < 1) blocks = 1;
+  cudaStream_t st = (cudaStream_t)stream;
+  dot_terms_kernel<<<(unsigned)blocks, 256, 0, st>>>(
+      (const __nv_bfloat16*)t0, (const __nv_bfloat16*)t1, (const __nv_bfloat16*)t2, ld_t, G,
+      ld_g, rows, cols, partials);
+  GSQ_CHECK_LAUNCH();
+  scaled_sum_f64_kernel<<<1, 256, 0, st>>>(partials, (int)blocks, scale, out);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }

@@ -163,11 +163,17 @@ class SoftLinear:
 
 class LinearStep:
     """The qk-stage step of the linears that read the same rows X [M, in] (staged.py:322-329).
-    Per resample r: R_r = X (w_bar_r - W)^T on the tensor cores (epilogue: loss partials and
-    R_r as bf16 terms), then G_r = 2 / (M out) R_r^T X with R_r and X read as MN-major operands
-    (their transposes, never stored). One fused pass per linear then runs
-    the backward, the resample mean, Lion, and the next step's soft weights and probabilities.
-    All GEMM operands are bf16 terms (three for float32 data, one for exactly-bf16 rows)."""
+
+    A linear's loss is mean((X D^T)^2) with D = w_bar - W, and its weight gradient is
+    2 / (M out) (X D^T)^T X = 2 / (M out) D (X^T X): both see X only through the micro-batch
+    Gram matrix Hm = X^T X [in, in]. Per step one tensor-core GEMM forms Hm (X read MN-major,
+    shared by every linear and resample; summed over the ranks under data parallelism); then
+    per linear and resample G_r = 2 / (M out) D_r Hm (D_r: the three bf16 terms the soft step
+    writes) and the loss sum D_r * (D_r Hm) = (M out / 2) sum D_r * G_r. At the qk shapes
+    (M = 4094 rows, in = 896) that is a third of the FLOPs of forming R = X D^T and R^T X. One
+    fused pass per linear then runs the backward, the resample mean, Lion, and the next step's
+    soft weights and probabilities. All GEMM operands are bf16 terms (three for float32 data,
+    one for exactly-bf16 rows)."""
 
     def __init__(self, lins, M, in_f, resamples, x_terms=3, M_total=None):
         """M: rows of this rank's micro-batch share; M_total: rows of the whole micro-batch (the
@@ -176,7 +182,7 @@ class LinearStep:
         self.lins, self.M, self.in_f, self.R = lins, int(M), int(in_f), int(resamples)
         self.M_total = int(M if M_total is None else M_total)
         self.nx = int(x_terms)
-        self.X = Terms(M, in_f, self.nx, dev)   # A of the residual GEMM, B of the gradient
+        self.X = Terms(M, in_f, self.nx, dev)   # read MN-major (as X^T) on both sides of Hm
         R = self.R
         self.Dbuf = {l.name: torch.zeros(R, 3, l.out_f, l.in_f, device=dev, dtype=torch.bfloat16)
                      for l in lins}
@@ -184,11 +190,11 @@ class LinearStep:
                            for r in range(R)] for l in lins}
         self.probs = {l.name: torch.zeros(R, l.K, l.d, device=dev, dtype=torch.float32)
                       for l in lins}
-        self.Rres = {l.name: Terms(M, l.out_f, 3, dev) for l in lins}
+        self.Hf = torch.empty(in_f, in_f, device=dev, dtype=torch.float32)
+        self.Hm = Terms(in_f, in_f, 3, dev)
         self.gflat, views = _flat_views(dev, [(R,) + l.shape for l in lins])
         self.grads = {l.name: v for l, v in zip(lins, views)}
-        tiles = max(((M + 127) // 128) * ((l.out_f + 127) // 128) for l in lins)
-        self.sq = torch.zeros(tiles, device=dev, dtype=torch.float64)
+        self.partials = torch.zeros(1024, device=dev, dtype=torch.float64)
         self.loss = torch.zeros(len(lins) * R, device=dev, dtype=torch.float64)
         self.seq = torch.zeros(64, device=dev, dtype=torch.int32)
         self.dev = dev
@@ -213,18 +219,26 @@ class LinearStep:
                 lin.soft(tau, kappa, t, r, noise_seed, w_ref=targets[lin.name], noise=noise,
                          terms=self.Dbuf[lin.name][r], probs=self.probs[lin.name][r])
 
-    def contract(self):
-        """Residuals, losses and weight gradients of every linear and resample."""
+    def contract(self, dp=None):
+        """Gram matrix of the micro-batch (summed over the ranks of ``dp``), then the weight
+        gradients and losses of every linear and resample (global: no further reduction)."""
+        from ..gemm import split_into
+        st = _lib.stream_ptr()
+        gemm(self.X, self.X, M=self.in_f, N=self.in_f, K=self.M, C=self.Hf, a_major=1,
+             b_major=1)
+        if dp is not None:
+            dp.allreduce(self.Hf)
+        split_into(self.Hf, self.Hm)
         for li, lin in enumerate(self.lins):
-            Rr, G = self.Rres[lin.name], self.grads[lin.name]
-            tiles = ((self.M + 127) // 128) * ((lin.out_f + 127) // 128)
+            G = self.grads[lin.name]
+            norm = self.M_total * lin.out_f
             for r in range(self.R):
-                gemm(self.X, self.D[lin.name][r], c_terms=Rr, sq_partial=self.sq)
+                gemm(self.D[lin.name][r], self.Hm, alpha=2.0 / norm, C=G[r])
+                t = self.D[lin.name][r].t
                 slot = self.loss[li * self.R + r:li * self.R + r + 1]
-                _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(slot),
-                          _lib.stream_ptr())
-                gemm(Rr, self.X, M=lin.out_f, N=self.in_f, K=self.M,
-                     alpha=2.0 / (self.M_total * lin.out_f), C=G[r], a_major=1, b_major=1)
+                _lib.call("gsq_dot_terms", _lib.ptr(t[0]), _lib.ptr(t[1]), _lib.ptr(t[2]),
+                          lin.in_f, _lib.ptr(G[r]), lin.in_f, lin.out_f, lin.in_f, norm / 2.0,
+                          _lib.ptr(self.partials), _lib.ptr(slot), st)
 
     def update(self, targets, t, tau, kappa, opts, noise_seed, nxt=None, noise_of=None):
         """Fused backward + Lion of step t; nxt = (t1, tau1, kappa1) also runs step t1's forward."""
@@ -280,8 +294,7 @@ def train_linears(lins, x_all, targets, n_seqs, opts: BlockOpts, seed, noise_of=
         tau, kappa = gs_schedules(t, opts.steps)
         idx = dp.draw(rng, n_seqs, m)
         step.stage(flat, idx, p1 - p0, T, p0)
-        step.contract()
-        dp.allreduce(step.gflat, step.loss)
+        step.contract(dp)
         nxt = (t + 1, *gs_schedules(t + 1, opts.steps)) if t + 1 < opts.steps else None
         step.update(targets, t, tau, kappa, opts, noise_seed, nxt=nxt, noise_of=noise_of)
         hist[t].copy_(step.loss)  # a device copy; summed on the host at the end

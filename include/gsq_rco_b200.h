@@ -236,6 +236,15 @@ int gsq_transpose_bf16(const void *in, int rows, int cols, int64_t ld_in, int64_
 int gsq_head_group_sum_t(const float *dv, int S, int nh, int rep, int T, void *o0, void *o1,
                          void *o2, int64_t ld_o, void *stream);
 
+/* out[0] = scale * sum over r < rows, c < cols of (t0 + t1 + t2)[r][c] * G[r][c] for a matrix
+ * held as bf16 terms (t1, t2 may be NULL; rows of ld_t elements) and a float32 G (rows of ld_g),
+ * products and sums in float64, deterministic. partials: >= 1024 doubles. The qk-stage loss
+ * mean((X D^T)^2) = sum D (D X^T X) / (M out) from D = w_bar - W and G = 2 D X^T X / (M out)
+ * (src/gsq_rco/gsq/staged.py:327-328). */
+int gsq_dot_terms(const void *t0, const void *t1, const void *t2, int64_t ld_t, const float *G,
+                  int64_t ld_g, int rows, int cols, double scale, double *partials, double *out,
+                  void *stream);
+
 /* out[0] = sum of x[0..n) in float64 (one block; the loss from per-tile partials). */
 int gsq_sum_f64(const double *x, int n, double *out, void *stream);
 

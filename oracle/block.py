@@ -250,14 +250,16 @@ def _hard_weight(codes, s16, bits, group_size):
 
 def quantize_block(h_seqs, W, bits, steps, layer=0, opt_seed=0, n_heads=14, n_kv=2,
                    group_size=64, damp=0.01, block_size=128, micro_batch=2, resamples=2,
-                   eps=1e-6, warm_start=None):
+                   eps=1e-6, warm_start=None, follow=None):
     """The block quantizer of staged.py:405-522 on the CPU: for each stage, Hessians of the
     linears' inputs under the weights hardened so far, GPTQ warm starts (fp16 scales), 200
     Lion steps with Philox noise keyed as the CUDA path keys it, hardening (argmax codes, fp16
     scales). h_seqs: bf16 [T, H] inputs of the calibration sequences; W: bf16 block weights.
     warm_start {name: {codes, scales}}: continue from these GPTQ results instead of this chain's
     own (which are still computed and returned), so that a comparison of the training stages
-    does not count a GPTQ near-tie twice.
+    does not count a GPTQ near-tie twice. follow {name: {codes, scales}}: after each stage,
+    record this chain's hardened result but continue from these (another run's hardened
+    weights), so that every stage starts from the same weights as that run's.
     Returns (shard {name: {codes, scales, bits}}, {stage: loss history},
     {name: this chain's own GPTQ (codes, float16 scales)})."""
     from .gptq import quantize_gptq
@@ -283,8 +285,11 @@ def quantize_block(h_seqs, W, bits, steps, layer=0, opt_seed=0, n_heads=14, n_kv
     def harden(name):
         st = states[name]
         codes, s16 = st.hard_codes(), st.stored_scales()
-        Wcur[name] = _hard_weight(codes, s16, st.bits, group_size)
         shard[name] = {"codes": codes, "scales": s16, "bits": st.bits}
+        if follow is not None:
+            codes = np.asarray(follow[name]["codes"], dtype=np.uint8)
+            s16 = np.asarray(follow[name]["scales"], dtype=np.float16)
+        Wcur[name] = _hard_weight(codes, s16, st.bits, group_size)
 
     def fwd(Wb):
         return [block_hard(h, {k: v.float() for k, v in Wb.items()}, n_heads, n_kv, eps)

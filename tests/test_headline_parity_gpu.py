@@ -94,28 +94,30 @@ def test_down_proj_gptq_parity():
 
 
 def test_quantize_block_end_to_end_parity(c_oracle):
-    """quantize_block against the oracle's chain of the same steps. The GPTQ warm starts are
-    compared with the oracle's own solves on the oracle's own Hessians (codes >= 99.9 %); the
-    oracle chain then continues from the GPU's warm starts, so that the stages (training,
-    hardening, the forwards under the hardened weights that build the next stage's inputs and
-    targets) are compared without counting a GPTQ near-tie twice: the signed-scale choice of a
-    group whose two errors are within rounding of each other may go either way, and flips the
-    whole group's codes."""
+    """quantize_block against the oracle's chain of the same steps, stage by stage. The GPTQ
+    warm starts are compared with the oracle's own solves on the oracle's own Hessians; then
+    the oracle trains each stage from the GPU's warm starts and continues from the GPU's
+    hardened weights at each stage boundary, so that each stage (its inputs and targets from
+    the forwards under the hardened weights, 200 Lion steps, hardening) is compared from the
+    same state: a GPTQ near-tie (a group's signed-scale choice whose two errors are within
+    rounding of each other, which flips the whole group's codes) or one flipped hard code is
+    not carried into the next stage's comparison. 48 sequences x 128 positions give 6096 rows,
+    more than the widest input (4864), so every Hessian has full rank."""
     from tests.test_block_gpu import small_block
     from gsq_rco_mlx_b200.gsq.e2e import BlockConfig, LIN_ORDER
     from gsq_rco_mlx_b200.gsq.staged import BlockOpts, quantize_block
     cfg = BlockConfig(hidden=896, n_heads=14, n_kv=2, inter=4864)
     W = small_block(0, H=896, nh=14, nkv=2, inter=4864, scale=0.02)
-    N, T, steps = 4, 128, 200
+    N, T, steps = 48, 128, 200
     g = torch.Generator().manual_seed(11)
     h = (0.02 * torch.randn(N * T, cfg.hidden, generator=g)).bfloat16()
     bits = {n: 3 for n in LIN_ORDER}
     shard, stats, _ = quantize_block(h.to(DEV), {k: v.to(DEV) for k, v in W.items()}, bits,
-                                     BlockOpts(steps=steps), layer=0, cfg=cfg, T=T, chunk_seqs=2,
+                                     BlockOpts(steps=steps), layer=0, cfg=cfg, T=T, chunk_seqs=8,
                                      log=lambda *a: None)
     warm = stats["warm_start"]
     shard_o, hist_o, own = ob.quantize_block([h[i * T:(i + 1) * T] for i in range(N)], W, bits,
-                                             steps, layer=0, warm_start=warm)
+                                             steps, layer=0, warm_start=warm, follow=shard)
     fails = []
     for stage, names in ob.STAGE_LINEARS.items():
         loss = stats["stages"][stage]["soft_loss_last"]
