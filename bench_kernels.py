@@ -77,6 +77,8 @@ def mlp_gemms(dev, g):
             DR, DIN, C=grad_d, a_major=1, b_major=1)),
         "B2 swiglu bwd (3x3)": (6 * 2 * M * I * H, lambda: gemm(
             DR, Dd, b_major=1, epi=3, aux0=gg, aux1=uu, c_terms=DGU, ct_up_rows=I)),
+        "B2 swiglu bwd (3x3) bn 64": (6 * 2 * M * I * H, lambda: gemm(
+            DR, Dd, b_major=1, epi=3, aux0=gg, aux1=uu, c_terms=DGU, ct_up_rows=I, bn=64)),
         "B3 gradWgu (3x1, MN-major)": (3 * 2 * 2 * I * H * M, b3),
         "hard swiglu bf16 (1x1)": (2 * R * 2 * I * H, lambda: gemm(
             MNt, Wg1, B2=Wu1, epi=5, c_terms=Terms(R, I, 1, ld=I, tensors=[d_in]))),

@@ -1505,7 +1505,7 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   for (int i = 0; i < d->nct; ++i)
     if (!d->ct[i] || ((uintptr_t)d->ct[i] & 15)) return GSQ_EINVAL;
   if (epi == 1 && !d->target) return GSQ_EINVAL;
-  if ((epi == 2 || epi == 3 || epi == 6) && (!d->aux0 || !d->aux1 || d->bn != 128))
+  if ((epi == 2 || epi == 3 || epi == 6) && (!d->aux0 || !d->aux1 || (d->bn != 128 && epi != 3)))
     return GSQ_EINVAL;
   if (epi == 5 && (!d->aux0) != (!d->aux1)) return GSQ_EINVAL;
   if (epi == 6 && (d->ncs > 1 || d->nct > 1)) return GSQ_EINVAL;
@@ -1634,6 +1634,7 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
     if (epi == 0) return tc::launch<64, 0>(p, d->batch, st);
     if (epi == 1) return tc::launch<64, 1>(p, d->batch, st);
     if (epi == 4) return tc::launch<64, 4>(p, d->batch, st);
+    if (epi == 3) return tc::launch<64, 3>(p, d->batch, st);
     return GSQ_EINVAL;
   }
   switch (epi) {

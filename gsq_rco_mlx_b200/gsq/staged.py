@@ -749,7 +749,7 @@ def _hard_bf16(codes_t, scales16, bits, group_size):
 
 
 def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None, T=None,
-                   chunk_seqs=8, log=print, noise_of=None, timer=None, dp=None):
+                   chunk_seqs=8, log=print, noise_of=None, timer=None, dp=None, record=None):
     """Quantize the seven linears of one block on the calibration stream (staged.py:405-522).
 
     h: bf16 CUDA [N*T, H], the block inputs of the N calibration sequences (the quantized
@@ -760,6 +760,8 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
     dp: a DataParallel over the ranks of a process group (each rank computes its position
     window of every micro-batch sequence; the stage gradients are summed over the ranks); the
     Hessian passes and GPTQ run on every rank alike, so every rank returns the same result.
+    record: a dict that receives record["warm_start"][name] = {"codes", "scales"}, the GPTQ
+    warm start of each linear (host arrays).
     """
     from .e2e import BlockConfig, BlockWeights, LIN_ORDER, Qwen2Block
     from .gptq import gptq_factor, quantize_gptq
@@ -811,7 +813,8 @@ def quantize_block(h, W: dict, bits: dict, opts: BlockOpts, layer: int, cfg=None
         codes = g["codes"].cpu().numpy()
         Wcur[name] = _hard_bf16(g["codes"], s16, bits[name], gs)
         stats["linears"].setdefault(name, {"bits": bits[name]})["err_gptq"] = float(g["err"].item())
-        stats.setdefault("warm_start", {})[name] = {"codes": codes, "scales": s16}
+        if record is not None:
+            record.setdefault("warm_start", {})[name] = {"codes": codes, "scales": s16}
         if bits[name] == 8:
             shard[name] = {"codes": codes, "scales": s16, "bits": 8}
             return None

@@ -93,7 +93,8 @@ def test_linear_windows_sum_to_full_step():
         st.contract()
     torch.cuda.synchronize()
     assert _rel(parts[0].gflat + parts[1].gflat, full.gflat) < 2e-6
-    assert _rel(parts[0].loss + parts[1].loss, full.loss) < 1e-9
+    # the qk loss is sum D * G of the float32 gradients: float32 accuracy
+    assert _rel(parts[0].loss + parts[1].loss, full.loss) < 1e-6
 
 
 def _dp_worker(rank, world, port, q):

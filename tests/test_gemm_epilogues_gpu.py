@@ -141,3 +141,25 @@ def test_auto_split_policy():
     assert auto_split(896, 896, 4094) > 1        # 49 tiles
     assert auto_split(128, 896, 4094) > 1        # 7 tiles
     assert auto_split(4096, 4864, 896) == 1      # 1216 tiles
+
+
+def test_swiglu_backward_bn64_equals_bn128():
+    """The SwiGLU-backward epilogue on 128 x 64 tiles (more TMEM chunk slots ahead of the
+    epilogue) writes the same [dg | du] row terms as on 128 x 128 tiles, bit for bit: each
+    output element is folded from the same k-block chunks in the same order."""
+    from gsq_rco_mlx_b200.gemm import Terms, gemm
+    torch.manual_seed(3)
+    M, W, Nout = 700, 384, 256
+    g_in = torch.randn(M, W, device=DEV)
+    u_in = torch.randn(M, W, device=DEV)
+    dR = torch.randn(M, Nout, device=DEV)
+    Wd = 0.05 * torch.randn(Nout, W, device=DEV)
+    outs = []
+    for bn in (128, 64):
+        rows = Terms(M, 2 * W)
+        gemm(terms_of(dR), terms_of(Wd.T.contiguous()), epi=3, aux0=g_in, aux1=u_in,
+             c_terms=rows, ct_up_rows=W, bn=bn)
+        check()
+        outs.append([t.clone() for t in rows.t])
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)

@@ -112,10 +112,11 @@ def test_quantize_block_end_to_end_parity(c_oracle):
     g = torch.Generator().manual_seed(11)
     h = (0.02 * torch.randn(N * T, cfg.hidden, generator=g)).bfloat16()
     bits = {n: 3 for n in LIN_ORDER}
+    rec = {}
     shard, stats, _ = quantize_block(h.to(DEV), {k: v.to(DEV) for k, v in W.items()}, bits,
                                      BlockOpts(steps=steps), layer=0, cfg=cfg, T=T, chunk_seqs=8,
-                                     log=lambda *a: None)
-    warm = stats["warm_start"]
+                                     log=lambda *a: None, record=rec)
+    warm = rec["warm_start"]
     shard_o, hist_o, own = ob.quantize_block([h[i * T:(i + 1) * T] for i in range(N)], W, bits,
                                              steps, layer=0, warm_start=warm, follow=shard)
     fails = []

@@ -1,0 +1,108 @@
+"""The vo and mlp stage optimisers at the block's widths (hidden 896, 14 / 2 heads of 64,
+SwiGLU 4864) for 200 Lion steps, against the oracle (src/gsq_rco/gsq/staged.py:332-354,
+357-400): both sides train from the same warm start on the same cached stage inputs (the GPU
+forward's bf16 hn, A, mn, h1, Y); the vo stage's attention probabilities come from each side's
+own computation from hn and the hard q / k weights. 4 sequences x 256 positions keep the
+oracle's float64 autograd to minutes."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import block as ob
+from oracle import gsq as ogsq
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+N, T, STEPS = 4, 256, 200
+
+
+@pytest.fixture
+def c_oracle():
+    prev = ogsq.set_backend("c")
+    yield
+    ogsq.set_backend(prev)
+
+
+def _rel(a, b):
+    return float(np.linalg.norm(np.asarray(a, np.float64) - b) / np.linalg.norm(b))
+
+
+def _setup(seed):
+    from tests.test_block_gpu import small_block
+    from gsq_rco_mlx_b200.gsq.e2e import BlockConfig, BlockWeights, Qwen2Block
+    cfg = BlockConfig(hidden=896, n_heads=14, n_kv=2, inter=4864)
+    W = small_block(seed, H=896, nh=14, nkv=2, inter=4864, scale=0.02)
+    h = (0.02 * torch.randn(N * T, cfg.hidden, generator=torch.Generator().manual_seed(seed))
+         ).bfloat16()
+    blk = Qwen2Block(cfg, N, T)
+    Wd = BlockWeights({k: v.to(DEV) for k, v in W.items()})
+    return cfg, W, Wd, blk, h.to(DEV)
+
+
+def _report(pairs, hist, hist_o, tag):
+    out = []
+    for lin, st in pairs:
+        rl = _rel(lin.logits.cpu().numpy(), st.logits)
+        rs = _rel(lin.scales.cpu().numpy(), st.scales)
+        eq = (lin.hard_codes() == st.hard_codes()).mean()
+        print(f"{tag} {lin.name}: logits {rl:.2e} scales {rs:.2e} codes {eq:.6f}")
+        out.append((lin.name, rl, rs, eq))
+    rloss = abs(hist[-1] - hist_o[-1]) / hist_o[-1]
+    print(f"{tag} loss {rloss:.2e}")
+    return out, rloss
+
+
+def test_mlp_stage_full_width(c_oracle):
+    from tests.test_stages_gpu import _pair
+    from gsq_rco_mlx_b200.gsq.staged import BlockOpts, MLPStep, train_stage
+    cfg, W, Wd, blk, h = _setup(1)
+    Y = blk.forward(h, Wd).clone()
+    mn, h1 = blk.mn.clone(), blk.h1.clone()
+    pairs = [_pair(n, W[n].float().numpy(), 3, i + 4) for i, n in
+             enumerate(("gate_proj", "up_proj", "down_proj"))]
+    step = MLPStep([p[0] for p in pairs], cfg, 2, T, 2)
+    hist = train_stage(step, lambda idx: (mn, h1, Y, idx), N, BlockOpts(steps=STEPS), seed=5,
+                       noise_seed=9)[0]
+    seqs = lambda x: [x[i * T:(i + 1) * T].float().cpu() for i in range(N)]
+    hist_o = ob.train_mlp([p[1] for p in pairs], seqs(mn), seqs(h1), seqs(Y), STEPS, seed=5,
+                          noise_seed=9)
+    res, rloss = _report(pairs, hist, hist_o, "mlp")
+    for name, rl, rs, eq in res:
+        assert rl <= 1e-3 and rs <= 1e-3 and eq >= 0.999, (name, rl, rs, eq)
+    assert rloss <= 1e-3, rloss
+
+
+def test_vo_stage_full_width(c_oracle):
+    from tests.test_stages_gpu import _pair
+    from gsq_rco_mlx_b200.gemm import gemm
+    from gsq_rco_mlx_b200.gsq.e2e import wterms
+    from gsq_rco_mlx_b200.gsq.staged import BlockOpts, VOStep, _bf16_rows, train_stage
+    cfg, W, Wd, blk, h = _setup(2)
+    A = torch.empty(N * T, cfg.hidden, device=DEV, dtype=torch.bfloat16)
+    blk.forward(h, Wd, attn_out=A)
+    hn = blk.hn.clone()
+    qkw = (cfg.n_heads + cfg.n_kv) * cfg.head_dim
+    qk = torch.empty(N * T, qkw, device=DEV, dtype=torch.bfloat16)
+    gemm(_bf16_rows(hn), wterms(Wd.qk), epi=4, bias=Wd.qk_bias, c_terms=_bf16_rows(qk))
+    pairs = [_pair(n, W[n].float().numpy(), 3, i + 2) for i, n in enumerate(("v_proj", "o_proj"))]
+    step = VOStep([p[0] for p in pairs], cfg, 2, T, 2, Wd.W["v_bias"])
+    hist = train_stage(step, lambda idx: (hn, A, qk, idx), N, BlockOpts(steps=STEPS), seed=6,
+                       noise_seed=11)[0]
+    seqs = lambda x: [x[i * T:(i + 1) * T].float().cpu() for i in range(N)]
+    Wf = {k: v.float() for k, v in W.items()}
+    hn_s = seqs(hn)
+    Ps = [ob.attention_probs(x, Wf, cfg.n_heads, cfg.n_kv) for x in hn_s]
+    # the GPU's probabilities of sequence 0 against the oracle's, for the record
+    step.stage(hn, A, qk, [0, 1])
+    torch.cuda.synchronize()
+    Pg = step.P.t[0].float().cpu().view(2, cfg.n_heads, T, -1)[0, :, :, :T]
+    mask = torch.tril(torch.ones(T, T, dtype=torch.bool))
+    same = float((Pg == Ps[0])[:, mask].float().mean())
+    rel_p = float((Pg - Ps[0]).norm() / Ps[0].norm())
+    print(f"vo P: bitwise equal {same:.6f}, relative difference {rel_p:.2e}")
+    hist_o = ob.train_vo([p[1] for p in pairs], hn_s, seqs(A), lambda t, idx: [Ps[i] for i in idx],
+                         Wf["v_bias"], STEPS, cfg.n_heads, cfg.n_kv, seed=6, noise_seed=11)
+    res, rloss = _report(pairs, hist, hist_o, "vo")
+    for name, rl, rs, eq in res:
+        assert rl <= 1e-3 and rs <= 1e-3 and eq >= 0.999, (name, rl, rs, eq)
+    assert rloss <= 1e-3, rloss
