@@ -68,11 +68,16 @@ __host__ __device__ inline NoiseKey make_noise_key(uint64_t seed, uint32_t linea
 
 // u = (b + 0.5) 2^-24 as one fused multiply-add (b < 2^24 converts exactly; scaling by a power
 // of two commutes with rounding, so this equals rounding b + 0.5 and then scaling), clipped to
-// [1e-7, 1 - 1e-7]; g = -log(-log u).
+// [1e-7, 1 - 1e-7]; g = -log(-log u). The inner logarithm needs relative accuracy (-log u is as
+// small as 1e-7 near u = 1) and is the accurate logf; the outer one, of E = -log u in
+// [1e-7, 16.2], needs absolute accuracy only (g enters the softmax additively) and is the
+// hardware base-2 logarithm (__log2f, absolute error about 2^-22 in log2 E) times ln 2: one
+// special-function instruction instead of a second accurate logarithm, the soft passes' largest
+// instruction count per weight.
 __device__ __forceinline__ float gumbel_from_24(uint32_t b) {
   float u = __fmaf_rn((float)b, 5.9604644775390625e-08f, 2.98023223876953125e-08f);
   u = fminf(fmaxf(u, 1e-7f), 1.0f - 1e-7f);
-  return -logf(-logf(u));
+  return __fmul_rn(-0.693147180559945309f, __log2f(-logf(u)));
 }
 
 template <int K>
