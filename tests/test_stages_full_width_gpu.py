@@ -52,7 +52,15 @@ def _report(pairs, hist, hist_o, tag):
     return out, rloss
 
 
-def test_mlp_stage_full_width(c_oracle):
+def _host_noise(seed):
+    """Host-supplied Gumbel planes (the oracle's own draws) for the GPU steps."""
+    from oracle import gsq_fast
+    return lambda t, r, lin: torch.as_tensor(
+        gsq_fast.gumbel_planes(seed, lin.linear_id, t, r, lin.d, lin.K), device=DEV)
+
+
+@pytest.mark.parametrize("noise", ["host", "philox"])
+def test_mlp_stage_full_width(c_oracle, noise):
     from tests.test_stages_gpu import _pair
     from gsq_rco_mlx_b200.gsq.staged import BlockOpts, MLPStep, train_stage
     cfg, W, Wd, blk, h = _setup(1)
@@ -62,17 +70,18 @@ def test_mlp_stage_full_width(c_oracle):
              enumerate(("gate_proj", "up_proj", "down_proj"))]
     step = MLPStep([p[0] for p in pairs], cfg, 2, T, 2)
     hist = train_stage(step, lambda idx: (mn, h1, Y, idx), N, BlockOpts(steps=STEPS), seed=5,
-                       noise_seed=9)[0]
+                       noise_seed=9, noise_of=_host_noise(9) if noise == "host" else None)[0]
     seqs = lambda x: [x[i * T:(i + 1) * T].float().cpu() for i in range(N)]
     hist_o = ob.train_mlp([p[1] for p in pairs], seqs(mn), seqs(h1), seqs(Y), STEPS, seed=5,
                           noise_seed=9)
-    res, rloss = _report(pairs, hist, hist_o, "mlp")
+    res, rloss = _report(pairs, hist, hist_o, f"mlp ({noise} noise)")
     for name, rl, rs, eq in res:
         assert rl <= 1e-3 and rs <= 1e-3 and eq >= 0.999, (name, rl, rs, eq)
     assert rloss <= 1e-3, rloss
 
 
-def test_vo_stage_full_width(c_oracle):
+@pytest.mark.parametrize("noise", ["host", "philox"])
+def test_vo_stage_full_width(c_oracle, noise):
     from tests.test_stages_gpu import _pair
     from gsq_rco_mlx_b200.gemm import gemm
     from gsq_rco_mlx_b200.gsq.e2e import wterms
@@ -87,7 +96,7 @@ def test_vo_stage_full_width(c_oracle):
     pairs = [_pair(n, W[n].float().numpy(), 3, i + 2) for i, n in enumerate(("v_proj", "o_proj"))]
     step = VOStep([p[0] for p in pairs], cfg, 2, T, 2, Wd.W["v_bias"])
     hist = train_stage(step, lambda idx: (hn, A, qk, idx), N, BlockOpts(steps=STEPS), seed=6,
-                       noise_seed=11)[0]
+                       noise_seed=11, noise_of=_host_noise(11) if noise == "host" else None)[0]
     seqs = lambda x: [x[i * T:(i + 1) * T].float().cpu() for i in range(N)]
     Wf = {k: v.float() for k, v in W.items()}
     hn_s = seqs(hn)
@@ -102,7 +111,7 @@ def test_vo_stage_full_width(c_oracle):
     print(f"vo P: bitwise equal {same:.6f}, relative difference {rel_p:.2e}")
     hist_o = ob.train_vo([p[1] for p in pairs], hn_s, seqs(A), lambda t, idx: [Ps[i] for i in idx],
                          Wf["v_bias"], STEPS, cfg.n_heads, cfg.n_kv, seed=6, noise_seed=11)
-    res, rloss = _report(pairs, hist, hist_o, "vo")
+    res, rloss = _report(pairs, hist, hist_o, f"vo ({noise} noise)")
     for name, rl, rs, eq in res:
         assert rl <= 1e-3 and rs <= 1e-3 and eq >= 0.999, (name, rl, rs, eq)
     assert rloss <= 1e-3, rloss
