@@ -115,3 +115,35 @@ def test_vo_stage_full_width(c_oracle, noise):
     for name, rl, rs, eq in res:
         assert rl <= 1e-3 and rs <= 1e-3 and eq >= 0.999, (name, rl, rs, eq)
     assert rloss <= 1e-3, rloss
+
+
+def test_mlp_step_gradients_full_width():
+    """One mlp-stage step at the block's widths: the GPU's weight gradients dL/dw_bar against
+    float64 autograd of the reference loss on the GPU's own soft weights (the sum of the bf16
+    terms the soft step wrote) and caches: the contraction chain alone, no training."""
+    from tests.test_stages_gpu import _pair
+    from gsq_rco_mlx_b200.gsq.staged import MLPStep
+    cfg, W, Wd, blk, h = _setup(1)
+    Y = blk.forward(h, Wd).clone()
+    mn, h1 = blk.mn.clone(), blk.h1.clone()
+    lins = [_pair(n, W[n].float().numpy(), 3, i + 4)[0] for i, n in
+            enumerate(("gate_proj", "up_proj", "down_proj"))]
+    step = MLPStep(lins, cfg, 2, T, 2)
+    step.first_forward(0, 1.0, 300.0, 9)
+    idx = [1, 2]
+    step.stage(mn, h1, Y, idx)
+    step.contract()
+    torch.cuda.synchronize()
+    rows = lambda x: torch.cat([x[i * T + 1:(i + 1) * T].float().cpu() for i in idx])
+    for r in range(2):
+        w = [sum(t.double() for t in step.Dbuf[l.name][r].cpu()) for l in lins]
+        loss, gg, gu, gd = ob.mlp_loss_and_grads(rows(mn), rows(h1), rows(Y), *w)
+        got = [step.grad_gu[0, r], step.grad_gu[1, r], step.grad_d[r]]
+        for name, g_ref, g in zip(("gate", "up", "down"), (gg, gu, gd), got):
+            g = g.double().cpu().numpy()
+            rel = float(np.linalg.norm(g - g_ref) / np.linalg.norm(g_ref))
+            print(f"mlp step gradient {name} r={r}: relative error {rel:.2e}")
+            assert rel < 1e-5, (name, r, rel)
+        l_gpu = float(step.loss[r].item()) / step.count
+        print(f"mlp step loss r={r}: {l_gpu:.6e} vs {loss:.6e}")
+        assert abs(l_gpu - loss) <= 1e-6 * loss
