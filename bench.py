@@ -347,7 +347,7 @@ def run_block(args):
         del h, h_dev, h_host
         torch.cuda.empty_cache()
         res["config"].update(measure_gptq_rco(dev, world, barrier, max_over_ranks))
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_block()
     if rank == 0:
         print(json.dumps(res), flush=True)
@@ -575,7 +575,7 @@ def run_gptq(args):
         "gpu_launches": int(launches),
         "clocks": clk,
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline_gptq()
     if rank == 0:
         print(json.dumps(out), flush=True)
@@ -712,7 +712,7 @@ def run_rco(args):
         "gpu_launches": int(launches),
         "clocks": clk,
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline_rco()
     if rank == 0:
         print(json.dumps(out), flush=True)
@@ -940,7 +940,7 @@ def run_eval(args):
                              "once)"},
         "clocks": clk,
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline_eval()
     if rank == 0:
         print(json.dumps(out), flush=True)
@@ -1259,7 +1259,7 @@ def run_linear(args):
                      if "hbm_gbs" in peaks else "fallback 6650 GB/s"},
         "clocks": clk,
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_linear(W, X, lin_codes=g["codes"].cpu().numpy(),
                                                   s16=g["scales"].cpu().numpy().astype(np.float16),
                                                   n_steps=2)
