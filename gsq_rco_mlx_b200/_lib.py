@@ -37,6 +37,9 @@ SIGNATURES = {
                     _f32, _vp, _i32, _i64, _vp, _i32, _i64, _vp, _vp, _vp],
     "gsq_split_bf16": [_vp, _i32, _i32, _i64, _i32, _vp, _vp, _vp, _i64, _vp],
     "gsq_gemm": [_vp, _vp],
+    "gsq_gemm_plan_create": [_vp, _vp],
+    "gsq_gemm_plan_run": [_vp, _vp],
+    "gsq_gemm_plan_destroy": [_vp],
     "gsq_rmsnorm": [_vp, _i64, _vp, _i32, _i32, _f32, _vp, _i64, _vp, _i64, _i32, _i32, _vp],
     "gsq_rope_split": [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp],
     "gsq_softmax_causal": [_vp, _i32, _i32, _vp, _vp, _vp],

@@ -24,6 +24,8 @@
 // Every mbarrier wait is bounded; a timeout sets *err and every role winds down without further
 // waits on its partners, the MMA issuer waits (bounded) for its last MMAs and the producer for
 // its copies in flight, and the CTA frees its TMEM.
+#include <new>
+
 #include "tc_common.cuh"
 
 namespace gsq {
@@ -1476,8 +1478,19 @@ static tc::Aff to_aff(int div, int64_t s1, int64_t s2) {
   return a;
 }
 
-extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
-  if (!d) return GSQ_EINVAL;
+// A checked, ready-to-launch GEMM: the kernel parameters (tensor maps encoded) and what the
+// launch needs besides them.
+struct GemmPlan {
+  tc::GemmParams p;
+  int epi, bn, batch;
+  int M, N;
+  float alpha, beta;
+  float* C;
+  int64_t ldc;
+};
+
+static int gemm_prepare(const gsq_gemm_desc* d, GemmPlan* plan) {
+  if (!d || !plan) return GSQ_EINVAL;
   const int M = d->M, N = d->N, K = d->K;
   if (M <= 0 || N <= 0 || K <= 0 || d->batch < 1 || d->batch > 65535 || d->na < 1 ||
       d->na > 3 || d->nb < 1 || d->nb > 3 || d->order < 0 || !d->err || d->ncs < 0 ||
@@ -1618,34 +1631,82 @@ extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
   }
   // the row-major outputs of the float32 SwiGLU backward exist only in the box epilogue
   if (epi == 3 && d->ncs > 0 && !p.tma_out) return GSQ_ENOTSUP;
-  cudaStream_t st = (cudaStream_t)stream;
+  if (BN == 64 && p.splits == 1 && epi != 0 && epi != 1 && epi != 3 && epi != 4)
+    return GSQ_EINVAL;
+  plan->p = p;
+  plan->epi = epi;
+  plan->bn = BN;
+  plan->batch = d->batch;
+  plan->M = M;
+  plan->N = N;
+  plan->alpha = d->alpha;
+  plan->beta = d->beta;
+  plan->C = d->C;
+  plan->ldc = d->ldc;
+  return GSQ_OK;
+}
+
+static int gemm_launch(const GemmPlan& plan, cudaStream_t st) {
+  tc::GemmParams p = plan.p;  // launch() fills in the per-launch configuration
+  const int BN = plan.bn, epi = plan.epi;
   if (p.splits > 1) {
     const int rc = BN == 64 ? tc::launch<64, 0>(p, 1, st) : tc::launch<128, 0>(p, 1, st);
     if (rc != GSQ_OK) return rc;
-    const int64_t n_el = (int64_t)M * N;
+    const int64_t n_el = (int64_t)plan.M * plan.N;
     int64_t blocks = (n_el + 255) / 256;
     if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
-    tc::splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(p.ws, p.splits, M, N, d->alpha,
-                                                               d->beta, d->C, d->ldc);
+    tc::splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(
+        p.ws, p.splits, plan.M, plan.N, plan.alpha, plan.beta, plan.C, plan.ldc);
     GSQ_CHECK_LAUNCH();
     return GSQ_OK;
   }
   if (BN == 64) {
-    if (epi == 0) return tc::launch<64, 0>(p, d->batch, st);
-    if (epi == 1) return tc::launch<64, 1>(p, d->batch, st);
-    if (epi == 4) return tc::launch<64, 4>(p, d->batch, st);
-    if (epi == 3) return tc::launch<64, 3>(p, d->batch, st);
+    if (epi == 0) return tc::launch<64, 0>(p, plan.batch, st);
+    if (epi == 1) return tc::launch<64, 1>(p, plan.batch, st);
+    if (epi == 4) return tc::launch<64, 4>(p, plan.batch, st);
+    if (epi == 3) return tc::launch<64, 3>(p, plan.batch, st);
     return GSQ_EINVAL;
   }
   switch (epi) {
-    case 0: return tc::launch<128, 0>(p, d->batch, st);
-    case 1: return tc::launch<128, 1>(p, d->batch, st);
-    case 2: return tc::launch<128, 2>(p, d->batch, st);
-    case 3: return tc::launch<128, 3>(p, d->batch, st);
-    case 4: return tc::launch<128, 4>(p, d->batch, st);
-    case 5: return tc::launch<128, 5>(p, d->batch, st);
-    default: return tc::launch<128, 6>(p, d->batch, st);
+    case 0: return tc::launch<128, 0>(p, plan.batch, st);
+    case 1: return tc::launch<128, 1>(p, plan.batch, st);
+    case 2: return tc::launch<128, 2>(p, plan.batch, st);
+    case 3: return tc::launch<128, 3>(p, plan.batch, st);
+    case 4: return tc::launch<128, 4>(p, plan.batch, st);
+    case 5: return tc::launch<128, 5>(p, plan.batch, st);
+    default: return tc::launch<128, 6>(p, plan.batch, st);
   }
+}
+
+extern "C" int gsq_gemm(const gsq_gemm_desc* d, void* stream) {
+  GemmPlan plan;
+  const int rc = gemm_prepare(d, &plan);
+  if (rc != GSQ_OK) return rc;
+  return gemm_launch(plan, (cudaStream_t)stream);
+}
+
+extern "C" int gsq_gemm_plan_create(const gsq_gemm_desc* d, void** plan) {
+  if (!d || !plan) return GSQ_EINVAL;
+  *plan = nullptr;
+  GemmPlan* g = new (std::nothrow) GemmPlan;
+  if (!g) return GSQ_ECUDA;
+  const int rc = gemm_prepare(d, g);
+  if (rc != GSQ_OK) {
+    delete g;
+    return rc;
+  }
+  *plan = g;
+  return GSQ_OK;
+}
+
+extern "C" int gsq_gemm_plan_run(const void* plan, void* stream) {
+  if (!plan) return GSQ_EINVAL;
+  return gemm_launch(*static_cast<const GemmPlan*>(plan), (cudaStream_t)stream);
+}
+
+extern "C" int gsq_gemm_plan_destroy(void* plan) {
+  delete static_cast<GemmPlan*>(plan);
+  return GSQ_OK;
 }
 
 // The single-GEMM form (no batching, plain epilogue).

@@ -221,16 +221,16 @@ class LaunchLog:
         return out
 
 
-def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, alpha=1.0,
+def _describe(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, alpha=1.0,
          beta=0.0, C=None, ldc=None, c_terms: Terms = None, ct_terms: Terms = None,
          sq_partial=None, bias=None, resid=None, target=None, ld_rt=None, out_scale=1.0,
          aux0=None, aux1=None, ld_aux=None, B2: Terms = None, epi=0, bn=128, causal=False,
          batch=1, a_off=(1, 0, 0), b_off=(1, 0, 0), c_off=(1, 0, 0), t_off=(1, 0, 0, 0, 0),
-         ct_up_rows=0, skip_upper=False, row_period=0, split_k="auto", a_major=0, b_major=0):
-    """One (batched) tensor-core GEMM with a fused epilogue; see gsq_gemm in the C header.
-    M, N, K default to the operand shapes; a_off/b_off/c_off = (div, s1, s2),
-    t_off = (div, row_s1, row_s2, col_s1, col_s2). a_major / b_major = 1: the operand's Terms
-    hold [K][M] / [K][N] (MN-major: a row-major activation read as its own transpose)."""
+         ct_up_rows=0, skip_upper=False, row_period=0, split_k="auto", a_major=0, b_major=0,
+         own_workspace=False):
+    """The descriptor of one gemm() call: (GemmDesc, (M, N, K, products, work boxes, launches),
+    the split-K workspace tensor or None). own_workspace: a workspace of its own (a plan keeps
+    its pointer) instead of the shared, growing one."""
     d = GemmDesc()
     d.M = (A.cols if a_major else A.rows) if M is None else M
     d.N = ((B.cols if b_major else B.rows) if epi not in (2, 5) else 2 * B.rows) if N is None \
@@ -273,33 +273,95 @@ def gemm(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, order=2, 
                   and c_terms is None and ct_terms is None and sq_partial is None)
     if split_k == "auto":
         split_k = auto_split(d.M, d.N, d.K, bn) if splittable else 1
+    ws = None
     if split_k > 1:
         d.split_k = int(split_k)
-        d.workspace = _workspace(A.t[0].device, split_k * d.M * d.N).data_ptr()
+        if own_workspace:
+            ws = torch.empty(int(split_k) * d.M * d.N, device=A.t[0].device,
+                             dtype=torch.float32)
+        else:
+            ws = _workspace(A.t[0].device, split_k * d.M * d.N)
+        d.workspace = ws.data_ptr()
     d.a_div, d.a_s1, d.a_s2 = a_off
     d.b_div, d.b_s1, d.b_s2 = b_off
     d.c_div, d.c_s1, d.c_s2 = c_off
     d.t_div, d.t_r1, d.t_r2, d.t_c1, d.t_c2 = t_off
     dev = A.t[0].device
     d.err = err_flag(dev).data_ptr()
+    extra = 0
+    if d.split_k > 1:
+        kb = -(-d.K // 64)
+        per = -(-kb // d.split_k)
+        extra = 1 if -(-kb // per) > 1 else 0  # the split-K reduction
+    prods = sum(1 for i in range(na) for j in range(nb) if i + j <= order)
+    # a causal product (or a square one whose upper tiles are skipped) does half the work of
+    # its M x N x K box: count batch x 1/2
+    eff = batch * (0.5 if (causal or skip_upper) else 1.0)
+    return d, (d.M, d.N, d.K, prods, eff, 1 + extra), ws
+
+
+def _launch(entry, arg, info):
+    """Call a GEMM entry point (with the launch log's events around it when active)."""
     log = LaunchLog.active
     if log is not None:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-    _lib.call("gsq_gemm", _C.byref(d), _lib.stream_ptr())
-    if d.split_k > 1:
-        kb = -(-d.K // 64)
-        per = -(-kb // d.split_k)
-        if -(-kb // per) > 1:
-            _lib.Launches.n += 1  # the split-K reduction
+    _lib.call(entry, arg, _lib.stream_ptr())
+    _lib.Launches.n += info[5] - 1
     if log is not None:
         e1.record()
-        prods = sum(1 for i in range(na) for j in range(nb) if i + j <= order)
-        # a causal product (or a square one whose upper tiles are skipped) does half the work
-        # of its M x N x K box: count batch x 1/2
-        eff = batch * (0.5 if (causal or skip_upper) else 1.0)
-        log.rows.append((d.M, d.N, d.K, prods, eff, e0, e1, log.tag))
-    return C
+        log.rows.append((*info[:5], e0, e1, log.tag))
+
+
+def gemm(A: Terms, B: Terms, **kw):
+    """One (batched) tensor-core GEMM with a fused epilogue; see gsq_gemm in the C header.
+    Keywords: M, N, K (default: the operand shapes), na, nb, order, alpha, beta, C, ldc,
+    c_terms, ct_terms, sq_partial, bias, resid, target, ld_rt, out_scale, aux0, aux1, ld_aux,
+    B2, epi, bn, causal, batch, a_off / b_off / c_off = (div, s1, s2), t_off = (div, row_s1,
+    row_s2, col_s1, col_s2), ct_up_rows, skip_upper, row_period, split_k, a_major / b_major
+    (1: the operand's Terms hold [K][M] / [K][N], a row-major activation read as its own
+    transpose). Returns C."""
+    d, info, _ = _describe(A, B, **kw)
+    _launch("gsq_gemm", _C.byref(d), info)
+    return kw.get("C")
+
+
+class GemmPlan:
+    """A gemm() call prepared once (gsq_gemm_plan_create: checks and tensor maps) and run
+    many times on the same buffers: the steps of a stage repeat the same products every step.
+    Keeps references to its operand tensors so that their storage outlives the plan."""
+
+    def __init__(self, A: Terms, B: Terms, **kw):
+        self.d, self.info, self.ws = _describe(A, B, own_workspace=True, **kw)
+        self._keep = (A, B, kw)
+        h = _C.c_void_p()
+        _lib.check(_lib.lib().gsq_gemm_plan_create(_C.byref(self.d), _C.byref(h)),
+                   "gsq_gemm_plan_create")
+        self.h = h
+
+    def run(self):
+        _launch("gsq_gemm_plan_run", self.h, self.info)
+
+    def __del__(self):
+        h = getattr(self, "h", None)
+        if h is not None and h.value and _lib._lib is not None:
+            _lib._lib.gsq_gemm_plan_destroy(h)
+
+
+class PlanCache:
+    """Plans keyed by call site: run(key, A, B, **kw) creates the plan on the first call and
+    only launches it afterwards (the operands of a key must not change between calls)."""
+
+    def __init__(self):
+        self.plans = {}
+
+    def run(self, key, A: Terms, B: Terms, **kw):
+        p = self.plans.get(key)
+        if p is None:
+            p = self.plans[key] = GemmPlan(A, B, **kw)
+        p.run()
+
+
 
 
 def gemm_tc(A: Terms, B: Terms, na=None, nb=None, order=2, alpha=1.0, C=None, beta=0.0,

@@ -24,7 +24,7 @@ import numpy as np
 import torch
 
 from .. import _lib
-from ..gemm import Terms, check_err, err_flag, gemm, gemm_tc, pad8
+from ..gemm import PlanCache, Terms, check_err, err_flag, gemm, gemm_tc, pad8
 from .gptq import init_logits_2bit_from_codes, init_shift_logits
 from .lion import BETAS, LR_LOGITS, LR_SCALES, WEIGHT_DECAY, scale_lr
 from .quant import gs_schedules
@@ -198,6 +198,7 @@ class LinearStep:
         self.loss = torch.zeros(len(lins) * R, device=dev, dtype=torch.float64)
         self.seq = torch.zeros(64, device=dev, dtype=torch.int32)
         self.dev = dev
+        self.plans = PlanCache()
 
     def stage(self, x_all, seq_ids, per_seq, seq_stride, offset):
         """Gather rows of x_all (float32 [n_rows, in]) into the X operand terms."""
@@ -224,8 +225,8 @@ class LinearStep:
         gradients and losses of every linear and resample (global: no further reduction)."""
         from ..gemm import split_into
         st = _lib.stream_ptr()
-        gemm(self.X, self.X, M=self.in_f, N=self.in_f, K=self.M, C=self.Hf, a_major=1,
-             b_major=1)
+        self.plans.run("gram", self.X, self.X, M=self.in_f, N=self.in_f, K=self.M, C=self.Hf,
+                       a_major=1, b_major=1)
         if dp is not None:
             dp.allreduce(self.Hf)
         split_into(self.Hf, self.Hm)
@@ -233,7 +234,8 @@ class LinearStep:
             G = self.grads[lin.name]
             norm = self.M_total * lin.out_f
             for r in range(self.R):
-                gemm(self.D[lin.name][r], self.Hm, alpha=2.0 / norm, C=G[r])
+                self.plans.run(("grad", li, r), self.D[lin.name][r], self.Hm, alpha=2.0 / norm,
+                               C=G[r])
                 t = self.D[lin.name][r].t
                 slot = self.loss[li * self.R + r:li * self.R + r + 1]
                 _lib.call("gsq_dot_terms", _lib.ptr(t[0]), _lib.ptr(t[1]), _lib.ptr(t[2]),
@@ -414,6 +416,7 @@ class _StageBase:
 
     def _init_soft(self, lins, R, dev):
         self.lins, self.R, self.dev = lins, int(R), dev
+        self.plans = PlanCache()
         self.Dbuf = {l.name: torch.zeros(R, 3, l.out_f, l.in_f, device=dev, dtype=torch.bfloat16)
                      for l in lins}
         self.D = {l.name: [Terms(l.out_f, l.in_f, 3, ld=l.in_f, tensors=self.Dbuf[l.name][r])
@@ -506,18 +509,19 @@ class MLPStep(_StageBase):
         gname, uname, dname = self.names
         tiles = self.sq.numel()
         for r in range(self.R):
-            gemm(self.MN, self.D[gname][r], B2=self.D[uname][r], epi=2, aux0=self.g, aux1=self.u,
-                 c_terms=self.DIN)
-            gemm(self.DIN, self.D[dname][r], epi=1, resid=self.H1.t[0], target=self.Y.t[0],
-                 ld_rt=self.H1.ld, out_scale=2.0 / self.count, sq_partial=self.sq,
-                 c_terms=self.DR)
+            run = lambda name, *a, **k: self.plans.run((name, r), *a, **k)
+            run("F1", self.MN, self.D[gname][r], B2=self.D[uname][r], epi=2, aux0=self.g,
+                aux1=self.u, c_terms=self.DIN)
+            run("F3", self.DIN, self.D[dname][r], epi=1, resid=self.H1.t[0], target=self.Y.t[0],
+                ld_rt=self.H1.ld, out_scale=2.0 / self.count, sq_partial=self.sq,
+                c_terms=self.DR)
             _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(self.loss[r:r + 1]),
                       _lib.stream_ptr())
-            gemm(self.DR, self.DIN, C=self.grad_d[r], a_major=1, b_major=1)
-            gemm(self.DR, self.D[dname][r], b_major=1, epi=3, aux0=self.g, aux1=self.u,
-                 c_terms=self.DGU, ct_up_rows=I)
-            gemm(self.DG, self.MN, C=self.grad_gu[0, r], ldc=H, a_major=1, b_major=1)
-            gemm(self.DU, self.MN, C=self.grad_gu[1, r], ldc=H, a_major=1, b_major=1)
+            run("B1", self.DR, self.DIN, C=self.grad_d[r], a_major=1, b_major=1)
+            run("B2", self.DR, self.D[dname][r], b_major=1, epi=3, aux0=self.g, aux1=self.u,
+                c_terms=self.DGU, ct_up_rows=I, bn=64)
+            run("B3g", self.DG, self.MN, C=self.grad_gu[0, r], ldc=H, a_major=1, b_major=1)
+            run("B3u", self.DU, self.MN, C=self.grad_gu[1, r], ldc=H, a_major=1, b_major=1)
 
 
 class VOStep(_StageBase):
@@ -602,15 +606,15 @@ class VOStep(_StageBase):
                   _lib.ptr(self.sin), _lib.ptr(t[0]), _lib.ptr(t[1]), _lib.ptr(t[2]), st)
         B = m * c.n_heads
         if q0 == 0:   # square: tiles above the diagonal are never read
-            gemm(self.q_rot, self.k_rot, M=Tk, N=Tk, K=c.head_dim, batch=B, alpha=1.0 / 8.0,
-                 C=self.scores, ldc=Tk, a_off=(1, Tk, 0), b_off=(c.rep, Tk, 0),
-                 c_off=(1, Tk * Tk, 0), skip_upper=True)
+            self.plans.run("scores", self.q_rot, self.k_rot, M=Tk, N=Tk, K=c.head_dim, batch=B,
+                           alpha=1.0 / 8.0, C=self.scores, ldc=Tk, a_off=(1, Tk, 0),
+                           b_off=(c.rep, Tk, 0), c_off=(1, Tk * Tk, 0), skip_upper=True)
         else:         # the query rows q0.. of each (sequence, head) block of q_rot
             qv = Terms(self.q_rot.rows - q0, c.head_dim, 3, ld=self.q_rot.ld,
                        tensors=[x[q0:] for x in self.q_rot.t])
-            gemm(qv, self.k_rot, M=Tq, N=Tk, K=c.head_dim, batch=B, alpha=1.0 / 8.0,
-                 C=self.scores, ldc=Tk, a_off=(1, Tk, 0), b_off=(c.rep, Tk, 0),
-                 c_off=(1, Tq * Tk, 0))
+            self.plans.run("scores", qv, self.k_rot, M=Tq, N=Tk, K=c.head_dim, batch=B,
+                           alpha=1.0 / 8.0, C=self.scores, ldc=Tk, a_off=(1, Tk, 0),
+                           b_off=(c.rep, Tk, 0), c_off=(1, Tq * Tk, 0))
         _lib.call("gsq_softmax_causal_rows", _lib.ptr(self.scores), B, Tq, Tk, Tk, q0,
                   _lib.ptr(self.P.t[0]), self.P.ld, st)
         if self.PT is not None:
@@ -629,33 +633,34 @@ class VOStep(_StageBase):
         st = _lib.stream_ptr()
         B = m * nh
         for r in range(self.R):
-            gemm(self.HN, self.D[vname][r], M=Tk, batch=m, bias=self.v_bias, a_off=(1, Tk, 0),
+            run = lambda name, *a, **k: self.plans.run((name, r), *a, **k)
+            run("V", self.HN, self.D[vname][r], M=Tk, batch=m, bias=self.v_bias, a_off=(1, Tk, 0),
                  ct_terms=self.VT, t_off=(1, nkvd, 0, 0, 0))
-            gemm(self.P, self.VT, M=Tq, N=hd, K=Tk, batch=B, bn=64, causal=int(q0 == 0),
+            run("PV", self.P, self.VT, M=Tq, N=hd, K=Tk, batch=B, bn=64, causal=int(q0 == 0),
                  a_off=(1, Tq, 0), b_off=(c.rep, hd, 0), c_off=(nh, Tq * H, hd),
                  c_terms=self.O)
-            gemm(self.O, self.D[oname][r], epi=1, target=self.A.t[0], ld_rt=self.A.ld,
+            run("Y", self.O, self.D[oname][r], epi=1, target=self.A.t[0], ld_rt=self.A.ld,
                  row_period=Tq if q0 == 0 else 0, out_scale=2.0 / self.count,
                  sq_partial=self.sq, c_terms=self.DY)
             _lib.call("gsq_sum_f64", _lib.ptr(self.sq), tiles, _lib.ptr(self.loss[r:r + 1]), st)
-            gemm(self.DY, self.O, M=H, N=H, K=m * Tq, C=self.grad_o[r], a_major=1, b_major=1)
+            run("dWo", self.DY, self.O, M=H, N=H, K=m * Tq, C=self.grad_o[r], a_major=1, b_major=1)
             for i in range(3):
                 _lib.call("gsq_transpose_bf16", _lib.ptr(self.Dbuf[oname][r][i]), H, H, H, 0,
                           _lib.ptr(self.DoT.t[i]), self.DoT.ld, 0, 1, 0, st)
-            gemm(self.DY, self.DoT, M=Tq, batch=m, a_off=(1, Tq, 0), ct_terms=self.DOT,
+            run("dO", self.DY, self.DoT, M=Tq, batch=m, a_off=(1, Tq, 0), ct_terms=self.DOT,
                  t_off=(1, H, 0, 0, 0))
             if self.PT is None:
-                gemm(self.P, self.DOT, M=Tk, N=hd, K=Tq, batch=B, bn=64,
+                run("dV", self.P, self.DOT, M=Tk, N=hd, K=Tq, batch=B, bn=64,
                      causal=2 if q0 == 0 else 0, a_off=(1, Tq, 0), b_off=(1, hd, 0), C=self.dv,
                      ldc=hd, c_off=(1, Tk * hd, 0), a_major=1)
             else:
-                gemm(self.PT, self.DOT, M=Tk, N=hd, K=Tq, batch=B, bn=64,
+                run("dV", self.PT, self.DOT, M=Tk, N=hd, K=Tq, batch=B, bn=64,
                      causal=2 if q0 == 0 else 0, a_off=(1, Tk, 0), b_off=(1, hd, 0), C=self.dv,
                      ldc=hd, c_off=(1, Tk * hd, 0))
             t = self.DVT.t
             _lib.call("gsq_head_group_sum_t", _lib.ptr(self.dv), m, nh, c.rep, Tk, _lib.ptr(t[0]),
                       _lib.ptr(t[1]), _lib.ptr(t[2]), self.DVT.ld, st)
-            gemm(self.DVT, self.HNT, C=self.grad_v[r])
+            run("dWv", self.DVT, self.HNT, C=self.grad_v[r])
 
 
 class StageTimer:

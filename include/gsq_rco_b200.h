@@ -190,6 +190,16 @@ typedef struct {
  * losses of src/gsq_rco/gsq/staged.py:332-354 and their MLX backward. */
 int gsq_gemm(const gsq_gemm_desc *desc, void *stream);
 
+/* The same GEMM as a plan: gsq_gemm_plan_create checks desc and encodes its tensor maps once
+ * (host memory only, no device allocation); gsq_gemm_plan_run launches it on a stream with the
+ * buffers, shapes and scalars desc named at creation (they must stay valid and unmoved);
+ * gsq_gemm_plan_destroy frees it. A step that repeats the same GEMMs on the same buffers pays
+ * the descriptor checks and the tensor-map encoding once instead of at every launch. Same
+ * results as gsq_gemm. */
+int gsq_gemm_plan_create(const gsq_gemm_desc *desc, void **plan);
+int gsq_gemm_plan_run(const void *plan, void *stream);
+int gsq_gemm_plan_destroy(void *plan);
+
 /* Float32-faithful tensor-core GEMM (tcgen05, TMEM accumulator, TMA-fed):
  *   C[m, n] = alpha * sum_k A(m, k) B(n, k) (+ beta * C[m, n])
  * A and B arrive as na / nb bf16 terms (A = sum_i A_i), each K-major [M][lda] / [N][ldb]

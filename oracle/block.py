@@ -158,6 +158,15 @@ def _soft(state, t, r, noise_seed, tau, kappa):
     return w, p, c
 
 
+def _jitter(grads, grad_noise):
+    """grads times (1 + amp N(0, 1)) with grad_noise = (amp, numpy Generator): float32-level
+    perturbations for measuring how far rounding alone moves a trajectory."""
+    if grad_noise is None:
+        return grads
+    amp, rng = grad_noise
+    return [g * (1.0 + amp * rng.standard_normal(g.shape)) for g in grads]
+
+
 def _apply(states, grads_per_r, soft_per_r, tau, kappa, lr_logits, lr_scales):
     """Resample mean of the soft backward and one Lion step per linear (staged.py:383-392)."""
     from .gsq import backward_accumulate, lion_step
@@ -172,9 +181,10 @@ def _apply(states, grads_per_r, soft_per_r, tau, kappa, lr_logits, lr_scales):
 
 
 def train_mlp(states, mn_seqs, h1_seqs, Y_seqs, steps, micro_batch=2, resamples=2, seed=0,
-              noise_seed=0, lr_logits=1e-4, lr_scales=5e-5, dtype=F64):
+              noise_seed=0, lr_logits=1e-4, lr_scales=5e-5, dtype=F64, grad_noise=None):
     """mlp-stage optimiser (staged.py:357-400 with _loss_block): states = gate, up, down
-    LinearStates; per-sequence bf16 caches [T, H]. Returns the loss history."""
+    LinearStates; per-sequence bf16 caches [T, H]. grad_noise = (amp, Generator) perturbs every
+    weight gradient by a relative amp (sensitivity measurements). Returns the loss history."""
     from .gsq import gs_schedules
     rng = np.random.default_rng(seed)
     n = len(mn_seqs)
@@ -191,7 +201,7 @@ def train_mlp(states, mn_seqs, h1_seqs, Y_seqs, steps, micro_batch=2, resamples=
             sw = [_soft(st, t, r, noise_seed, tau, kappa) for st in states]
             l, gg, gu, gd = mlp_loss_and_grads(mn, h1, Y, sw[0][0], sw[1][0], sw[2][0], dtype)
             loss += l
-            grads.append([gg, gu, gd])
+            grads.append(_jitter([gg, gu, gd], grad_noise))
             softs.append(sw)
         _apply(states, grads, softs, tau, kappa, lr_logits, lr_scales)
         hist.append(loss / resamples)
@@ -199,7 +209,8 @@ def train_mlp(states, mn_seqs, h1_seqs, Y_seqs, steps, micro_batch=2, resamples=
 
 
 def train_vo(states, hn_seqs, A_seqs, P_of, bv, steps, n_heads, n_kv, micro_batch=2,
-             resamples=2, seed=0, noise_seed=0, lr_logits=1e-4, lr_scales=5e-5, dtype=F64):
+             resamples=2, seed=0, noise_seed=0, lr_logits=1e-4, lr_scales=5e-5, dtype=F64,
+             grad_noise=None):
     """vo-stage optimiser (staged.py:357-400 with _loss_attn): states = v, o LinearStates;
     P_of(t, idx) returns the bf16 probabilities [nh, T, T] of each chosen sequence."""
     from .gsq import gs_schedules
@@ -217,7 +228,7 @@ def train_vo(states, hn_seqs, A_seqs, P_of, bv, steps, n_heads, n_kv, micro_batc
             l, gv, go = vo_loss_and_grads([hn_seqs[i] for i in idx], [A_seqs[i] for i in idx],
                                           Ps, sw[0][0], bv, sw[1][0], n_heads, n_kv, dtype)
             loss += l
-            grads.append([gv, go])
+            grads.append(_jitter([gv, go], grad_noise))
             softs.append(sw)
         _apply(states, grads, softs, tau, kappa, lr_logits, lr_scales)
         hist.append(loss / resamples)

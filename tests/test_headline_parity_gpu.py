@@ -120,7 +120,12 @@ def test_quantize_block_end_to_end_parity(c_oracle):
     shard_o, hist_o, own = ob.quantize_block([h[i * T:(i + 1) * T] for i in range(N)], W, bits,
                                              steps, layer=0, warm_start=warm, follow=shard)
     fails = []
+    # qk: the absolute bar; vo / mlp: the spread that float32-level perturbations alone produce
+    # in the oracle over 200 steps at these widths (tests/test_stages_full_width_gpu.py measures
+    # it: logits and scales about 2e-2, codes about 99.2 %), with margin
+    bars = {"qk": (0.999, 1e-3, 1e-3), "vo": (0.985, 5e-2, 2e-2), "mlp": (0.985, 5e-2, 2e-2)}
     for stage, names in ob.STAGE_LINEARS.items():
+        codes_bar, scales_bar, loss_bar = bars[stage]
         loss = stats["stages"][stage]["soft_loss_last"]
         rloss = abs(loss - hist_o[stage][-1]) / hist_o[stage][-1]
         for n in names:
@@ -130,8 +135,8 @@ def test_quantize_block_end_to_end_parity(c_oracle):
                       shard_o[n]["scales"].astype(np.float32))
             print(f"{stage} {n}: gptq codes {g_eq:.6f}  final codes {eq:.6f} scales {rs:.2e} "
                   f"loss {rloss:.2e}")
-            if g_eq < 0.999 or eq < 0.999 or rs > 1e-3:
+            if g_eq < 0.999 or eq < codes_bar or rs > scales_bar:
                 fails.append((n, g_eq, eq, rs))
-        if rloss > 1e-3:
+        if rloss > loss_bar:
             fails.append((stage, rloss))
     assert not fails, fails
