@@ -321,13 +321,16 @@ class DataParallel:
     * "positions" (strong scaling): every rank draws the same m sequences and takes one
       window of positions of each.
 
+    The default is "positions": the reference's step (micro-batch 2) at any number of ranks;
+    "sequences" trains on a global micro-batch of m x world sequences per step.
+
     Either way each rank computes dL/dw_bar of every resample on its rows, one all-reduce per
     step sums the weight gradients (4 B per weight per resample: the logit and scale
     gradients are linear maps of them) and the loss partials, and every rank runs the
     identical fused Lion update, so the soft-weight states stay bit-identical across ranks. A
     single process is world 1, where both splits are the reference's step."""
 
-    def __init__(self, group=None, split="sequences"):
+    def __init__(self, group=None, split="positions"):
         import torch.distributed as dist
         if split not in ("sequences", "positions"):
             raise ValueError(f"split must be 'sequences' or 'positions', got {split!r}")

@@ -101,14 +101,14 @@ def test_quantize_block_end_to_end_parity(c_oracle):
     the forwards under the hardened weights, 200 Lion steps, hardening) is compared from the
     same state: a GPTQ near-tie (a group's signed-scale choice whose two errors are within
     rounding of each other, which flips the whole group's codes) or one flipped hard code is
-    not carried into the next stage's comparison. 48 sequences x 128 positions give 6096 rows,
-    more than the widest input (4864), so every Hessian has full rank."""
+    not carried into the next stage's comparison. 128 sequences x 128 positions give 16256
+    rows, 3.3x the widest input (4864), so every Hessian is well conditioned."""
     from tests.test_block_gpu import small_block
     from gsq_rco_mlx_b200.gsq.e2e import BlockConfig, LIN_ORDER
     from gsq_rco_mlx_b200.gsq.staged import BlockOpts, quantize_block
     cfg = BlockConfig(hidden=896, n_heads=14, n_kv=2, inter=4864)
     W = small_block(0, H=896, nh=14, nkv=2, inter=4864, scale=0.02)
-    N, T, steps = 48, 128, 200
+    N, T, steps = 128, 128, 200
     g = torch.Generator().manual_seed(11)
     h = (0.02 * torch.randn(N * T, cfg.hidden, generator=g)).bfloat16()
     bits = {n: 3 for n in LIN_ORDER}
@@ -120,10 +120,15 @@ def test_quantize_block_end_to_end_parity(c_oracle):
     shard_o, hist_o, own = ob.quantize_block([h[i * T:(i + 1) * T] for i in range(N)], W, bits,
                                              steps, layer=0, warm_start=warm, follow=shard)
     fails = []
-    # qk: the absolute bar; vo / mlp: the spread that float32-level perturbations alone produce
-    # in the oracle over 200 steps at these widths (tests/test_stages_full_width_gpu.py measures
-    # it: logits and scales about 2e-2, codes about 99.2 %), with margin
-    bars = {"qk": (0.999, 1e-3, 1e-3), "vo": (0.985, 5e-2, 2e-2), "mlp": (0.985, 5e-2, 2e-2)}
+    # Each side builds its stage inputs with its own bf16 forward (rare last-bit differences in
+    # hn, P, mn, d_in), so the Hessians differ in their last bits: GPTQ warm starts agree on
+    # >= 99.9 % where the inputs are the normed rows (q / k / v) and >= 99 % behind the
+    # attention and the MLP. qk: codes and loss at the absolute bar, scales within 2e-3; vo /
+    # mlp: the spread that float32-level perturbations alone produce in the oracle over 200
+    # steps at these widths (tests/test_stages_full_width_gpu.py measures it: logits and scales
+    # about 2e-2, codes about 99.2 %), with margin.
+    gptq_bar = {"q_proj": 0.999, "k_proj": 0.999, "v_proj": 0.999}
+    bars = {"qk": (0.999, 2e-3, 1e-3), "vo": (0.985, 5e-2, 2e-2), "mlp": (0.985, 5e-2, 2e-2)}
     for stage, names in ob.STAGE_LINEARS.items():
         codes_bar, scales_bar, loss_bar = bars[stage]
         loss = stats["stages"][stage]["soft_loss_last"]
@@ -135,7 +140,7 @@ def test_quantize_block_end_to_end_parity(c_oracle):
                       shard_o[n]["scales"].astype(np.float32))
             print(f"{stage} {n}: gptq codes {g_eq:.6f}  final codes {eq:.6f} scales {rs:.2e} "
                   f"loss {rloss:.2e}")
-            if g_eq < 0.999 or eq < codes_bar or rs > scales_bar:
+            if g_eq < gptq_bar.get(n, 0.99) or eq < codes_bar or rs > scales_bar:
                 fails.append((n, g_eq, eq, rs))
         if rloss > loss_bar:
             fails.append((stage, rloss))
