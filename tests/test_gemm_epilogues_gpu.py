@@ -163,3 +163,23 @@ def test_swiglu_backward_bn64_equals_bn128():
         outs.append([t.clone() for t in rows.t])
     for a, b in zip(*outs):
         assert torch.equal(a, b)
+
+
+def test_plan_runs_equal_single_calls():
+    """A GemmPlan (checks and tensor maps built once) run twice gives the bits of gemm() on the
+    same operands, also when the operands' contents change between runs."""
+    from gsq_rco_mlx_b200.gemm import GemmPlan, gemm
+    torch.manual_seed(5)
+    M, N, K = 300, 260, 1000
+    A, B = torch.randn(M, K, device=DEV), torch.randn(N, K, device=DEV)
+    At, Bt = terms_of(A), terms_of(B)
+    ref, got = torch.zeros(M, N, device=DEV), torch.zeros(M, N, device=DEV)
+    plan = GemmPlan(At, Bt, C=got, alpha=0.5)
+    for _ in range(2):
+        gemm(At, Bt, C=ref, alpha=0.5)
+        plan.run()
+        check()
+        assert torch.equal(ref, got)
+        A2 = torch.randn(M, K, device=DEV)
+        for dst, src in zip(At.t, terms_of(A2).t):
+            dst.copy_(src)
