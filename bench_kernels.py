@@ -79,6 +79,19 @@ def mlp_gemms(dev, g):
             DR, Dd, b_major=1, epi=3, aux0=gg, aux1=uu, c_terms=DGU, ct_up_rows=I)),
         "B2 swiglu bwd (3x3) bn 64": (6 * 2 * M * I * H, lambda: gemm(
             DR, Dd, b_major=1, epi=3, aux0=gg, aux1=uu, c_terms=DGU, ct_up_rows=I, bn=64)),
+        "B2 bn 64, 1 small acc": (6 * 2 * M * I * H, lambda: gemm(
+            DR, Dd, b_major=1, epi=3, aux0=gg, aux1=uu, c_terms=DGU, ct_up_rows=I, bn=64,
+            small_bufs=1)),
+        "B2 bn 128, 1 small acc": (6 * 2 * M * I * H, lambda: gemm(
+            DR, Dd, b_major=1, epi=3, aux0=gg, aux1=uu, c_terms=DGU, ct_up_rows=I,
+            small_bufs=1)),
+        "F1 1 small acc": (3 * 2 * M * 2 * I * H, lambda: gemm(
+            MN, Dg, B2=Du, epi=2, aux0=gg, aux1=uu, c_terms=DIN, small_bufs=1)),
+        "F3 1 small acc": (6 * 2 * M * H * I, lambda: gemm(
+            DIN, Dd, epi=1, resid=H1.t[0], target=Y.t[0], ld_rt=H1.ld, out_scale=1e-3,
+            sq_partial=sq, c_terms=DR, small_bufs=1)),
+        "B1 1 small acc": (6 * 2 * H * I * M, lambda: gemm(
+            DR, DIN, C=grad_d, a_major=1, b_major=1, small_bufs=1)),
         "B3 gradWgu (3x1, MN-major)": (3 * 2 * 2 * I * H * M, b3),
         "hard swiglu bf16 (1x1)": (2 * R * 2 * I * H, lambda: gemm(
             MNt, Wg1, B2=Wu1, epi=5, c_terms=Terms(R, I, 1, ld=I, tensors=[d_in]))),

@@ -95,6 +95,7 @@ struct GemmParams {
   int tiles_m, tiles_n;
   int n_fast;  // tile order: n fastest (A the larger operand) instead of m fastest
   int causal_order;  // causal products: longest k-ranges first, in a snake over the CTAs
+  int small_bufs;    // 1 or 2 TMEM accumulators for a tile's cross products (see launch)
   int64_t total_tiles;
   int skip_upper;  // output tiles entirely above the diagonal (n >= m) are not computed
   int row_period;  // epi 1: rows with (row % row_period) == 0 have a zero residual
@@ -1139,7 +1140,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       for (int64_t L = blockIdx.x; L < p.total_tiles && ok; L += gridDim.x) {
         TileInfo t;
         if (!tile_at<BN>(p, L, t)) continue;
-        const uint32_t tb = tcount & 1u, tph = (tcount >> 1) & 1u;
+        const uint32_t tb = p.small_bufs == 2 ? (tcount & 1u) : 0u;
+        const uint32_t tph = p.small_bufs == 2 ? ((tcount >> 1) & 1u) : (tcount & 1u);
         ++tcount;
         const uint32_t small = tmem + small_col + tb * (uint32_t)BN;
         if (has_small) {
@@ -1240,7 +1242,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     for (int64_t L = blockIdx.x; L < p.total_tiles; L += gridDim.x) {
       TileInfo t;
       if (!tile_at<BN>(p, L, t)) continue;
-      const uint32_t tb = tcount & 1u, tph = (tcount >> 1) & 1u;
+      const uint32_t tb = p.small_bufs == 2 ? (tcount & 1u) : 0u;
+      const uint32_t tph = p.small_bufs == 2 ? ((tcount >> 1) & 1u) : (tcount & 1u);
       ++tcount;
       prefetch_row_inputs<BN, EPI>(p, t, lane, q, h);
       float acc[kAcc];
@@ -1422,7 +1425,11 @@ static int launch(GemmParams& p, int batch, cudaStream_t st) {
   if (products == 1 && (EPI == EPI_BF16 || EPI == EPI_SWIGLU_BF16 || EPI == EPI_SWIGLU_BWD_BF16))
     p.kb_per_chunk = 8;
   const bool has_small = (p.na > 1 || p.nb > 1) && p.order > 0;
-  int nbig = (int)((kTmemCols - (has_small ? 2u * BN : 0u)) / BN);
+  // cross-product ("small") accumulators: two let the next tile's MMAs start before the
+  // epilogue has read this tile's; one leaves a further chunk slot to the hi x hi ring, so the
+  // MMAs run further ahead while the epilogue writes a tile's outputs
+  if (p.small_bufs != 1) p.small_bufs = 2;
+  int nbig = (int)((kTmemCols - (has_small ? (uint32_t)p.small_bufs * BN : 0u)) / BN);
   p.n_big = nbig > kMaxBig ? kMaxBig : nbig;
   p.tiles_m = (p.M + BM - 1) / BM;
   p.tiles_n = (p.N + BN - 1) / BN;
@@ -1539,6 +1546,8 @@ static int gemm_prepare(const gsq_gemm_desc* d, GemmPlan* plan) {
     if (!ok) return GSQ_EINVAL;
   }
   p.a_mn = amn;
+  if (d->small_bufs < 0 || d->small_bufs > 2) return GSQ_EINVAL;
+  p.small_bufs = d->small_bufs == 1 ? 1 : 2;
   p.b_mn = bmn;
   for (int j = 0; j < d->nb; ++j) {
     const bool ok = bmn ? tc::make_map(&p.tma_b[j], d->b[j], d->b_rows, N, d->ldb, 64)

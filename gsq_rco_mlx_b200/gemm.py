@@ -151,6 +151,7 @@ class GemmDesc(_C.Structure):
         ("workspace", _C.c_void_p),
         ("a_major", _C.c_int),
         ("b_major", _C.c_int),
+        ("small_bufs", _C.c_int),
     ]
 
 
@@ -227,7 +228,7 @@ def _describe(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, orde
          aux0=None, aux1=None, ld_aux=None, B2: Terms = None, epi=0, bn=128, causal=False,
          batch=1, a_off=(1, 0, 0), b_off=(1, 0, 0), c_off=(1, 0, 0), t_off=(1, 0, 0, 0, 0),
          ct_up_rows=0, skip_upper=False, row_period=0, split_k="auto", a_major=0, b_major=0,
-         own_workspace=False):
+         small_bufs=0, own_workspace=False):
     """The descriptor of one gemm() call: (GemmDesc, (M, N, K, products, work boxes, launches),
     the split-K workspace tensor or None). own_workspace: a workspace of its own (a plan keeps
     its pointer) instead of the shared, growing one."""
@@ -269,6 +270,7 @@ def _describe(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, orde
     d.ld_aux = (d.N // 2 if epi in (2, 5) else d.N) if ld_aux is None else ld_aux
     d.skip_upper = int(skip_upper)
     d.row_period = int(row_period)
+    d.small_bufs = int(small_bufs)
     splittable = (epi == 0 and batch == 1 and not causal and C is not None and bias is None
                   and c_terms is None and ct_terms is None and sq_partial is None)
     if split_k == "auto":

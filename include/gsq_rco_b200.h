@@ -164,6 +164,10 @@ typedef struct {
    * range and no SwiGLU pairing (b2); an MN-major A may be batched (a_off then moves along its
    * K rows) or causal when K is a multiple of 64. */
   int a_major, b_major;
+  /* TMEM accumulators for a tile's cross products (the products below hi x hi) when there are
+   * any: 2 (default; also 0) lets the next tile's MMAs start before the epilogue has read this
+   * tile's; 1 gives that TMEM to one more chunk of the hi x hi ring instead. Same results. */
+  int small_bufs;
 } gsq_gemm_desc;
 
 /* Batched float32-faithful tensor-core GEMM with a fused epilogue (see gsq_gemm_tc for the

@@ -183,3 +183,30 @@ def test_plan_runs_equal_single_calls():
         A2 = torch.randn(M, K, device=DEV)
         for dst, src in zip(At.t, terms_of(A2).t):
             dst.copy_(src)
+
+
+@pytest.mark.parametrize("bn", [64, 128])
+def test_one_small_accumulator_equals_two(bn):
+    """One TMEM accumulator for the cross products (and one more hi x hi chunk slot) gives the
+    bits of two: the same products are folded in the same order. 256+ tiles, so every CTA
+    reuses the single accumulator."""
+    from gsq_rco_mlx_b200.gemm import Terms, gemm
+    torch.manual_seed(9)
+    M, N, K = 4096, 1024, 896
+    A, B = torch.randn(M, K, device=DEV), torch.randn(N, K, device=DEV)
+    R = torch.randn(M, N, device=DEV).bfloat16()
+    Tg = (R.float() + 1e-3 * torch.randn(M, N, device=DEV)).bfloat16()
+    outs = []
+    for sb in (2, 1):
+        C = torch.zeros(M, N, device=DEV)
+        rows = Terms(M, N)
+        sq = torch.zeros((M // 128) * (N // 128), device=DEV, dtype=torch.float64)
+        gemm(terms_of(A), terms_of(B), C=C, bn=bn, small_bufs=sb)
+        gemm(terms_of(A), terms_of(B), epi=1, resid=R, target=Tg, out_scale=0.5, sq_partial=sq,
+             c_terms=rows, bn=bn, small_bufs=sb)
+        check()
+        outs.append((C, [t.clone() for t in rows.t], sq.clone()))
+    (c2, r2, s2), (c1, r1, s1) = outs
+    assert torch.equal(c1, c2) and torch.equal(s1, s2)
+    for a, b in zip(r1, r2):
+        assert torch.equal(a, b)
