@@ -108,22 +108,47 @@ __global__ void sum_f64_kernel(const double* __restrict__ x, int n, double* out)
 }
 
 // Block partials of sum (t0 + t1 + t2)[r, c] * G[r, c] over a [rows][cols] matrix held as bf16
-// terms (t1 / t2 may be null), products and sums in float64; one partial per block.
+// terms (t1 / t2 may be null), products and sums in float64; one partial per block. Blocks take
+// whole rows; with cols, ld_t and ld_g multiples of 8 (16-byte rows) a thread reads 8 columns
+// per step (one 16-byte load per term, two per G).
 __global__ void __launch_bounds__(256)
 dot_terms_kernel(const __nv_bfloat16* __restrict__ t0, const __nv_bfloat16* __restrict__ t1,
                  const __nv_bfloat16* __restrict__ t2, int64_t ld_t, const float* __restrict__ G,
-                 int64_t ld_g, int rows, int cols, double* __restrict__ partials) {
+                 int64_t ld_g, int rows, int cols, int vec, double* __restrict__ partials) {
   __shared__ double sh[8];
-  const int64_t n = (int64_t)rows * cols;
   double s = 0.0;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = e / cols, c = e - r * cols;
-    const int64_t it = r * ld_t + c;
-    float d = __bfloat162float(t0[it]);
-    if (t1) d = __fadd_rn(d, __bfloat162float(t1[it]));
-    if (t2) d = __fadd_rn(d, __bfloat162float(t2[it]));
-    s += (double)d * (double)G[r * ld_g + c];
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const __nv_bfloat16* a0 = t0 + (int64_t)r * ld_t;
+    const __nv_bfloat16* a1 = t1 ? t1 + (int64_t)r * ld_t : nullptr;
+    const __nv_bfloat16* a2 = t2 ? t2 + (int64_t)r * ld_t : nullptr;
+    const float* g = G + (int64_t)r * ld_g;
+    if (vec) {
+      for (int c = 8 * threadIdx.x; c < cols; c += 8 * blockDim.x) {
+        const uint4 u0 = *reinterpret_cast<const uint4*>(a0 + c);
+        const uint4 u1 = a1 ? *reinterpret_cast<const uint4*>(a1 + c) : make_uint4(0, 0, 0, 0);
+        const uint4 u2 = a2 ? *reinterpret_cast<const uint4*>(a2 + c) : make_uint4(0, 0, 0, 0);
+        const float4 g0 = *reinterpret_cast<const float4*>(g + c);
+        const float4 g1 = *reinterpret_cast<const float4*>(g + c + 4);
+        const __nv_bfloat16* b0 = reinterpret_cast<const __nv_bfloat16*>(&u0);
+        const __nv_bfloat16* b1 = reinterpret_cast<const __nv_bfloat16*>(&u1);
+        const __nv_bfloat16* b2 = reinterpret_cast<const __nv_bfloat16*>(&u2);
+        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float d = __bfloat162float(b0[j]);
+          if (a1) d = __fadd_rn(d, __bfloat162float(b1[j]));
+          if (a2) d = __fadd_rn(d, __bfloat162float(b2[j]));
+          s += (double)d * (double)gv[j];
+        }
+      }
+    } else {
+      for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        float d = __bfloat162float(a0[c]);
+        if (a1) d = __fadd_rn(d, __bfloat162float(a1[c]));
+        if (a2) d = __fadd_rn(d, __bfloat162float(a2[c]));
+        s += (double)d * (double)g[c];
+      }
+    }
   }
   s = warp_sum_d(s);
   if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
@@ -316,16 +341,15 @@ extern "C" int gsq_dot_terms(const void* t0, const void* t1, const void* t2, int
                              double* partials, double* out, void* stream) {
   if (!t0 || !G || !partials || !out || rows <= 0 || cols <= 0 || ld_t < cols || ld_g < cols)
     return GSQ_EINVAL;
-  const int64_t n = (int64_t)rows * cols;
-  int64_t blocks = (n + 256 * 16 - 1) / (256 * 16);
-  if (blocks > 1024) blocks = 1024;
-  if (blocks < 1) blocks = 1;
+  const uintptr_t al = (uintptr_t)t0 | (uintptr_t)t1 | (uintptr_t)t2 | (uintptr_t)G;
+  const int vec = ((cols | ld_t | ld_g) & 7) == 0 && (al & 15) == 0;
+  const int blocks = rows < 1024 ? rows : 1024;
   cudaStream_t st = (cudaStream_t)stream;
-  dot_terms_kernel<<<(unsigned)blocks, 256, 0, st>>>(
+  dot_terms_kernel<<<blocks, 256, 0, st>>>(
       (const __nv_bfloat16*)t0, (const __nv_bfloat16*)t1, (const __nv_bfloat16*)t2, ld_t, G,
-      ld_g, rows, cols, partials);
+      ld_g, rows, cols, vec, partials);
   GSQ_CHECK_LAUNCH();
-  scaled_sum_f64_kernel<<<1, 256, 0, st>>>(partials, (int)blocks, scale, out);
+  scaled_sum_f64_kernel<<<1, 256, 0, st>>>(partials, blocks, scale, out);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
 }

@@ -44,10 +44,10 @@ def test_gram_step_matches_residual_form(x_terms):
             assert abs(loss - loss_ref) <= 1e-6 * loss_ref, (lin.name, r, loss, loss_ref)
 
 
-def test_dot_terms_matches_float64():
+@pytest.mark.parametrize("rows,cols,ld", [(300, 200, 208), (37, 203, 211), (2000, 896, 896)])
+def test_dot_terms_matches_float64(rows, cols, ld):
     from gsq_rco_mlx_b200 import _lib
     g = torch.Generator().manual_seed(1)
-    rows, cols, ld = 300, 200, 208
     x = torch.randn(rows, cols, generator=g)
     t0 = x.bfloat16()
     t1 = (x - t0.float()).bfloat16()
