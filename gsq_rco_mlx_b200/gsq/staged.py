@@ -522,7 +522,7 @@ class MLPStep(_StageBase):
                       _lib.stream_ptr())
             run("B1", self.DR, self.DIN, C=self.grad_d[r], a_major=1, b_major=1)
             run("B2", self.DR, self.D[dname][r], b_major=1, epi=3, aux0=self.g, aux1=self.u,
-                c_terms=self.DGU, ct_up_rows=I, bn=64)
+                c_terms=self.DGU, ct_up_rows=I)
             run("B3g", self.DG, self.MN, C=self.grad_gu[0, r], ldc=H, a_major=1, b_major=1)
             run("B3u", self.DU, self.MN, C=self.grad_gu[1, r], ldc=H, a_major=1, b_major=1)
 

@@ -165,8 +165,9 @@ typedef struct {
    * K rows) or causal when K is a multiple of 64. */
   int a_major, b_major;
   /* TMEM accumulators for a tile's cross products (the products below hi x hi) when there are
-   * any: 2 (default; also 0) lets the next tile's MMAs start before the epilogue has read this
-   * tile's; 1 gives that TMEM to one more chunk of the hi x hi ring instead. Same results. */
+   * any: 2 lets the next tile's MMAs start before the epilogue has read this tile's; 1 gives
+   * that TMEM to one more chunk of the hi x hi ring instead; 0 = 1 for epi 1, 2, 3 and 2 for
+   * the others. Same results either way. */
   int small_bufs;
 } gsq_gemm_desc;
 
