@@ -196,19 +196,18 @@ class LinearStep:
         self.grads = {l.name: v for l, v in zip(lins, views)}
         self.partials = torch.zeros(1024, device=dev, dtype=torch.float64)
         self.loss = torch.zeros(len(lins) * R, device=dev, dtype=torch.float64)
-        self.seq = torch.zeros(64, device=dev, dtype=torch.int32)
+        self.seq = SeqIds(dev)
         self.dev = dev
         self.plans = PlanCache()
 
     def stage(self, x_all, seq_ids, per_seq, seq_stride, offset):
         """Gather rows of x_all (float32 [n_rows, in]) into the X operand terms."""
-        ids = torch.as_tensor(np.asarray(seq_ids, dtype=np.int32))
-        self.seq[:len(ids)].copy_(ids, non_blocking=True)
+        ids = self.seq(seq_ids)
         rows = len(ids) * per_seq
         if rows != self.M:
             raise ValueError(f"micro-batch has {rows} rows, step expects {self.M}")
         _lib.call("gsq_gather_split", _lib.ptr(x_all), int(x_all.dtype == torch.bfloat16),
-                  x_all.shape[-1], _lib.ptr(self.seq),
+                  x_all.shape[-1], _lib.ptr(ids),
                   int(per_seq), int(seq_stride), int(offset), self.M, self.in_f, self.nx,
                   self.X.ptrs(), self.X.ld, None, 0, _lib.stream_ptr())
 
@@ -386,8 +385,32 @@ def _flat_views(dev, shapes):
     return flat, views
 
 
-def _seq_ids(dev, ids):
-    return torch.as_tensor(np.asarray(ids, dtype=np.int32)).to(dev, non_blocking=True)
+class SeqIds:
+    """A step's micro-batch sequence ids on the device without stalling the host: the ids go
+    through a ring of pinned host slots (a copy from pageable memory would wait for the stream
+    to drain, so the host could never launch ahead of the GPU). A host slot is rewritten only
+    after its previous copy has completed (one CUDA event per slot); the device slots are
+    reused in stream order."""
+
+    def __init__(self, dev, n=64, slots=4):
+        self.host = torch.empty(slots, n, dtype=torch.int32).pin_memory()
+        self.dev = torch.zeros(slots, n, dtype=torch.int32, device=dev)
+        self.events = [None] * slots
+        self.k = 0
+
+    def __call__(self, ids):
+        k = self.k
+        self.k = (k + 1) % len(self.events)
+        if self.events[k] is not None:
+            self.events[k].synchronize()
+        a = np.asarray(ids, dtype=np.int32)
+        self.host[k, :a.size] = torch.from_numpy(a)
+        d = self.dev[k, :a.size]
+        d.copy_(self.host[k, :a.size], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self.events[k] = ev
+        return d
 
 
 def _gather(src, ids_t, per_seq, stride, offset, rows, cols, n_terms, row_terms=None,
@@ -420,6 +443,7 @@ class _StageBase:
     def _init_soft(self, lins, R, dev):
         self.lins, self.R, self.dev = lins, int(R), dev
         self.plans = PlanCache()
+        self.seq = SeqIds(dev)
         self.Dbuf = {l.name: torch.zeros(R, 3, l.out_f, l.in_f, device=dev, dtype=torch.bfloat16)
                      for l in lins}
         self.D = {l.name: [Terms(l.out_f, l.in_f, 3, ld=l.in_f, tensors=self.Dbuf[l.name][r])
@@ -502,7 +526,7 @@ class MLPStep(_StageBase):
     def stage(self, mn_all, h1_all, y_all, seq_ids):
         """Positions 1.. of the chosen sequences of the caches (bf16 [N*T, H])."""
         H, T = self.cfg.hidden, self.T
-        ids = _seq_ids(self.dev, seq_ids)
+        ids = self.seq(seq_ids)
         _gather(mn_all, ids, self.w, T, self.p0, self.M, H, 1, self.MN)
         _gather(h1_all, ids, self.w, T, self.p0, self.M, H, 1, self.H1)
         _gather(y_all, ids, self.w, T, self.p0, self.M, H, 1, self.Y)
@@ -592,7 +616,7 @@ class VOStep(_StageBase):
         their keys (and P^T)."""
         c, T, m = self.cfg, self.T, self.m
         H, Tq, Tk, q0 = c.hidden, self.Tq, self.Tk, self.q0
-        ids = _seq_ids(self.dev, seq_ids)
+        ids = self.seq(seq_ids)
         _gather(hn_all, ids, Tk, T, 0, m * Tk, H, 1, self.HN, self.HNT)
         _gather(a_all, ids, Tq, T, q0, m * Tq, H, 1, self.A)
         qkw = qk_all.shape[1]
