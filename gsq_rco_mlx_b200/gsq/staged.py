@@ -8,9 +8,10 @@ probabilities, the resample mean and Lion (staged.py:383-392 with lion.py:44-56)
 step's soft weights.
 
 ``train_linears`` is the qk-stage optimiser (staged.py:357-400 with the linear loss of
-:322-329): per step the schedules, a sorted micro-batch draw from the numpy stream, R
-resamples of (residual GEMM with the loss in its epilogue, weight-gradient GEMM), then one
-fused step launch per linear.
+:322-329): per step the schedules, a sorted micro-batch draw from the numpy stream, the
+micro-batch Gram matrix X^T X, R resamples of (weight gradient D X^T X, loss sum D * G), then
+one fused step launch per linear. ``train_stage`` runs the vo / mlp stage steps (``VOStep``,
+``MLPStep``) the same way; every stage step repeats its GEMMs as prepared plans.
 
 Gumbel noise: Philox4x32-10 keyed by (stage seed, linear id) with counter (weight, block,
 step, resample), drawn inside the kernels, or host-supplied planes for parity runs.
@@ -661,8 +662,9 @@ class VOStep(_StageBase):
         B = m * nh
         for r in range(self.R):
             run = lambda name, *a, **k: self.plans.run((name, r), *a, **k)
+            # 128 x 64 tiles: 2 x 16 x 2 = 64 CTAs for the two 64-wide kv heads of 2 sequences
             run("V", self.HN, self.D[vname][r], M=Tk, batch=m, bias=self.v_bias, a_off=(1, Tk, 0),
-                 ct_terms=self.VT, t_off=(1, nkvd, 0, 0, 0))
+                ct_terms=self.VT, t_off=(1, nkvd, 0, 0, 0), bn=64)
             run("PV", self.P, self.VT, M=Tq, N=hd, K=Tk, batch=B, bn=64, causal=int(q0 == 0),
                  a_off=(1, Tq, 0), b_off=(c.rep, hd, 0), c_off=(nh, Tq * H, hd),
                  c_terms=self.O)
