@@ -188,12 +188,12 @@ def embed(E_dev, ids, dev):
     return h
 
 
-# DRAM bytes (read + write) per gemm_tc_kernel launch, mean over the six GEMMs of one mlp-stage
-# resample, from the ncu capture summarised in profiles/gemm_tc_mlp_stage.md
-GEMM_TRAFFIC_PER_LAUNCH = int(round((60 + 227 + 297 + 18 + 161 + 11 + 335 + 219 + 246 + 14 +
-                                     246 + 13) / 6 * 1e6))
+# DRAM bytes (read + write) per gemm_tc_kernel launch, mean over the four GEMMs of one mlp-stage
+# resample in the ncu capture summarised in profiles/gemm_tc_mlp_stage.md (F1, F3, B1, B2 as the
+# stage issues them)
+GEMM_TRAFFIC_PER_LAUNCH = int(round((60 + 227 + 200 + 16 + 162 + 10 + 342 + 217) / 4 * 1e6))
 GEMM_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum, mean per launch over "
-                       "the six GEMMs of one mlp-stage resample (profiles/gemm_tc_mlp_stage.md)")
+                       "F1, F3, B1, B2 of one mlp-stage resample (profiles/gemm_tc_mlp_stage.md)")
 
 
 def gemm_flops_of_mlp_stage(M):
@@ -1043,7 +1043,12 @@ def run_pipeline(args):
         np.int32)
     ev_win = np.random.default_rng(2).integers(0, VOCAB, size=(EVAL_WINDOWS, T_SEQ)).astype(
         np.int32)
-    work = tempfile.mkdtemp(prefix="gsq_pipeline_")
+    # one work directory for every rank (rank 0 writes the shards and the export, every rank
+    # loads the export for the eval)
+    work = [tempfile.mkdtemp(prefix="gsq_pipeline_") if rank == 0 else None]
+    if world > 1:
+        dist.broadcast_object_list(work, src=0)
+    work = work[0]
     quiet = lambda *a: None
     t = {}
     clocks = Clocks(local)
