@@ -409,6 +409,153 @@ __global__ void __launch_bounds__(256, 3) soft_step_v2_kernel(const StepArgs a) 
   }
 }
 
+// Ternary soft weights (1 bit, grid [-1, 0, 1]): two logit planes per weight, the mask lm and
+// the sign lb, and four Gumbel draws g0..g3. m = sigmoid((2 kappa lm + (g1 - g0)) / tau) is the
+// probability that the weight is active, v = sigmoid((2 kappa lb + (g3 - g2)) / tau) that its
+// sign is +, and the soft value is c = m (2 v - 1). The stored probability planes are (m, v).
+struct Ternary {
+  __device__ __forceinline__ static float sigmoid(float z) {
+    return __frcp_rn(__fadd_rn(1.f, expf(-z)));
+  }
+  __device__ __forceinline__ static void probs(float lm, float lb, const float g[4],
+                                               float inv_tau, float two_kappa, float& m,
+                                               float& v) {
+    m = sigmoid(__fmul_rn(__fadd_rn(__fmul_rn(two_kappa, lm), __fsub_rn(g[1], g[0])), inv_tau));
+    v = sigmoid(__fmul_rn(__fadd_rn(__fmul_rn(two_kappa, lb), __fsub_rn(g[3], g[2])), inv_tau));
+  }
+  __device__ __forceinline__ static float value(float m, float v) {
+    return __fmul_rn(m, __fsub_rn(__fmul_rn(2.f, v), 1.f));
+  }
+  // one draw's dL/dlm and dL/dlb from sG = s dL/dw and kt2 = 2 kappa / tau:
+  // dc/dlm = kt2 (2 v - 1) m (1 - m), dc/dlb = kt2 m 2 v (1 - v)
+  __device__ __forceinline__ static void grads(float m, float v, float sG, float kt2, float& gm,
+                                               float& gb) {
+    const float b = __fsub_rn(__fmul_rn(2.f, v), 1.f);
+    gm = __fmul_rn(kt2, __fmul_rn(__fmul_rn(sG, b), __fmul_rn(m, __fsub_rn(1.f, m))));
+    gb = __fmul_rn(kt2, __fmul_rn(__fmul_rn(sG, m),
+                                  __fmul_rn(2.f, __fmul_rn(v, __fsub_rn(1.f, v)))));
+  }
+  __device__ __forceinline__ static void noise(const float* __restrict__ noise_r, int64_t d,
+                                               int64_t i, const PhiloxKey& key, uint32_t step,
+                                               uint32_t resample, float g[4]) {
+    if (noise_r) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) g[k] = noise_r[k * d + i];
+    } else {
+      gumbel_weight<4>(key, (uint32_t)i, step, resample, g);
+    }
+  }
+};
+
+__global__ void __launch_bounds__(256)
+soft_fwd_ternary_kernel(const float* __restrict__ logits, const float* __restrict__ scales,
+                        const float* __restrict__ noise, NoiseKey nk, int out_f, int in_f, int G,
+                        int gs, float inv_tau, float two_kappa, const float* __restrict__ w_ref,
+                        float* __restrict__ w_out, __nv_bfloat16* __restrict__ terms,
+                        float* __restrict__ p_out) {
+  const int64_t d = (int64_t)out_f * in_f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < d;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float g[4], m, v;
+    Ternary::noise(noise, d, i, nk.key, nk.step, nk.resample, g);
+    Ternary::probs(logits[i], logits[d + i], g, inv_tau, two_kappa, m, v);
+    const int row = (int)(i / in_f), col = (int)(i - (int64_t)row * in_f);
+    float w = __fmul_rn(scales[(int64_t)row * G + col / gs], Ternary::value(m, v));
+    if (w_ref) w = __fsub_rn(w, w_ref[i]);
+    store_soft(w, i, d, w_out, terms);
+    if (p_out) {
+      p_out[i] = m;
+      p_out[d + i] = v;
+    }
+  }
+}
+
+// The fused step for ternary weights, one warp per (row, group) with the group's columns strided
+// over the lanes: pass 1 sums G c over the group and resamples (float64 warp sums, one float32
+// sum per resample) and takes the Lion step of the group scale; pass 2 forms the mask and sign
+// logit gradients of every draw from the stored (m, v), takes their Lion steps and runs the next
+// step's forward with the new logits and scale.
+__global__ void __launch_bounds__(256) soft_step_ternary_kernel(const StepArgs a) {
+  const int64_t d = (int64_t)a.out_f * a.in_f;
+  const int lane = threadIdx.x & 31;
+  const int64_t n_units = (int64_t)a.out_f * a.G;
+  const float fR = (float)a.R;
+  const float kt2 = __fmul_rn(2.f, a.kt);
+  const float two_kappa1 = __fmul_rn(2.f, a.kappa1);
+  for (int64_t unit = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; unit < n_units;
+       unit += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int row = (int)(unit / a.G), grp = (int)(unit - (int64_t)row * a.G);
+    const float s = a.scales[unit];
+    const int c_begin = grp * a.gs, c_end = min(c_begin + a.gs, a.in_f);
+    float gsum = 0.f;
+#pragma unroll 1
+    for (int r = 0; r < a.R; ++r) {
+      const float* p_r = a.probs + (int64_t)r * 2 * d;
+      const float* g_r = a.grad_w + (int64_t)r * d;
+      double part = 0.0;
+      for (int col = c_begin + lane; col < c_end; col += 32) {
+        const int64_t i = (int64_t)row * a.in_f + col;
+        part += (double)g_r[i] * (double)Ternary::value(p_r[i], p_r[d + i]);
+      }
+      const float gr = (float)warp_sum_d(part);
+      gsum = r == 0 ? gr : __fadd_rn(gsum, gr);
+    }
+    float s_new = s;
+    if (lane == 0) {
+      float mv = a.mom_s[unit];
+      lion1(s_new, mv, __fdiv_rn(gsum, fR), a.lr_s, a.lc);
+      a.scales[unit] = s_new;
+      a.mom_s[unit] = mv;
+    }
+    s_new = __shfl_sync(0xffffffffu, s_new, 0);
+    for (int col = c_begin + lane; col < c_end; col += 32) {
+      const int64_t i = (int64_t)row * a.in_f + col;
+      float am = 0.f, ab = 0.f;
+#pragma unroll 1
+      for (int r = 0; r < a.R; ++r) {
+        const float* p_r = a.probs + (int64_t)r * 2 * d;
+        float gm, gb;
+        Ternary::grads(p_r[i], p_r[d + i], __fmul_rn(s, a.grad_w[(int64_t)r * d + i]), kt2, gm,
+                       gb);
+        am = r == 0 ? gm : __fadd_rn(am, gm);
+        ab = r == 0 ? gb : __fadd_rn(ab, gb);
+      }
+      float lm = a.logits[i], mm = a.mom[i], lb = a.logits[d + i], mb = a.mom[d + i];
+      lion1(lm, mm, __fdiv_rn(am, fR), a.lr_l, a.lc);
+      lion1(lb, mb, __fdiv_rn(ab, fR), a.lr_l, a.lc);
+      a.logits[i] = lm;
+      a.mom[i] = mm;
+      a.logits[d + i] = lb;
+      a.mom[d + i] = mb;
+      if (!a.next) continue;
+      const float wr = a.w_ref ? a.w_ref[i] : 0.f;
+#pragma unroll 1
+      for (int r = 0; r < a.R; ++r) {
+        float g[4], m, v;
+        Ternary::noise(a.noise ? a.noise + (int64_t)r * 4 * d : nullptr, d, i, a.key,
+                       a.next_step, (uint32_t)r, g);
+        Ternary::probs(lm, lb, g, a.inv_tau1, two_kappa1, m, v);
+        float w = __fmul_rn(s_new, Ternary::value(m, v));
+        if (a.w_ref) w = __fsub_rn(w, wr);
+        store_soft(w, i, d, a.w_out ? a.w_out + (int64_t)r * d : nullptr,
+                   a.terms ? a.terms + (int64_t)r * 3 * d : nullptr);
+        float* pn = a.probs + (int64_t)r * 2 * d;
+        pn[i] = m;
+        pn[d + i] = v;
+      }
+    }
+  }
+}
+
+// Ternary decode (the mask and sign signs): code 1 (value 0) where lm < 0, else 2 (+1) where
+// lb >= 0 and 0 (-1) where lb < 0.
+__global__ void harden_ternary_kernel(const float* __restrict__ logits, int64_t d,
+                                      uint8_t* __restrict__ codes) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < d;
+       i += (int64_t)gridDim.x * blockDim.x)
+    codes[i] = logits[i] >= 0.f ? (logits[d + i] >= 0.f ? 2 : 0) : 1;
+}
+
 template <int K>
 __global__ void harden_kernel(const float* __restrict__ logits, const uint8_t* __restrict__ j0,
                               int64_t d, int bits, uint8_t* __restrict__ codes) {
@@ -447,7 +594,10 @@ inline LionConst lion_const(double wd, double b1, double b2) {
   return c;
 }
 
-inline int n_logit_planes(int bits) { return bits == 2 ? 4 : (bits >= 3 && bits <= 7 ? 5 : 0); }
+// logit planes per weight: ternary mask + sign, the 2-bit grid, the 5 local shifts
+inline int n_logit_planes(int bits) {
+  return bits == 1 ? 2 : bits == 2 ? 4 : (bits >= 3 && bits <= 7 ? 5 : 0);
+}
 
 inline unsigned grid_for(int64_t n, int threads) {
   int64_t b = (n + threads - 1) / threads;
@@ -478,7 +628,11 @@ extern "C" int gsq_soft_fwd(const float* logits, const uint8_t* j0, const float*
   const float inv_tau = 1.0f / tau;  // IEEE division on the host
   cudaStream_t st = (cudaStream_t)stream;
   auto* terms = (__nv_bfloat16*)w_terms;
-  if (K == 5)
+  if (K == 2)
+    soft_fwd_ternary_kernel<<<grid_for(d, 256), 256, 0, st>>>(
+        logits, scales, noise, nk, out_f, in_f, G, group_size, inv_tau, 2.0f * kappa, w_ref,
+        w_out, terms, p_out);
+  else if (K == 5)
     soft_fwd_kernel<5><<<grid_for(d, 256), 256, 0, st>>>(logits, j0, scales, noise, nk, out_f,
                                                         in_f, G, group_size, bits, inv_tau,
                                                         kappa, w_ref, w_out, terms, p_out);
@@ -507,7 +661,7 @@ extern "C" int gsq_soft_step(float* logits, float* mom_logits, const uint8_t* j0
   if (next && (!(tau_next > 0.f) || (!w_out && !w_terms))) return GSQ_EINVAL;
   if ((int64_t)out_f * in_f > 0xFFFFFFFFll) return GSQ_EINVAL;
   const int per_lane = (group_size + 31) / 32;
-  if (per_lane > 8) return GSQ_ENOTSUP;
+  if (K != 2 && per_lane > 8) return GSQ_ENOTSUP;
   StepArgs a;
   a.logits = logits; a.mom = mom_logits; a.j0 = j0; a.scales = scales; a.mom_s = mom_scales;
   a.probs = probs; a.grad_w = grad_w;
@@ -524,6 +678,11 @@ extern "C" int gsq_soft_step(float* logits, float* mom_logits, const uint8_t* j0
   const int64_t units = (int64_t)out_f * a.G;
   const unsigned grid = grid_for(units * 32, 256);
   cudaStream_t st = (cudaStream_t)stream;
+  if (K == 2) {
+    soft_step_ternary_kernel<<<grid, 256, 0, st>>>(a);
+    GSQ_CHECK_LAUNCH();
+    return GSQ_OK;
+  }
   // vectorised path: 64-column chunks, 8-byte aligned planes, resamples 1 or 2
   const bool vec = (group_size % 64 == 0) && (in_f % 64 == 0) && (resamples <= 2) &&
                    ((uintptr_t)logits % 8 == 0) && ((uintptr_t)mom_logits % 8 == 0) &&
@@ -562,7 +721,9 @@ extern "C" int gsq_harden(const float* logits, const uint8_t* j0, int out_f, int
   if (out_f <= 0 || in_f <= 0 || !logits || !codes || (K == 5 && !j0)) return GSQ_EINVAL;
   const int64_t d = (int64_t)out_f * in_f;
   cudaStream_t st = (cudaStream_t)stream;
-  if (K == 5)
+  if (K == 2)
+    harden_ternary_kernel<<<grid_for(d, 256), 256, 0, st>>>(logits, d, codes);
+  else if (K == 5)
     harden_kernel<5><<<grid_for(d, 256), 256, 0, st>>>(logits, j0, d, bits, codes);
   else
     harden_kernel<4><<<grid_for(d, 256), 256, 0, st>>>(logits, j0, d, bits, codes);

@@ -181,12 +181,12 @@ def init_shift_logits(numel, alpha=6.0, std=0.01, seed=0):
 
 
 def init_ternary_logits(q_gptq, alpha=3.0, std=0.01, seed=0):
-    """Ternary mask and sign logits (reference gptq.py:222-232)."""
+    """Ternary mask and sign logits (reference gptq.py:222-232), each std (N(0,1) + alpha base):
+    the mask base is +1 where the GPTQ value is kept and -1 where it is pruned, the sign base is
+    sign(q); the mask's normals are drawn first. Returns (lm, lb), float32 [d]."""
     q = np.asarray(q_gptq).reshape(-1)
-    lm = np.where(q != 0, 1.0, -1.0).astype(np.float32)
-    lb = np.where(q > 0, 1.0, np.where(q < 0, -1.0, 0.0)).astype(np.float32)
     rng = np.random.default_rng(seed)
-    eps_m = rng.standard_normal(q.shape).astype(np.float32)
-    eps_b = rng.standard_normal(q.shape).astype(np.float32)
-    return ((std * (eps_m + alpha * lm)).astype(np.float32),
-            (std * (eps_b + alpha * lb)).astype(np.float32))
+    normals = [rng.standard_normal(q.shape).astype(np.float32) for _ in range(2)]
+    bases = (np.where(q != 0, 1.0, -1.0), np.sign(q))
+    return tuple((std * (e + alpha * b.astype(np.float32))).astype(np.float32)
+                 for e, b in zip(normals, bases))

@@ -26,11 +26,12 @@ import torch
 
 from .. import _lib
 from ..gemm import CausalSoftmax, PlanCache, Terms, check_err, err_flag, gemm, gemm_tc, pad8
-from .gptq import init_logits_2bit_from_codes, init_shift_logits
+from .gptq import init_logits_2bit_from_codes, init_shift_logits, init_ternary_logits
 from .lion import BETAS, LR_LOGITS, LR_SCALES, WEIGHT_DECAY, scale_lr
-from .quant import gs_schedules
+from .quant import get_grid, gs_schedules
 
 ALPHA_SCALAR = 6.0
+ALPHA_TERNARY = 3.0
 INIT_STD = 0.01
 STAGES = ("qk", "vo", "mlp")
 STAGE_LAYERS = {"qk": ("q_proj", "k_proj"), "vo": ("v_proj", "o_proj"),
@@ -82,11 +83,12 @@ class SoftLinear:
 
     def __init__(self, name, bits, codes, scales16, group_size, seed, linear_id=0, logits0=None):
         """logits0: the initial logits [K, d] float32 (init_shift_logits of (d, seed),
-        transposed) when computed ahead, e.g. by ShiftInitPool."""
+        transposed) when computed ahead, e.g. by ShiftInitPool. bits 1 is ternary: two logit
+        planes per weight (mask, sign; staged.py:251-253) and four Gumbel planes per draw."""
         self.name, self.bits = name, int(bits)
-        if not 2 <= self.bits <= 7:
+        if not 1 <= self.bits <= 7:
             raise NotImplementedError(
-                f"{name}: soft weights cover 2..7 bits (8-bit linears are GPTQ only)")
+                f"{name}: soft weights cover 1..7 bits (8-bit linears are GPTQ only)")
         codes = np.asarray(codes, dtype=np.uint8)
         self.shape = codes.shape
         self.out_f, self.in_f = self.shape
@@ -98,14 +100,18 @@ class SoftLinear:
         d = codes.size
         if logits0 is not None:
             lt = np.asarray(logits0, dtype=np.float32)
-            if self.bits == 2 or lt.shape[1] != d:
+            if self.bits <= 2 or lt.shape[1] != d:
                 raise ValueError(f"{name}: precomputed logits {lt.shape} do not fit {d} weights")
+        elif self.bits == 1:
+            lt = np.stack(init_ternary_logits(get_grid(1)[codes.reshape(-1)],
+                                              alpha=ALPHA_TERNARY, std=INIT_STD, seed=seed))
         elif self.bits == 2:
             lt = init_logits_2bit_from_codes(codes, 4, alpha=ALPHA_SCALAR, std=INIT_STD,
                                              seed=seed).T
         else:
             lt = _shift_init_t(d, seed)
         self.K = lt.shape[0]
+        self.n_noise = 4 if self.bits == 1 else self.K   # Gumbel planes per draw
         self.logits = torch.as_tensor(np.ascontiguousarray(lt), device=dev)
         self.mom = torch.zeros_like(self.logits)
         self.scales = torch.as_tensor(np.asarray(scales16, dtype=np.float32), device=dev).contiguous()
@@ -119,7 +125,8 @@ class SoftLinear:
              terms=None, probs=None):
         """w_bar (or w_bar - w_ref) of one Gumbel draw: float32 [out, in] into ``out``, and/or
         three bf16 terms into ``terms`` (a [3, out, in] tensor, the residual GEMM's B operand);
-        ``probs`` ([K, d] float32) receives the draw's probabilities for the backward."""
+        ``probs`` ([K, d] float32) receives the draw's probabilities for the backward (ternary:
+        the mask and sign probabilities). noise: host Gumbel planes [n_noise, d] or None."""
         if out is None and terms is None and probs is None:
             out = torch.empty(self.shape, device=self.logits.device, dtype=torch.float32)
         _lib.call("gsq_soft_fwd", _lib.ptr(self.logits), _lib.ptr(self.j0), _lib.ptr(self.scales),
@@ -133,7 +140,8 @@ class SoftLinear:
              nxt=None):
         """Fused backward of this step (stored probs [R, K, d], grad_w [R, out, in]), resample
         mean and Lion; with nxt = dict(step, tau, kappa, seed, w_ref, terms | out, noise) also
-        the next step's forward (probs updated in place, soft weights written)."""
+        the next step's forward (probs updated in place, soft weights written; noise
+        [R, n_noise, d] or None)."""
         R = grad_w.shape[0]
         n = nxt or {}
         _lib.call("gsq_soft_step", _lib.ptr(self.logits), _lib.ptr(self.mom), _lib.ptr(self.j0),
@@ -147,7 +155,8 @@ class SoftLinear:
                   _lib.stream_ptr())
 
     def hard_codes(self) -> np.ndarray:
-        """Argmax codes of the learned logits (staged.py:300-314)."""
+        """Argmax codes of the learned logits; ternary: the signs of the mask and sign logits
+        (staged.py:300-314)."""
         codes = torch.empty(self.shape, device=self.logits.device, dtype=torch.uint8)
         _lib.call("gsq_harden", _lib.ptr(self.logits), _lib.ptr(self.j0), self.out_f, self.in_f,
                   self.bits, _lib.ptr(codes), _lib.stream_ptr())

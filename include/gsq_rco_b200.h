@@ -51,8 +51,13 @@ const char *gsq_status_string(int status);
  * u = (bits + 0.5) 2^-24 clipped to [1e-7, 1 - 1e-7].
  * Outputs (at least one): w_out float32 [out_f][in_f]; w_terms bf16 [3][out_f][in_f] with
  * out == t0 + t1 + t2 to float32 precision (the GEMM operand); p_out float32 [K][d].
+ * bits 1 (ternary, grid [-1, 0, 1]): logits are the two planes [2][d] (mask lm, sign lb), the
+ * Gumbel planes are four [4][d] (all four Philox words' high 24 bits), and
+ *   m = sigmoid((2 kappa lm + (g1 - g0)) * (1 / tau)),  v = sigmoid((2 kappa lb + (g3 - g2)) * (1 / tau)),
+ *   c = m (2 v - 1);  p_out holds the planes (m, v); j0 is unused.
  * Replaces: src/gsq_rco/gsq/staged.py:271-298 (_Linear.soft) with :82-84 (_gs_softmax),
- * :92-96 (_gumbel), :99-106 (_grid_rows, _shift_rows); the residual of staged.py:327. */
+ * :87-89 (_binary_gs), :92-96 (_gumbel), :99-106 (_grid_rows, _shift_rows), :109-115
+ * (_ternary_rows); the residual of staged.py:327. */
 int gsq_soft_fwd(const float *logits, const uint8_t *j0, const float *scales, const float *noise,
                  uint64_t seed, uint32_t linear_id, uint32_t step, uint32_t resample,
                  int out_f, int in_f, int group_size, int bits, float tau, float kappa,
@@ -69,8 +74,11 @@ int gsq_soft_fwd(const float *logits, const uint8_t *j0, const float *scales, co
  *   probabilities into probs (in place) and the soft weights (minus w_ref) into w_out
  *   [R][out_f][in_f] float32 and/or w_terms bf16 [R][3][out_f][in_f]. noise_next: host-supplied
  *   Gumbel planes [R][K][d] of the next step, or NULL for Philox (as gsq_soft_fwd).
+ * bits 1 (ternary): probs holds the planes (m, v) per resample ([R][2][d]), noise_next is
+ * [R][4][d], and the logit gradients are
+ *   dL/dlm = (2 kappa / tau) s G (2 v - 1) m (1 - m),  dL/dlb = (2 kappa / tau) s G m 2 v (1 - v).
  * The betas and wd are the caller's float64 values, each of b, 1 - b, wd rounded to float32
- * once (MLX's treatment of Python scalars). resamples: 1..8; group_size <= 256.
+ * once (MLX's treatment of Python scalars). resamples: 1..8; group_size <= 256 (any for bits 1).
  * Replaces: the MLX autodiff of staged.py:322-329 through :271-298, the resample average of
  * staged.py:383-390, lion_update src/gsq_rco/gsq/lion.py:44-56, and the next step's
  * _Linear.soft (staged.py:271-298). */
@@ -83,7 +91,8 @@ int gsq_soft_step(float *logits, float *mom_logits, const uint8_t *j0, float *sc
                   void *w_terms, void *stream);
 
 /* Argmax decode of trained logits to uint8 codes [out_f][in_f] (first maximum wins;
- * local shift clipped to the grid). Replaces staged.py:300-314 (_Linear.hard_codes) and
+ * local shift clipped to the grid; ternary: code 1 (value 0) where lm < 0, else 2 (+1) where
+ * lb >= 0 and 0 (-1) where lb < 0). Replaces staged.py:300-314 (_Linear.hard_codes) and
  * src/gsq_rco/gsq/quant.py:75-83 (local_shift_indices). */
 int gsq_harden(const float *logits, const uint8_t *j0, int out_f, int in_f, int bits,
                uint8_t *codes, void *stream);

@@ -4,8 +4,10 @@ TEST INFRASTRUCTURE ONLY (see oracle/__init__.py).
 
 Follows the reference egesabanci/gsq-rco-mlx:
   grid / schedules / local shift   src/gsq_rco/gsq/quant.py:38-46, 51-61, 75-108
-  App-A logit inits                src/gsq_rco/gsq/gptq.py:192-219
+  App-A logit inits                src/gsq_rco/gsq/gptq.py:192-232 (ternary :222-232)
   Gumbel-softmax soft weight       src/gsq_rco/gsq/staged.py:82-106, 271-298
+  ternary (1-bit) soft weight      src/gsq_rco/gsq/staged.py:87-89, 109-115, 251-253, 305-308
+                                   (tests/oracles.py:92-103, 126-160)
   qk stage loss                    src/gsq_rco/gsq/staged.py:322-329
   analytic gradients               tests/oracles.py:311-347 (full grid), extended here to the
                                    5-neighbour local shift: u_k = s * G * C_k
@@ -19,8 +21,9 @@ are passed in (host-supplied noise), or drawn from oracle.philox with the counte
 CUDA kernels use.
 
 Device layout shared with the CUDA path: logits and their momentum are plane-major
-[K, d] (K = 5 local-shift candidates, or 4 grid values at 2 bits); d = out * in,
-weight i = row * in + col; scales [out, G] with G = ceil(in / group_size).
+[K, d] (K = 5 local-shift candidates, 4 grid values at 2 bits, or the mask and sign logits of
+ternary weights, whose draws take 4 Gumbel planes); d = out * in, weight i = row * in + col;
+scales [out, G] with G = ceil(in / group_size).
 """
 from __future__ import annotations
 
@@ -92,7 +95,10 @@ def local_shift_indices(j0, logits_dk, n_levels: int) -> np.ndarray:
 
 def candidate_values(bits: int, j0) -> np.ndarray:
     """Candidate grid values per weight, plane-major [K, d]: the local shift for 3..7 bits
-    (staged.py:263-266), the full grid for 2 bits (staged.py:255-257)."""
+    (staged.py:263-266), the full grid for 2 bits (staged.py:255-257); None for ternary
+    weights, whose value is the product of a mask and a sign draw."""
+    if bits == 1:
+        return None
     grid = get_grid(bits)
     j0 = np.asarray(j0).reshape(-1)
     if bits == 2:
@@ -126,9 +132,22 @@ def init_logits_2bit_from_codes(codes, K, alpha=ALPHA_SCALAR, std=INIT_STD, seed
     return noisy_alpha_init(base.astype(np.float32), alpha, std, seed)
 
 
+def init_ternary_logits(q, alpha=3.0, std=INIT_STD, seed=0):
+    """gptq.py:222-232: mask logits std (N(0,1) + alpha (+1 if q != 0 else -1)) and sign logits
+    std (N(0,1) + alpha sign(q)), the mask's normals drawn first. [2, d] float32."""
+    q = np.asarray(q).reshape(-1)
+    rng = np.random.default_rng(seed)
+    eps = [rng.standard_normal(q.shape).astype(np.float32) for _ in range(2)]
+    base = [np.where(q != 0, 1.0, -1.0), np.sign(q)]
+    return np.stack([(std * (e + alpha * b.astype(np.float32))).astype(np.float32)
+                     for e, b in zip(eps, base)])
+
+
 def init_logits(bits, codes, seed):
-    """Initial logits of one linear, plane-major [K, d] float32 (staged.py:255-266)."""
+    """Initial logits of one linear, plane-major [K, d] float32 (staged.py:250-266)."""
     codes = np.asarray(codes)
+    if bits == 1:
+        return init_ternary_logits(get_grid(1)[codes.reshape(-1)], seed=seed)
     if bits == 2:
         l = init_logits_2bit_from_codes(codes, 4, seed=seed)
     else:
@@ -156,6 +175,51 @@ def gs_probs(logits_kd, noise_kd, tau, kappa):
     return e * inv
 
 
+def _sigmoid32(z):
+    one = np.float32(1.0)
+    with np.errstate(over="ignore"):
+        return one / (one + np.exp(-z))
+
+
+def ternary_probs(logits_2d, noise_4d, tau, kappa):
+    """staged.py:87-89 and 109-115 in float32: the mask probability
+    m = sigmoid((2 kappa lm + (g1 - g0)) / tau) and the sign probability
+    v = sigmoid((2 kappa lb + (g3 - g2)) / tau); the division by tau a multiplication by its
+    float32 reciprocal (the CUDA kernels' order). Returns [2, d] = (m, v)."""
+    inv_tau = np.float32(1.0) / np.float32(tau)
+    k2 = np.float32(2.0) * np.float32(kappa)
+    l = np.asarray(logits_2d, dtype=np.float32)
+    g = np.asarray(noise_4d, dtype=np.float32)
+    m = _sigmoid32((k2 * l[0] + (g[1] - g[0])) * inv_tau)
+    v = _sigmoid32((k2 * l[1] + (g[3] - g[2])) * inv_tau)
+    return np.stack([m, v]).astype(np.float32)
+
+
+def ternary_value(p):
+    """c = m (2 v - 1) (staged.py:113-115), float32."""
+    return (p[0] * (np.float32(2.0) * p[1] - np.float32(1.0))).astype(np.float32)
+
+
+def ternary_backward(G, p, c, scales, group_size, tau, kappa):
+    """Gradients of the ternary soft weight w = s m (2 v - 1) given G = dL/dw, float64:
+    dL/dlm = (2 kappa / tau) s G (2 v - 1) m (1 - m), dL/dlb = (2 kappa / tau) s G m 2 v (1 - v)
+    (the sigmoid's derivative through z = (2 kappa l + g' - g) / tau), dL/ds = group_sum(G c)."""
+    out_f, in_f = G.shape
+    sG = (expand_scales(scales, in_f, group_size).astype(np.float64) * G).reshape(-1)
+    m, v = p[0].astype(np.float64), p[1].astype(np.float64)
+    kt2 = 2.0 * kappa / tau
+    glog = np.stack([kt2 * sG * (2.0 * v - 1.0) * m * (1.0 - m),
+                     kt2 * sG * m * 2.0 * v * (1.0 - v)])
+    return glog, group_sum(G * c.astype(np.float64), group_size)
+
+
+def ternary_hard_codes(logits_2d):
+    """staged.py:305-308: m = lm >= 0, b = lb >= 0, code = m (2 b - 1) + 1 (grid [-1, 0, 1])."""
+    m = (np.asarray(logits_2d[0]) >= 0).astype(np.int64)
+    b = (np.asarray(logits_2d[1]) >= 0).astype(np.int64)
+    return (m * (2 * b - 1) + 1).astype(np.uint8)
+
+
 def expand_scales(scales, in_f, group_size):
     """Per-(row, group) scales -> per-weight [out, in] (staged.py:298 mx.take over gid)."""
     return np.repeat(np.asarray(scales, dtype=np.float32), group_size, axis=1)[:, :in_f]
@@ -172,7 +236,12 @@ def group_sum(A, group_size):
 
 def soft_weight(logits_kd, noise_kd, Ckd, scales, shape, group_size, tau, kappa):
     """staged.py:271-298: w_bar = s[:, col // gs] * sum_k p_k C_k, float32 [out, in].
-    Returns (w_bar, p [K, d], c [out, in])."""
+    Returns (w_bar, p [K, d], c [out, in]). Ckd None: ternary weights (c = m (2 v - 1))."""
+    if Ckd is None:
+        p = ternary_probs(logits_kd, noise_kd, tau, kappa)
+        c = ternary_value(p).reshape(shape)
+        w = expand_scales(scales, shape[1], group_size) * c
+        return w.astype(np.float32), p, c
     if fast():
         from . import gsq_fast
         return gsq_fast.soft_weight(logits_kd, noise_kd, Ckd, scales, shape, group_size, tau,
@@ -188,7 +257,10 @@ def soft_backward(G, p, Ckd, c, scales, group_size, tau, kappa):
 
     tests/oracles.py:340-344 for the full grid; the local shift replaces grid_k by C_k:
       u_k = s * G * C_k,   dL/dl = (kappa / tau) * p * (u - <p, u>),   dL/ds = group_sum(G * c).
+    Ckd None: the ternary gradients (ternary_backward).
     """
+    if Ckd is None:
+        return ternary_backward(G, p, c, scales, group_size, tau, kappa)
     out_f, in_f = G.shape
     sG = (expand_scales(scales, in_f, group_size).astype(np.float64) * G).reshape(-1)
     u = sG[None, :] * Ckd.astype(np.float64)
@@ -201,7 +273,7 @@ def soft_backward(G, p, Ckd, c, scales, group_size, tau, kappa):
 def backward_accumulate(acc, G, p, Ckd, c, scales, group_size, tau, kappa):
     """Add one draw's float32 logit and scale gradients to acc = [glog, gscale] (None entries
     start the sums), the resample accumulation of staged.py:386."""
-    if fast():
+    if fast() and Ckd is not None:
         from . import gsq_fast
         if acc[0] is None:
             acc[0] = np.zeros(p.shape, dtype=np.float32)
@@ -274,10 +346,18 @@ class LinearState:
 
     @property
     def K(self):
-        return self.Ckd.shape[0]
+        return self.logits.shape[0]
+
+    @property
+    def n_noise(self):
+        """Gumbel planes per draw: four for ternary weights, else one per candidate."""
+        return 4 if self.bits == 1 else self.K
 
     def hard_codes(self):
-        """staged.py:300-314: argmax decode (local shift clipped to the grid; 2-bit argmax)."""
+        """staged.py:300-314: argmax decode (local shift clipped to the grid; 2-bit argmax;
+        ternary: the mask and sign logits' signs)."""
+        if self.bits == 1:
+            return ternary_hard_codes(self.logits).reshape(self.shape)
         if self.bits == 2:
             return self.logits.argmax(axis=0).astype(np.uint8).reshape(self.shape)
         j = local_shift_indices(self.codes0.reshape(-1), self.logits.T, 2 ** self.bits)
@@ -291,8 +371,9 @@ class LinearState:
         if fast():
             from . import gsq_fast
             return gsq_fast.gumbel_planes(seed, self.linear_id, step, resample,
-                                          self.codes0.size, self.K)
-        return gumbel_planes(seed, self.linear_id, step, resample, self.codes0.size, self.K)
+                                          self.codes0.size, self.n_noise)
+        return gumbel_planes(seed, self.linear_id, step, resample, self.codes0.size,
+                             self.n_noise)
 
 
 def lion_step(state: LinearState, glog, gs, lr_logits=LR_LOGITS, lr_scales=LR_SCALES):

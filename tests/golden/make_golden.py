@@ -237,6 +237,28 @@ def gen_gsq(gptq, quant, oracles):
     np.savez_compressed(OUT / "gsq.npz", **out)
 
 
+def gen_ternary(gptq, oracles):
+    """Ternary (1-bit) soft weights: the mask / sign logit init (gsq/gptq.py:222-232) and the
+    reference test oracle's soft and hard ternary weights (tests/oracles.py:92-103, 126-160)
+    from fixed Gumbel draws, at a moderate and a saturating (tau, kappa)."""
+    out = {}
+    r = np.random.default_rng(21)
+    q = r.integers(-1, 2, size=600).astype(np.float32)
+    lm, lb = gptq.init_ternary_logits(q, alpha=3.0, std=0.01, seed=4)
+    out.update(init_q=q, init_lm=lm, init_lb=lb)
+    lm = r.standard_normal(600).astype(np.float32) * 0.05
+    lb = r.standard_normal(600).astype(np.float32) * 0.05
+    noise = np.stack([oracles.sample_gumbel((600,), rng=r) for _ in range(4)]).astype(np.float32)
+    out.update(lm=lm, lb=lb, noise=noise, scale=np.float32(0.037))
+    for j, (tau, kappa) in enumerate(((1.7, 6.0), (0.5, 200.0))):
+        out[f"tau{j}"], out[f"kappa{j}"] = np.float64(tau), np.float64(kappa)
+        out[f"soft{j}"] = np.asarray(oracles.ternary_soft(lm, lb, 0.037, tau, kappa,
+                                                          noise=tuple(noise)))
+    w, (m, b) = oracles.ternary_hard(lm, lb, 0.037)
+    out.update(hard=np.asarray(w), hard_m=np.asarray(m), hard_b=np.asarray(b))
+    np.savez_compressed(OUT / "ternary.npz", **out)
+
+
 def gen_export():
     """Packed words of the MLX affine export (gsq/export.py:61-73, pack_codes; mlx_bits :52-58;
     bits_report :218-250 on the hand-made case of tests/test_export.py:139-150). export.py
@@ -275,13 +297,19 @@ def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reference", required=True,
                     help="path of a checkout of the reference repository")
-    REF = Path(ap.parse_args().reference).resolve()
+    ap.add_argument("--only", default="gptq,dp,rco_host,gsq,ternary,export",
+                    help="comma-separated fixture names to (re)generate")
+    args = ap.parse_args()
+    REF = Path(args.reference).resolve()
+    only = set(args.only.split(","))
     gptq, quant, manifold, loop, oracles = _import_reference()
-    gen_gptq(gptq)
-    gen_dp(manifold, loop)
-    gen_rco_host(manifold, loop)
-    gen_gsq(gptq, quant, oracles)
-    gen_export()
+    gens = {"gptq": lambda: gen_gptq(gptq), "dp": lambda: gen_dp(manifold, loop),
+            "rco_host": lambda: gen_rco_host(manifold, loop),
+            "gsq": lambda: gen_gsq(gptq, quant, oracles),
+            "ternary": lambda: gen_ternary(gptq, oracles), "export": gen_export}
+    for name, gen in gens.items():
+        if name in only:
+            gen()
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

@@ -116,6 +116,66 @@ def test_local_shift_grads_finite_differences():
         assert abs(fd - gsc[o, g]) <= 1e-6 * max(abs(fd), 1e-12) + 1e-14
 
 
+def test_ternary_matches_reference_oracle():
+    """Ternary (1-bit) soft weights: the mask / sign logit init against gsq/gptq.py:222-232 and
+    the soft / hard weight against the reference test oracle (tests/oracles.py:126-160) from the
+    same Gumbel draws. The reference oracle divides by tau and clips the sigmoid's argument to
+    +-50; the restatement multiplies by 1 / tau in float32: equal to a few float32 ulps of m and
+    v (an absolute 1e-6 s where 2 v - 1 nearly cancels)."""
+    from gsq_rco_mlx_b200.gsq.gptq import init_ternary_logits
+    z = load("ternary.npz")
+    q = z["init_q"]
+    lm, lb = init_ternary_logits(q, alpha=3.0, std=0.01, seed=4)
+    assert np.array_equal(lm, z["init_lm"]) and np.array_equal(lb, z["init_lb"])
+    assert np.array_equal(ogsq.init_ternary_logits(q, alpha=3.0, seed=4),
+                          np.stack([z["init_lm"], z["init_lb"]]))
+    L = np.stack([z["lm"], z["lb"]])
+    for j in range(2):
+        tau, kappa = float(z[f"tau{j}"]), float(z[f"kappa{j}"])
+        p = ogsq.ternary_probs(L, z["noise"], tau, kappa)
+        w = np.float32(z["scale"]) * ogsq.ternary_value(p)
+        np.testing.assert_allclose(w, z[f"soft{j}"], rtol=2e-6, atol=1e-6 * float(z["scale"]))
+    codes = ogsq.ternary_hard_codes(L)
+    np.testing.assert_array_equal(np.float32(z["scale"]) * ogsq.get_grid(1)[codes], z["hard"])
+    np.testing.assert_array_equal(codes != 1, z["hard_m"] != 0)
+
+
+def test_ternary_grads_finite_differences():
+    """Ternary mask / sign logit and scale gradients vs central differences of the qk-stage loss
+    through w = s m (2 v - 1) (float64)."""
+    rng = np.random.default_rng(4)
+    out_f, in_f, gs = 8, 64, 32
+    W = 0.02 * rng.standard_normal((out_f, in_f))
+    X = rng.standard_normal((40, in_f))
+    r = og.quantize_rtn(W, 1, gs)
+    lg = ogsq.init_logits(1, r["codes"], seed=2).astype(np.float64) + \
+        0.3 * rng.standard_normal((2, W.size))
+    sc = r["scales"].astype(np.float64)
+    noise = gumbel_planes(1, 0, 0, 0, W.size, 4).astype(np.float64)
+    tau, kappa = 2.0, 3.0
+    sig = lambda x: 1.0 / (1.0 + np.exp(-x))
+
+    def loss(lg_, sc_):
+        m = sig((2 * kappa * lg_[0] + noise[1] - noise[0]) / tau)
+        v = sig((2 * kappa * lg_[1] + noise[3] - noise[2]) / tau)
+        c = (m * (2 * v - 1)).reshape(W.shape)
+        R = X @ (np.repeat(sc_, gs, axis=1) * c - W).T
+        return (R * R).mean(), np.stack([m, v]), c, R
+
+    L0, p, c, R = loss(lg, sc)
+    G = (2.0 / (X.shape[0] * out_f)) * (R.T @ X)
+    gl, gsc = ogsq.soft_backward(G, p, None, c, sc, gs, tau, kappa)
+    h = 1e-7
+    for (k, i) in [(0, 3), (1, 100), (0, 511), (1, 257)]:
+        e = np.zeros_like(lg); e[k, i] = h
+        fd = (loss(lg + e, sc)[0] - loss(lg - e, sc)[0]) / (2 * h)
+        assert abs(fd - gl[k, i]) <= 1e-4 * max(abs(fd), 1e-12) + 1e-15
+    for (o, g) in [(0, 0), (5, 1), (7, 1)]:
+        e = np.zeros_like(sc); e[o, g] = 1e-7
+        fd = (loss(lg, sc + e)[0] - loss(lg, sc - e)[0]) / 2e-7
+        assert abs(fd - gsc[o, g]) <= 1e-6 * max(abs(fd), 1e-12) + 1e-14
+
+
 def test_lion_matches_reference_oracle():
     z = load("gsq.npz")
     P = z["lion_traj"][0]
