@@ -60,7 +60,6 @@ SIGNATURES = {
     "gsq_transpose_bf16": [_vp, _i32, _i32, _i64, _i64, _vp, _i64, _i64, _i32, _i32, _vp],
     "gsq_head_group_sum_t": [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
     "gsq_sum_f64": [_vp, _i32, _vp, _vp],
-    "gsq_softmax_rows_reduce": [_i32, _vp, _i32, _i32, _i32, _vp, _vp, _vp],
     "gsq_dot_terms": [_vp, _vp, _vp, _i64, _vp, _i64, _i32, _i32, _f64, _vp, _vp, _vp],
     "hessian_accum": [_vp, _i64, _i32, _vp, _i64, _vp],
     "gptq_factor": [_vp, _i32, _f64, _vp, _vp, _vp, _vp, _vp],

@@ -352,41 +352,6 @@ extern "C" int gsq_softmax_causal(const float* S, int B, int T, void* P, void* P
   return GSQ_OK;
 }
 
-// Row statistics of the three-pass softmax: one thread per row of batch x T rows, reading the
-// first 2 (t / 128 + 1) of its slots partials (the tiles on and below the diagonal).
-__global__ void __launch_bounds__(256)
-softmax_rows_reduce_kernel(int phase, const void* __restrict__ part, int64_t n_rows, int T,
-                           int slots, float* __restrict__ m, float* __restrict__ inv) {
-  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n_rows;
-       r += (int64_t)gridDim.x * blockDim.x) {
-    const int t = (int)(r % T);
-    const int ns = min(slots, 2 * (t / 128 + 1));
-    if (phase == 1) {
-      const float* p = static_cast<const float*>(part) + r * slots;
-      float mx = -INFINITY;
-      for (int s = 0; s < ns; ++s) mx = fmaxf(mx, p[s]);
-      m[r] = mx;
-    } else {
-      const double* p = static_cast<const double*>(part) + r * slots;
-      double sum = 0.0;
-      for (int s = 0; s < ns; ++s) sum += p[s];
-      inv[r] = __frcp_rn((float)sum);
-    }
-  }
-}
-
-extern "C" int gsq_softmax_rows_reduce(int phase, const void* part, int batch, int T, int slots,
-                                       float* m, float* inv, void* stream) {
-  if ((phase != 1 && phase != 2) || !part || batch <= 0 || T <= 0 ||
-      slots < 2 * ((T + 127) / 128) || (phase == 1 && !m) || (phase == 2 && !inv))
-    return GSQ_EINVAL;
-  const int64_t n = (int64_t)batch * T;
-  softmax_rows_reduce_kernel<<<blocks(n, 256), 256, 0, (cudaStream_t)stream>>>(
-      phase, part, n, T, slots, m, inv);
-  GSQ_CHECK_LAUNCH();
-  return GSQ_OK;
-}
-
 extern "C" int gsq_softmax_causal_rows(const float* S, int B, int rows, int cols, int64_t ld_s,
                                        int row0, void* P, int64_t ld_p, void* stream) {
   if (!S || !P || B <= 0 || rows <= 0 || cols <= 0 || row0 < 0 || ld_s < cols || ld_p < cols ||

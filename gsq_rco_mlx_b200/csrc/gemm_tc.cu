@@ -96,13 +96,6 @@ struct GemmParams {
   int n_fast;  // tile order: n fastest (A the larger operand) instead of m fastest
   int causal_order;  // causal products: longest k-ranges first, in a snake over the CTAs
   int small_bufs;    // 1 or 2 TMEM accumulators for a tile's cross products (see launch)
-  // causal row softmax of square scores in three passes (gsq_gemm_desc.softmax_phase):
-  // 1 = per-row maxima of each tile half, 2 = per-row sums of exp(x - m) of each tile half,
-  // 3 = P = bf16(exp(x - m) / sum) as the cs term
-  int sm_phase, sm_slots;
-  void* sm_part;        // phase 1: float, phase 2: double, [batch][M][sm_slots]
-  const float* sm_m;    // [batch][M] row maxima (from phase 1)
-  const float* sm_inv;  // [batch][M] 1 / row sums (from phase 2)
   int64_t total_tiles;
   int skip_upper;  // output tiles entirely above the diagonal (n >= m) are not computed
   int row_period;  // epi 1: rows with (row % row_period) == 0 have a zero residual
@@ -694,65 +687,6 @@ __device__ __forceinline__ double epilogue_tma(const GemmParams& p, const TileIn
     ring_flush(ring, lane);
   }
   return sq;
-}
-
-// The three passes of the causal row softmax of square scores x = alpha acc (row r of batch z
-// sees keys k <= r; tiles above the diagonal are not computed). Thread (q, h) holds row
-// tile_m + 32 q + lane and the columns tile_n + 64 jc + 32 h + u; its partials go to slot
-// 2 (tile_n / BN) + h of the row. Pass 1 writes the maxima of the valid x, pass 2 the float64
-// sums of expf(x - m) with m the row maximum, pass 3 writes bf16(expf(x - m) * inv) (zero at
-// masked keys) through the cs box stores: the arithmetic of the one-warp-per-row softmax
-// kernel, without writing or reading float32 scores.
-template <int BN>
-__device__ __forceinline__ void epilogue_softmax(const GemmParams& p, const TileInfo& t,
-                                                 float* acc, BoxRing& ring, int lane, int q,
-                                                 int h) {
-  constexpr int kNC = BN / 64;
-  const int row0 = t.tile_m + 32 * q, row = row0 + lane;
-  const bool row_ok = row < p.M;
-  const int zr = t.z % p.c_off.div, zq = t.z / p.c_off.div;
-  const int64_t rix = (int64_t)t.z * p.M + row;
-  const int64_t slot = rix * p.sm_slots + 2 * (t.tile_n / BN) + h;
-#pragma unroll
-  for (int i = 0; i < BN / 2; ++i) acc[i] = __fmul_rn(p.alpha, acc[i]);
-  if (p.sm_phase == 1) {
-    float mx = -INFINITY;
-#pragma unroll
-    for (int jc = 0; jc < kNC; ++jc)
-#pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const int col = t.tile_n + 64 * jc + 32 * h + u;
-        if (col <= row && col < p.N) mx = fmaxf(mx, acc[32 * jc + u]);
-      }
-    if (row_ok) static_cast<float*>(p.sm_part)[slot] = mx;
-  } else if (p.sm_phase == 2) {
-    const float m = row_ok ? p.sm_m[rix] : 0.f;
-    double sum = 0.0;
-#pragma unroll
-    for (int jc = 0; jc < kNC; ++jc)
-#pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const int col = t.tile_n + 64 * jc + 32 * h + u;
-        if (col <= row && col < p.N) sum += (double)expf(__fsub_rn(acc[32 * jc + u], m));
-      }
-    if (row_ok) static_cast<double*>(p.sm_part)[slot] = sum;
-  } else {
-    const float m = row_ok ? p.sm_m[rix] : 0.f, inv = row_ok ? p.sm_inv[rix] : 0.f;
-#pragma unroll
-    for (int jc = 0; jc < kNC; ++jc) {
-      const int n0 = t.tile_n + 64 * jc + 32 * h;
-      if (n0 >= p.N) continue;
-      float* a = acc + 32 * jc;
-#pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const int col = n0 + u;
-        a[u] = (row_ok && col <= row && col < p.N) ? __fmul_rn(expf(__fsub_rn(a[u], m)), inv)
-                                                   : 0.f;
-      }
-      out_terms(ring, p, a, 1, n0, 0, row0, zr, zq, t.z, lane);
-    }
-    ring_flush(ring, lane);
-  }
 }
 
 // The fused outputs of one tile from the folded accumulator. Epilogue warp (q, h) holds rows
@@ -1363,9 +1297,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       }
       double sq = 0.0;
       if (ok) {
-        if (EPI == EPI_PLAIN && p.sm_phase)
-          epilogue_softmax<BN>(p, t, acc, ring, lane, q, h);
-        else if (p.tma_out)
+        if (p.tma_out)
           sq = epilogue_tma<BN, EPI>(p, t, acc, ring, lane, q, h);
         else
           sq = epilogue_out<BN, EPI>(p, t, acc, stg, lane, q, h);
@@ -1573,15 +1505,7 @@ static int gemm_prepare(const gsq_gemm_desc* d, GemmPlan* plan) {
     return GSQ_EINVAL;
   if (d->bn != 64 && d->bn != 128) return GSQ_EINVAL;
   const int epi = d->epi;
-  const int smp = d->softmax_phase;
-  if (smp < 0 || smp > 3) return GSQ_EINVAL;
-  if (!d->C && d->ncs == 0 && d->nct == 0 && !d->sq_partial && smp != 1 && smp != 2)
-    return GSQ_EINVAL;
-  if (smp && (epi != 0 || !d->skip_upper || M != N || d->bn != 128 || d->causal ||
-              d->split_k > 1 || d->C || d->nct || d->sq_partial || d->bias ||
-              (smp < 3 && (d->ncs || !d->softmax_part)) || (smp >= 2 && !d->softmax_m) ||
-              (smp == 3 && (d->ncs != 1 || !d->softmax_inv))))
-    return GSQ_EINVAL;
+  if (!d->C && d->ncs == 0 && d->nct == 0 && !d->sq_partial) return GSQ_EINVAL;
   const int amn = d->a_major != 0, bmn = d->b_major != 0;
   if (d->a_major < 0 || d->a_major > 1 || d->b_major < 0 || d->b_major > 1) return GSQ_EINVAL;
   if ((amn ? (d->lda < M || d->a_rows < K) : d->lda < K) ||
@@ -1622,11 +1546,6 @@ static int gemm_prepare(const gsq_gemm_desc* d, GemmPlan* plan) {
     if (!ok) return GSQ_EINVAL;
   }
   p.a_mn = amn;
-  p.sm_phase = smp;
-  p.sm_slots = 2 * ((N + 127) / 128);
-  p.sm_part = d->softmax_part;
-  p.sm_m = d->softmax_m;
-  p.sm_inv = d->softmax_inv;
   if (d->small_bufs < 0 || d->small_bufs > 2) return GSQ_EINVAL;
   // default: the epilogues that read row inputs and write several outputs per element (residual
   // loss, SwiGLU forward / backward) keep one cross-product accumulator and give its TMEM to
@@ -1724,7 +1643,6 @@ static int gemm_prepare(const gsq_gemm_desc* d, GemmPlan* plan) {
   }
   // the row-major outputs of the float32 SwiGLU backward exist only in the box epilogue
   if (epi == 3 && d->ncs > 0 && !p.tma_out) return GSQ_ENOTSUP;
-  if (smp == 3 && !p.tma_out) return GSQ_ENOTSUP;  // P leaves through the cs box stores
   if (BN == 64 && p.splits == 1 && epi != 0 && epi != 1 && epi != 3 && epi != 4)
     return GSQ_EINVAL;
   plan->p = p;

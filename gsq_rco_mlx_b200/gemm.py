@@ -152,10 +152,6 @@ class GemmDesc(_C.Structure):
         ("a_major", _C.c_int),
         ("b_major", _C.c_int),
         ("small_bufs", _C.c_int),
-        ("softmax_phase", _C.c_int),
-        ("softmax_part", _C.c_void_p),
-        ("softmax_m", _C.c_void_p),
-        ("softmax_inv", _C.c_void_p),
     ]
 
 
@@ -196,8 +192,7 @@ class LaunchLog:
     """Optional per-launch CUDA events of gemm() calls (for roofline measurements): while
     active, every call records (M, N, K, products, batch, start, end, tag); ``tag`` is the
     log's current tag (a stage name) at the call. ``batch`` is the work in M x N x K boxes:
-    the batch count, halved for causal and skip-upper (triangular) products, and 0 for the
-    statistics passes of the softmax epilogue (their time counts, their recomputed work not)."""
+    the batch count, halved for causal and skip-upper (triangular) products."""
     active = None
 
     def __init__(self):
@@ -233,8 +228,7 @@ def _describe(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, orde
          aux0=None, aux1=None, ld_aux=None, B2: Terms = None, epi=0, bn=128, causal=False,
          batch=1, a_off=(1, 0, 0), b_off=(1, 0, 0), c_off=(1, 0, 0), t_off=(1, 0, 0, 0, 0),
          ct_up_rows=0, skip_upper=False, row_period=0, split_k="auto", a_major=0, b_major=0,
-         small_bufs=0, softmax_phase=0, softmax_part=None, softmax_m=None, softmax_inv=None,
-         own_workspace=False):
+         small_bufs=0, own_workspace=False):
     """The descriptor of one gemm() call: (GemmDesc, (M, N, K, products, work boxes, launches),
     the split-K workspace tensor or None). own_workspace: a workspace of its own (a plan keeps
     its pointer) instead of the shared, growing one."""
@@ -277,9 +271,6 @@ def _describe(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, orde
     d.skip_upper = int(skip_upper)
     d.row_period = int(row_period)
     d.small_bufs = int(small_bufs)
-    d.softmax_phase = int(softmax_phase)
-    d.softmax_part, d.softmax_m, d.softmax_inv = (_tp(softmax_part), _tp(softmax_m),
-                                                   _tp(softmax_inv))
     splittable = (epi == 0 and batch == 1 and not causal and C is not None and bias is None
                   and c_terms is None and ct_terms is None and sq_partial is None)
     if split_k == "auto":
@@ -308,8 +299,6 @@ def _describe(A: Terms, B: Terms, M=None, N=None, K=None, na=None, nb=None, orde
     # a causal product (or a square one whose upper tiles are skipped) does half the work of
     # its M x N x K box: count batch x 1/2
     eff = batch * (0.5 if (causal or skip_upper) else 1.0)
-    if softmax_phase in (1, 2):
-        eff = 0.0   # the softmax's statistics passes recompute the scores: no new work
     return d, (d.M, d.N, d.K, prods, eff, 1 + extra), ws
 
 
@@ -375,6 +364,8 @@ class PlanCache:
         p.run()
 
 
+
+
 def gemm_tc(A: Terms, B: Terms, na=None, nb=None, order=2, alpha=1.0, C=None, beta=0.0,
             c_terms: Terms = None, ct_terms: Terms = None, sq_partial=None):
     """C = alpha A B^T on tcgen05 with split-bf16 operands (see include/gsq_rco_b200.h)."""
@@ -392,36 +383,3 @@ def gemm_tc(A: Terms, B: Terms, na=None, nb=None, order=2, alpha=1.0, C=None, be
               0 if ct_terms is None else ct_terms.ld, _lib.ptr(sq_partial),
               _lib.ptr(err_flag(dev)), _lib.stream_ptr())
     return C
-
-
-class CausalSoftmax:
-    """P = bf16(causal row softmax of x = alpha q k^T) for batches of square T x T scores,
-    computed inside the scores GEMM in three passes (gsq_gemm_desc.softmax_phase): the row
-    maxima, the row sums of expf(x - m), then P itself; two small reductions turn each pass's
-    per-tile partials into the row statistics. The float32 scores are never written (the
-    one-warp-per-row softmax needs them written and read back: 8 B per score against 2 B for P
-    here). The arithmetic is the softmax kernel's: P is the same bf16 values."""
-
-    def __init__(self, batch, T, dev):
-        self.batch, self.T = int(batch), int(T)
-        self.slots = 2 * ((self.T + 127) // 128)
-        self.part = torch.empty(self.batch * self.T * self.slots, device=dev, dtype=torch.float64)
-        self.m = torch.empty(self.batch * self.T, device=dev, dtype=torch.float32)
-        self.inv = torch.empty(self.batch * self.T, device=dev, dtype=torch.float32)
-
-    def run(self, q: Terms, k: Terms, P: Terms, plans=None, key="softmax", **kw):
-        """kw: the scores GEMM's batching arguments (M = N = T, K, batch, alpha, a_off, b_off,
-        c_off for P); plans: a PlanCache to run the three GEMMs from (or single calls)."""
-        st = _lib.stream_ptr()
-        common = dict(skip_upper=True, softmax_part=self.part, softmax_m=self.m,
-                      softmax_inv=self.inv, **kw)
-        go = (lambda tag, **a: plans.run((key, tag), q, k, **a)) if plans is not None else \
-            (lambda tag, **a: gemm(q, k, **a))
-        go(1, softmax_phase=1, **common)
-        _lib.call("gsq_softmax_rows_reduce", 1, _lib.ptr(self.part), self.batch, self.T,
-                  self.slots, _lib.ptr(self.m), None, st)
-        go(2, softmax_phase=2, **common)
-        _lib.call("gsq_softmax_rows_reduce", 2, _lib.ptr(self.part), self.batch, self.T,
-                  self.slots, None, _lib.ptr(self.inv), st)
-        go(3, softmax_phase=3, c_terms=P, **common)
-

@@ -9,10 +9,7 @@ bf16, as seven tensor-core GEMMs with fused epilogues plus four elementwise kern
   v^T = bf16(bf16(hn Wv^T) + bv), transposed per seq   gemm, batched over sequences
   rope(q), rope(k) as float32 operand terms            gsq_rope_split
   S   = rope(q) rope(k)^T / 8 (float32-faithful)       gemm, batched (seq, head), causal tiles
-  P   = bf16(softmax(S)) (causal)                      three passes of the S gemm with the
-                                                       softmax epilogue (S never stored), or
-                                                       S stored + gsq_softmax_causal when
-                                                       the backward needs S
+  P   = bf16(softmax(S)) (causal)                      gsq_softmax_causal
   o   = bf16(P v)                                      gemm, batched (seq, head), causal k-range
   h1  = bf16(h + bf16(o Wo^T))                         gemm, bf16 chain with residual
   mn  = rmsnorm(h1)                                    gsq_rmsnorm
@@ -31,7 +28,7 @@ import numpy as np
 import torch
 
 from .. import _lib
-from ..gemm import CausalSoftmax, Terms, err_flag, gemm, pad8
+from ..gemm import Terms, err_flag, gemm, pad8
 
 LIN_ORDER = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
 TAPS = ("hn", "o", "mn", "d_in")  # inputs of q/k/v, o, gate/up, down
@@ -134,11 +131,8 @@ class Qwen2Block:
         return self.taps_t[name]
 
     # ------------------------------------------------------------------------ forward ---
-    def attention(self, hn, W: BlockWeights, S, o_out, o_tap=None, probs_t=None,
-                  keep_scores=False):
-        """Causal GQA self-attention before o_proj of S sequences: o_out bf16 [S*T, H].
-        keep_scores: write the float32 scores (self.scores, for the backward) and take P from
-        them; otherwise P comes out of the scores GEMM's three-pass softmax epilogue."""
+    def attention(self, hn, W: BlockWeights, S, o_out, o_tap=None, probs_t=None):
+        """Causal GQA self-attention before o_proj of S sequences: o_out bf16 [S*T, H]."""
         c, T = self.cfg, self.T
         R = S * T
         st = _lib.stream_ptr()
@@ -162,18 +156,11 @@ class Qwen2Block:
                   _lib.ptr(t[2]), st)
         # scores (seq, head) = q_rot k_rot^T / sqrt(64), causal tiles only
         B = S * c.n_heads
-        if keep_scores or probs_t is not None:
-            gemm(self.q_rot, self.k_rot, M=T, N=T, K=c.head_dim, batch=B, alpha=1.0 / 8.0,
-                 C=self.scores, ldc=T, a_off=(1, T, 0), b_off=(c.rep, T, 0),
-                 c_off=(1, T * T, 0), skip_upper=True)
-            _lib.call("gsq_softmax_causal", _lib.ptr(self.scores), B, T, _lib.ptr(self.P.t[0]),
-                      _lib.ptr(probs_t), st)
-        else:
-            if getattr(self, "_softmax", None) is None or self._softmax.batch < B:
-                self._softmax = CausalSoftmax(self.S * c.n_heads, T, self.dev)
-            self._softmax.run(self.q_rot, self.k_rot, self.P, M=T, N=T, K=c.head_dim, batch=B,
-                              alpha=1.0 / 8.0, a_off=(1, T, 0), b_off=(c.rep, T, 0),
-                              c_off=(1, T * T, 0))
+        gemm(self.q_rot, self.k_rot, M=T, N=T, K=c.head_dim, batch=B, alpha=1.0 / 8.0,
+             C=self.scores, ldc=T, a_off=(1, T, 0), b_off=(c.rep, T, 0), c_off=(1, T * T, 0),
+             skip_upper=True)
+        _lib.call("gsq_softmax_causal", _lib.ptr(self.scores), B, T, _lib.ptr(self.P.t[0]),
+                  _lib.ptr(probs_t), st)
         # o (seq, head) = P v, written at columns h * 64 of row s * T + t
         Ot = Terms(R, c.hidden, 1, ld=c.hidden, tensors=[o_out])
         gemm(self.P, self.vT, M=T, N=c.head_dim, K=T, batch=B, bn=64, causal=1, epi=4,
@@ -182,15 +169,14 @@ class Qwen2Block:
              ct_terms=o_tap, t_off=(c.n_heads, 0, c.head_dim, T, 0))
 
     def forward(self, h, W: BlockWeights, S=None, out=None, taps=(), attn_out=None, upto=None,
-                mn=None, gu=None, keep_scores=False):
+                mn=None, gu=None):
         """Block forward of S sequences h bf16 [S*T, H] -> out bf16 [S*T, H]. taps: names of
         TAPS to write transposed (self.tap(name)), position-0 columns zeroed.
         attn_out: also the attention output after o_proj (no residual; the vo-stage target);
         without `out` the forward ends there. upto: end after the named site ("hn", "o", "mn",
         "d_in") when only its tap is wanted. mn: bf16 [S*T, H] post-attention-norm rows of an
         earlier pass; the forward then starts at the MLP, with h the attention block output h1
-        (unused for upto="d_in"). keep_scores: also write the float32 attention scores
-        (self.scores, which the backward reads)."""
+        (unused for upto="d_in")."""
         c, T = self.cfg, self.T
         S = self.S if S is None else S
         R = S * T
@@ -204,7 +190,7 @@ class Qwen2Block:
         if upto == "hn":
             return None
         o_tap = self.tap("o") if "o" in taps else None
-        self.attention(self.hn[:R], W, S, self.o[:R], o_tap=o_tap, keep_scores=keep_scores)
+        self.attention(self.hn[:R], W, S, self.o[:R], o_tap=o_tap)
         if o_tap is not None:
             _lib.call("gsq_zero_cols", _lib.ptr(o_tap.t[0]), c.hidden, o_tap.ld, R, T, st)
         if upto == "o":
@@ -320,8 +306,7 @@ class Qwen2Block:
         beta = 1.0 if accumulate else 0.0
         dh = torch.empty(R, H, device=dev, dtype=torch.bfloat16) if dh is None else dh
         # forward recompute, keeping the intermediates (and bf16 g, u)
-        self.forward(h, W, S=S, out=b["out"][:R], gu=(b["g"][:R], b["u"][:R]),
-                     keep_scores=True)
+        self.forward(h, W, S=S, out=b["out"][:R], gu=(b["g"][:R], b["u"][:R]))
         rows = lambda x, n=None: Terms(x.shape[0] if n is None else n, x.shape[1], 1,
                                        ld=x.shape[1], tensors=[x if n is None else x[:n]])
         # weight gradients dW = dY^T X: both row-major [R, .] activations read as MN-major

@@ -25,7 +25,7 @@ import numpy as np
 import torch
 
 from .. import _lib
-from ..gemm import CausalSoftmax, PlanCache, Terms, check_err, err_flag, gemm, gemm_tc, pad8
+from ..gemm import PlanCache, Terms, check_err, err_flag, gemm, gemm_tc, pad8
 from .gptq import init_logits_2bit_from_codes, init_shift_logits, init_ternary_logits
 from .lion import BETAS, LR_LOGITS, LR_SCALES, WEIGHT_DECAY, scale_lr
 from .quant import get_grid, gs_schedules
@@ -595,14 +595,8 @@ class VOStep(_StageBase):
         self.QK = torch.empty(m * Tk, (nh + nkv) * hd, device=dev, dtype=torch.bfloat16)
         self.q_rot = Terms(m * nh * Tk, hd, 3, dev)
         self.k_rot = Terms(m * nkv * Tk, hd, 3, dev)
+        self.scores = torch.empty(m * nh, Tq, Tk, device=dev, dtype=torch.float32)
         self.P = Terms(m * nh * Tq, Tk, 1, dev)
-        # the whole causal square (q0 = 0): P from the scores GEMM's three-pass softmax
-        # epilogue; a query window: float32 scores and the row-windowed softmax kernel
-        if self.q0 == 0:
-            self.softmax, self.scores = CausalSoftmax(m * nh, Tk, dev), None
-        else:
-            self.softmax = None
-            self.scores = torch.empty(m * nh, Tq, Tk, device=dev, dtype=torch.float32)
         # dV = P^T dO reads P as an MN-major operand when the query window is whole k-blocks;
         # otherwise through a transposed copy
         self.PT = None if Tq % 64 == 0 else Terms(m * nh * Tk, Tq, 1, dev)
@@ -649,17 +643,17 @@ class VOStep(_StageBase):
                   _lib.ptr(self.sin), _lib.ptr(t[0]), _lib.ptr(t[1]), _lib.ptr(t[2]), st)
         B = m * c.n_heads
         if q0 == 0:   # square: tiles above the diagonal are never read
-            self.softmax.run(self.q_rot, self.k_rot, self.P, plans=self.plans, M=Tk, N=Tk,
-                             K=c.head_dim, batch=B, alpha=1.0 / 8.0, a_off=(1, Tk, 0),
-                             b_off=(c.rep, Tk, 0), c_off=(1, Tk * self.P.ld, 0))
+            self.plans.run("scores", self.q_rot, self.k_rot, M=Tk, N=Tk, K=c.head_dim, batch=B,
+                           alpha=1.0 / 8.0, C=self.scores, ldc=Tk, a_off=(1, Tk, 0),
+                           b_off=(c.rep, Tk, 0), c_off=(1, Tk * Tk, 0), skip_upper=True)
         else:         # the query rows q0.. of each (sequence, head) block of q_rot
             qv = Terms(self.q_rot.rows - q0, c.head_dim, 3, ld=self.q_rot.ld,
                        tensors=[x[q0:] for x in self.q_rot.t])
             self.plans.run("scores", qv, self.k_rot, M=Tq, N=Tk, K=c.head_dim, batch=B,
                            alpha=1.0 / 8.0, C=self.scores, ldc=Tk, a_off=(1, Tk, 0),
                            b_off=(c.rep, Tk, 0), c_off=(1, Tq * Tk, 0))
-            _lib.call("gsq_softmax_causal_rows", _lib.ptr(self.scores), B, Tq, Tk, Tk, q0,
-                      _lib.ptr(self.P.t[0]), self.P.ld, st)
+        _lib.call("gsq_softmax_causal_rows", _lib.ptr(self.scores), B, Tq, Tk, Tk, q0,
+                  _lib.ptr(self.P.t[0]), self.P.ld, st)
         if self.PT is not None:
             # P^T feeds the causal dV GEMM when q0 = 0: the transposes of P's zero tiles are unread
             _lib.call("gsq_transpose_bf16", _lib.ptr(self.P.t[0]), Tq, Tk, self.P.ld,

@@ -178,18 +178,6 @@ typedef struct {
    * that TMEM to one more chunk of the hi x hi ring instead; 0 = 1 for epi 1, 2, 3 and 2 for
    * the others. Same results either way. */
   int small_bufs;
-  /* Causal row softmax of square scores (epi 0, skip_upper, M == N, bn 128, no C / ct / bias /
-   * split-K) in three passes of the same GEMM, each x = alpha acc of key k <= query r:
-   * 1: softmax_part float [batch][M][2 ceil(N / 128)] = the maxima of each tile half of a row;
-   * 2: softmax_part double (same shape) = the sums of expf(x - m) with m = softmax_m[z][r];
-   * 3: cs (1 term) = bf16(expf(x - m) * softmax_inv[z][r]), zero at masked keys of the tiles
-   *    on the diagonal. gsq_softmax_rows_reduce turns the partials of 1 into softmax_m and of
-   *    2 into softmax_inv = 1 / sum. P equals gsq_softmax_causal's from the float32 scores
-   *    (the same float32 arithmetic) without the scores ever being written. 0: off. */
-  int softmax_phase;
-  void *softmax_part;
-  const float *softmax_m;
-  const float *softmax_inv;
 } gsq_gemm_desc;
 
 /* Batched float32-faithful tensor-core GEMM with a fused epilogue (see gsq_gemm_tc for the
@@ -280,13 +268,6 @@ int gsq_head_group_sum_t(const float *dv, int S, int nh, int rep, int T, void *o
 int gsq_dot_terms(const void *t0, const void *t1, const void *t2, int64_t ld_t, const float *G,
                   int64_t ld_g, int rows, int cols, double scale, double *partials, double *out,
                   void *stream);
-
-/* Row statistics of the three-pass causal softmax (gsq_gemm_desc.softmax_phase) for batch x T
- * rows with slots partials each (row r of a batch uses the first 2 (r / 128 + 1)): phase 1:
- * m[row] = max of the float partials; phase 2: inv[row] = 1 / float(sum of the double partials
- * in slot order). Replaces the row passes of the softmax of src/gsq_rco/gsq/e2e.py:149-155. */
-int gsq_softmax_rows_reduce(int phase, const void *part, int batch, int T, int slots, float *m,
-                            float *inv, void *stream);
 
 /* out[0] = sum of x[0..n) in float64 (one block; the loss from per-tile partials). */
 int gsq_sum_f64(const double *x, int n, double *out, void *stream);

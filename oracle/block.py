@@ -259,6 +259,15 @@ def _hard_weight(codes, s16, bits, group_size):
     return torch.as_tensor(np.asarray(w, dtype=np.float32)).bfloat16()
 
 
+def recon_error(W, codes, s16, bits, group_size, H):
+    """The GPTQ objective tr((W - Q) H (W - Q)^T) of codes with float16 scales under the
+    Hessian H (gptq.py:123-187 minimises it column by column), float64."""
+    from .gptq import dequantize
+    Q = dequantize(codes, np.asarray(s16, dtype=np.float32), bits, group_size)
+    D = np.asarray(W, dtype=np.float64) - np.asarray(Q, dtype=np.float64)
+    return float(np.einsum("ij,ij->", D @ np.asarray(H, dtype=np.float64), D))
+
+
 def quantize_block(h_seqs, W, bits, steps, layer=0, opt_seed=0, n_heads=14, n_kv=2,
                    group_size=64, damp=0.01, block_size=128, micro_batch=2, resamples=2,
                    eps=1e-6, warm_start=None, follow=None):
@@ -272,7 +281,8 @@ def quantize_block(h_seqs, W, bits, steps, layer=0, opt_seed=0, n_heads=14, n_kv
     record this chain's hardened result but continue from these (another run's hardened
     weights), so that every stage starts from the same weights as that run's.
     Returns (shard {name: {codes, scales, bits}}, {stage: loss history},
-    {name: this chain's own GPTQ (codes, float16 scales)})."""
+    {name: this chain's own GPTQ (codes, float16 scales, {"own": its objective under this
+    chain's Hessian, "warm": the warm start's objective under the same Hessian or None})})."""
     from .gptq import quantize_gptq
     from .gsq import LinearState, train_linear
     Wf = {k: v.float() for k, v in W.items()}
@@ -282,12 +292,15 @@ def quantize_block(h_seqs, W, bits, steps, layer=0, opt_seed=0, n_heads=14, n_kv
     states = {}
 
     def gptq(name, H, pos):
-        g = quantize_gptq(Wf[name].numpy(), H, bits[name], group_size, damp, block_size)
+        w = Wf[name].numpy()
+        g = quantize_gptq(w, H, bits[name], group_size, damp, block_size)
         codes, s16 = g["codes"], g["scales"].astype(np.float16)
-        gptq_codes[name] = (codes, s16)
+        errs = {"own": recon_error(w, codes, s16, bits[name], group_size, H), "warm": None}
+        gptq_codes[name] = (codes, s16, errs)
         if warm_start is not None:
             codes = np.asarray(warm_start[name]["codes"], dtype=np.uint8)
             s16 = np.asarray(warm_start[name]["scales"], dtype=np.float16)
+            errs["warm"] = recon_error(w, codes, s16, bits[name], group_size, H)
         Wcur[name] = _hard_weight(codes, s16, bits[name], group_size)
         states[name] = LinearState(bits[name], codes, s16, group_size, seed=seed + 10 * pos,
                                    linear_id=layer * 8 + pos)

@@ -95,7 +95,10 @@ def test_down_proj_gptq_parity():
 
 def test_quantize_block_end_to_end_parity(c_oracle):
     """quantize_block against the oracle's chain of the same steps, stage by stage. The GPTQ
-    warm starts are compared with the oracle's own solves on the oracle's own Hessians; then
+    warm starts are compared with the oracle's own solves on the oracle's own Hessians (codes
+    where both sides' inputs are the same normed rows; elsewhere the GPTQ objective under the
+    oracle's Hessian, since one flipped near-tie early in a 4864-wide row moves the error fed
+    to every later column of it, and so its codes, without changing the objective); then
     the oracle trains each stage from the GPU's warm starts and continues from the GPU's
     hardened weights at each stage boundary, so that each stage (its inputs and targets from
     the forwards under the hardened weights, 200 Lion steps, hardening) is compared from the
@@ -122,12 +125,14 @@ def test_quantize_block_end_to_end_parity(c_oracle):
     fails = []
     # Each side builds its stage inputs with its own bf16 forward (rare last-bit differences in
     # hn, P, mn, d_in), so the Hessians differ in their last bits: GPTQ warm starts agree on
-    # >= 99.9 % where the inputs are the normed rows (q / k / v) and >= 99 % behind the
-    # attention and the MLP. qk: codes and loss at the absolute bar, scales within 2e-3; vo /
+    # >= 99.9 % of the codes where the inputs are the normed rows (q / k / v), and behind the
+    # attention and the MLP the GPU's warm start scores within 1e-3 of the oracle's own solve
+    # on the GPTQ objective under the oracle's Hessian. qk: codes and loss at the absolute bar,
+    # scales within 2e-3; vo /
     # mlp: the spread that float32-level perturbations alone produce in the oracle over 200
     # steps at these widths (tests/test_stages_full_width_gpu.py measures it: logits and scales
     # about 2e-2, codes about 99.2 %), with margin.
-    gptq_bar = {"q_proj": 0.999, "k_proj": 0.999, "v_proj": 0.999}
+    codes_same_rows = {"q_proj", "k_proj", "v_proj"}
     bars = {"qk": (0.999, 2e-3, 1e-3), "vo": (0.985, 5e-2, 2e-2), "mlp": (0.985, 5e-2, 2e-2)}
     for stage, names in ob.STAGE_LINEARS.items():
         codes_bar, scales_bar, loss_bar = bars[stage]
@@ -135,13 +140,15 @@ def test_quantize_block_end_to_end_parity(c_oracle):
         rloss = abs(loss - hist_o[stage][-1]) / hist_o[stage][-1]
         for n in names:
             g_eq = (warm[n]["codes"] == own[n][0]).mean()
+            g_obj = abs(own[n][2]["warm"] - own[n][2]["own"]) / own[n][2]["own"]
             eq = (shard[n]["codes"] == shard_o[n]["codes"]).mean()
             rs = _rel(shard[n]["scales"].astype(np.float32),
                       shard_o[n]["scales"].astype(np.float32))
-            print(f"{stage} {n}: gptq codes {g_eq:.6f}  final codes {eq:.6f} scales {rs:.2e} "
-                  f"loss {rloss:.2e}")
-            if g_eq < gptq_bar.get(n, 0.99) or eq < codes_bar or rs > scales_bar:
-                fails.append((n, g_eq, eq, rs))
+            print(f"{stage} {n}: gptq codes {g_eq:.6f} objective {g_obj:.2e}  final codes "
+                  f"{eq:.6f} scales {rs:.2e} loss {rloss:.2e}")
+            gptq_ok = g_eq >= 0.999 if n in codes_same_rows else g_obj <= 1e-3
+            if not gptq_ok or eq < codes_bar or rs > scales_bar:
+                fails.append((n, g_eq, g_obj, eq, rs))
         if rloss > loss_bar:
             fails.append((stage, rloss))
     assert not fails, fails

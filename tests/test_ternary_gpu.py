@@ -37,7 +37,8 @@ def test_ternary_soft_weight(host_noise):
         w_o, p_o, _ = ogsq.soft_weight(st.logits, noise, None, st.scales, W.shape, 64, tau, kappa)
         P = torch.empty(2, W.size, device=DEV)
         nz = torch.as_tensor(noise, device=DEV) if host_noise else None
-        got = lin.soft(tau, kappa, step, r, 11, noise=nz, probs=P).cpu().numpy()
+        got = lin.soft(tau, kappa, step, r, 11, noise=nz, probs=P,
+                       out=torch.empty(W.shape, device=DEV)).cpu().numpy()
         s = np.abs(w_o).max()
         np.testing.assert_allclose(got, w_o, rtol=2e-6, atol=2e-6 * s)
         np.testing.assert_allclose(P.cpu().numpy(), p_o, rtol=2e-6, atol=1e-30)
