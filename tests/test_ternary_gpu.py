@@ -41,7 +41,10 @@ def test_ternary_soft_weight(host_noise):
                        out=torch.empty(W.shape, device=DEV)).cpu().numpy()
         s = np.abs(w_o).max()
         np.testing.assert_allclose(got, w_o, rtol=2e-6, atol=2e-6 * s)
-        np.testing.assert_allclose(P.cpu().numpy(), p_o, rtol=2e-6, atol=1e-30)
+        # probabilities to float32 accuracy in absolute terms: the in-kernel Gumbel transform
+        # uses the hardware base-2 logarithm, a few ulps from the oracle's, which moves a
+        # saturated sigmoid (m ~ 1e-9) by more than its own relative precision
+        np.testing.assert_allclose(P.cpu().numpy(), p_o, rtol=2e-6, atol=2e-7)
 
 
 def test_ternary_step_and_next_forward():
