@@ -158,26 +158,28 @@ def quantize_rtn(W, bits, group_size=64, signed_scale=True, device=False):
 
 # ------------------------------------------------------------------ App-A inits (host) ---
 
-def _noisy_alpha_init(base, alpha, std, seed):
-    """l = std * (eps + alpha * (base - mean_k base)), eps ~ N(0, 1) from default_rng(seed)."""
-    rng = np.random.default_rng(seed)
-    b = base - base.mean(axis=-1, keepdims=True)
-    eps = rng.standard_normal(base.shape).astype(np.float32)
-    return (std * (eps + alpha * b)).astype(np.float32)
+def _app_a_logits(base, alpha, std, seed):
+    """Eq. 4 of the GSQ paper's App. A: std (N(0, 1) + alpha (base - its mean over the
+    candidates)), the normals one default_rng(seed) draw of base's shape; float32 [d, K]."""
+    centred = base - base.mean(axis=-1, keepdims=True)
+    normals = np.random.default_rng(seed).standard_normal(base.shape).astype(np.float32)
+    return (std * (normals + alpha * centred)).astype(np.float32)
 
 
 def init_logits_2bit_from_codes(codes, K, alpha=6.0, std=0.01, seed=0):
-    """2-bit full grid: base_k = -(k - q_i)^2 / 2 (reference gptq.py:202-210). [d, K]."""
-    kk = np.arange(K, dtype=np.float32)
-    base = -((kk[None, :] - np.asarray(codes).reshape(-1)[:, None].astype(np.float32)) ** 2) / 2.0
-    return _noisy_alpha_init(base.astype(np.float32), alpha, std, seed)
+    """2-bit full grid (reference gptq.py:202-210): the base of weight i at grid level k is
+    -(k - q_i)^2 / 2, peaked at its GPTQ code q_i. [d, K]."""
+    q = np.asarray(codes).reshape(-1, 1).astype(np.float32)
+    levels = np.arange(K, dtype=np.float32)[None, :]
+    return _app_a_logits(-0.5 * np.square(levels - q), alpha, std, seed)
 
 
 def init_shift_logits(numel, alpha=6.0, std=0.01, seed=0):
-    """Local shift: base_k = -(k - 2)^2 / 2 (reference gptq.py:213-219). [d, 5]."""
-    c = np.array([-2, -1, 0, 1, 2], dtype=np.float32)
-    base = np.tile(-(c ** 2) / 2.0, (int(numel), 1))
-    return _noisy_alpha_init(base, alpha, std, seed)
+    """Local shift (reference gptq.py:213-219): every weight's base over the shifts -2..2 is
+    -shift^2 / 2, peaked at the GPTQ code itself. [d, 5]."""
+    shifts = np.arange(-2, 3, dtype=np.float32)
+    base = np.broadcast_to(-0.5 * np.square(shifts), (int(numel), shifts.size))
+    return _app_a_logits(base, alpha, std, seed)
 
 
 def init_ternary_logits(q_gptq, alpha=3.0, std=0.01, seed=0):

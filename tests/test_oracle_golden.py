@@ -51,6 +51,16 @@ def test_grid_schedule_local_shift_inits():
                           z["init2"])
 
 
+def test_product_inits_match_reference():
+    """The product's App-A logit inits (host numpy, gsq/gptq.py) against the reference's own
+    outputs: the same normals and float32 arithmetic, bit for bit."""
+    from gsq_rco_mlx_b200.gsq import gptq as pg
+    z = load("gsq.npz")
+    assert np.array_equal(pg.init_shift_logits(300, 6.0, 0.01, seed=5), z["init_shift"])
+    assert np.array_equal(pg.init_logits_2bit_from_codes(z["init2_codes"], 4, 6.0, 0.01, seed=6),
+                          z["init2"])
+
+
 def test_linear_grads_match_reference_oracle_2bit():
     """The restated loss/gradients equal tests/oracles.py:311-347 on the same Gumbel draws."""
     z = load("gsq.npz")
