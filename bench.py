@@ -11,19 +11,19 @@ configuration's shapes and distributions; every stage step's working set (the bl
 weights, probabilities, momenta: > 1 GB) exceeds the 126 MB L2.
 
 Workload "linear": one up_proj-shaped linear (W 4864 x 896, X 16384 x 896 as 32 x 512), the
-qk-stage step of one linear (BASELINE config 1).
+qk-stage step of one linear.
 
 Workload "gptq": GPTQ of the 168 linears of a random-init 24-layer stack at 2, 3 and 4 bits from
-Hessians over 128 x 2048 tokens (BASELINE config 3); value = seconds per model (lower is
+Hessians over 128 x 2048 tokens; value = seconds per model (lower is
 better); under torchrun the windows and solves are sharded (strong scaling, NCCL all-reduce of
 the Hessians).
 
-Workload "rco": RCO allocation (BASELINE config 4) on the same stack and a GPTQ database at
+Workload "rco": RCO allocation on the same stack and a GPTQ database at
 2 / 3 / 4 bits: seconds per RCO step of 8 Gumbel samples x 32 windows x 2048 tokens (forward,
 KL head, backward through 24 blocks, straight-through dots); at most 2 timed steps after 3
 warm-up steps (a step takes seconds); windows sharded over ranks under torchrun.
 
-Workload "eval": the quantized-model eval (BASELINE config 5) on the same stack: packed
+Workload "eval": the quantized-model eval on the same stack: packed
 mixed 2 / 3 / 4-bit MLX-affine linears (a 3.0-bit allocation from the GPTQ database, fp16 g64
 scales), 146 windows x 2048 ids, next-token NLL; value = scored tokens per second of one pass
 over all windows (each window's 8-window batch dequantizes every layer into L2-resident bf16
@@ -31,7 +31,8 @@ scratch, then runs the bf16 tensor-core forward and the head + NLL row pass).
 
 Workload "pipeline": the full 3-bit pipeline on the stack (build-db, RCO allocate, quantize the
 24 blocks on the quantized stream, export, eval), each phase timed; value = wall-clock seconds
-with the allocate phase extrapolated to 100 RCO steps from --rco-steps measured ones.
+with the allocate phase at 100 RCO steps (those of the 100 not among the --rco-steps measured
+ones counted at the measured mean).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--workload block|linear|gptq|rco|eval|pipeline] [--rco-steps S]
@@ -306,7 +307,7 @@ def run_block(args):
         "higher_is_better": True, "scaling": "weak" if args.split == "sequences" else "strong",
         "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: random-init bf16 block and embedding, uniform-random token ids",
-        "config": {"workload": "config 2: one Qwen2.5-0.5B block, calib 128 x 2048, micro-batch 2, R=2",
+        "config": {"workload": "one Qwen2.5-0.5B block, calib 128 x 2048, micro-batch 2, R=2",
                    "stage_ms_per_step": {k: round(v, 4) for k, v in ms.items()},
                    "block_seconds_200_steps": round(e2e_ms / 1000, 3),
                    "parallelism": (f"one block, data-parallel over {world} GPU(s): each rank "
@@ -483,7 +484,7 @@ def run_reference(args):
            "value": round(v, 5), "unit": "block steps/s", "n_gpus": world, "steps": steps,
            "warmup": warmup, "ms_per_step": round(1000 / v, 1), "higher_is_better": True,
            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": "config 2: one Qwen2.5-0.5B block, calib 128 x 2048, micro-batch 2, R=2"},
+           "config": {"workload": "one Qwen2.5-0.5B block, calib 128 x 2048, micro-batch 2, R=2"},
            "cpu_baseline": cb,
            "e2e": {"value": round(v, 5), "unit": "block steps/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
@@ -565,7 +566,7 @@ def run_gptq(args):
         "warmup": args.warmup, "ms_per_step": round(sec * 1000, 1), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "f64 solves, bf16/f32 Hessians",
         "data": "synthetic: random-init bf16 24-layer stack, uniform-random token ids",
-        "config": {"workload": "config 3: 24-layer GPTQ, options (2, 3, 4), g64, damp 0.01",
+        "config": {"workload": "24-layer GPTQ, options (2, 3, 4), g64, damp 0.01",
                    "phase_seconds_per_model": phase,
                    "parallelism": f"windows and solves sharded over {world} rank(s)",
                    "l2": "per-layer working set (470 MB of hidden states) > L2"},
@@ -618,7 +619,7 @@ def run_reference_gptq(args):
            "value": cb["value"], "unit": "s/model", "n_gpus": world, "steps": 1, "warmup": 0,
            "ms_per_step": round(cb["value"] * 1000, 1), "higher_is_better": False,
            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-           "config": {"workload": "config 3: 24-layer GPTQ, options (2, 3, 4), g64, damp 0.01"},
+           "config": {"workload": "24-layer GPTQ, options (2, 3, 4), g64, damp 0.01"},
            "cpu_baseline": cb,
            "e2e": {"value": cb["value"], "unit": "s/model", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
@@ -700,7 +701,7 @@ def run_rco(args):
         "warmup": warmup, "ms_per_step": round(sec * 1000, 1), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16 model, f32/f64 objective",
         "data": "synthetic: random-init 24-layer stack, uniform-random token windows",
-        "config": {"workload": "config 4: RCO allocation, windows_per_sample 32, g 8, Adam lr 0.1",
+        "config": {"workload": "RCO allocation, windows_per_sample 32, g 8, Adam lr 0.1",
                    "decoded_avg_bits": res["decoded_avg_bits"],
                    "parallelism": f"windows of each sample sharded over {world} rank(s)",
                    "l2": "25 decoder states of 32 x 2048 tokens (3 GB) > L2"},
@@ -771,7 +772,7 @@ def run_reference_rco(args):
            "value": cb["value"], "unit": "s/step", "n_gpus": world, "steps": 1, "warmup": 0,
            "ms_per_step": round(cb["value"] * 1000, 1), "higher_is_better": False,
            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-           "config": {"workload": "config 4: RCO allocation, windows_per_sample 32, g 8"},
+           "config": {"workload": "RCO allocation, windows_per_sample 32, g 8"},
            "cpu_baseline": cb,
            "e2e": {"value": cb["value"], "unit": "s/step", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
@@ -917,7 +918,7 @@ def run_eval(args):
         "warmup": warmup, "ms_per_step": round(sec * 1000, 2), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init 24-layer stack, GPTQ database, uniform-random windows",
-        "config": {"workload": "config 5: packed-model eval, 146 windows x 2048",
+        "config": {"workload": "packed-model eval, 146 windows x 2048",
                    **info, "nll_per_token": round(nll, 6), "windows_per_batch": EVAL_CHUNK,
                    "parallelism": f"windows sharded over {world} rank(s), NCCL all-reduce of "
                                   "the NLL sum",
@@ -997,7 +998,7 @@ def run_reference_eval(args):
            "ms_per_step": round(EVAL_WINDOWS * (T_SEQ - 1) / cb["value"] * 1000, 1),
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
            "data": "synthetic",
-           "config": {"workload": "config 5: packed-model eval, 146 windows x 2048"},
+           "config": {"workload": "packed-model eval, 146 windows x 2048"},
            "cpu_baseline": cb,
            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
@@ -1145,7 +1146,7 @@ def make_inputs(seed=0):
 
 
 def run_linear(args):
-    """the qk-stage step of one up_proj-shaped linear."""
+    """The qk-stage step of one up_proj-shaped linear (W 4864 x 896, X 16384 x 896)."""
     import torch
     import torch.distributed as dist
     from gsq_rco_mlx_b200 import _lib
@@ -1252,7 +1253,7 @@ def run_linear(args):
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1) x lognormal channels, random-init weights)",
-        "config": {"workload": "config 1: single linear GSQ (W 4864x896, X 16384x896 as 32x512)",
+        "config": {"workload": "single linear GSQ (W 4864x896, X 16384x896 as 32x512)",
                    "rows_per_step": M, "resamples": RESAMPLES, "bits": 3, "group_size": 64,
                    "parallelism": f"replicas x{world}", "l2": "per-step working set > L2 (126 MB)"},
         "e2e": {"value": round(world * args.steps / (ms_e2e * 1e-3), 3), "unit": "steps/s",

@@ -47,7 +47,8 @@ def gen_gptq(gptq):
     out = {}
     rng = np.random.default_rng(100)
     cases = []
-    # config-1 statistics at a reduced shape: W ~ 0.02 N(0,1), X = N(0,1) * lognormal channel scales
+    # the single-linear workload's statistics at a reduced shape: W ~ 0.02 N(0,1),
+    # X = N(0,1) * lognormal channel scales
     for ci, (o, i, bits, gs, bsz) in enumerate([(96, 256, 3, 64, 128), (64, 256, 2, 64, 128),
                                                  (64, 256, 4, 64, 128), (48, 320, 3, 64, 128),
                                                  (40, 100, 3, 64, 128), (32, 192, 3, 64, 64)]):
