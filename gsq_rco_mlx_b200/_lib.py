@@ -26,6 +26,9 @@ SIGNATURES = {
     "gsq_soft_step": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32,
                       _f32, _f32, _f32, _f64, _f64, _f64, _i32, _vp, _u64, _u32, _u32, _f32,
                       _f32, _vp, _vp, _vp, _vp],
+    "gsq_soft_bwd_lion": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32,
+                          _f32, _f32, _f32, _f32, _f64, _f64, _f64, _i32, _vp, _u64, _u32, _u32,
+                          _f32, _f32, _vp, _vp, _vp, _vp],
     "gsq_harden": [_vp, _vp, _i32, _i32, _i32, _vp, _vp],
     "gsq_lion_f32": [_vp, _vp, _vp, _i64, _f32, _f64, _f64, _f64, _vp],
     "gsq_gemm_f32": [_i32, _i32, _i32, _f32, _vp, _i64, _i64, _vp, _i64, _i64, _f32, _vp, _i64,
@@ -45,6 +48,8 @@ SIGNATURES = {
     "gsq_softmax_causal": [_vp, _i32, _i32, _vp, _vp, _vp],
     "gsq_softmax_causal_rows": [_vp, _i32, _i32, _i32, _i64, _i32, _vp, _i64, _vp],
     "gsq_kl_rows": [_vp, _vp, _i32, _i32, _i64, _vp, _i64, _vp, _vp, _vp],
+    "kl_head_fwd_bwd": [_vp, _vp, _i32, _i32, _vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp,
+                        _vp, _vp, _vp, _vp],
     "gsq_div_bf16": [_vp, _i64, _f32, _vp],
     "gsq_dequant_bf16": [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp],
     "gsq_rmsnorm_bwd": [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _f64, _vp],

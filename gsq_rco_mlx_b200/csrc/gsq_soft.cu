@@ -714,6 +714,21 @@ extern "C" int gsq_soft_step(float* logits, float* mom_logits, const uint8_t* j0
   return GSQ_OK;
 }
 
+extern "C" int gsq_soft_bwd_lion(float* logits, float* mom_logits, const uint8_t* j0,
+                                 float* scales, float* mom_scales, float* probs,
+                                 const float* grad_w, int resamples, int out_f, int in_f,
+                                 int group_size, int bits, float tau, float kappa,
+                                 float lr_logits, float lr_scales, double wd, double beta1,
+                                 double beta2, int next, const float* noise_next, uint64_t seed,
+                                 uint32_t linear_id, uint32_t next_step, float tau_next,
+                                 float kappa_next, const float* w_ref, float* w_out,
+                                 void* w_terms, void* stream) {
+  return gsq_soft_step(logits, mom_logits, j0, scales, mom_scales, probs, grad_w, resamples,
+                       out_f, in_f, group_size, bits, tau, kappa, lr_logits, lr_scales, wd,
+                       beta1, beta2, next, noise_next, seed, linear_id, next_step, tau_next,
+                       kappa_next, w_ref, w_out, w_terms, stream);
+}
+
 extern "C" int gsq_harden(const float* logits, const uint8_t* j0, int out_f, int in_f, int bits,
                           uint8_t* codes, void* stream) {
   const int K = n_logit_planes(bits);

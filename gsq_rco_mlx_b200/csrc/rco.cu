@@ -13,6 +13,7 @@
 // reference weight W (bf16), dot_k = sum G (f32(bf16(s_k grid_k[code_k])) - f32(W)) for the K
 // database options, accumulated in float64 (deterministic two-level reduction).
 #include <math.h>
+#include <string.h>
 
 #include "common.cuh"
 
@@ -309,6 +310,62 @@ extern "C" int gsq_kl_rows(const void* zq, const void* zr, int n, int V, int64_t
       kl_rows, lse);
   GSQ_CHECK_LAUNCH();
   return GSQ_OK;
+}
+
+// One bf16 product out = bf16(A B^T) of single-term row-major operands (A [M][lda], B [N][ldb],
+// the reduction index contiguous) through gsq_gemm's bf16-chain epilogue: the descriptor the
+// library's Python gemm() builds for the same call.
+static int bf16_product(const void* A, int64_t lda, int M, const void* B, int64_t ldb, int N,
+                        int K, void* out, int64_t ldo, int* err, void* stream) {
+  gsq_gemm_desc d;
+  memset(&d, 0, sizeof(d));
+  d.M = M;
+  d.N = N;
+  d.K = K;
+  d.batch = 1;
+  d.a[0] = A;
+  d.na = 1;
+  d.lda = lda;
+  d.a_rows = M;
+  d.b[0] = B;
+  d.nb = 1;
+  d.ldb = ldb;
+  d.b_rows = N;
+  d.order = 2;
+  d.epi = 4;
+  d.bn = 128;
+  d.alpha = 1.f;
+  d.ldc = N;
+  d.cs[0] = out;
+  d.ncs = 1;
+  d.ldcs = ldo;
+  d.ld_rt = N;
+  d.out_scale = 1.f;
+  d.ld_aux = N;
+  d.a_div = d.b_div = d.c_div = d.t_div = 1;
+  d.err = err;
+  return gsq_gemm(&d, stream);
+}
+
+extern "C" int kl_head_fwd_bwd(const void* h_q, const void* h_ref, int n, int H, const void* E,
+                               const void* ET, int64_t ld_et, int V, int chunk, void* zq,
+                               void* zr, void* D, double* kl_rows, double* total, void* grad,
+                               int* err, void* stream) {
+  if (!h_q || !h_ref || !E || !ET || !zq || !zr || !D || !kl_rows || !total || !grad || !err ||
+      n <= 0 || H <= 0 || (H & 7) || V <= 0 || (V & 7) || chunk <= 0 || ld_et < V || (ld_et & 7))
+    return GSQ_EINVAL;
+  const auto* hq = static_cast<const __nv_bfloat16*>(h_q);
+  const auto* hr = static_cast<const __nv_bfloat16*>(h_ref);
+  auto* g = static_cast<__nv_bfloat16*>(grad);
+  for (int a = 0; a < n; a += chunk) {
+    const int m = n - a < chunk ? n - a : chunk;
+    int rc = bf16_product(hq + (int64_t)a * H, H, m, E, H, V, H, zq, V, err, stream);
+    if (rc == GSQ_OK) rc = bf16_product(hr + (int64_t)a * H, H, m, E, H, V, H, zr, V, err, stream);
+    if (rc == GSQ_OK) rc = gsq_kl_rows(zq, zr, m, V, V, D, V, kl_rows + a, nullptr, stream);
+    if (rc == GSQ_OK) rc = bf16_product(D, V, m, ET, ld_et, H, V, g + (int64_t)a * H, H, err, stream);
+    if (rc != GSQ_OK) return rc;
+  }
+  return gsq_sum_f64(kl_rows, n, total, stream);
 }
 
 extern "C" int ste_dots(const float* G, const void* W, int out_f, int in_f, int group_size,

@@ -90,6 +90,16 @@ int gsq_soft_step(float *logits, float *mom_logits, const uint8_t *j0, float *sc
                   float tau_next, float kappa_next, const float *w_ref, float *w_out,
                   void *w_terms, void *stream);
 
+/* gsq_soft_step under the name the reference-facing contract gives the fused soft backward +
+ * Lion step (+ the next step's forward): identical arguments, behaviour and status codes. */
+int gsq_soft_bwd_lion(float *logits, float *mom_logits, const uint8_t *j0, float *scales,
+                      float *mom_scales, float *probs, const float *grad_w, int resamples,
+                      int out_f, int in_f, int group_size, int bits, float tau, float kappa,
+                      float lr_logits, float lr_scales, double wd, double beta1, double beta2,
+                      int next, const float *noise_next, uint64_t seed, uint32_t linear_id,
+                      uint32_t next_step, float tau_next, float kappa_next, const float *w_ref,
+                      float *w_out, void *w_terms, void *stream);
+
 /* Argmax decode of trained logits to uint8 codes [out_f][in_f] (first maximum wins;
  * local shift clipped to the grid; ternary: code 1 (value 0) where lm < 0, else 2 (+1) where
  * lb >= 0 and 0 (-1) where lb < 0). Replaces staged.py:300-314 (_Linear.hard_codes) and
@@ -394,6 +404,21 @@ int mckp_dp_f64_noalloc(const double *scores, const int64_t *step, int n_inst, i
  * [n][2] (lse_q, lse_r). The logit GEMMs and D E run through gsq_gemm (epi 4). */
 int gsq_kl_rows(const void *zq, const void *zr, int n, int V, int64_t ld, void *D, int64_t ld_d,
                 double *kl_rows, float *lse, void *stream);
+
+/* The RCO objective's KL head, forward and backward, over n rows in chunks of <= chunk rows:
+ * per chunk zq = bf16(h_q E^T) and zr = bf16(h_ref E^T) (tensor-core GEMMs, bf16-chain
+ * epilogue), kl_rows[r] = KL(p_ref || p_q) and D = bf16(q - p) (gsq_kl_rows), grad =
+ * bf16(D E) (tensor-core GEMM against ET); then total[0] = the float64 sum of kl_rows.
+ * h_q, h_ref bf16 [n][H]; E bf16 [V][H]; ET bf16 [H][ld_et] (E transposed); zq, zr, D bf16
+ * work buffers [chunk][V]; kl_rows float64 [n]; grad bf16 [n][H], the gradient of the sum (the
+ * mean's is grad / n: gsq_div_bf16). err: the GEMMs' device error word (zeroed by the caller,
+ * nonzero after a bounded wait gave up). H, V and ld_et multiples of 8, ld_et >= V. The
+ * launches and their order are those of the library's Python KL head (rco/kl.py).
+ * Replaces src/gsq_rco/common/evaluate.py:111-151 (kl_value_and_grad_hidden with its 64-row
+ * chunks, :28-33 the tied-embedding logits). */
+int kl_head_fwd_bwd(const void *h_q, const void *h_ref, int n, int H, const void *E,
+                    const void *ET, int64_t ld_et, int V, int chunk, void *zq, void *zr, void *D,
+                    double *kl_rows, double *total, void *grad, int *err, void *stream);
 
 /* w bf16 [out][in] = bf16(scales[r][c / gs] * grid[codes[r, c]]): a database candidate
  * assembled in the model dtype (src/gsq_rco/rco/database.py:244-256, allocate.py:117). */

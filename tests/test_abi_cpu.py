@@ -54,6 +54,18 @@ def test_bad_arguments_are_rejected_without_launch():
     assert lib.mckp_dp_f64_noalloc(fake, fake, 1, 168, 300, 100, fake, None) == _lib.GSQ_EINVAL
     assert lib.gptq_sweep(None, None, None, 4, 4, 3, 64, 128, 1, None, None, None,
                           None) == _lib.GSQ_EINVAL
+    # the KL head entry: null pointers, widths that are not multiples of 8, a short ET stride
+    kl = lambda *a: lib.kl_head_fwd_bwd(*a)
+    ok = [fake, fake, 40, 896, fake, fake, 151936, 151936, 32, fake, fake, fake, fake, fake,
+          fake, fake, None]
+    for i, bad in [(0, None), (4, None), (15, None), (3, 900), (7, 151930), (6, 151928),
+                   (8, 0), (2, 0)]:
+        args = list(ok)
+        args[i] = bad
+        assert kl(*args) == _lib.GSQ_EINVAL, (i, bad)
+    assert lib.gsq_soft_bwd_lion(None, None, None, None, None, None, None, 2, 4, 4, 64, 3, 1.0,
+                                 100.0, 1e-4, 5e-5, 1.0, 0.9, 0.95, 0, None, 0, 0, 0, 1.0, 1.0,
+                                 None, None, None, None) == _lib.GSQ_EINVAL
 
 
 def test_product_path_refuses_to_run_without_gpu():

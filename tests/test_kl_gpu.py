@@ -34,6 +34,32 @@ def test_kl_head_matches_oracle(V, n, chunk):
     assert float((gg == grad_o).double().mean()) >= 0.90
 
 
+def test_kl_head_c_entry_equals_python_head():
+    """kl_head_fwd_bwd (the KL head as one C-ABI call) against the Python KL head on the same
+    inputs: the same launches in the same order, so the same bits."""
+    from gsq_rco_mlx_b200 import _lib
+    from gsq_rco_mlx_b200.gemm import err_flag
+    from gsq_rco_mlx_b200.rco.kl import KLHead
+    V, n, chunk, H = 4096, 300, 128, 896
+    E, hq, hr = _case(V, n, H, seed=4)
+    head = KLHead(E.to(DEV), chunk=chunk)
+    hq, hr = hq.to(DEV), hr.to(DEV)
+    total, grad = head.kl_sum_and_grad(hq, hr)
+    zq = torch.empty(chunk, V, device=DEV, dtype=torch.bfloat16)
+    zr, D = torch.empty_like(zq), torch.empty_like(zq)
+    rows = torch.empty(n, device=DEV, dtype=torch.float64)
+    total_c = torch.empty(1, device=DEV, dtype=torch.float64)
+    grad_c = torch.empty(n, H, device=DEV, dtype=torch.bfloat16)
+    err = err_flag(torch.device(DEV))
+    _lib.call("kl_head_fwd_bwd", _lib.ptr(hq), _lib.ptr(hr), n, H, _lib.ptr(head.E),
+              _lib.ptr(head.ET.t[0]), head.ET.ld, V, chunk, _lib.ptr(zq), _lib.ptr(zr),
+              _lib.ptr(D), _lib.ptr(rows), _lib.ptr(total_c), _lib.ptr(grad_c), _lib.ptr(err),
+              _lib.stream_ptr())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(total_c, total) and torch.equal(grad_c, grad)
+
+
 def test_ste_dots_matches_oracle():
     from gsq_rco_mlx_b200.rco.kl import ste_dots
     rng = np.random.default_rng(3)
