@@ -34,6 +34,30 @@ def test_library_exports_every_declared_symbol():
     assert lib.gsq_status_string(1) == b"invalid argument"
 
 
+def declared_arities():
+    """{name: parameter count} of every function the headers declare (void lists count 0)."""
+    out = {}
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if not fn.endswith(".h"):
+            continue
+        text = re.sub(r"/\*.*?\*/", " ", open(os.path.join(ROOT, "include", fn)).read(),
+                      flags=re.S)
+        for m in re.finditer(r"^(?:int|const char \*)\s*(\w+)\(([^)]*)\);", text, flags=re.M):
+            params = m.group(2).strip()
+            out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every ctypes argument list in the package has as many entries as the declaration in
+    include/ has parameters (an ABI drift would pass wrong values silently)."""
+    arity = declared_arities()
+    assert len(arity) == len(declared_symbols())
+    for name, argtypes in _lib.SIGNATURES.items():
+        assert name in arity, name
+        assert len(argtypes) == arity[name], (name, len(argtypes), arity[name])
+
+
 def test_bad_arguments_are_rejected_without_launch():
     """Argument validation happens before any CUDA call (no device needed)."""
     lib = _lib.load()
